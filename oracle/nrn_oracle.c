@@ -1,0 +1,399 @@
+/*
+ * nrn_oracle.c -- CPU restatement of libnrn's per-timestep hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY (the checker).  The product never links or calls
+ * this file.  It is pinned against outputs of the reference itself, compiled
+ * from its own sources (oracle/Makefile, ref_harness.cpp), through the golden
+ * fixtures under tests/golden/.
+ *
+ * One step follows the phase order of the reference's sim_step
+ * (src/simulation/runner.cpp:95-173):
+ *   P1 zero the synaptic input of every population           (:99-104)
+ *   P2 deliver, for every projection, the spikes emitted d steps ago through
+ *      each synapse of delay d (the reference reads SpikeBuffer::read(1),
+ *      src/simulation/spike_buffer.cpp:32-49; per-synapse delays are the
+ *      extension the reference's ConnectivityTensor::delays declares but
+ *      sim_step never reads, runner.cpp:113)                 (:106-124)
+ *      + external drive (Philox; the reference has none)
+ *   P3 neuron update (oracle_common.h, one function per model)(:127-129)
+ *   P4 push spikes into the history                          (:131-139)
+ *   P5 pair STDP at slow-clock boundaries, src/plasticity/stdp.cpp:43-141,
+ *      restated per neuron trace (the reference's per-synapse traces are
+ *      identical along each row/column, stdp.cpp:118-128)    (:142-150)
+ *   P6 spike recording, ascending ids, src/monitor/spike_recorder.cpp:33-58
+ * Before the first step every population runs one update with dt = 0, as
+ * sim_create does (runner.cpp:36-38).
+ *
+ * Delivery sums each target's input in CSR order (projection, then source,
+ * then synapse); the reference sums per 64..256-wide block with BLAS sgemv.
+ * Both are fp32; they agree exactly when the weights are dyadic rationals
+ * whose partial sums are exact, and to rounding otherwise.
+ */
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+#include <math.h>
+
+#include "oracle_common.h"
+
+#define ORC_EXPORT __attribute__((visibility("default")))
+
+static int model_np(int model) {
+    return model == ORC_LIF ? ORC_NP_LIF : model == ORC_ADEX ? ORC_NP_ADEX : ORC_NP_IZH;
+}
+
+/* Parameter k of neuron i: per-neuron array when given, else uniform. */
+static inline float par(const orc_pop* P, int k, int i) {
+    return P->hp ? P->hp[(size_t)k * P->n + i] : (float)P->p[k];
+}
+
+typedef struct {
+    float* v;
+    float* aux;     /* w (AdEx) or u (Izh) */
+    float* ref;
+    float* ge;      /* conductances (AdEx with conductance input) */
+    float* gi;
+    int cond;       /* population receives conductance input */
+} pop_state;
+
+static void init_pop(const orc_pop* P, pop_state* S) {
+    int n = P->n;
+    S->v = (float*)calloc((size_t)n, sizeof(float));
+    S->aux = (float*)calloc((size_t)n, sizeof(float));
+    S->ref = (float*)calloc((size_t)n, sizeof(float));
+    S->ge = (float*)calloc((size_t)n, sizeof(float));
+    S->gi = (float*)calloc((size_t)n, sizeof(float));
+    for (int i = 0; i < n; ++i) {
+        float v0, a0 = 0.0f;
+        if (P->model == ORC_IZH) {
+            /* izh_create: v = v_init, u = b*v_init (double product, then
+             * float), src/neuron/izhikevich.cpp:45-46; v_init = -65. */
+            v0 = -65.0f;
+            a0 = (float)(P->p[1] * -65.0);
+        } else {
+            v0 = (float)P->p[0];   /* v_rest */
+        }
+        S->v[i] = P->init_v ? P->init_v[i] : v0;
+        S->aux[i] = P->init_aux ? P->init_aux[i] : a0;
+    }
+}
+
+static void free_pop(pop_state* S) {
+    free(S->v); free(S->aux); free(S->ref); free(S->ge); free(S->gi);
+}
+
+/* One update of population P with per-neuron inputs I[], conductance
+ * inputs ie[]/ii[] (may be NULL), step length dt; spk[] receives 0/1. */
+static void update_pop(const orc_pop* P, pop_state* S, const float* I,
+                       const float* ie, const float* ii, double dt, uint8_t* spk) {
+    int n = P->n;
+    float dtf = (float)dt;
+    if (P->model == ORC_LIF) {
+        for (int i = 0; i < n; ++i) {
+            spk[i] = (uint8_t)orc_lif_step(&S->v[i], &S->ref[i], I[i], dtf,
+                par(P, 0, i), par(P, 1, i), par(P, 2, i), par(P, 3, i),
+                par(P, 4, i), par(P, 5, i), par(P, 6, i));
+        }
+    } else if (P->model == ORC_ADEX) {
+        float dec_e = 1.0f, dec_i = 1.0f;
+        if (S->cond) {
+            dec_e = (float)exp(-dt / P->cond[0]);
+            dec_i = (float)exp(-dt / P->cond[1]);
+        }
+        for (int i = 0; i < n; ++i) {
+            float Ii = I[i];
+            if (S->cond) {
+                Ii = orc_cond_current(Ii, &S->ge[i], &S->gi[i], ie ? ie[i] : 0.0f,
+                                      ii ? ii[i] : 0.0f, dec_e, dec_i,
+                                      (float)P->cond[2], (float)P->cond[3], S->v[i]);
+            }
+            spk[i] = (uint8_t)orc_adex_step(&S->v[i], &S->aux[i], &S->ref[i], Ii, dtf,
+                par(P, 0, i), par(P, 1, i), par(P, 2, i), par(P, 3, i),
+                par(P, 5, i), par(P, 6, i), par(P, 7, i), par(P, 8, i),
+                par(P, 9, i), par(P, 10, i), par(P, 11, i), par(P, 12, i));
+        }
+    } else {
+        double dt_ms = dt * 1000.0;
+        float half = (float)(0.5 * dt_ms);
+        float dtm = (float)dt_ms;
+        for (int i = 0; i < n; ++i) {
+            spk[i] = (uint8_t)orc_izh_step(&S->v[i], &S->aux[i], I[i], half, dtm,
+                par(P, 0, i), par(P, 1, i), par(P, 2, i), par(P, 3, i), par(P, 4, i));
+        }
+    }
+}
+
+/* ------------------------------------------------------------------------ */
+/* Neuron-only run: per-step input currents, as the reference's neuron tests */
+/* call *_forward directly (tests/neuron/test_neuron_dynamics.cpp:24-232).   */
+/* ------------------------------------------------------------------------ */
+ORC_EXPORT int orc_neuron_run(const orc_pop* P, int steps, double dt,
+                              const float* I /* [steps][n] or NULL */,
+                              float* out_v, float* out_aux, float* out_ref,
+                              uint8_t* out_spike /* each [steps][n] or NULL */) {
+    pop_state S;
+    memset(&S, 0, sizeof(S));
+    init_pop(P, &S);
+    int n = P->n;
+    float* zero = (float*)calloc((size_t)n, sizeof(float));
+    uint8_t* spk = (uint8_t*)calloc((size_t)n, 1);
+    for (int t = 0; t < steps; ++t) {
+        const float* It = I ? I + (size_t)t * n : zero;
+        update_pop(P, &S, It, NULL, NULL, dt, spk);
+        size_t o = (size_t)t * n;
+        if (out_v) memcpy(out_v + o, S.v, (size_t)n * sizeof(float));
+        if (out_aux) memcpy(out_aux + o, S.aux, (size_t)n * sizeof(float));
+        if (out_ref) memcpy(out_ref + o, S.ref, (size_t)n * sizeof(float));
+        if (out_spike) memcpy(out_spike + o, spk, (size_t)n);
+    }
+    free(zero); free(spk); free_pop(&S);
+    return 0;
+}
+
+/* ------------------------------------------------------------------------ */
+/* Network run                                                              */
+/* ------------------------------------------------------------------------ */
+ORC_EXPORT int orc_net_run(const orc_net* net) {
+    int np = net->npop, nq = net->nproj;
+    int64_t N = 0;
+    for (int p = 0; p < np; ++p) {
+        if (net->pops[p].offset != N) return -1;   /* offsets must be dense */
+        N += net->pops[p].n;
+    }
+    int maxd = 1;
+    for (int q = 0; q < nq; ++q) {
+        const orc_proj* Q = &net->projs[q];
+        for (int64_t k = 0; k < Q->nnz; ++k) {
+            if (Q->delay[k] < 1) return -2;
+            if (Q->delay[k] > maxd) maxd = Q->delay[k];
+        }
+    }
+    int H = maxd + 1;
+
+    pop_state* S = (pop_state*)calloc((size_t)np, sizeof(pop_state));
+    for (int p = 0; p < np; ++p) init_pop(&net->pops[p], &S[p]);
+    for (int q = 0; q < nq; ++q) {
+        if (net->projs[q].receptor != ORC_RECV_CURRENT)
+            S[net->projs[q].tgt_pop].cond = 1;
+    }
+    for (int p = 0; p < np; ++p)
+        if (net->pops[p].drive_kind == ORC_DRIVE_POISSON_GEXC) S[p].cond = 1;
+
+    float* I = (float*)calloc((size_t)N, sizeof(float));
+    float* ie = (float*)calloc((size_t)N, sizeof(float));
+    float* ii = (float*)calloc((size_t)N, sizeof(float));
+    uint8_t* hist = (uint8_t*)calloc((size_t)H * N, 1);
+
+    /* Working copies of the weights and STDP traces. */
+    float** W = (float**)calloc((size_t)(nq > 0 ? nq : 1), sizeof(float*));
+    float** xpre = (float**)calloc((size_t)(nq > 0 ? nq : 1), sizeof(float*));
+    float** xpost = (float**)calloc((size_t)(nq > 0 ? nq : 1), sizeof(float*));
+    for (int q = 0; q < nq; ++q) {
+        const orc_proj* Q = &net->projs[q];
+        W[q] = (float*)malloc((size_t)(Q->nnz > 0 ? Q->nnz : 1) * sizeof(float));
+        memcpy(W[q], Q->w, (size_t)Q->nnz * sizeof(float));
+        if (Q->plastic) {
+            xpre[q] = (float*)calloc((size_t)net->pops[Q->src_pop].n, sizeof(float));
+            xpost[q] = (float*)calloc((size_t)net->pops[Q->tgt_pop].n, sizeof(float));
+        }
+    }
+
+    /* sim_create: one update with dt = 0 and zero input; not recorded. */
+    for (int p = 0; p < np; ++p) {
+        const orc_pop* P = &net->pops[p];
+        update_pop(P, &S[p], I + P->offset, ie + P->offset, ii + P->offset, 0.0,
+                   hist + P->offset /* scratch, cleared below */);
+    }
+    memset(hist, 0, (size_t)H * N);
+
+    int64_t nspk = 0;
+    int slow = net->slow_ratio > 0 ? net->slow_ratio : 1;
+    for (int t = 0; t < net->steps; ++t) {
+        /* P1 */
+        memset(I, 0, (size_t)N * sizeof(float));
+        memset(ie, 0, (size_t)N * sizeof(float));
+        memset(ii, 0, (size_t)N * sizeof(float));
+        /* P2: arrival-time delivery with the weights as they are now. */
+        for (int q = 0; q < nq; ++q) {
+            const orc_proj* Q = &net->projs[q];
+            int so = net->pops[Q->src_pop].offset, to = net->pops[Q->tgt_pop].offset;
+            float* acc = Q->receptor == ORC_RECV_CURRENT ? I
+                       : Q->receptor == ORC_RECV_GEXC ? ie : ii;
+            for (int64_t k = 0; k < Q->nnz; ++k) {
+                int d = Q->delay[k];
+                if (t - d < 0) continue;
+                if (hist[(size_t)((t - d) % H) * N + so + Q->src[k]])
+                    acc[to + Q->tgt[k]] += W[q][k];
+            }
+        }
+        /* external drive */
+        for (int p = 0; p < np; ++p) {
+            const orc_pop* P = &net->pops[p];
+            if (P->drive_kind == ORC_DRIVE_NONE) continue;
+            float d0 = (float)P->drive[0], d1 = (float)P->drive[1];
+            float en = (float)exp(-P->drive[0]);
+            float* dst = P->drive_kind == ORC_DRIVE_POISSON_GEXC ? ie : I;
+            for (int i = 0; i < P->n; ++i) {
+                uint32_t gid = (uint32_t)(P->offset + i);
+                dst[gid] += orc_drive_value(P->drive_kind, d0, d1, en, net->seed, gid,
+                                            (uint32_t)t);
+            }
+        }
+        /* P3 + P4 */
+        uint8_t* h = hist + (size_t)(t % H) * N;
+        for (int p = 0; p < np; ++p) {
+            const orc_pop* P = &net->pops[p];
+            update_pop(P, &S[p], I + P->offset, ie + P->offset, ii + P->offset,
+                       net->dt, h + P->offset);
+        }
+        /* P5: STDP (stdp.cpp:43-141), every synapse, every slow boundary. */
+        if (t % slow == 0) {
+            for (int q = 0; q < nq; ++q) {
+                const orc_proj* Q = &net->projs[q];
+                if (!Q->plastic) continue;
+                const orc_pop* Ps = &net->pops[Q->src_pop];
+                const orc_pop* Pt = &net->pops[Q->tgt_pop];
+                const uint8_t* pre = h + Ps->offset;
+                const uint8_t* post = h + Pt->offset;
+                float dpre = (float)exp(-net->dt / Q->stdp[0]);
+                float dpost = (float)exp(-net->dt / Q->stdp[1]);
+                float ap = (float)Q->stdp[2];
+                float am = (float)fabs(Q->stdp[3]);
+                float wmin = (float)Q->stdp[4], wmax = (float)Q->stdp[5];
+                float lr = (float)Q->stdp[6];
+                for (int j = 0; j < Ps->n; ++j)
+                    xpre[q][j] = xpre[q][j] * dpre + (float)pre[j];
+                for (int i = 0; i < Pt->n; ++i)
+                    xpost[q][i] = xpost[q][i] * dpost + (float)post[i];
+                for (int64_t k = 0; k < Q->nnz; ++k) {
+                    int j = Q->src[k], i = Q->tgt[k];
+                    float dw = (ap * xpre[q][j]) * (float)post[i]
+                             - (am * xpost[q][i]) * (float)pre[j];
+                    float wn = W[q][k] + ((dw * lr) * 1.0f) * 1.0f;
+                    if (wn < wmin) wn = wmin;
+                    if (wn > wmax) wn = wmax;
+                    W[q][k] = wn;
+                }
+            }
+        }
+        /* P6 */
+        for (int64_t g = 0; g < N; ++g) {
+            if (!h[g]) continue;
+            if (nspk < net->spike_cap) {
+                net->spike_step[nspk] = t;
+                net->spike_id[nspk] = (int32_t)g;
+            }
+            ++nspk;
+        }
+        if (net->trace_n > 0 && net->trace_v) {
+            for (int k = 0; k < net->trace_n; ++k) {
+                int32_t g = net->trace_ids[k];
+                int p = 0;
+                while (p + 1 < np && net->pops[p + 1].offset <= g) ++p;
+                net->trace_v[(size_t)t * net->trace_n + k] = S[p].v[g - net->pops[p].offset];
+            }
+        }
+    }
+    if (net->n_spikes) *net->n_spikes = nspk;
+
+    for (int p = 0; p < np; ++p) {
+        const orc_pop* P = &net->pops[p];
+        if (net->final_v) memcpy(net->final_v + P->offset, S[p].v, (size_t)P->n * 4);
+        if (net->final_aux) memcpy(net->final_aux + P->offset, S[p].aux, (size_t)P->n * 4);
+        if (net->final_ref) memcpy(net->final_ref + P->offset, S[p].ref, (size_t)P->n * 4);
+    }
+    for (int q = 0; q < nq; ++q) {
+        const orc_proj* Q = &net->projs[q];
+        if (Q->w_out) memcpy(Q->w_out, W[q], (size_t)Q->nnz * sizeof(float));
+        free(W[q]); free(xpre[q]); free(xpost[q]);
+    }
+    free(W); free(xpre); free(xpost);
+    for (int p = 0; p < np; ++p) free_pop(&S[p]);
+    free(S); free(I); free(ie); free(ii); free(hist);
+    return nspk > net->spike_cap ? 1 : 0;
+}
+
+/* ------------------------------------------------------------------------ */
+/* Connectivity generators (the reference has Erdos-Renyi only,             */
+/* src/connectivity/topology/random.cpp:25-95; fixed in/out-degree are      */
+/* defined here and on the device with the same Philox stream).             */
+/*                                                                          */
+/* Draw for (target i, slot k) of projection `proj`:                        */
+/*   words = Philox(seed; c0 = tgt_offset + i, c1 = k, c2 = proj,           */
+/*                  c3 = ORC_STREAM_CONN)                                   */
+/*   source = (w0 * m) >> 32, m = n_src (or n_src-1 without autapses, the   */
+/*            draw then skipping the target's own index)                    */
+/*   delay  = dmin + ((w1 * (dmax-dmin+1)) >> 32)                           */
+/*   weight = w_lo + w_span * u01(w2)                                       */
+/* Fixed out-degree swaps the roles: c0 = src_offset + j draws targets.     */
+/* Synapses are emitted in source-major order, ties kept in (i, k) order    */
+/* (a stable sort by source).                                               */
+/* ------------------------------------------------------------------------ */
+static inline void conn_words(uint64_t seed, uint32_t c0, uint32_t c1, uint32_t c2,
+                              uint32_t w[4]) {
+    w[0] = c0; w[1] = c1; w[2] = c2; w[3] = ORC_STREAM_CONN;
+    orc_philox4x32_10(w, (uint32_t)seed, (uint32_t)(seed >> 32));
+}
+
+ORC_EXPORT int64_t orc_gen_fixed_degree(
+    int out_degree_mode, uint64_t seed, uint32_t proj,
+    int32_t n_src, int32_t src_offset, int32_t n_tgt, int32_t tgt_offset,
+    int32_t degree, int autapses_excluded, int32_t dmin, int32_t dmax,
+    float w_lo, float w_span,
+    int32_t* out_src, int32_t* out_tgt, float* out_w, uint8_t* out_delay) {
+    int64_t total = (int64_t)(out_degree_mode ? n_src : n_tgt) * degree;
+    int32_t* s = (int32_t*)malloc((size_t)total * 4);
+    int32_t* tg = (int32_t*)malloc((size_t)total * 4);
+    float* ww = (float*)malloc((size_t)total * 4);
+    uint8_t* dd = (uint8_t*)malloc((size_t)total);
+    int32_t span = dmax - dmin + 1;
+    int same = autapses_excluded && (n_src == n_tgt) && (src_offset == tgt_offset);
+    int64_t e = 0;
+    int32_t nrow = out_degree_mode ? n_src : n_tgt;
+    int32_t ncol = out_degree_mode ? n_tgt : n_src;
+    int32_t roff = out_degree_mode ? src_offset : tgt_offset;
+    for (int32_t r = 0; r < nrow; ++r) {
+        for (int32_t k = 0; k < degree; ++k) {
+            uint32_t w[4];
+            conn_words(seed, (uint32_t)(roff + r), (uint32_t)k, proj, w);
+            uint32_t m = (uint32_t)(same ? ncol - 1 : ncol);
+            uint32_t c = (uint32_t)(((uint64_t)w[0] * m) >> 32);
+            if (same && c >= (uint32_t)r) c += 1;
+            uint32_t d = (uint32_t)dmin + (uint32_t)(((uint64_t)w[1] * (uint32_t)span) >> 32);
+            float wt = w_lo + w_span * orc_u01(w[2]);
+            if (out_degree_mode) { s[e] = r; tg[e] = (int32_t)c; }
+            else { s[e] = (int32_t)c; tg[e] = r; }
+            ww[e] = wt; dd[e] = (uint8_t)d;
+            ++e;
+        }
+    }
+    /* stable counting sort by source */
+    int64_t* cnt = (int64_t*)calloc((size_t)n_src + 1, sizeof(int64_t));
+    for (int64_t k = 0; k < total; ++k) cnt[s[k] + 1]++;
+    for (int32_t j = 0; j < n_src; ++j) cnt[j + 1] += cnt[j];
+    for (int64_t k = 0; k < total; ++k) {
+        int64_t pos = cnt[s[k]]++;
+        out_src[pos] = s[k]; out_tgt[pos] = tg[k]; out_w[pos] = ww[k]; out_delay[pos] = dd[k];
+    }
+    free(cnt); free(s); free(tg); free(ww); free(dd);
+    return total;
+}
+
+/* Drive samples, for checking the device RNG. */
+ORC_EXPORT void orc_drive_values(int kind, double d0, double d1, uint64_t seed,
+                                 int32_t offset, int32_t n, int32_t step, float* out) {
+    float en = (float)exp(-d0);
+    for (int i = 0; i < n; ++i)
+        out[i] = orc_drive_value(kind, (float)d0, (float)d1, en, seed,
+                                 (uint32_t)(offset + i), (uint32_t)step);
+}
+
+ORC_EXPORT void orc_philox(uint64_t seed, uint32_t c0, uint32_t c1, uint32_t c2,
+                           uint32_t c3, uint32_t* out4) {
+    out4[0] = c0; out4[1] = c1; out4[2] = c2; out4[3] = c3;
+    orc_philox4x32_10(out4, (uint32_t)seed, (uint32_t)(seed >> 32));
+}
+
+ORC_EXPORT float orc_normal_from_words(uint32_t a, uint32_t b) {
+    return orc_normal(orc_u01(a), orc_u01(b));
+}
