@@ -1,0 +1,67 @@
+"""Realises a workload spec (libnrn_b200.workloads) as an oracle network:
+host-generated synapse lists (oracle generator, same Philox counters as the
+device generator) and per-neuron arrays."""
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+from libnrn_b200 import workloads as W  # noqa: E402
+from oracle import oracle as O  # noqa: E402
+
+
+def gen_args(spec: dict, q: dict):
+    """Arguments of the fixed-degree generator for projection q."""
+    ps, pt = spec["pops"][q["src"]], spec["pops"][q["tgt"]]
+    g = q["gen"]
+    out = g["mode"] == "out"
+    if out:
+        if g.get("cols") == "all":
+            col_off, col_n = 0, spec["n_total"]
+        else:
+            col_off, col_n = pt["offset"], pt["n"]
+        args = (spec["seed"], g["id"], ps["n"], ps["offset"], col_n, col_off, g["degree"])
+    else:
+        args = (spec["seed"], g["id"], ps["n"], ps["offset"], pt["n"], pt["offset"], g["degree"])
+    kw = dict(out_degree=out, no_autapses=True, dmin=g["dmin"], dmax=g["dmax"],
+              w_lo=g["w_lo"], w_span=g["w_span"], keep=(pt["offset"], pt["offset"] + pt["n"]))
+    return args, kw
+
+
+def realize(spec: dict, *, steps=None, trace_ids=None) -> dict:
+    net = {"steps": steps if steps is not None else spec["steps"], "dt": spec["dt"],
+           "seed": spec["seed"], "slow_ratio": spec.get("slow_ratio", 1), "pops": [], "projs": []}
+    for p in spec["pops"]:
+        arr = W.population_arrays(spec, p)
+        net["pops"].append({"model": p["model"], "n": p["n"], "params": p["params"],
+                            "drive": p.get("drive"), "cond": p.get("cond"),
+                            "init_v": arr["init_v"], "init_aux": arr["init_aux"], "hp": arr["hp"]})
+    for q in spec["projs"]:
+        args, kw = gen_args(spec, q)
+        s, t, w, d = O.gen_fixed_degree(*args, **kw)
+        net["projs"].append({"src": q["src"], "tgt": q["tgt"], "receptor": q["receptor"],
+                             "src_idx": s, "tgt_idx": t, "w": w, "delay": d,
+                             "plastic": q.get("plastic", False),
+                             "stdp": q.get("stdp", [0.02, 0.02, 0.01, -0.012, 0.0, 1.0, 1.0])})
+    if trace_ids is not None:
+        net["trace_ids"] = list(trace_ids)
+    return net
+
+
+def small_brunel(stdp=True, steps=400, slow_ratio=1, seed=11):
+    return W.brunel(800, 200, 80, 20, steps=steps, stdp=stdp, seed=seed, slow_ratio=slow_ratio)
+
+
+def small_adex(steps=300, seed=12):
+    # in-degree scaled 1000 -> 50; weights scaled to keep k*w
+    return W.adex_cond(500, 50, steps=steps, seed=seed, w_exc=0.5e-9 * 6, w_inh=2.5e-9 * 6)
+
+
+def small_izh(steps=300, seed=13):
+    return W.izhikevich(500, 50, steps=steps, seed=seed, w_scale=20.0)
