@@ -1,0 +1,313 @@
+"""Benchmark: synaptic events/s, neuron updates/s and real-time factor of the
+per-timestep simulation loop on B200.
+
+Workload (default): the Brunel balanced LIF network with pair STDP on E->E,
+1,048,576 neurons per GPU (838,860 E + 209,716 I), fixed in-degree 1,000 E +
+250 I (1.31e9 synapses per GPU), delay 15 steps, dt 0.1 ms, Poisson drive at
+2 nu_thr, weights clipped to [0, 2J].  Connectivity is generated on the GPU
+from Philox (synthetic, seeded).  One bench step = one simulation timestep.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload brunel_stdp|brunel|adex|izh]
+
+Prints one JSON line (rank 0).  `value` is delivered synaptic events per
+second over the timed steps with the network resident in HBM; `e2e` is the
+same run through the C ABI with the initial state uploaded from pinned host
+memory and the spike raster downloaded, inside the timed region.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p, "measured"
+    except Exception:
+        return PEAKS_FALLBACK, "fallback"
+
+
+def workload_spec(name: str, world: int, steps: int):
+    from libnrn_b200 import workloads as W
+    if name == "brunel_stdp":
+        return W.brunel_stdp_per_gpu(world, steps=steps)
+    if name == "brunel":
+        return W.brunel(10_000 * world, 2_500 * world, 1_000, 250, steps=steps)
+    if name == "adex":
+        return W.adex_cond(1_048_576 * world, 1_000, steps=steps)
+    if name == "izh":
+        return W.izhikevich(1_000_000 * world, 1_000, steps=steps)
+    raise SystemExit(f"unknown workload {name}")
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        mhz, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            try:
+                mhz.append(float(r[1]))
+                mx = float(r[2])
+                for k, nm in enumerate(names):
+                    if r[5 + k].lower().startswith("active"):
+                        reasons.add(nm)
+            except Exception:
+                continue
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(mhz)}
+
+
+def cpu_reference(args, world_steps_hint=None):
+    """The reference implementation (compiled from its sources into
+    oracle/_ref) on a bounded sample of the workload, all host threads."""
+    sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+    import numpy as np
+    from libnrn_b200 import workloads as W
+    from oracle import oracle as O
+    import specs as S
+
+    threads = os.cpu_count() or 1
+    steps = int(os.environ.get("NRN_CPU_SAMPLE_STEPS", "30"))
+    if args.workload in ("brunel_stdp", "brunel"):
+        spec = W.brunel(10_000, 2_500, 1_000, 250, steps=steps, stdp=args.workload == "brunel_stdp")
+        sample = (f"Brunel LIF 10,000 E + 2,500 I, in-degree 1,000 + 250, delay 15, "
+                  f"{'STDP on E->E, ' if args.workload == 'brunel_stdp' else ''}{steps} steps, block 256")
+    elif args.workload == "adex":
+        spec = W.adex_cond(16_384, 1_000, steps=steps)
+        sample = f"AdEx conductance network 16,384 neurons, in-degree 1,000, {steps} steps, block 256"
+    else:
+        spec = W.izhikevich(16_000, 1_000, dt=1e-3, steps=steps)
+        sample = f"Izhikevich 16,000 neurons, out-degree 1,000, {steps} steps, block 256"
+    net = S.realize(spec)
+    net["threads"] = threads
+    kind = "reference" if O.reference_available() else "port"
+    t0 = time.perf_counter()
+    if kind == "reference":
+        res = O.run_reference(net, block=256)
+        elapsed = res["elapsed_s"]
+    else:
+        res = O.run_oracle(net)
+        elapsed = time.perf_counter() - t0
+    # delivered events: spikes whose delay has elapsed within the sample
+    n_total = spec["n_total"]
+    outdeg = np.zeros(n_total, np.int64)
+    delay_of = {}
+    for q, p in zip(net["projs"], spec["projs"]):
+        off = spec["pops"][p["src"]]["offset"]
+        np.add.at(outdeg, q["src_idx"] + off, 1)
+        delay_of[p["src"]] = int(q["delay"].min()) if len(q["delay"]) else 1
+    dmin = min(delay_of.values()) if delay_of else 1
+    st, gid = res["spike_step"], res["spike_id"]
+    ev = int(outdeg[gid[st + dmin < steps]].sum())
+    return {
+        "events_per_s": ev / elapsed, "neuron_updates_per_s": n_total * steps / elapsed,
+        "rtf": elapsed / (steps * spec["dt"]), "elapsed_s": elapsed, "cores": threads, "kind": kind,
+        "sample": sample,
+    }
+
+
+def run_reference_arm(args, rank: int):
+    if rank != 0:
+        return
+    r = cpu_reference(args)
+    line = {
+        "impl": "reference", "metric": "synaptic_events_per_s", "value": r["events_per_s"],
+        "unit": "events/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": True, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.workload + " (bounded CPU sample)"},
+        "neuron_updates_per_s": r["neuron_updates_per_s"], "rtf": r["rtf"],
+        "cpu_baseline": {"value": r["events_per_s"], "unit": "events/s", "cores": r["cores"],
+                         "kind": r["kind"], "sample": r["sample"]},
+        "e2e": {"value": r["events_per_s"], "unit": "events/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10_000)
+    ap.add_argument("--warmup", type=int, default=200)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="brunel_stdp", choices=["brunel_stdp", "brunel", "adex", "izh"])
+    ap.add_argument("--chunk", type=int, default=0)
+    ap.add_argument("--profile-steps", type=int, default=300)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        run_reference_arm(args, rank)
+        return
+    if world > 1:
+        raise SystemExit("multi-GPU runs are launched through torchrun; see the partitioned engine")
+
+    import numpy as np
+    import torch
+
+    from libnrn_b200.engine import Network
+
+    peaks, peaks_kind = load_peaks()
+    torch.cuda.set_device(local)
+    spec = workload_spec(args.workload, 1, args.steps)
+    t_setup = time.perf_counter()
+    nw = Network.from_spec(spec, device=local, record=True)
+    torch.cuda.synchronize()
+    setup_s = time.perf_counter() - t_setup
+    nnz = sum(p["nnz"] for p in nw.projs)
+    n_total = spec["n_total"]
+    stream = torch.cuda.ExternalStream(nw.stream())
+
+    nw.run(args.warmup, args.chunk)
+    nw.sync()
+    nw.raster()
+    s0, e0 = nw.counters()
+    with ClockSampler(local) as clk:
+        ev_a = torch.cuda.Event(enable_timing=True)
+        ev_b = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        ev_a.record(stream)
+        nw.run(args.steps, args.chunk)
+        ev_b.record(stream)
+        torch.cuda.synchronize()
+    ms = ev_a.elapsed_time(ev_b)
+    s1, e1 = nw.counters()
+    st, gid = nw.raster()
+    events = e1 - e0
+    spikes = s1 - s0
+    sec = ms / 1e3
+    value = events / sec
+
+    # Per-kernel device times (eager launches, events around each phase).
+    ps0, pe0 = nw.counters()
+    prof = nw.profile(args.profile_steps)
+    ps1, pe1 = nw.counters()
+    nw.raster()
+    ev_p, sp_p = pe1 - pe0, ps1 - ps0
+    phases = {"deliver": prof[0], "neuron": prof[1], "stdp": prof[2]}
+    # algorithmic bytes: delivery 8 B per event (target + weight)
+    # + 16 B per (spike, delay) segment; neuron update 28 B per LIF neuron
+    # (+ drive computed in-kernel); STDP per step: traces 12 B per neuron,
+    # pre rows 12 B per synapse, post in-lists 16 B per synapse.
+    deliver_bytes = 8.0 * ev_p + 16.0 * sp_p * 4
+    dom = max(phases, key=phases.get)
+    alg = {"deliver": deliver_bytes, "neuron": 28.0 * n_total * args.profile_steps}
+    achieved = alg.get("deliver") / (phases["deliver"] / 1e3) / 1e9 if phases["deliver"] > 0 else 0.0
+
+    # e2e: initial state from pinned host, run, raster to host, all timed.
+    host_state = []
+    for p in nw.pops:
+        for k in ("v", "ref"):
+            t = p[k]
+            if t is not None:
+                host_state.append((t, t.cpu().pin_memory()))
+    h2d = sum(h.numel() * 4 for _, h in host_state)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    with torch.cuda.stream(stream):
+        for dev_t, h in host_state:
+            dev_t.copy_(h, non_blocking=True)
+    e_s0, e_e0 = nw.counters()
+    nw.run(args.steps, args.chunk)
+    st2, gid2 = nw.raster()
+    e_s1, e_e1 = nw.counters()
+    t1 = time.perf_counter()
+    d2h = len(gid2) * 8
+    e2e = (e_e1 - e_e0) / (t1 - t0)
+
+    cpu = None
+    if not args.no_cpu:
+        try:
+            cpu = cpu_reference(args)
+        except Exception as ex:  # report, do not fail the GPU line
+            cpu = {"error": str(ex)[:200]}
+
+    clocks = clk.summary()
+    kernels_per_step = 1 + len(nw.pops) + 2 * sum(1 for q in spec["projs"] if q.get("plastic"))
+    chunk = args.chunk if args.chunk > 0 else min(args.steps, 50)
+    line = {
+        "metric": "synaptic_events_per_s", "value": value, "unit": "events/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (Philox-generated connectivity and drive)",
+        "config": {"workload": args.workload, "neurons": n_total, "synapses": nnz,
+                   "dt_ms": spec["dt"] * 1e3, "l2": "inputs larger than L2 (synapse store "
+                   f"{nnz * 8 / 1e9:.1f} GB)", "parallelism": "single GPU"},
+        "neuron_updates_per_s": n_total * args.steps / sec,
+        "rtf": sec / (args.steps * spec["dt"]),
+        "spikes": int(spikes), "rate_hz": spikes / n_total / (args.steps * spec["dt"]),
+        "setup_s": setup_s,
+        "gpu_launches": kernels_per_step * args.steps + (args.steps + chunk - 1) // chunk,
+        "phase_ms_per_step": {k: v / args.profile_steps for k, v in phases.items()},
+        "roofline": {"kernel": "deliver", "dominant_phase": dom, "bound": "hbm", "achieved": achieved,
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
+                     "peak_kind": peaks_kind, "traffic": None},
+        "e2e": {"value": e2e, "unit": "events/s", "h2d_bytes_per_step": h2d / args.steps,
+                "d2h_bytes_per_step": d2h / args.steps},
+        "clocks": clocks,
+    }
+    if cpu is not None:
+        if "error" in cpu:
+            line["cpu_baseline"] = cpu
+        else:
+            line["cpu_baseline"] = {"value": cpu["events_per_s"], "unit": "events/s", "cores": cpu["cores"],
+                                    "kind": cpu["kind"], "sample": cpu["sample"],
+                                    "neuron_updates_per_s": cpu["neuron_updates_per_s"], "rtf": cpu["rtf"]}
+    nw.close()
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

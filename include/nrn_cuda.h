@@ -1,0 +1,320 @@
+/*
+ * nrn_cuda.h -- C ABI of libnrn_b200's device layer (libnrn_cuda.so).
+ *
+ * The B200 engine for libnrn's per-timestep simulation hot path.  Plain C:
+ * raw device pointers, sizes, plain structs and CUDA streams; no C++ or
+ * LibTorch types cross this boundary.  Every entry point returns an
+ * nrn_status_t; nrn_last_error() gives the message of the last failure on
+ * the calling thread.
+ *
+ * Two levels:
+ *
+ *  1. Kernel entry points (stateless, enqueue on the given stream):
+ *       nrn_cuda_pop_step     one fused neuron update of a population
+ *                             (replaces the reference's internal
+ *                             nrn::neuron::cuda::{lif,adex,izhikevich}_forward_cuda,
+ *                             declared in src/neuron/lif.cpp:7-21,
+ *                             src/neuron/adex.cpp:7-28,
+ *                             src/neuron/izhikevich.cpp:7-19)
+ *       nrn_cuda_deliver      event-driven spike delivery through a
+ *                             source-major CSR (replaces the per-block
+ *                             torch::mv loop of connection_deliver,
+ *                             src/connectivity/connect.cpp:36-79, and the stub
+ *                             launch_synaptic_current_block_dense,
+ *                             src/synapse/kernels/synapse_kernels.cu:56-79)
+ *       nrn_cuda_stdp_*       pair STDP (src/plasticity/stdp.cpp:43-141)
+ *       nrn_cuda_bsr_spmm     batched-trial block-sparse product on the
+ *                             tensor cores (the stub's intended block-dense
+ *                             matmul, synapse_kernels.cu:30-51, for many trials)
+ *
+ *  2. Engine entry points (a network resident on one GPU, stepped in CUDA
+ *     graphs), which the C++ nrn:: layer's sim_create/sim_step/sim_run
+ *     (src/simulation/runner.cpp:17-173) drive:
+ *       nrn_engine_create / _add_population / _add_projection /
+ *       _set_stdp / _finalize / _run / _sync / _raster / _weights / _destroy
+ *
+ * Spike semantics follow the reference's sim_step: a spike emitted at step s
+ * through a synapse of delay d is added to the target's input at step s + d,
+ * before the target's update of that step (SpikeBuffer::read(d),
+ * src/simulation/spike_buffer.cpp:32-49).
+ */
+#ifndef NRN_CUDA_H
+#define NRN_CUDA_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define NRN_API __attribute__((visibility("default")))
+#else
+#define NRN_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* A CUDA stream (cudaStream_t); NULL is the legacy default stream. */
+typedef struct CUstream_st* nrn_stream_t;
+
+typedef enum {
+    NRN_OK = 0,
+    NRN_ERR_INVALID = 1,      /* bad argument (reference: TORCH_CHECK failure) */
+    NRN_ERR_CUDA = 2,         /* CUDA runtime error                             */
+    NRN_ERR_OOM = 3,          /* device allocation failed                       */
+    NRN_ERR_CAPACITY = 4,     /* a fixed-capacity buffer overflowed             */
+    NRN_ERR_UNSUPPORTED = 5,  /* no device / wrong architecture                 */
+    NRN_ERR_COMM = 6,         /* collective (NCCL) failure                      */
+    NRN_ERR_TIMEOUT = 7,      /* a bounded device-side wait gave up             */
+    NRN_ERR_STATE = 8         /* call out of order (e.g. run before finalize)   */
+} nrn_status_t;
+
+NRN_API const char* nrn_status_string(nrn_status_t s);
+NRN_API const char* nrn_last_error(void);
+/* Library version "major.minor.patch" and the compiled device architecture. */
+NRN_API const char* nrn_version(void);
+
+/* ------------------------------------------------------------------------ */
+/* Neuron models                                                            */
+/* ------------------------------------------------------------------------ */
+
+enum { NRN_MODEL_LIF = 0, NRN_MODEL_ADEX = 1, NRN_MODEL_IZH = 2 };
+
+/* Parameter slots (param[] / uniform[] below), in the reference's option
+ * order (include/nrn/neuron/options.h):
+ *   LIF : 0 v_rest 1 v_thresh 2 v_reset 3 tau_m 4 tau_ref 5 c_m 6 i_bg
+ *   AdEx: 0 v_rest 1 v_thresh 2 v_reset 3 v_peak 4 tau_m 5 tau_w 6 tau_ref
+ *         7 c_m 8 g_l 9 a 10 b 11 delta_t 12 i_bg
+ *   Izh : 0 a 1 b 2 c 3 d 4 v_peak                                          */
+#define NRN_MAX_PARAMS 13
+
+/* External drive drawn on the device per (neuron, step) from Philox4x32-10
+ * keyed by (seed; global id, step, 0, 0x44524956). */
+enum {
+    NRN_DRIVE_NONE = 0,
+    NRN_DRIVE_POISSON_CURRENT = 1,   /* i_syn += amp * Poisson(lambda)          */
+    NRN_DRIVE_GAUSS_CURRENT = 2,     /* i_syn += mean + std * N(0,1)            */
+    NRN_DRIVE_POISSON_GEXC = 3       /* gin_exc += amp * Poisson(lambda)        */
+};
+
+typedef struct {
+    int32_t kind;
+    float p0;            /* lambda per step (Poisson) or mean (Gauss)        */
+    float p1;            /* amplitude (Poisson) or standard deviation        */
+    uint64_t seed;
+} nrn_drive_t;
+
+/* One update of a population: reads the input, integrates one step, writes
+ * the spike flags and appends the ids of spiking neurons.  Operation order
+ * and rounding follow the reference's CPU path (each operation rounded to
+ * fp32, no fused multiply-add), so LIF and Izhikevich agree bit for bit and
+ * AdEx to the last-bit difference of exp. */
+typedef struct {
+    int32_t model;
+    int32_t n;
+    int32_t gid_offset;        /* global id of neuron 0 (drive counter)     */
+    int32_t pad0;
+    double dt;                 /* seconds; 0 performs the initialising update */
+    float* v;                  /* [n] membrane potential                    */
+    float* aux;                /* [n] w (AdEx) / u (Izh); NULL for LIF      */
+    float* refractory;         /* [n] remaining refractory time; NULL (Izh) */
+    float* spike;              /* [n] 0/1 output, or NULL                   */
+    float* i_syn;              /* [n] input current, read then zeroed; NULL = 0 */
+    /* conductance input (AdEx only; all NULL for current-based input) */
+    float* g_exc;              /* [n] conductance state                      */
+    float* g_inh;
+    float* gin_exc;            /* [n] conductance input this step, read then zeroed */
+    float* gin_inh;
+    float tau_syn_exc, tau_syn_inh, e_exc, e_inh;
+    const float* param[NRN_MAX_PARAMS];   /* per-neuron arrays, or NULL      */
+    float uniform[NRN_MAX_PARAMS];        /* used where param[k] is NULL     */
+    nrn_drive_t drive;
+    int64_t step;              /* absolute step index (drive counter)       */
+    const int64_t* step_base;  /* if non-NULL, the step is *step_base + step */
+    int32_t* spike_ids;        /* compacted local ids of spiking neurons, or NULL */
+    int32_t* spike_count;      /* [1] incremented by the number appended    */
+    /* When hist_depth > 0, spike_ids/spike_count are the bases of a spike
+     * history ring (nrn_spike_hist_t): the ids go to slot step % hist_depth,
+     * i.e. spike_ids + slot * hist_cap and spike_count + slot. */
+    int32_t hist_depth;
+    int32_t hist_cap;
+    /* spike raster (the reference's spike recorder, src/monitor/spike_recorder.cpp):
+     * if raster_gid is non-NULL every spike is also appended as (step, global id);
+     * entries past raster_cap are counted but not written. */
+    int32_t* raster_step;
+    int32_t* raster_gid;
+    unsigned long long* raster_count;
+    int64_t raster_cap;
+} nrn_pop_step_t;
+
+NRN_API nrn_status_t nrn_cuda_pop_step(const nrn_pop_step_t* a, nrn_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Spike delivery                                                           */
+/* ------------------------------------------------------------------------ */
+
+/* Compacted spike history of one population: ring of depth `depth` steps,
+ * slot s % depth holding the local ids of the neurons that spiked at s. */
+typedef struct {
+    int32_t* ids;              /* [depth][cap]                              */
+    int32_t* count;            /* [depth]                                   */
+    int32_t cap;
+    int32_t depth;
+} nrn_spike_hist_t;
+
+/* A projection on the device: synapses sorted by (source, delay); the
+ * synapses of source j with delay dmin + k are [seg_ptr[j*nd+k], seg_ptr[j*nd+k+1]). */
+typedef struct {
+    int32_t n_src;
+    int32_t n_tgt;
+    int32_t dmin;              /* smallest delay, steps (>= 1)              */
+    int32_t nd;                /* number of delay values dmin .. dmin+nd-1  */
+    int32_t src_hist;          /* index of the source's nrn_spike_hist_t    */
+    int32_t pad0;
+    const int64_t* seg_ptr;    /* [n_src*nd + 1]                            */
+    const uint32_t* tgt;       /* [nnz] local target index                  */
+    const float* w;            /* [nnz] weight                              */
+    const float* mod;          /* [nnz] modulatory gain, or NULL (all 1)    */
+    float* acc;                /* [n_tgt] target input accumulator          */
+} nrn_proj_t;
+
+#define NRN_MAX_PROJ 32
+#define NRN_MAX_POPS 32
+
+/* Delivers, for every projection, the spikes emitted at step - d through the
+ * synapses of delay d, adding w (times mod) into acc.  Also clears the
+ * history slot of `step` for every population (ready for this step's
+ * updates).  step = *step_base + step_off when step_base is non-NULL. */
+NRN_API nrn_status_t nrn_cuda_deliver(const nrn_proj_t* projs, int32_t nproj,
+                              const nrn_spike_hist_t* hists, int32_t nhist,
+                              int64_t step_off, const int64_t* step_base,
+                              nrn_stream_t stream);
+/* As nrn_cuda_deliver; also adds the number of synaptic events delivered to
+ * *events (device counter) when it is non-NULL. */
+NRN_API nrn_status_t nrn_cuda_deliver_counted(const nrn_proj_t* projs, int32_t nproj,
+                                      const nrn_spike_hist_t* hists, int32_t nhist,
+                                      int64_t step_off, const int64_t* step_base,
+                                      unsigned long long* events, nrn_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Pair STDP (src/plasticity/stdp.cpp:43-141), per-neuron traces            */
+/* ------------------------------------------------------------------------ */
+
+typedef struct {
+    nrn_proj_t proj;           /* the plastic projection (w is updated)     */
+    float* w_mut;              /* == proj.w, writable                       */
+    const int64_t* in_ptr;     /* [n_tgt+1] target-major index              */
+    const uint32_t* in_syn;    /* [nnz] synapse position of each in-synapse */
+    const uint32_t* in_src;    /* [nnz] its source                          */
+    float* x_pre;              /* [n_src] presynaptic trace                 */
+    float* x_post;             /* [n_tgt] postsynaptic trace                */
+    const float* spike_src;    /* [n_src] this step's 0/1 spikes            */
+    const float* spike_tgt;    /* [n_tgt]                                   */
+    nrn_spike_hist_t hist_src;
+    nrn_spike_hist_t hist_tgt;
+    float decay_pre, decay_post;      /* (float)exp(-dt/tau_plus|minus)     */
+    float a_plus, a_minus;            /* a_minus as |A-|                    */
+    float lr, w_min, w_max;
+    int32_t slow_ratio;        /* update only when step % slow_ratio == 0   */
+} nrn_stdp_t;
+
+/* Trace decay and increment, then the weight update of every synapse whose
+ * source or target spiked at `step`, clamped to [w_min, w_max]. */
+NRN_API nrn_status_t nrn_cuda_stdp_step(const nrn_stdp_t* s, int64_t step_off,
+                                 const int64_t* step_base, nrn_stream_t stream);
+/* Clamp all n weights to [lo, hi] (the reference clamps every entry on each
+ * update; after one full clamp only changed weights can leave the range). */
+NRN_API nrn_status_t nrn_cuda_clamp(float* w, int64_t n, float lo, float hi, nrn_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Engine: a network resident on one GPU                                   */
+/* ------------------------------------------------------------------------ */
+
+typedef struct nrn_engine nrn_engine;
+
+typedef struct {
+    int32_t model;
+    int32_t n;
+    int32_t gid_offset;
+    int32_t record;            /* 1: keep every spike in the raster          */
+    /* state, caller-owned device arrays (the reference's state tensors) */
+    float* v;
+    float* aux;
+    float* refractory;
+    float* spike;
+    float* i_syn;
+    /* conductance input: tau_syn_exc > 0 enables it (AdEx) */
+    float tau_syn_exc, tau_syn_inh, e_exc, e_inh;
+    const float* param[NRN_MAX_PARAMS];
+    float uniform[NRN_MAX_PARAMS];
+    nrn_drive_t drive;
+} nrn_pop_desc_t;
+
+enum { NRN_RECV_CURRENT = 0, NRN_RECV_GEXC = 1, NRN_RECV_GINH = 2 };
+
+/* Synapse list of a projection (host or device memory, see `on_device`),
+ * any order; delays in steps.  The engine keeps its own copy. */
+typedef struct {
+    int32_t src_pop;
+    int32_t tgt_pop;
+    int32_t receptor;
+    int32_t on_device;         /* 1: the arrays below are device pointers   */
+    int64_t nnz;
+    const int32_t* src;        /* [nnz] local source index                  */
+    const int32_t* tgt;        /* [nnz] local target index                  */
+    const float* w;            /* [nnz]                                     */
+    const uint8_t* delay;      /* [nnz] steps, >= 1                         */
+    const float* mod;          /* [nnz] modulatory gain, or NULL            */
+} nrn_proj_desc_t;
+
+/* Fixed in/out-degree connectivity generated on the device; the same draws
+ * as the oracle's generator (Philox keyed by (seed; row gid, slot, id)). */
+typedef struct {
+    int32_t src_pop;
+    int32_t tgt_pop;
+    int32_t receptor;
+    int32_t out_degree;        /* 0: rows are targets, 1: rows are sources  */
+    int32_t degree;
+    int32_t gen_id;
+    int32_t col_offset;        /* global id range the draws pick from       */
+    int32_t col_n;
+    int32_t dmin, dmax;
+    float w_lo, w_span;
+    uint64_t seed;
+} nrn_gen_desc_t;
+
+NRN_API nrn_status_t nrn_engine_create(nrn_engine** out, int device, double dt, int32_t slow_ratio);
+NRN_API nrn_status_t nrn_engine_destroy(nrn_engine* e);
+NRN_API nrn_status_t nrn_engine_add_population(nrn_engine* e, const nrn_pop_desc_t* d, int32_t* id);
+/* Update the uniform/per-neuron parameters of a population (between runs). */
+NRN_API nrn_status_t nrn_engine_set_params(nrn_engine* e, int32_t pop, const float* const* param,
+                                   const float* uniform);
+NRN_API nrn_status_t nrn_engine_add_projection(nrn_engine* e, const nrn_proj_desc_t* d, int32_t* id);
+NRN_API nrn_status_t nrn_engine_generate_projection(nrn_engine* e, const nrn_gen_desc_t* g, int32_t* id,
+                                            int64_t* nnz);
+/* stdp = {tau_plus, tau_minus, a_plus, a_minus, w_min, w_max, learning_rate} */
+NRN_API nrn_status_t nrn_engine_set_stdp(nrn_engine* e, int32_t proj, const double* stdp);
+/* Allocates the history and traces and runs the initialising update
+ * (dt = 0, as sim_create does, src/simulation/runner.cpp:36-38). */
+NRN_API nrn_status_t nrn_engine_finalize(nrn_engine* e, int32_t init_update);
+/* Enqueues `steps` steps (CUDA graphs of `chunk` steps; 0 picks a size). */
+NRN_API nrn_status_t nrn_engine_run(nrn_engine* e, int64_t steps, int32_t chunk);
+NRN_API nrn_status_t nrn_engine_sync(nrn_engine* e);
+NRN_API nrn_status_t nrn_engine_stream(nrn_engine* e, nrn_stream_t* stream);
+NRN_API int64_t nrn_engine_step(const nrn_engine* e);
+/* Recorded spikes since the last call (host buffers); *n receives the count
+ * (if above cap, nothing is copied and NRN_ERR_CAPACITY is returned). */
+NRN_API nrn_status_t nrn_engine_raster(nrn_engine* e, int32_t* step, int32_t* gid, int64_t cap, int64_t* n);
+/* Weights of a projection in the order the synapses were given (host). */
+NRN_API nrn_status_t nrn_engine_weights(nrn_engine* e, int32_t proj, float* out, int64_t n);
+NRN_API nrn_status_t nrn_engine_nnz(nrn_engine* e, int32_t proj, int64_t* nnz);
+/* Runs `steps` steps without graphs, timing each phase with CUDA events on
+ * the engine stream: ms[0] delivery, ms[1] neuron updates, ms[2] plasticity
+ * (summed over the steps).  For profiling; results equal nrn_engine_run. */
+NRN_API nrn_status_t nrn_engine_profile(nrn_engine* e, int64_t steps, double* ms);
+/* Counters: total spikes and delivered synaptic events since creation. */
+NRN_API nrn_status_t nrn_engine_counters(nrn_engine* e, int64_t* spikes, int64_t* events);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NRN_CUDA_H */

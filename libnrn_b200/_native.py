@@ -1,0 +1,155 @@
+"""ctypes binding of the device layer's C ABI (include/nrn_cuda.h).
+
+The shared library is libnrn_b200/_lib/libnrn_cuda.so, built in-tree by
+``libnrn_b200.build``.  There is no fallback: if the library is missing or a
+call fails, the error is raised.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "_lib", "libnrn_cuda.so")
+
+NRN_MAX_PARAMS = 13
+NRN_MAX_PROJ = 32
+NRN_MAX_POPS = 32
+
+MODEL = {"lif": 0, "adex": 1, "izh": 2}
+DRIVE = {None: 0, "poisson": 1, "gauss": 2, "poisson_gexc": 3}
+RECEPTOR = {"current": 0, "gexc": 1, "ginh": 2}
+
+# Public entry points of include/nrn_cuda.h (checked by the test suite).
+EXPORTS = [
+    "nrn_status_string", "nrn_last_error", "nrn_version",
+    "nrn_cuda_pop_step", "nrn_cuda_deliver", "nrn_cuda_deliver_counted", "nrn_cuda_stdp_step",
+    "nrn_cuda_clamp",
+    "nrn_engine_create", "nrn_engine_destroy", "nrn_engine_add_population", "nrn_engine_set_params",
+    "nrn_engine_add_projection", "nrn_engine_generate_projection", "nrn_engine_set_stdp",
+    "nrn_engine_finalize", "nrn_engine_run", "nrn_engine_sync", "nrn_engine_stream", "nrn_engine_step",
+    "nrn_engine_raster", "nrn_engine_weights", "nrn_engine_nnz", "nrn_engine_counters",
+    "nrn_engine_profile",
+]
+
+
+class NrnError(RuntimeError):
+    """A libnrn_b200 call failed (status code and message from the library)."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(message)
+        self.status = status
+
+
+class Drive(C.Structure):
+    _fields_ = [("kind", C.c_int32), ("p0", C.c_float), ("p1", C.c_float), ("seed", C.c_uint64)]
+
+
+class PopStep(C.Structure):
+    _fields_ = [
+        ("model", C.c_int32), ("n", C.c_int32), ("gid_offset", C.c_int32), ("pad0", C.c_int32),
+        ("dt", C.c_double), ("v", C.c_void_p), ("aux", C.c_void_p), ("refractory", C.c_void_p),
+        ("spike", C.c_void_p), ("i_syn", C.c_void_p), ("g_exc", C.c_void_p), ("g_inh", C.c_void_p),
+        ("gin_exc", C.c_void_p), ("gin_inh", C.c_void_p), ("tau_syn_exc", C.c_float),
+        ("tau_syn_inh", C.c_float), ("e_exc", C.c_float), ("e_inh", C.c_float),
+        ("param", C.c_void_p * NRN_MAX_PARAMS), ("uniform", C.c_float * NRN_MAX_PARAMS),
+        ("drive", Drive), ("step", C.c_int64), ("step_base", C.c_void_p), ("spike_ids", C.c_void_p),
+        ("spike_count", C.c_void_p), ("hist_depth", C.c_int32), ("hist_cap", C.c_int32),
+        ("raster_step", C.c_void_p), ("raster_gid", C.c_void_p), ("raster_count", C.c_void_p),
+        ("raster_cap", C.c_int64),
+    ]
+
+
+class SpikeHist(C.Structure):
+    _fields_ = [("ids", C.c_void_p), ("count", C.c_void_p), ("cap", C.c_int32), ("depth", C.c_int32)]
+
+
+class Proj(C.Structure):
+    _fields_ = [
+        ("n_src", C.c_int32), ("n_tgt", C.c_int32), ("dmin", C.c_int32), ("nd", C.c_int32),
+        ("src_hist", C.c_int32), ("pad0", C.c_int32), ("seg_ptr", C.c_void_p), ("tgt", C.c_void_p),
+        ("w", C.c_void_p), ("mod", C.c_void_p), ("acc", C.c_void_p),
+    ]
+
+
+class PopDesc(C.Structure):
+    _fields_ = [
+        ("model", C.c_int32), ("n", C.c_int32), ("gid_offset", C.c_int32), ("record", C.c_int32),
+        ("v", C.c_void_p), ("aux", C.c_void_p), ("refractory", C.c_void_p), ("spike", C.c_void_p),
+        ("i_syn", C.c_void_p), ("tau_syn_exc", C.c_float), ("tau_syn_inh", C.c_float),
+        ("e_exc", C.c_float), ("e_inh", C.c_float), ("param", C.c_void_p * NRN_MAX_PARAMS),
+        ("uniform", C.c_float * NRN_MAX_PARAMS), ("drive", Drive),
+    ]
+
+
+class ProjDesc(C.Structure):
+    _fields_ = [
+        ("src_pop", C.c_int32), ("tgt_pop", C.c_int32), ("receptor", C.c_int32), ("on_device", C.c_int32),
+        ("nnz", C.c_int64), ("src", C.c_void_p), ("tgt", C.c_void_p), ("w", C.c_void_p),
+        ("delay", C.c_void_p), ("mod", C.c_void_p),
+    ]
+
+
+class GenDesc(C.Structure):
+    _fields_ = [
+        ("src_pop", C.c_int32), ("tgt_pop", C.c_int32), ("receptor", C.c_int32), ("out_degree", C.c_int32),
+        ("degree", C.c_int32), ("gen_id", C.c_int32), ("col_offset", C.c_int32), ("col_n", C.c_int32),
+        ("dmin", C.c_int32), ("dmax", C.c_int32), ("w_lo", C.c_float), ("w_span", C.c_float),
+        ("seed", C.c_uint64),
+    ]
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """Loads libnrn_cuda.so (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise NrnError(5, f"libnrn_b200 device library not built: {LIB_PATH} "
+                              "(run `python -m libnrn_b200.build`)")
+        L = C.CDLL(LIB_PATH)
+        vp, i32, i64 = C.c_void_p, C.c_int32, C.c_int64
+        L.nrn_status_string.restype = C.c_char_p
+        L.nrn_status_string.argtypes = [C.c_int]
+        L.nrn_last_error.restype = C.c_char_p
+        L.nrn_version.restype = C.c_char_p
+        L.nrn_engine_step.restype = i64
+        L.nrn_engine_step.argtypes = [vp]
+        sig = {
+            "nrn_cuda_pop_step": [C.POINTER(PopStep), vp],
+            "nrn_cuda_deliver": [C.POINTER(Proj), i32, C.POINTER(SpikeHist), i32, i64, vp, vp],
+            "nrn_cuda_deliver_counted": [C.POINTER(Proj), i32, C.POINTER(SpikeHist), i32, i64, vp, vp, vp],
+            "nrn_cuda_clamp": [vp, i64, C.c_float, C.c_float, vp],
+            "nrn_engine_create": [C.POINTER(vp), C.c_int, C.c_double, i32],
+            "nrn_engine_destroy": [vp],
+            "nrn_engine_add_population": [vp, C.POINTER(PopDesc), C.POINTER(i32)],
+            "nrn_engine_set_params": [vp, i32, vp, vp],
+            "nrn_engine_add_projection": [vp, C.POINTER(ProjDesc), C.POINTER(i32)],
+            "nrn_engine_generate_projection": [vp, C.POINTER(GenDesc), C.POINTER(i32), C.POINTER(i64)],
+            "nrn_engine_set_stdp": [vp, i32, C.POINTER(C.c_double)],
+            "nrn_engine_finalize": [vp, i32],
+            "nrn_engine_run": [vp, i64, i32],
+            "nrn_engine_sync": [vp],
+            "nrn_engine_stream": [vp, C.POINTER(vp)],
+            "nrn_engine_raster": [vp, vp, vp, i64, C.POINTER(i64)],
+            "nrn_engine_weights": [vp, i32, vp, i64],
+            "nrn_engine_nnz": [vp, i32, C.POINTER(i64)],
+            "nrn_engine_counters": [vp, C.POINTER(i64), C.POINTER(i64)],
+            "nrn_engine_profile": [vp, i64, C.POINTER(C.c_double)],
+        }
+        for name, args in sig.items():
+            f = getattr(L, name)
+            f.argtypes = args
+            f.restype = C.c_int
+        _lib = L
+    return _lib
+
+
+def check(status: int, what: str) -> None:
+    if status != 0:
+        L = lib()
+        msg = L.nrn_last_error().decode(errors="replace")
+        kind = L.nrn_status_string(status).decode()
+        raise NrnError(status, f"{what}: {kind}: {msg}")

@@ -1,0 +1,316 @@
+// connect.cu -- projections on the device: fixed-degree generation and the
+// source-major CSR segmented by delay.
+//
+// The reference builds Erdos-Renyi block-dense connectivity on the host
+// (src/connectivity/topology/random.cpp:25-95) and multiplies every block
+// each step.  Here a projection is a synapse list sorted by (source, delay)
+// with a stable radix sort, so that one spike's delay-d synapses are one
+// contiguous segment; a second stable sort by target gives the
+// target-major index that plasticity needs.  Generation uses the same
+// Philox draws as the oracle's generator: synapse (row r, slot k) of
+// generator `id` comes from Philox(seed; row gid, k, id, 0x434F4E4E).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cub/device/device_radix_sort.cuh>
+#include <cub/device/device_scan.cuh>
+
+#include "common.cuh"
+#include "internal.h"
+#include "rng.cuh"
+
+namespace nrn {
+namespace {
+
+template <typename T>
+nrn_status_t dalloc(T** p, size_t n) {
+    if (n == 0) n = 1;
+    cudaError_t e = cudaMalloc(reinterpret_cast<void**>(p), n * sizeof(T));
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(NRN_ERR_OOM, "device allocation of " + std::to_string(n * sizeof(T)) + " bytes failed");
+    }
+    return NRN_OK;
+}
+
+template <typename T>
+void dfree(T*& p) {
+    if (p) cudaFree(p);
+    p = nullptr;
+}
+
+int grid_for(int64_t n, int threads = 256) {
+    return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((n + threads - 1) / threads, 32 * sm_count_current())));
+}
+
+__global__ void make_keys(const int32_t* src, const int32_t* tgt, const uint8_t* delay, int64_t n, int32_t n_src,
+                          int32_t n_tgt, int32_t dmin, int32_t nd, uint32_t* keys, uint32_t* idx, int* bad) {
+    for (int64_t k = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; k < n;
+         k += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int32_t s = src[k];
+        uint32_t key = 0xFFFFFFFFu;
+        if (s >= 0) {
+            const int32_t t = tgt[k];
+            const int32_t dk = static_cast<int32_t>(delay[k]) - dmin;
+            if (s >= n_src || t < 0 || t >= n_tgt || dk < 0 || dk >= nd) atomicExch(bad, 1);
+            else key = static_cast<uint32_t>(s) * static_cast<uint32_t>(nd) + static_cast<uint32_t>(dk);
+        }
+        keys[k] = key;
+        idx[k] = static_cast<uint32_t>(k);
+    }
+}
+
+__global__ void count_keys(const uint32_t* keys, int64_t n, uint32_t nkeys, int64_t* counts) {
+    for (int64_t k = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; k < n;
+         k += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const uint32_t key = keys[k];
+        if (key < nkeys) atomicAdd(reinterpret_cast<unsigned long long*>(counts + key), 1ull);
+    }
+}
+
+__global__ void gather_syn(const uint32_t* perm, int64_t n, const int32_t* tgt, const float* w, const float* mod,
+                           uint32_t* tgt_o, float* w_o, float* mod_o, int64_t* orig_o) {
+    for (int64_t k = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; k < n;
+         k += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const uint32_t p = perm[k];
+        tgt_o[k] = static_cast<uint32_t>(tgt[p]);
+        w_o[k] = w[p];
+        if (mod_o) mod_o[k] = mod[p];
+        if (orig_o) orig_o[k] = p;
+    }
+}
+
+__global__ void iota_u32(uint32_t* a, int64_t n) {
+    for (int64_t k = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; k < n;
+         k += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        a[k] = static_cast<uint32_t>(k);
+}
+
+// Source of every CSR position from seg_ptr: one thread per (source, delay) segment.
+__global__ void seg_sources(const int64_t* seg_ptr, int32_t n_src, int32_t nd, uint32_t* src_of) {
+    const int64_t nseg = static_cast<int64_t>(n_src) * nd;
+    for (int64_t g = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; g < nseg;
+         g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const uint32_t j = static_cast<uint32_t>(g / nd);
+        for (int64_t p = seg_ptr[g]; p < seg_ptr[g + 1]; ++p) src_of[p] = j;
+    }
+}
+
+__global__ void gather_u32(const uint32_t* perm, int64_t n, const uint32_t* in, uint32_t* out) {
+    for (int64_t k = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; k < n;
+         k += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        out[k] = in[perm[k]];
+}
+
+__global__ void gen_kernel(const GenArgs g, int32_t* src, int32_t* tgt, float* w, uint8_t* delay) {
+    const int64_t total = static_cast<int64_t>(g.n_rows) * g.degree;
+    const uint32_t span = static_cast<uint32_t>(g.dmax - g.dmin + 1);
+    for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
+         e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int32_t r = static_cast<int32_t>(e / g.degree);
+        const uint32_t k = static_cast<uint32_t>(e - static_cast<int64_t>(r) * g.degree);
+        const int32_t gid = g.row_offset + r;
+        const bool self = gid >= g.col_offset && gid < g.col_offset + g.col_n;
+        const uint32_t m = static_cast<uint32_t>(self ? g.col_n - 1 : g.col_n);
+        const U4 x = philox4x32_10(U4{static_cast<uint32_t>(gid), k, g.gen_id, kStreamConn}, g.seed);
+        uint32_t c = __umulhi(x.x, m);
+        if (self && c >= static_cast<uint32_t>(gid - g.col_offset)) c += 1;
+        const uint32_t d = static_cast<uint32_t>(g.dmin) + __umulhi(x.y, span);
+        const int32_t src_g = g.out_degree ? gid : g.col_offset + static_cast<int32_t>(c);
+        const int32_t tgt_g = g.out_degree ? g.col_offset + static_cast<int32_t>(c) : gid;
+        const bool keep = tgt_g >= g.keep_lo && tgt_g < g.keep_hi;
+        src[e] = keep ? src_g - g.src_offset : -1;
+        tgt[e] = tgt_g - g.keep_lo;
+        w[e] = g.w_lo + g.w_span * u01(x.z);
+        delay[e] = static_cast<uint8_t>(d);
+    }
+}
+
+}  // namespace
+
+int sm_count_current() {
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n > 0 ? n : 148;
+}
+
+void free_csr(DevCsr& c) {
+    dfree(c.seg_ptr);
+    dfree(c.tgt);
+    dfree(c.w);
+    dfree(c.mod);
+    dfree(c.orig);
+    dfree(c.in_ptr);
+    dfree(c.in_syn);
+    dfree(c.in_src);
+}
+
+nrn_status_t build_csr(DevCsr& c, int32_t n_src, int32_t n_tgt, const int32_t* src, const int32_t* tgt,
+                       const float* w, const uint8_t* delay, const float* mod, int64_t n_in, bool keep_orig,
+                       cudaStream_t s) {
+    NRN_CHECK_ARG(n_in >= 0 && n_in < (int64_t(1) << 32) - 1, "projection too large (2^32 synapses per GPU)");
+    NRN_CHECK_ARG(static_cast<uint64_t>(n_src) * c.nd < 0xFFFFFFFFull, "too many (source, delay) segments");
+    c.n_src = n_src;
+    c.n_tgt = n_tgt;
+    const uint32_t nkeys = static_cast<uint32_t>(n_src) * static_cast<uint32_t>(c.nd);
+    uint32_t *keys = nullptr, *keys2 = nullptr, *idx = nullptr, *idx2 = nullptr;
+    int64_t* counts = nullptr;
+    int* bad = nullptr;
+    void* tmp = nullptr;
+    size_t tmp_bytes = 0;
+    nrn_status_t st = NRN_OK;
+    int hbad = 0;
+    int end_bit = 1;
+    while (end_bit < 32 && (uint64_t(1) << end_bit) <= nkeys) ++end_bit;
+    auto cleanup = [&]() {
+        dfree(keys); dfree(keys2); dfree(idx); dfree(idx2); dfree(counts); dfree(bad);
+        if (tmp) cudaFree(tmp);
+        tmp = nullptr;
+    };
+#define STEP(x)                       \
+    do {                              \
+        st = (x);                     \
+        if (st != NRN_OK) {           \
+            cleanup();                \
+            return st;                \
+        }                             \
+    } while (0)
+#define CSTEP(x) STEP(((x) == cudaSuccess) ? NRN_OK : cuda_fail(cudaGetLastError(), #x))
+    STEP(dalloc(&keys, n_in));
+    STEP(dalloc(&keys2, n_in));
+    STEP(dalloc(&idx, n_in));
+    STEP(dalloc(&idx2, n_in));
+    STEP(dalloc(&bad, 1));
+    STEP(dalloc(&counts, static_cast<size_t>(nkeys) + 1));
+    CSTEP(cudaMemsetAsync(bad, 0, sizeof(int), s));
+    CSTEP(cudaMemsetAsync(counts, 0, (static_cast<size_t>(nkeys) + 1) * sizeof(int64_t), s));
+    if (n_in > 0) {
+        make_keys<<<grid_for(n_in), 256, 0, s>>>(src, tgt, delay, n_in, n_src, n_tgt, c.dmin, c.nd, keys, idx, bad);
+        CSTEP(cudaGetLastError());
+    }
+    CSTEP(cudaMemcpyAsync(&hbad, bad, sizeof(int), cudaMemcpyDeviceToHost, s));
+    CSTEP(cudaStreamSynchronize(s));
+    if (hbad) {
+        cleanup();
+        return fail(NRN_ERR_INVALID, "projection: source, target or delay out of range");
+    }
+    // stable sort of positions by (source, delay); dropped entries sort last
+    {
+        cub::DoubleBuffer<uint32_t> dk(keys, keys2), dv(idx, idx2);
+        const int bits = (nkeys > 0 && end_bit < 32) ? end_bit + 1 : 32;   // + the drop sentinel
+        CSTEP(cub::DeviceRadixSort::SortPairs(nullptr, tmp_bytes, dk, dv, static_cast<int>(n_in), 0, 32, s));
+        CSTEP(cudaMalloc(&tmp, tmp_bytes));
+        (void)bits;
+        CSTEP(cub::DeviceRadixSort::SortPairs(tmp, tmp_bytes, dk, dv, static_cast<int>(n_in), 0, 32, s));
+        if (dk.Current() != keys) std::swap(keys, keys2);
+        if (dv.Current() != idx) std::swap(idx, idx2);
+        cudaFree(tmp);
+        tmp = nullptr;
+    }
+    // segment offsets: exclusive scan of the per-key counts
+    if (n_in > 0) {
+        count_keys<<<grid_for(n_in), 256, 0, s>>>(keys, n_in, nkeys, counts);
+        CSTEP(cudaGetLastError());
+    }
+    STEP(dalloc(&c.seg_ptr, static_cast<size_t>(nkeys) + 1));
+    tmp_bytes = 0;
+    CSTEP(cub::DeviceScan::ExclusiveSum(nullptr, tmp_bytes, counts, c.seg_ptr, static_cast<int64_t>(nkeys) + 1, s));
+    CSTEP(cudaMalloc(&tmp, tmp_bytes));
+    CSTEP(cub::DeviceScan::ExclusiveSum(tmp, tmp_bytes, counts, c.seg_ptr, static_cast<int64_t>(nkeys) + 1, s));
+    int64_t nnz = 0;
+    CSTEP(cudaMemcpyAsync(&nnz, c.seg_ptr + nkeys, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
+    CSTEP(cudaStreamSynchronize(s));
+    c.nnz = nnz;
+    STEP(dalloc(&c.tgt, nnz));
+    STEP(dalloc(&c.w, nnz));
+    if (mod) STEP(dalloc(&c.mod, nnz));
+    if (keep_orig) STEP(dalloc(&c.orig, nnz));
+    if (nnz > 0) {
+        gather_syn<<<grid_for(nnz), 256, 0, s>>>(idx, nnz, tgt, w, mod, c.tgt, c.w, c.mod, c.orig);
+        CSTEP(cudaGetLastError());
+    }
+    CSTEP(cudaStreamSynchronize(s));
+    cleanup();
+    return NRN_OK;
+#undef CSTEP
+#undef STEP
+}
+
+nrn_status_t build_transpose(DevCsr& c, cudaStream_t s) {
+    const int64_t n = c.nnz;
+    uint32_t *keys = nullptr, *keys2 = nullptr, *pos = nullptr, *pos2 = nullptr, *src_of = nullptr;
+    int64_t* counts = nullptr;
+    void* tmp = nullptr;
+    size_t tmp_bytes = 0;
+    nrn_status_t st = NRN_OK;
+    auto cleanup = [&]() {
+        dfree(keys); dfree(keys2); dfree(pos); dfree(pos2); dfree(src_of); dfree(counts);
+        if (tmp) cudaFree(tmp);
+        tmp = nullptr;
+    };
+#define STEP(x)                       \
+    do {                              \
+        st = (x);                     \
+        if (st != NRN_OK) {           \
+            cleanup();                \
+            return st;                \
+        }                             \
+    } while (0)
+#define CSTEP(x) STEP(((x) == cudaSuccess) ? NRN_OK : cuda_fail(cudaGetLastError(), #x))
+    STEP(dalloc(&keys, n));
+    STEP(dalloc(&keys2, n));
+    STEP(dalloc(&pos, n));
+    STEP(dalloc(&pos2, n));
+    STEP(dalloc(&src_of, n));
+    STEP(dalloc(&counts, static_cast<size_t>(c.n_tgt) + 1));
+    CSTEP(cudaMemcpyAsync(keys, c.tgt, n * sizeof(uint32_t), cudaMemcpyDeviceToDevice, s));
+    if (n > 0) {
+        iota_u32<<<grid_for(n), 256, 0, s>>>(pos, n);
+        CSTEP(cudaGetLastError());
+        seg_sources<<<grid_for(static_cast<int64_t>(c.n_src) * c.nd), 256, 0, s>>>(c.seg_ptr, c.n_src, c.nd, src_of);
+        CSTEP(cudaGetLastError());
+    }
+    {
+        cub::DoubleBuffer<uint32_t> dk(keys, keys2), dv(pos, pos2);
+        CSTEP(cub::DeviceRadixSort::SortPairs(nullptr, tmp_bytes, dk, dv, static_cast<int>(n), 0, 32, s));
+        CSTEP(cudaMalloc(&tmp, tmp_bytes));
+        CSTEP(cub::DeviceRadixSort::SortPairs(tmp, tmp_bytes, dk, dv, static_cast<int>(n), 0, 32, s));
+        if (dk.Current() != keys) std::swap(keys, keys2);
+        if (dv.Current() != pos) std::swap(pos, pos2);
+        cudaFree(tmp);
+        tmp = nullptr;
+    }
+    CSTEP(cudaMemsetAsync(counts, 0, (static_cast<size_t>(c.n_tgt) + 1) * sizeof(int64_t), s));
+    if (n > 0) {
+        count_keys<<<grid_for(n), 256, 0, s>>>(keys, n, static_cast<uint32_t>(c.n_tgt), counts);
+        CSTEP(cudaGetLastError());
+    }
+    STEP(dalloc(&c.in_ptr, static_cast<size_t>(c.n_tgt) + 1));
+    tmp_bytes = 0;
+    CSTEP(cub::DeviceScan::ExclusiveSum(nullptr, tmp_bytes, counts, c.in_ptr, static_cast<int64_t>(c.n_tgt) + 1, s));
+    CSTEP(cudaMalloc(&tmp, tmp_bytes));
+    CSTEP(cub::DeviceScan::ExclusiveSum(tmp, tmp_bytes, counts, c.in_ptr, static_cast<int64_t>(c.n_tgt) + 1, s));
+    STEP(dalloc(&c.in_syn, n));
+    STEP(dalloc(&c.in_src, n));
+    CSTEP(cudaMemcpyAsync(c.in_syn, pos, n * sizeof(uint32_t), cudaMemcpyDeviceToDevice, s));
+    if (n > 0) {
+        gather_u32<<<grid_for(n), 256, 0, s>>>(pos, n, src_of, c.in_src);
+        CSTEP(cudaGetLastError());
+    }
+    CSTEP(cudaStreamSynchronize(s));
+    cleanup();
+    return NRN_OK;
+#undef CSTEP
+#undef STEP
+}
+
+nrn_status_t generate(const GenArgs& g, int32_t* src, int32_t* tgt, float* w, uint8_t* delay, cudaStream_t s) {
+    const int64_t total = static_cast<int64_t>(g.n_rows) * g.degree;
+    if (total == 0) return NRN_OK;
+    gen_kernel<<<grid_for(total), 256, 0, s>>>(g, src, tgt, w, delay);
+    NRN_CUDA_TRY(cudaGetLastError());
+    return NRN_OK;
+}
+
+}  // namespace nrn

@@ -1,0 +1,307 @@
+// deliver.cu -- event-driven spike delivery and pair STDP.
+//
+// Delivery (the reference's phase 2, src/simulation/runner.cpp:106-124, and
+// connection_deliver, src/connectivity/connect.cpp:36-79): at step t, every
+// projection adds, for each delay d, the weights of the delay-d synapses of
+// the neurons that spiked at step t - d into the target accumulator.  The
+// reference multiplies the whole (masked) block-dense weight matrix by the
+// dense spike vector; here only the synapses of spiking neurons are touched:
+// the source-major CSR is segmented by delay, one warp walks one (spike,
+// delay) segment, and each synapse is one fire-and-forget float reduction
+// (RED.ADD.F32) into the accumulator, which stays resident in L2.
+//
+// Bytes per delivered synaptic event: 4 (target) + 4 (weight) read,
+// 4 reduced into L2; 16 per spike and delay for the two segment offsets.
+//
+// STDP (src/plasticity/stdp.cpp:43-141): the reference keeps a trace per
+// synapse, but every row (column) of its trace blocks receives the same
+// decay and increments, so one trace per source (target) neuron is exact.
+// A weight changes only when its source or target spiked at this step, so
+// the update walks the out-synapses of the spiking sources (LTD term, plus
+// LTP when the target spiked too) and the in-synapses of the spiking
+// targets whose source did not spike (LTP term); no synapse is visited
+// twice, so no atomics are needed.  The per-step clamp of every weight in
+// the reference reduces to one clamp of all weights before the first update.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include <cub/block/block_scan.cuh>
+
+#include "common.cuh"
+
+namespace nrn {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kMaxPairs = 1024;   // (projection, delay) pairs per launch
+
+struct DeliverParams {
+    nrn_proj_t proj[NRN_MAX_PROJ];
+    nrn_spike_hist_t hist[NRN_MAX_POPS];
+    int nproj;
+    int nhist;
+    int npairs;
+    int pad;
+    long long step_off;
+    const long long* step_base;
+    unsigned long long* events;
+};
+
+struct PairTable {
+    long long start[kMaxPairs + 1];   // exclusive prefix of spike counts
+    short proj[kMaxPairs];
+    short k[kMaxPairs];
+    int slot[kMaxPairs];
+};
+
+__global__ void __launch_bounds__(kThreads) deliver_kernel(const __grid_constant__ DeliverParams P) {
+    __shared__ PairTable tab;
+    __shared__ unsigned long long blk_events;
+    using Scan = cub::BlockScan<long long, kThreads>;
+    __shared__ typename Scan::TempStorage scan_tmp;
+    __shared__ long long carry;
+
+    const long long step = P.step_off + (P.step_base ? *P.step_base : 0);
+    if (threadIdx.x == 0) { blk_events = 0; carry = 0; }
+    if (blockIdx.x == 0 && threadIdx.x < P.nhist) {
+        const nrn_spike_hist_t& h = P.hist[threadIdx.x];
+        h.count[step % h.depth] = 0;   // this step's slot, filled by the updates that follow
+    }
+    __syncthreads();
+
+    // Spike counts of every (projection, delay) pair, then their prefix.
+    for (int base = 0; base < P.npairs; base += kThreads) {
+        const int pi = base + threadIdx.x;
+        long long cnt = 0;
+        if (pi < P.npairs) {
+            int q = 0, acc = 0;
+            while (q < P.nproj && pi >= acc + P.proj[q].nd) { acc += P.proj[q].nd; ++q; }
+            const int k = pi - acc;
+            const nrn_proj_t& pr = P.proj[q];
+            const long long src_step = step - (pr.dmin + k);
+            tab.proj[pi] = static_cast<short>(q);
+            tab.k[pi] = static_cast<short>(k);
+            if (src_step >= 0) {
+                const nrn_spike_hist_t& h = P.hist[pr.src_hist];
+                const int slot = static_cast<int>(src_step % h.depth);
+                tab.slot[pi] = slot;
+                cnt = h.count[slot];
+            } else {
+                tab.slot[pi] = 0;
+            }
+        }
+        long long excl, total;
+        Scan(scan_tmp).ExclusiveSum(cnt, excl, total);
+        if (pi < P.npairs) tab.start[pi] = carry + excl;
+        __syncthreads();
+        if (threadIdx.x == 0) carry += total;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) tab.start[P.npairs] = carry;
+    __syncthreads();
+    const long long n_items = tab.start[P.npairs];
+
+    const int lane = threadIdx.x & 31;
+    const long long warp = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
+    const long long n_warps = (static_cast<long long>(gridDim.x) * kThreads) >> 5;
+    unsigned long long my_events = 0;
+    for (long long it = warp; it < n_items; it += n_warps) {
+        // pair containing item `it` (binary search over the prefix)
+        int lo = 0, hi = P.npairs - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (tab.start[mid] <= it) lo = mid; else hi = mid - 1;
+        }
+        const nrn_proj_t& pr = P.proj[tab.proj[lo]];
+        const nrn_spike_hist_t& h = P.hist[pr.src_hist];
+        const int j = h.ids[static_cast<long long>(tab.slot[lo]) * h.cap + (it - tab.start[lo])];
+        const long long seg = static_cast<long long>(j) * pr.nd + tab.k[lo];
+        const long long s0 = pr.seg_ptr[seg], s1 = pr.seg_ptr[seg + 1];
+        if (lane == 0) my_events += static_cast<unsigned long long>(s1 - s0);
+        if (pr.mod == nullptr) {
+            long long s = s0 + lane;
+            for (; s + 96 < s1; s += 128) {
+                const uint32_t t0 = __ldg(pr.tgt + s), t1 = __ldg(pr.tgt + s + 32);
+                const uint32_t t2 = __ldg(pr.tgt + s + 64), t3 = __ldg(pr.tgt + s + 96);
+                const float w0 = __ldg(pr.w + s), w1 = __ldg(pr.w + s + 32);
+                const float w2 = __ldg(pr.w + s + 64), w3 = __ldg(pr.w + s + 96);
+                atomicAdd(pr.acc + t0, w0);
+                atomicAdd(pr.acc + t1, w1);
+                atomicAdd(pr.acc + t2, w2);
+                atomicAdd(pr.acc + t3, w3);
+            }
+            for (; s < s1; s += 32) atomicAdd(pr.acc + __ldg(pr.tgt + s), __ldg(pr.w + s));
+        } else {
+            for (long long s = s0 + lane; s < s1; s += 32)
+                atomicAdd(pr.acc + __ldg(pr.tgt + s), __ldg(pr.w + s) * __ldg(pr.mod + s));
+        }
+    }
+    if (P.events && lane == 0 && my_events) atomicAdd(&blk_events, my_events);
+    __syncthreads();
+    if (P.events && threadIdx.x == 0 && blk_events) atomicAdd(P.events, blk_events);
+}
+
+// ---------------------------------------------------------------------------
+// STDP
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ bool stdp_active(const nrn_stdp_t& s, long long step) {
+    return s.slow_ratio <= 1 || (step % s.slow_ratio) == 0;
+}
+
+__global__ void stdp_trace_kernel(const __grid_constant__ nrn_stdp_t s, long long step_off, const long long* step_base) {
+    const long long step = step_off + (step_base ? *step_base : 0);
+    if (!stdp_active(s, step)) return;
+    const int n_src = s.proj.n_src, n_tgt = s.proj.n_tgt;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_src + n_tgt; i += gridDim.x * blockDim.x) {
+        if (i < n_src) s.x_pre[i] = s.x_pre[i] * s.decay_pre + s.spike_src[i];
+        else {
+            const int k = i - n_src;
+            s.x_post[k] = s.x_post[k] * s.decay_post + s.spike_tgt[k];
+        }
+    }
+}
+
+__device__ __forceinline__ float stdp_apply(const nrn_stdp_t& s, long long syn, float dw) {
+    float upd = (dw * s.lr) * 1.0f;
+    if (s.proj.mod) upd = upd * s.proj.mod[syn];
+    float w = s.w_mut[syn] + upd;
+    w = fmaxf(w, s.w_min);
+    w = fminf(w, s.w_max);
+    return w;
+}
+
+__global__ void __launch_bounds__(kThreads) stdp_update_kernel(const __grid_constant__ nrn_stdp_t s, long long step_off,
+                                                               const long long* step_base) {
+    const long long step = step_off + (step_base ? *step_base : 0);
+    if (!stdp_active(s, step)) return;
+    const int slot_s = static_cast<int>(step % s.hist_src.depth);
+    const int slot_t = static_cast<int>(step % s.hist_tgt.depth);
+    const int n_pre = s.hist_src.count[slot_s];
+    const int n_post = s.hist_tgt.count[slot_t];
+    const int lane = threadIdx.x & 31;
+    const long long warp = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
+    const long long n_warps = (static_cast<long long>(gridDim.x) * kThreads) >> 5;
+    const int nd = s.proj.nd;
+    for (long long it = warp; it < n_pre + n_post; it += n_warps) {
+        if (it < n_pre) {
+            // source j spiked: every out-synapse gets -A- x_post (+A+ x_pre if the target spiked)
+            const int j = s.hist_src.ids[static_cast<long long>(slot_s) * s.hist_src.cap + it];
+            const float ltp = s.a_plus * s.x_pre[j];
+            const long long b0 = s.proj.seg_ptr[static_cast<long long>(j) * nd];
+            const long long b1 = s.proj.seg_ptr[static_cast<long long>(j + 1) * nd];
+            for (long long syn = b0 + lane; syn < b1; syn += 32) {
+                const uint32_t i = s.proj.tgt[syn];
+                const float dw = ltp * s.spike_tgt[i] - (s.a_minus * s.x_post[i]) * 1.0f;
+                s.w_mut[syn] = stdp_apply(s, syn, dw);
+            }
+        } else {
+            // target i spiked: in-synapses from sources that did not spike get +A+ x_pre
+            const int i = s.hist_tgt.ids[static_cast<long long>(slot_t) * s.hist_tgt.cap + (it - n_pre)];
+            const float ltd = (s.a_minus * s.x_post[i]) * 0.0f;
+            const long long b0 = s.in_ptr[i], b1 = s.in_ptr[i + 1];
+            for (long long k = b0 + lane; k < b1; k += 32) {
+                const uint32_t j = s.in_src[k];
+                if (s.spike_src[j] != 0.0f) continue;   // handled with the source's row
+                const long long syn = s.in_syn[k];
+                const float dw = (s.a_plus * s.x_pre[j]) * 1.0f - ltd;
+                s.w_mut[syn] = stdp_apply(s, syn, dw);
+            }
+        }
+    }
+}
+
+__global__ void clamp_kernel(float* w, long long n, float lo, float hi) {
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<long long>(gridDim.x) * blockDim.x)
+        w[i] = fminf(fmaxf(w[i], lo), hi);
+}
+
+int sm_count() {
+    static int n = 0;
+    if (n == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+}  // namespace
+}  // namespace nrn
+
+extern "C" nrn_status_t nrn_cuda_deliver(const nrn_proj_t* projs, int32_t nproj, const nrn_spike_hist_t* hists,
+                                         int32_t nhist, int64_t step_off, const int64_t* step_base,
+                                         nrn_stream_t stream) {
+    using namespace nrn;
+    return nrn_cuda_deliver_counted(projs, nproj, hists, nhist, step_off, step_base, nullptr, stream);
+}
+
+extern "C" nrn_status_t nrn_cuda_deliver_counted(const nrn_proj_t* projs, int32_t nproj,
+                                                 const nrn_spike_hist_t* hists, int32_t nhist,
+                                                 int64_t step_off, const int64_t* step_base,
+                                                 unsigned long long* events, nrn_stream_t stream) {
+    using namespace nrn;
+    NRN_CHECK_ARG(nproj >= 0 && nproj <= NRN_MAX_PROJ, "nrn_cuda_deliver: too many projections");
+    NRN_CHECK_ARG(nhist >= 0 && nhist <= NRN_MAX_POPS, "nrn_cuda_deliver: too many populations");
+    NRN_CHECK_ARG(nproj == 0 || projs != nullptr, "nrn_cuda_deliver: null projections");
+    NRN_CHECK_ARG(nhist == 0 || hists != nullptr, "nrn_cuda_deliver: null histories");
+    DeliverParams P{};
+    int pairs = 0;
+    for (int q = 0; q < nproj; ++q) {
+        const nrn_proj_t& p = projs[q];
+        NRN_CHECK_ARG(p.dmin >= 1 && p.nd >= 1, "nrn_cuda_deliver: delays must be >= 1 step");
+        NRN_CHECK_ARG(p.src_hist >= 0 && p.src_hist < nhist, "nrn_cuda_deliver: bad source history");
+        NRN_CHECK_ARG(p.dmin + p.nd - 1 < hists[p.src_hist].depth,
+                      "nrn_cuda_deliver: history shallower than the longest delay");
+        NRN_CHECK_ARG(p.seg_ptr && p.tgt && p.w && p.acc, "nrn_cuda_deliver: null projection array");
+        P.proj[q] = p;
+        pairs += p.nd;
+    }
+    NRN_CHECK_ARG(pairs <= kMaxPairs, "nrn_cuda_deliver: too many (projection, delay) pairs");
+    for (int h = 0; h < nhist; ++h) {
+        NRN_CHECK_ARG(hists[h].depth >= 1 && hists[h].ids && hists[h].count, "nrn_cuda_deliver: bad history");
+        P.hist[h] = hists[h];
+    }
+    P.nproj = nproj;
+    P.nhist = nhist;
+    P.npairs = pairs;
+    P.step_off = step_off;
+    P.step_base = reinterpret_cast<const long long*>(step_base);
+    P.events = events;
+    const int blocks = 4 * sm_count();
+    deliver_kernel<<<blocks, kThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(P);
+    NRN_CUDA_TRY(cudaGetLastError());
+    return NRN_OK;
+}
+
+extern "C" nrn_status_t nrn_cuda_stdp_step(const nrn_stdp_t* s, int64_t step_off, const int64_t* step_base,
+                                           nrn_stream_t stream) {
+    using namespace nrn;
+    NRN_CHECK_ARG(s != nullptr, "nrn_cuda_stdp_step: null arguments");
+    NRN_CHECK_ARG(s->w_mut && s->in_ptr && s->in_syn && s->in_src && s->x_pre && s->x_post && s->spike_src &&
+                      s->spike_tgt && s->proj.seg_ptr && s->proj.tgt,
+                  "nrn_cuda_stdp_step: null array");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int n = s->proj.n_src + s->proj.n_tgt;
+    const int tb = 256;
+    const int trace_blocks = std::max(1, std::min((n + tb - 1) / tb, 8 * sm_count()));
+    const long long* base = reinterpret_cast<const long long*>(step_base);
+    stdp_trace_kernel<<<trace_blocks, tb, 0, st>>>(*s, step_off, base);
+    NRN_CUDA_TRY(cudaGetLastError());
+    stdp_update_kernel<<<4 * sm_count(), kThreads, 0, st>>>(*s, step_off, base);
+    NRN_CUDA_TRY(cudaGetLastError());
+    return NRN_OK;
+}
+
+extern "C" nrn_status_t nrn_cuda_clamp(float* w, int64_t n, float lo, float hi, nrn_stream_t stream) {
+    using namespace nrn;
+    NRN_CHECK_ARG(n >= 0 && (n == 0 || w != nullptr), "nrn_cuda_clamp: bad arguments");
+    if (n == 0) return NRN_OK;
+    const int blocks = static_cast<int>(std::min<int64_t>((n + 255) / 256, 16 * sm_count()));
+    clamp_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(w, n, lo, hi);
+    NRN_CUDA_TRY(cudaGetLastError());
+    return NRN_OK;
+}

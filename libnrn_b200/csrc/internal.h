@@ -1,0 +1,55 @@
+// internal.h -- device-side building blocks shared by the engine.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "nrn_cuda.h"
+
+namespace nrn {
+
+// A projection's synapses on the device, sorted by (source, delay).
+struct DevCsr {
+    int32_t n_src = 0, n_tgt = 0;
+    int32_t dmin = 1, nd = 1;
+    int64_t nnz = 0;
+    int64_t* seg_ptr = nullptr;   // [n_src*nd + 1]
+    uint32_t* tgt = nullptr;      // [nnz]
+    float* w = nullptr;           // [nnz]
+    float* mod = nullptr;         // [nnz] or null
+    int64_t* orig = nullptr;      // [nnz] index in the caller's list, or null
+    // target-major index (plasticity)
+    int64_t* in_ptr = nullptr;    // [n_tgt+1]
+    uint32_t* in_syn = nullptr;   // [nnz]
+    uint32_t* in_src = nullptr;   // [nnz]
+};
+
+void free_csr(DevCsr& c);
+
+// Builds `c` from a synapse list in device memory (src < 0 entries are
+// dropped).  keep_orig retains each synapse's index in the input list.
+nrn_status_t build_csr(DevCsr& c, int32_t n_src, int32_t n_tgt, const int32_t* src, const int32_t* tgt,
+                       const float* w, const uint8_t* delay, const float* mod, int64_t n_in, bool keep_orig,
+                       cudaStream_t s);
+// Adds the target-major index (in_ptr/in_syn/in_src).
+nrn_status_t build_transpose(DevCsr& c, cudaStream_t s);
+
+// Fixed in/out-degree generation into device arrays of length rows*degree;
+// entries whose target falls outside [keep_lo, keep_hi) get src = -1.
+struct GenArgs {
+    int out_degree;
+    int degree;
+    uint32_t gen_id;
+    int32_t n_src, src_offset;   // source population range (global ids)
+    int32_t col_offset, col_n;   // candidate column range (global ids)
+    int32_t row_offset, n_rows;  // rows: targets (in) or sources (out)
+    int32_t keep_lo, keep_hi;    // kept target range (global ids)
+    int32_t dmin, dmax;
+    float w_lo, w_span;
+    uint64_t seed;
+};
+nrn_status_t generate(const GenArgs& g, int32_t* src, int32_t* tgt, float* w, uint8_t* delay, cudaStream_t s);
+
+int sm_count_current();
+
+}  // namespace nrn

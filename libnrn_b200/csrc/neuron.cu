@@ -1,0 +1,289 @@
+// neuron.cu -- fused per-population neuron update (LIF, AdEx, Izhikevich).
+//
+// One thread per neuron: read the input (current and, for AdEx, conductance
+// input), add the external drive, integrate one step, detect the spike,
+// write state, zero the consumed input, and append spiking ids with one
+// warp-ballot compaction (one atomic per warp that has a spike).
+//
+// Each model's arithmetic restates the reference's CPU path operation by
+// operation (src/neuron/lif.cpp:80-97, src/neuron/adex.cpp:97-124,
+// src/neuron/izhikevich.cpp:76-98): this file is compiled with -fmad=false,
+// so every multiply and add rounds on its own as the torch ops do, and
+// scalars the reference passes as doubles are rounded to float on the host.
+//
+// Memory per neuron and step (uniform parameters): LIF 28 B, Izhikevich
+// 28 B (+20 B per-neuron a,b,c,d,v_peak), AdEx with conductances 64 B.
+#include <cuda_runtime.h>
+
+#include <cmath>
+
+#include "common.cuh"
+#include "rng.cuh"
+
+namespace nrn {
+namespace {
+
+struct PopArgs {
+    int n;
+    int gid_offset;
+    float dtf;                 // (float)dt
+    float half, dtm;           // Izhikevich: (float)(0.5*dt_ms), (float)dt_ms
+    float dec_e, dec_i;        // conductance decay per step
+    float e_exc, e_inh;
+    float* v;
+    float* aux;
+    float* ref;
+    float* spike;
+    float* i_syn;
+    float* g_exc;
+    float* g_inh;
+    float* gin_exc;
+    float* gin_inh;
+    const float* param[NRN_MAX_PARAMS];
+    float uniform[NRN_MAX_PARAMS];
+    int drive_kind;
+    float d0, d1, d_exp;       // drive parameters, expf(-lambda)
+    uint64_t seed;
+    int64_t step;
+    const int64_t* step_base;
+    int* spike_ids;
+    int* spike_count;
+    int hist_depth;
+    int hist_cap;
+    int* raster_step;
+    int* raster_gid;
+    unsigned long long* raster_count;
+    long long raster_cap;
+};
+
+template <bool HET>
+__device__ __forceinline__ float par(const PopArgs& a, int k, int i) {
+    if (HET) {
+        const float* p = a.param[k];
+        return p ? __ldg(p + i) : a.uniform[k];
+    }
+    return a.uniform[k];
+}
+
+__device__ __forceinline__ float drive_value(const PopArgs& a, uint32_t gid, uint32_t step) {
+    U4 w = philox4x32_10(U4{gid, step, 0u, kStreamDrive}, a.seed);
+    if (a.drive_kind == NRN_DRIVE_GAUSS_CURRENT) {
+        float z = normal_bm(u01(w.x), u01(w.y));
+        return a.d0 + a.d1 * z;
+    }
+    int k = poisson_inv(u01(w.x), a.d0, a.d_exp);
+    return a.d1 * static_cast<float>(k);
+}
+
+template <int MODEL, bool HET, bool COND>
+__global__ void __launch_bounds__(256) pop_step_kernel(const __grid_constant__ PopArgs a) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    const bool valid = i < a.n;
+    int spiked = 0;
+    long long step = a.step;
+    if (a.step_base) step += *a.step_base;
+    if (valid) {
+        float I = a.i_syn ? a.i_syn[i] : 0.0f;
+        float in_e = 0.0f, in_i = 0.0f;
+        if (COND) {
+            in_e = a.gin_exc[i];
+            in_i = a.gin_inh[i];
+        }
+        if (a.drive_kind != NRN_DRIVE_NONE) {
+            float x = drive_value(a, static_cast<uint32_t>(a.gid_offset + i), static_cast<uint32_t>(step));
+            if (a.drive_kind == NRN_DRIVE_POISSON_GEXC) in_e = in_e + x;
+            else I = I + x;
+        }
+        if (MODEL == NRN_MODEL_LIF) {
+            float v = a.v[i], ref = a.ref[i];
+            const float v_rest = par<HET>(a, 0, i), v_th = par<HET>(a, 1, i);
+            const float v_reset = par<HET>(a, 2, i), tau_m = par<HET>(a, 3, i);
+            const float tau_ref = par<HET>(a, 4, i), c_m = par<HET>(a, 5, i);
+            const float i_bg = par<HET>(a, 6, i);
+            const bool active = ref <= 0.0f;
+            float r = ref > 0.0f ? ref - a.dtf : ref;
+            float lk = (-(v - v_rest)) / tau_m;
+            float in = (I + i_bg) / c_m;
+            float dv = a.dtf * (lk + in);
+            float vn = active ? v + dv : v;
+            spiked = (vn >= v_th) && active;
+            if (spiked) { vn = v_reset; r = tau_ref; }
+            a.v[i] = vn;
+            a.ref[i] = r;
+        } else if (MODEL == NRN_MODEL_ADEX) {
+            float v = a.v[i], w = a.aux[i], ref = a.ref[i];
+            if (COND) {
+                float ge = a.g_exc[i] * a.dec_e + in_e;
+                float gi = a.g_inh[i] * a.dec_i + in_i;
+                a.g_exc[i] = ge;
+                a.g_inh[i] = gi;
+                I = I + ge * (a.e_exc - v);
+                I = I + gi * (a.e_inh - v);
+            }
+            const float v_rest = par<HET>(a, 0, i), v_th = par<HET>(a, 1, i);
+            const float v_reset = par<HET>(a, 2, i), v_peak = par<HET>(a, 3, i);
+            const float tau_w = par<HET>(a, 5, i), tau_ref = par<HET>(a, 6, i);
+            const float c_m = par<HET>(a, 7, i), g_l = par<HET>(a, 8, i);
+            const float pa = par<HET>(a, 9, i), pb = par<HET>(a, 10, i);
+            const float delta_t = par<HET>(a, 11, i), i_bg = par<HET>(a, 12, i);
+            const bool active = ref <= 0.0f;
+            float r = ref > 0.0f ? ref - a.dtf : ref;
+            float I_exp = (g_l * delta_t) * expf((v - v_th) / delta_t);
+            float acc = (-g_l) * (v - v_rest);
+            acc = acc + I_exp;
+            acc = acc - w;
+            acc = acc + I;
+            acc = acc + i_bg;
+            float dv = (a.dtf * acc) / c_m;
+            float vn = active ? v + dv : v;
+            float dw = (a.dtf * ((pa * (vn - v_rest)) - w)) / tau_w;
+            float wn = w + dw;
+            spiked = (vn >= v_peak) && active;
+            if (spiked) { vn = v_reset; wn = wn + pb; r = tau_ref; }
+            a.v[i] = vn;
+            a.aux[i] = wn;
+            a.ref[i] = r;
+        } else {
+            float v = a.v[i], u = a.aux[i];
+            const float pa = par<HET>(a, 0, i), pb = par<HET>(a, 1, i);
+            const float pc = par<HET>(a, 2, i), pd = par<HET>(a, 3, i);
+            const float v_peak = par<HET>(a, 4, i);
+            float dv1 = ((((0.04f * v) * v) + (5.0f * v)) + 140.0f - u) + I;
+            v = v + a.half * dv1;
+            float dv2 = ((((0.04f * v) * v) + (5.0f * v)) + 140.0f - u) + I;
+            v = v + a.half * dv2;
+            float du = (a.dtm * pa) * ((pb * v) - u);
+            u = u + du;
+            spiked = v >= v_peak;
+            if (spiked) { v = pc; u = u + pd; }
+            a.v[i] = v;
+            a.aux[i] = u;
+        }
+        if (a.spike) a.spike[i] = spiked ? 1.0f : 0.0f;
+        if (a.i_syn) a.i_syn[i] = 0.0f;
+        if (COND) {
+            a.gin_exc[i] = 0.0f;
+            a.gin_inh[i] = 0.0f;
+        }
+    }
+    // Warp-ballot compaction: ascending ids within a warp, one atomic per warp.
+    if (a.spike_ids != nullptr || a.raster_gid != nullptr) {
+        const unsigned mask = __ballot_sync(0xffffffffu, spiked);
+        if (mask) {
+            const int lane = threadIdx.x & 31;
+            const int leader = __ffs(mask) - 1;
+            const int cnt = __popc(mask);
+            const int rank = __popc(mask & ((1u << lane) - 1u));
+            if (a.spike_ids) {
+                int* ids = a.spike_ids;
+                int* count = a.spike_count;
+                if (a.hist_depth > 0) {
+                    const int slot = static_cast<int>(step % a.hist_depth);
+                    ids += static_cast<long long>(slot) * a.hist_cap;
+                    count += slot;
+                }
+                int base = 0;
+                if (lane == leader) base = atomicAdd(count, cnt);
+                base = __shfl_sync(0xffffffffu, base, leader);
+                if (spiked) ids[base + rank] = i;
+            }
+            if (a.raster_gid) {
+                unsigned long long rb = 0;
+                if (lane == leader) rb = atomicAdd(a.raster_count, static_cast<unsigned long long>(cnt));
+                rb = __shfl_sync(0xffffffffu, rb, leader);
+                const unsigned long long pos = rb + rank;
+                if (spiked && pos < static_cast<unsigned long long>(a.raster_cap)) {
+                    a.raster_step[pos] = static_cast<int>(step);
+                    a.raster_gid[pos] = a.gid_offset + i;
+                }
+            }
+        }
+    }
+}
+
+template <int MODEL>
+void launch_model(const PopArgs& a, bool het, bool cond, cudaStream_t s) {
+    const int threads = 256;
+    const int blocks = (a.n + threads - 1) / threads;
+    if (het) {
+        if (cond) pop_step_kernel<MODEL, true, true><<<blocks, threads, 0, s>>>(a);
+        else pop_step_kernel<MODEL, true, false><<<blocks, threads, 0, s>>>(a);
+    } else {
+        if (cond) pop_step_kernel<MODEL, false, true><<<blocks, threads, 0, s>>>(a);
+        else pop_step_kernel<MODEL, false, false><<<blocks, threads, 0, s>>>(a);
+    }
+}
+
+}  // namespace
+}  // namespace nrn
+
+extern "C" nrn_status_t nrn_cuda_pop_step(const nrn_pop_step_t* in, nrn_stream_t stream) {
+    using namespace nrn;
+    NRN_CHECK_ARG(in != nullptr, "nrn_cuda_pop_step: null arguments");
+    const nrn_pop_step_t& d = *in;
+    NRN_CHECK_ARG(d.model >= NRN_MODEL_LIF && d.model <= NRN_MODEL_IZH, "nrn_cuda_pop_step: unknown model");
+    NRN_CHECK_ARG(d.n >= 0, "nrn_cuda_pop_step: neuron count must be >= 0");
+    if (d.n == 0) return NRN_OK;
+    NRN_CHECK_ARG(d.v != nullptr, "nrn_cuda_pop_step: v is required");
+    NRN_CHECK_ARG(d.model == NRN_MODEL_LIF || d.aux != nullptr, "nrn_cuda_pop_step: aux (w/u) is required");
+    NRN_CHECK_ARG(d.model == NRN_MODEL_IZH || d.refractory != nullptr,
+                  "nrn_cuda_pop_step: refractory is required");
+    NRN_CHECK_ARG(d.dt >= 0.0, "nrn_cuda_pop_step: dt must be >= 0");
+    NRN_CHECK_ARG(d.spike_ids == nullptr || d.spike_count != nullptr,
+                  "nrn_cuda_pop_step: spike_ids needs spike_count");
+    NRN_CHECK_ARG(d.raster_gid == nullptr || (d.raster_step && d.raster_count),
+                  "nrn_cuda_pop_step: raster needs step and count arrays");
+    NRN_CHECK_ARG(d.drive.kind >= NRN_DRIVE_NONE && d.drive.kind <= NRN_DRIVE_POISSON_GEXC,
+                  "nrn_cuda_pop_step: unknown drive kind");
+    const bool cond = d.gin_exc != nullptr;
+    NRN_CHECK_ARG(!cond || (d.model == NRN_MODEL_ADEX && d.g_exc && d.g_inh && d.gin_inh),
+                  "nrn_cuda_pop_step: conductance input needs an AdEx population and all four arrays");
+    NRN_CHECK_ARG(d.drive.kind != NRN_DRIVE_POISSON_GEXC || cond,
+                  "nrn_cuda_pop_step: conductance drive needs conductance input");
+    PopArgs a{};
+    a.n = d.n;
+    a.gid_offset = d.gid_offset;
+    a.dtf = static_cast<float>(d.dt);
+    const double dt_ms = d.dt * 1000.0;
+    a.half = static_cast<float>(0.5 * dt_ms);
+    a.dtm = static_cast<float>(dt_ms);
+    if (cond) {
+        NRN_CHECK_ARG(d.tau_syn_exc > 0.0f && d.tau_syn_inh > 0.0f, "nrn_cuda_pop_step: tau_syn must be > 0");
+        a.dec_e = static_cast<float>(std::exp(-d.dt / static_cast<double>(d.tau_syn_exc)));
+        a.dec_i = static_cast<float>(std::exp(-d.dt / static_cast<double>(d.tau_syn_inh)));
+    }
+    a.e_exc = d.e_exc;
+    a.e_inh = d.e_inh;
+    a.v = d.v; a.aux = d.aux; a.ref = d.refractory; a.spike = d.spike; a.i_syn = d.i_syn;
+    a.g_exc = d.g_exc; a.g_inh = d.g_inh; a.gin_exc = d.gin_exc; a.gin_inh = d.gin_inh;
+    bool het = false;
+    for (int k = 0; k < NRN_MAX_PARAMS; ++k) {
+        a.param[k] = d.param[k];
+        a.uniform[k] = d.uniform[k];
+        het = het || d.param[k] != nullptr;
+    }
+    a.drive_kind = d.drive.kind;
+    a.d0 = d.drive.p0;
+    a.d1 = d.drive.p1;
+    a.d_exp = static_cast<float>(std::exp(-static_cast<double>(d.drive.p0)));
+    a.seed = d.drive.seed;
+    a.step = d.step;
+    a.step_base = d.step_base;
+    a.spike_ids = d.spike_ids;
+    a.spike_count = d.spike_count;
+    NRN_CHECK_ARG(d.hist_depth <= 0 || d.hist_cap >= d.n, "nrn_cuda_pop_step: history capacity below n");
+    a.hist_depth = d.hist_depth;
+    a.hist_cap = d.hist_cap;
+    a.raster_step = d.raster_step;
+    a.raster_gid = d.raster_gid;
+    a.raster_count = d.raster_count;
+    a.raster_cap = d.raster_cap;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    switch (d.model) {
+        case NRN_MODEL_LIF: launch_model<NRN_MODEL_LIF>(a, het, false, s); break;
+        case NRN_MODEL_ADEX: launch_model<NRN_MODEL_ADEX>(a, het, cond, s); break;
+        default: launch_model<NRN_MODEL_IZH>(a, het, false, s); break;
+    }
+    NRN_CUDA_TRY(cudaGetLastError());
+    return NRN_OK;
+}

@@ -1,0 +1,230 @@
+"""Host-side driver of the device engine (include/nrn_cuda.h, nrn_engine_*).
+
+``Network`` holds a network resident on one GPU: population state lives in
+torch CUDA tensors owned here (torch is the allocator only), synapses and
+spike histories inside the engine.  It mirrors the reference's
+sim_create / sim_run_steps / sim_get_spikes sequence
+(src/simulation/runner.cpp:17-197) for Python callers: the test suite and
+bench.py.  Every step runs in the CUDA library; nothing here computes.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import torch
+
+from . import _native as N
+
+NPARAM = {"lif": 7, "adex": 13, "izh": 5}
+
+
+def _ptr(t):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+class Network:
+    def __init__(self, dt: float, slow_ratio: int = 1, device: int = 0):
+        self.L = N.lib()
+        self.device = device
+        self.dt = float(dt)
+        self.dev = torch.device("cuda", device)
+        h = C.c_void_p()
+        N.check(self.L.nrn_engine_create(C.byref(h), device, self.dt, int(slow_ratio)), "nrn_engine_create")
+        self.h = h
+        self.pops: list[dict] = []
+        self.projs: list[dict] = []
+        self._keep: list = []
+        self.finalized = False
+
+    # -- construction -------------------------------------------------------
+    def add_population(self, model: str, n: int, params, *, hp=None, drive=None, cond=None,
+                       init_v=None, init_aux=None, record: bool = True, seed: int = 0) -> int:
+        f32 = dict(dtype=torch.float32, device=self.dev)
+        off = sum(p["n"] for p in self.pops)
+        if init_v is None:
+            v = torch.full((n,), -65.0 if model == "izh" else float(params[0]), **f32)
+        else:
+            v = torch.as_tensor(np.asarray(init_v, np.float32)).to(self.dev)
+        aux = None
+        if model != "lif":
+            if init_aux is not None:
+                aux = torch.as_tensor(np.asarray(init_aux, np.float32)).to(self.dev)
+            elif model == "izh":
+                aux = torch.full((n,), np.float32(float(params[1]) * -65.0), **f32)
+            else:
+                aux = torch.zeros(n, **f32)
+        ref = torch.zeros(n, **f32) if model != "izh" else None
+        spike = torch.zeros(n, **f32)
+        i_syn = torch.zeros(n, **f32)
+        d = N.PopDesc()
+        d.model = N.MODEL[model]
+        d.n = n
+        d.gid_offset = off
+        d.record = int(record)
+        d.v, d.aux, d.refractory, d.spike, d.i_syn = (_ptr(t) for t in (v, aux, ref, spike, i_syn))
+        if cond is not None:
+            d.tau_syn_exc, d.tau_syn_inh, d.e_exc, d.e_inh = (float(x) for x in cond)
+        for k, x in enumerate(params):
+            d.uniform[k] = float(x)
+        hpt = None
+        if hp is not None:
+            hpt = torch.as_tensor(np.asarray(hp, np.float32)).to(self.dev).contiguous()
+            for k in range(hpt.shape[0]):
+                d.param[k] = hpt[k].data_ptr()
+        if drive is not None:
+            d.drive.kind = N.DRIVE[drive[0]]
+            d.drive.p0 = float(drive[1])
+            d.drive.p1 = float(drive[2])
+            d.drive.seed = int(seed)
+        pid = C.c_int32()
+        N.check(self.L.nrn_engine_add_population(self.h, C.byref(d), C.byref(pid)), "add_population")
+        self.pops.append({"model": model, "n": n, "offset": off, "v": v, "aux": aux, "ref": ref,
+                          "spike": spike, "i_syn": i_syn, "hp": hpt, "record": record})
+        return pid.value
+
+    def add_projection(self, src: int, tgt: int, src_idx, tgt_idx, w, delay, *, receptor="current",
+                       mod=None) -> int:
+        arrs = [np.ascontiguousarray(src_idx, np.int32), np.ascontiguousarray(tgt_idx, np.int32),
+                np.ascontiguousarray(w, np.float32), np.ascontiguousarray(delay, np.uint8)]
+        m = None if mod is None else np.ascontiguousarray(mod, np.float32)
+        d = N.ProjDesc()
+        d.src_pop, d.tgt_pop, d.receptor, d.on_device = src, tgt, N.RECEPTOR[receptor], 0
+        d.nnz = len(arrs[0])
+        d.src, d.tgt, d.w, d.delay = (a.ctypes.data for a in arrs)
+        d.mod = None if m is None else m.ctypes.data
+        qid = C.c_int32()
+        N.check(self.L.nrn_engine_add_projection(self.h, C.byref(d), C.byref(qid)), "add_projection")
+        self.projs.append({"src": src, "tgt": tgt, "nnz": d.nnz})
+        return qid.value
+
+    def generate_projection(self, src: int, tgt: int, *, out_degree: bool, degree: int, gen_id: int,
+                            dmin: int, dmax: int, w_lo: float, w_span: float, seed: int,
+                            cols=None, receptor="current") -> int:
+        g = N.GenDesc()
+        g.src_pop, g.tgt_pop, g.receptor = src, tgt, N.RECEPTOR[receptor]
+        g.out_degree, g.degree, g.gen_id = int(out_degree), degree, gen_id
+        g.col_offset, g.col_n = cols if cols is not None else (0, 0)
+        g.dmin, g.dmax, g.w_lo, g.w_span, g.seed = dmin, dmax, w_lo, w_span, seed
+        qid = C.c_int32()
+        nnz = C.c_int64()
+        N.check(self.L.nrn_engine_generate_projection(self.h, C.byref(g), C.byref(qid), C.byref(nnz)),
+                "generate_projection")
+        self.projs.append({"src": src, "tgt": tgt, "nnz": nnz.value})
+        return qid.value
+
+    def set_stdp(self, proj: int, params) -> None:
+        arr = (C.c_double * 7)(*[float(x) for x in params])
+        N.check(self.L.nrn_engine_set_stdp(self.h, proj, arr), "set_stdp")
+
+    def finalize(self, init_update: bool = True) -> None:
+        N.check(self.L.nrn_engine_finalize(self.h, int(init_update)), "finalize")
+        self.finalized = True
+
+    # -- running -----------------------------------------------------------
+    def run(self, steps: int, chunk: int = 0) -> None:
+        N.check(self.L.nrn_engine_run(self.h, int(steps), int(chunk)), "run")
+
+    def profile(self, steps: int):
+        """Runs steps eagerly; returns summed device ms of (delivery, neuron
+        updates, plasticity) measured with CUDA events on the engine stream."""
+        ms = (C.c_double * 3)()
+        N.check(self.L.nrn_engine_profile(self.h, int(steps), ms), "profile")
+        return tuple(ms)
+
+    def sync(self) -> None:
+        N.check(self.L.nrn_engine_sync(self.h), "sync")
+
+    def stream(self) -> int:
+        s = C.c_void_p()
+        N.check(self.L.nrn_engine_stream(self.h, C.byref(s)), "stream")
+        return s.value or 0
+
+    @property
+    def step(self) -> int:
+        return int(self.L.nrn_engine_step(self.h))
+
+    def raster(self, cap: int | None = None):
+        """Spikes recorded since the last call: (step, gid), sorted by step then id."""
+        n = C.c_int64()
+        cap = cap if cap is not None else 1 << 26
+        st = np.empty(cap, np.int32)
+        gd = np.empty(cap, np.int32)
+        N.check(self.L.nrn_engine_raster(self.h, st.ctypes.data, gd.ctypes.data, cap, C.byref(n)), "raster")
+        st, gd = st[:n.value], gd[:n.value]
+        o = np.lexsort((gd, st))
+        return st[o], gd[o]
+
+    def weights(self, proj: int) -> np.ndarray:
+        nnz = C.c_int64()
+        N.check(self.L.nrn_engine_nnz(self.h, proj, C.byref(nnz)), "nnz")
+        out = np.empty(nnz.value, np.float32)
+        N.check(self.L.nrn_engine_weights(self.h, proj, out.ctypes.data, nnz.value), "weights")
+        return out
+
+    def counters(self):
+        s, e = C.c_int64(), C.c_int64()
+        N.check(self.L.nrn_engine_counters(self.h, C.byref(s), C.byref(e)), "counters")
+        return s.value, e.value
+
+    def state(self, name: str) -> np.ndarray:
+        """Concatenated state variable over all populations (host copy)."""
+        self.sync()
+        parts = []
+        for p in self.pops:
+            t = p[name]
+            parts.append(np.zeros(p["n"], np.float32) if t is None else t.cpu().numpy())
+        return np.concatenate(parts)
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            self.L.nrn_engine_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # -- builders ----------------------------------------------------------
+    @classmethod
+    def from_net(cls, net: dict, device: int = 0, record: bool = True) -> "Network":
+        """From a network description with explicit synapse lists (the
+        oracle's form)."""
+        nw = cls(net["dt"], net.get("slow_ratio", 1), device)
+        for p in net["pops"]:
+            nw.add_population(p["model"], p["n"], p["params"], hp=p.get("hp"), drive=p.get("drive"),
+                              cond=p.get("cond"), init_v=p.get("init_v"), init_aux=p.get("init_aux"),
+                              record=record, seed=net.get("seed", 0))
+        for q in net.get("projs", []):
+            qid = nw.add_projection(q["src"], q["tgt"], q["src_idx"], q["tgt_idx"], q["w"], q["delay"],
+                                    receptor=q.get("receptor", "current"), mod=q.get("mod"))
+            if q.get("plastic"):
+                nw.set_stdp(qid, q["stdp"])
+        nw.finalize(True)
+        return nw
+
+    @classmethod
+    def from_spec(cls, spec: dict, device: int = 0, record: bool = True) -> "Network":
+        """From a workload spec (libnrn_b200.workloads), connectivity
+        generated on the device."""
+        from . import workloads as W
+
+        nw = cls(spec["dt"], spec.get("slow_ratio", 1), device)
+        for p in spec["pops"]:
+            arr = W.population_arrays(spec, p)
+            nw.add_population(p["model"], p["n"], p["params"], hp=arr["hp"], drive=p.get("drive"),
+                              cond=p.get("cond"), init_v=arr["init_v"], init_aux=arr["init_aux"],
+                              record=record, seed=spec["seed"])
+        for q in spec["projs"]:
+            g = q["gen"]
+            cols = (0, spec["n_total"]) if g.get("cols") == "all" else None
+            qid = nw.generate_projection(q["src"], q["tgt"], out_degree=g["mode"] == "out",
+                                         degree=g["degree"], gen_id=g["id"], dmin=g["dmin"], dmax=g["dmax"],
+                                         w_lo=g["w_lo"], w_span=g["w_span"], seed=spec["seed"], cols=cols,
+                                         receptor=q["receptor"])
+            if q.get("plastic"):
+                nw.set_stdp(qid, q["stdp"])
+        nw.finalize(True)
+        return nw

@@ -43,7 +43,8 @@ def _offsets(spec):
 
 def brunel(n_exc: int = 10_000, n_inh: int = 2_500, c_exc: int = 1_000, c_inh: int = 250, *,
            delay: int = 15, dt: float = 1e-4, steps: int = 10_000, g: float = 5.0,
-           j_psp: float = 0.1e-3, stdp: bool = False, seed: int = 1, slow_ratio: int = 1) -> dict:
+           j_psp: float = 0.1e-3, stdp: bool = False, seed: int = 1, slow_ratio: int = 1,
+           v0_uniform: bool = True) -> dict:
     """Brunel (2000) balanced LIF network, model A.
 
     Rest 0, threshold 20 mV, reset 10 mV, tau_m 20 ms, t_ref 2 ms, c_m 250 pF.
@@ -51,7 +52,8 @@ def brunel(n_exc: int = 10_000, n_inh: int = 2_500, c_exc: int = 1_000, c_inh: i
     weights are -g*w.  External drive: nu_ext = 2*nu_thr through C_E
     sources, i.e. Poisson(2) events of w per step.  With stdp=True, pair
     STDP on E->E (A+ 0.01, A- 0.0105, tau 20 ms, weights clipped to [0, 2w],
-    learning rate w so that A+/A- are relative to w)."""
+    learning rate w so that A+/A- are relative to w).  Initial potentials
+    V0 ~ U(0, threshold) when v0_uniform (else all at rest)."""
     c_m = LIF_BRUNEL[5]
     w = j_psp * c_m / dt
     lam = 2.0 * LIF_BRUNEL[1] * dt / (j_psp * LIF_BRUNEL[3])
@@ -65,6 +67,9 @@ def brunel(n_exc: int = 10_000, n_inh: int = 2_500, c_exc: int = 1_000, c_inh: i
         ],
         "projs": [],
     }
+    if v0_uniform:
+        for p in spec["pops"]:
+            p["init"] = {"v": ("uniform", 0.0, LIF_BRUNEL[1], 0)}
     stdp_p = [0.020, 0.020, 0.01, -0.0105, 0.0, 2.0 * w, w]
     for gid, (s, t, deg, wt) in enumerate([(0, 0, c_exc, w), (0, 1, c_exc, w),
                                           (1, 0, c_inh, -g * w), (1, 1, c_inh, -g * w)]):

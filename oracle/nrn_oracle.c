@@ -318,16 +318,18 @@ ORC_EXPORT int orc_net_run(const orc_net* net) {
 /* src/connectivity/topology/random.cpp:25-95; fixed in/out-degree are      */
 /* defined here and on the device with the same Philox stream).             */
 /*                                                                          */
-/* Draw for (target i, slot k) of projection `proj`:                        */
-/*   words = Philox(seed; c0 = tgt_offset + i, c1 = k, c2 = proj,           */
-/*                  c3 = ORC_STREAM_CONN)                                   */
-/*   source = (w0 * m) >> 32, m = n_src (or n_src-1 without autapses, the   */
-/*            draw then skipping the target's own index)                    */
+/* A draw belongs to (row r, slot k) of generator `gen`; rows are targets   */
+/* (fixed in-degree) or sources (fixed out-degree), identified by global    */
+/* id g_r = row_offset + r:                                                 */
+/*   words  = Philox(seed; c0 = g_r, c1 = k, c2 = gen, c3 = ORC_STREAM_CONN) */
+/*   column = (w0 * m) >> 32 over the m = n_col candidate columns, or over  */
+/*            n_col - 1 when autapses are excluded and g_r lies inside the  */
+/*            column range, the draw then skipping g_r's own column         */
 /*   delay  = dmin + ((w1 * (dmax-dmin+1)) >> 32)                           */
 /*   weight = w_lo + w_span * u01(w2)                                       */
-/* Fixed out-degree swaps the roles: c0 = src_offset + j draws targets.     */
-/* Synapses are emitted in source-major order, ties kept in (i, k) order    */
-/* (a stable sort by source).                                               */
+/* Only synapses whose target global id lies in [keep_lo, keep_hi) are      */
+/* kept (one draw stream can feed several target populations).  Synapses   */
+/* are emitted source-major, ties in (row, slot) order (a stable sort).     */
 /* ------------------------------------------------------------------------ */
 static inline void conn_words(uint64_t seed, uint32_t c0, uint32_t c1, uint32_t c2,
                               uint32_t w[4]) {
@@ -335,48 +337,70 @@ static inline void conn_words(uint64_t seed, uint32_t c0, uint32_t c1, uint32_t 
     orc_philox4x32_10(w, (uint32_t)seed, (uint32_t)(seed >> 32));
 }
 
+/* Returns the number of synapses written (source/target as local indices of
+ * the source range and of the kept target range), or the count alone when
+ * the output pointers are NULL. */
 ORC_EXPORT int64_t orc_gen_fixed_degree(
-    int out_degree_mode, uint64_t seed, uint32_t proj,
+    int out_degree_mode, uint64_t seed, uint32_t gen,
     int32_t n_src, int32_t src_offset, int32_t n_tgt, int32_t tgt_offset,
     int32_t degree, int autapses_excluded, int32_t dmin, int32_t dmax,
-    float w_lo, float w_span,
+    float w_lo, float w_span, int32_t keep_lo, int32_t keep_hi,
     int32_t* out_src, int32_t* out_tgt, float* out_w, uint8_t* out_delay) {
-    int64_t total = (int64_t)(out_degree_mode ? n_src : n_tgt) * degree;
-    int32_t* s = (int32_t*)malloc((size_t)total * 4);
-    int32_t* tg = (int32_t*)malloc((size_t)total * 4);
-    float* ww = (float*)malloc((size_t)total * 4);
-    uint8_t* dd = (uint8_t*)malloc((size_t)total);
-    int32_t span = dmax - dmin + 1;
-    int same = autapses_excluded && (n_src == n_tgt) && (src_offset == tgt_offset);
-    int64_t e = 0;
     int32_t nrow = out_degree_mode ? n_src : n_tgt;
     int32_t ncol = out_degree_mode ? n_tgt : n_src;
     int32_t roff = out_degree_mode ? src_offset : tgt_offset;
+    int32_t coff = out_degree_mode ? tgt_offset : src_offset;
+    int64_t total = (int64_t)nrow * degree;
+    int32_t* s = (int32_t*)malloc((size_t)(total > 0 ? total : 1) * 4);
+    int32_t* tg = (int32_t*)malloc((size_t)(total > 0 ? total : 1) * 4);
+    float* ww = (float*)malloc((size_t)(total > 0 ? total : 1) * 4);
+    uint8_t* dd = (uint8_t*)malloc((size_t)(total > 0 ? total : 1));
+    uint32_t span = (uint32_t)(dmax - dmin + 1);
+    int64_t e = 0;
     for (int32_t r = 0; r < nrow; ++r) {
+        int32_t g = roff + r;
+        int self = autapses_excluded && g >= coff && g < coff + ncol;
+        uint32_t m = (uint32_t)(self ? ncol - 1 : ncol);
         for (int32_t k = 0; k < degree; ++k) {
             uint32_t w[4];
-            conn_words(seed, (uint32_t)(roff + r), (uint32_t)k, proj, w);
-            uint32_t m = (uint32_t)(same ? ncol - 1 : ncol);
+            conn_words(seed, (uint32_t)g, (uint32_t)k, gen, w);
             uint32_t c = (uint32_t)(((uint64_t)w[0] * m) >> 32);
-            if (same && c >= (uint32_t)r) c += 1;
-            uint32_t d = (uint32_t)dmin + (uint32_t)(((uint64_t)w[1] * (uint32_t)span) >> 32);
-            float wt = w_lo + w_span * orc_u01(w[2]);
-            if (out_degree_mode) { s[e] = r; tg[e] = (int32_t)c; }
-            else { s[e] = (int32_t)c; tg[e] = r; }
-            ww[e] = wt; dd[e] = (uint8_t)d;
+            if (self && c >= (uint32_t)(g - coff)) c += 1;
+            uint32_t d = (uint32_t)dmin + (uint32_t)(((uint64_t)w[1] * span) >> 32);
+            int32_t src_g = out_degree_mode ? g : coff + (int32_t)c;
+            int32_t tgt_g = out_degree_mode ? coff + (int32_t)c : g;
+            if (tgt_g < keep_lo || tgt_g >= keep_hi) continue;
+            s[e] = src_g - src_offset;
+            tg[e] = tgt_g - keep_lo;
+            ww[e] = w_lo + w_span * orc_u01(w[2]);
+            dd[e] = (uint8_t)d;
             ++e;
         }
     }
-    /* stable counting sort by source */
-    int64_t* cnt = (int64_t*)calloc((size_t)n_src + 1, sizeof(int64_t));
-    for (int64_t k = 0; k < total; ++k) cnt[s[k] + 1]++;
-    for (int32_t j = 0; j < n_src; ++j) cnt[j + 1] += cnt[j];
-    for (int64_t k = 0; k < total; ++k) {
-        int64_t pos = cnt[s[k]]++;
-        out_src[pos] = s[k]; out_tgt[pos] = tg[k]; out_w[pos] = ww[k]; out_delay[pos] = dd[k];
+    if (out_src) {
+        /* stable counting sort by source */
+        int64_t* cnt = (int64_t*)calloc((size_t)n_src + 1, sizeof(int64_t));
+        for (int64_t k = 0; k < e; ++k) cnt[s[k] + 1]++;
+        for (int32_t j = 0; j < n_src; ++j) cnt[j + 1] += cnt[j];
+        for (int64_t k = 0; k < e; ++k) {
+            int64_t pos = cnt[s[k]]++;
+            out_src[pos] = s[k]; out_tgt[pos] = tg[k]; out_w[pos] = ww[k]; out_delay[pos] = dd[k];
+        }
+        free(cnt);
     }
-    free(cnt); free(s); free(tg); free(ww); free(dd);
-    return total;
+    free(s); free(tg); free(ww); free(dd);
+    return e;
+}
+
+/* Per-neuron initial values: lo + span * u01(Philox(seed; gid, which, 0,
+ * ORC_STREAM_INIT)[0]). */
+ORC_EXPORT void orc_init_uniform(uint64_t seed, uint32_t which, int32_t offset, int32_t n,
+                                 float lo, float span, float* out) {
+    for (int32_t i = 0; i < n; ++i) {
+        uint32_t w[4] = {(uint32_t)(offset + i), which, 0u, ORC_STREAM_INIT};
+        orc_philox4x32_10(w, (uint32_t)seed, (uint32_t)(seed >> 32));
+        out[i] = lo + span * orc_u01(w[0]);
+    }
 }
 
 /* Drive samples, for checking the device RNG. */

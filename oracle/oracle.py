@@ -106,7 +106,10 @@ def _lib(which: str):
             lib.orc_neuron_run.argtypes = [C.POINTER(OrcPop), C.c_int, C.c_double] + [C.c_void_p] * 5
             lib.orc_gen_fixed_degree.restype = C.c_int64
             lib.orc_gen_fixed_degree.argtypes = [C.c_int, C.c_uint64, C.c_uint32] + [C.c_int32] * 5 + \
-                [C.c_int, C.c_int32, C.c_int32, C.c_float, C.c_float] + [C.c_void_p] * 4
+                [C.c_int, C.c_int32, C.c_int32, C.c_float, C.c_float, C.c_int32, C.c_int32] + \
+                [C.c_void_p] * 4
+            lib.orc_init_uniform.argtypes = [C.c_uint64, C.c_uint32, C.c_int32, C.c_int32, C.c_float,
+                                             C.c_float, C.c_void_p]
             lib.orc_drive_values.argtypes = [C.c_int, C.c_double, C.c_double, C.c_uint64,
                                              C.c_int32, C.c_int32, C.c_int32, C.c_void_p]
             lib.orc_philox.argtypes = [C.c_uint64] + [C.c_uint32] * 4 + [C.c_void_p]
@@ -250,21 +253,31 @@ def neuron_reference(pop: dict, steps: int, dt: float, I=None) -> dict:
     return _neuron("harness", pop, steps, dt, I)
 
 
-def gen_fixed_degree(seed: int, proj: int, n_src: int, src_offset: int, n_tgt: int,
+def gen_fixed_degree(seed: int, gen: int, n_src: int, src_offset: int, n_tgt: int,
                      tgt_offset: int, degree: int, *, out_degree: bool = False,
                      no_autapses: bool = True, dmin: int = 1, dmax: int = 1,
-                     w_lo: float = 1.0, w_span: float = 0.0):
-    """Fixed in-degree (or out-degree) synapse list in source-major order."""
-    total = (n_src if out_degree else n_tgt) * degree
+                     w_lo: float = 1.0, w_span: float = 0.0, keep=None):
+    """Fixed in-degree (or out-degree) synapse list in source-major order.
+
+    Sources are local to [src_offset, src_offset + n_src); kept targets are
+    local to keep = (lo, hi) (default: the whole target range)."""
+    lo, hi = keep if keep is not None else (tgt_offset, tgt_offset + n_tgt)
+    lib = _lib("oracle")
+    args = (int(out_degree), seed, gen, n_src, src_offset, n_tgt, tgt_offset, degree,
+            int(no_autapses), dmin, dmax, float(w_lo), float(w_span), lo, hi)
+    total = lib.orc_gen_fixed_degree(*args, None, None, None, None)
     s = np.zeros(total, np.int32)
     t = np.zeros(total, np.int32)
     w = np.zeros(total, np.float32)
     d = np.zeros(total, np.uint8)
-    _lib("oracle").orc_gen_fixed_degree(int(out_degree), seed, proj, n_src, src_offset, n_tgt,
-                                        tgt_offset, degree, int(no_autapses), dmin, dmax,
-                                        float(w_lo), float(w_span), s.ctypes.data, t.ctypes.data,
-                                        w.ctypes.data, d.ctypes.data)
+    lib.orc_gen_fixed_degree(*args, s.ctypes.data, t.ctypes.data, w.ctypes.data, d.ctypes.data)
     return s, t, w, d
+
+
+def init_uniform(seed: int, which: int, offset: int, n: int, lo: float, span: float):
+    out = np.zeros(n, np.float32)
+    _lib("oracle").orc_init_uniform(seed, which, offset, n, float(lo), float(span), out.ctypes.data)
+    return out
 
 
 def drive_values(kind: str, d0: float, d1: float, seed: int, offset: int, n: int, step: int):
