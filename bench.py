@@ -41,9 +41,12 @@ def load_peaks():
         return PEAKS_FALLBACK, "fallback"
 
 
-def workload_spec(name: str, world: int, steps: int):
+def workload_spec(name: str, world: int, steps: int, scale: float = 1.0):
     from libnrn_b200 import workloads as W
     if name == "brunel_stdp":
+        if scale != 1.0:
+            return W.brunel(int(838_860 * world * scale), int(209_716 * world * scale), 1_000, 250,
+                            steps=steps, stdp=True)
         return W.brunel_stdp_per_gpu(world, steps=steps)
     if name == "brunel":
         return W.brunel(10_000 * world, 2_500 * world, 1_000, 250, steps=steps)
@@ -182,6 +185,8 @@ def main():
     ap.add_argument("--chunk", type=int, default=0)
     ap.add_argument("--profile-steps", type=int, default=300)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--scale", type=float, default=1.0,
+                    help="network size factor (profiling of small cases only; the bench line uses 1)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     rank = int(os.environ.get("RANK", "0"))
@@ -201,7 +206,7 @@ def main():
 
     peaks, peaks_kind = load_peaks()
     torch.cuda.set_device(local)
-    spec = workload_spec(args.workload, 1, args.steps)
+    spec = workload_spec(args.workload, 1, args.steps, args.scale)
     t_setup = time.perf_counter()
     nw = Network.from_spec(spec, device=local, record=True)
     torch.cuda.synchronize()
@@ -247,6 +252,7 @@ def main():
     achieved = alg.get("deliver") / (phases["deliver"] / 1e3) / 1e9 if phases["deliver"] > 0 else 0.0
 
     # e2e: initial state from pinned host, run, raster to host, all timed.
+    # The copies run on torch's stream; the engine stream starts after them.
     host_state = []
     for p in nw.pops:
         for k in ("v", "ref"):
@@ -256,9 +262,9 @@ def main():
     h2d = sum(h.numel() * 4 for _, h in host_state)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    with torch.cuda.stream(stream):
-        for dev_t, h in host_state:
-            dev_t.copy_(h, non_blocking=True)
+    for dev_t, h in host_state:
+        dev_t.copy_(h, non_blocking=True)
+    torch.cuda.current_stream().synchronize()
     e_s0, e_e0 = nw.counters()
     nw.run(args.steps, args.chunk)
     st2, gid2 = nw.raster()
@@ -266,6 +272,8 @@ def main():
     t1 = time.perf_counter()
     d2h = len(gid2) * 8
     e2e = (e_e1 - e_e0) / (t1 - t0)
+    del host_state
+    torch.cuda.synchronize()
 
     cpu = None
     if not args.no_cpu:
@@ -305,6 +313,8 @@ def main():
             line["cpu_baseline"] = {"value": cpu["events_per_s"], "unit": "events/s", "cores": cpu["cores"],
                                     "kind": cpu["kind"], "sample": cpu["sample"],
                                     "neuron_updates_per_s": cpu["neuron_updates_per_s"], "rtf": cpu["rtf"]}
+    del stream
+    torch.cuda.synchronize()
     nw.close()
     print(json.dumps(line), flush=True)
 

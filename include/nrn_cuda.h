@@ -301,7 +301,8 @@ NRN_API nrn_status_t nrn_engine_run(nrn_engine* e, int64_t steps, int32_t chunk)
 NRN_API nrn_status_t nrn_engine_sync(nrn_engine* e);
 NRN_API nrn_status_t nrn_engine_stream(nrn_engine* e, nrn_stream_t* stream);
 NRN_API int64_t nrn_engine_step(const nrn_engine* e);
-/* Recorded spikes since the last call (host buffers); *n receives the count
+/* Recorded spikes since the last call (host buffers), sorted by step and,
+ * within a step, by ascending global id; *n receives the count
  * (if above cap, nothing is copied and NRN_ERR_CAPACITY is returned). */
 NRN_API nrn_status_t nrn_engine_raster(nrn_engine* e, int32_t* step, int32_t* gid, int64_t cap, int64_t* n);
 /* Weights of a projection in the order the synapses were given (host). */

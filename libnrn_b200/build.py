@@ -23,7 +23,7 @@ OBJ = os.path.join(OUT, "obj")
 LIB = os.path.join(OUT, "libnrn_cuda.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-FLAGS = ["-std=c++17", "-O3", "-lineinfo", "-fmad=false", "-Xcompiler", "-fPIC", "-Xcompiler",
+FLAGS = ["-std=c++17", "-O3", "-lineinfo", "-fmad=false", "-cudart=shared", "-Xcompiler", "-fPIC", "-Xcompiler",
          "-fvisibility=hidden", f"-I{os.path.join(ROOT, 'include')}", f"-I{CSRC}"]
 SOURCES = ["neuron.cu", "deliver.cu", "connect.cu", "engine.cu"]
 
@@ -60,7 +60,10 @@ def build(force: bool = False, verbose: bool = False) -> str:
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 4)) as ex:
         objs = list(ex.map(_compile, srcs))
     if _stale(LIB, objs):
-        cmd = [NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-Xlinker", "--no-undefined"]
+        # one CUDA runtime per process: link the shared runtime (in a torch
+        # process the runtime torch loaded is reused)
+        cmd = [NVCC, *ARCH, "-shared", "-cudart=shared", "-o", LIB, *objs, "-Xlinker", "--no-undefined",
+               "-Xlinker", "-rpath,/usr/local/cuda/lib64"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stderr[-4000:]}")

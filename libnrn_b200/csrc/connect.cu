@@ -102,6 +102,21 @@ __global__ void gather_u32(const uint32_t* perm, int64_t n, const uint32_t* in, 
         out[k] = in[perm[k]];
 }
 
+__global__ void raster_pack(const int32_t* step, const int32_t* gid, int64_t n, unsigned long long* key) {
+    for (int64_t k = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; k < n;
+         k += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        key[k] = (static_cast<unsigned long long>(static_cast<uint32_t>(step[k])) << 32) |
+                 static_cast<uint32_t>(gid[k]);
+}
+
+__global__ void raster_unpack(const unsigned long long* key, int64_t n, int32_t* step, int32_t* gid) {
+    for (int64_t k = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; k < n;
+         k += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        step[k] = static_cast<int32_t>(key[k] >> 32);
+        gid[k] = static_cast<int32_t>(key[k] & 0xFFFFFFFFull);
+    }
+}
+
 __global__ void gen_kernel(const GenArgs g, int32_t* src, int32_t* tgt, float* w, uint8_t* delay) {
     const int64_t total = static_cast<int64_t>(g.n_rows) * g.degree;
     const uint32_t span = static_cast<uint32_t>(g.dmax - g.dmin + 1);
@@ -303,6 +318,33 @@ nrn_status_t build_transpose(DevCsr& c, cudaStream_t s) {
     return NRN_OK;
 #undef CSTEP
 #undef STEP
+}
+
+nrn_status_t sort_raster(int32_t* step, int32_t* gid, int64_t n, cudaStream_t s) {
+    if (n <= 1) return NRN_OK;
+    NRN_CHECK_ARG(n < (int64_t(1) << 31), "raster too large to sort at once");
+    unsigned long long *a = nullptr, *b = nullptr;
+    void* tmp = nullptr;
+    size_t tmp_bytes = 0;
+    nrn_status_t st = dalloc(&a, n);
+    if (st == NRN_OK) st = dalloc(&b, n);
+    if (st == NRN_OK) {
+        raster_pack<<<grid_for(n), 256, 0, s>>>(step, gid, n, a);
+        cub::DoubleBuffer<unsigned long long> db(a, b);
+        cudaError_t e = cub::DeviceRadixSort::SortKeys(nullptr, tmp_bytes, db, static_cast<int>(n), 0, 64, s);
+        if (e == cudaSuccess) e = cudaMalloc(&tmp, tmp_bytes);
+        if (e == cudaSuccess) e = cub::DeviceRadixSort::SortKeys(tmp, tmp_bytes, db, static_cast<int>(n), 0, 64, s);
+        if (e == cudaSuccess) {
+            raster_unpack<<<grid_for(n), 256, 0, s>>>(db.Current(), n, step, gid);
+            e = cudaGetLastError();
+        }
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) st = cuda_fail(e, "raster sort");
+    }
+    if (tmp) cudaFree(tmp);
+    dfree(a);
+    dfree(b);
+    return st;
 }
 
 nrn_status_t generate(const GenArgs& g, int32_t* src, int32_t* tgt, float* w, uint8_t* delay, cudaStream_t s) {

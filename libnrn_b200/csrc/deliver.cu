@@ -119,22 +119,25 @@ __global__ void __launch_bounds__(kThreads) deliver_kernel(const __grid_constant
         const long long seg = static_cast<long long>(j) * pr.nd + tab.k[lo];
         const long long s0 = pr.seg_ptr[seg], s1 = pr.seg_ptr[seg + 1];
         if (lane == 0) my_events += static_cast<unsigned long long>(s1 - s0);
-        if (pr.mod == nullptr) {
-            long long s = s0 + lane;
-            for (; s + 96 < s1; s += 128) {
-                const uint32_t t0 = __ldg(pr.tgt + s), t1 = __ldg(pr.tgt + s + 32);
-                const uint32_t t2 = __ldg(pr.tgt + s + 64), t3 = __ldg(pr.tgt + s + 96);
-                const float w0 = __ldg(pr.w + s), w1 = __ldg(pr.w + s + 32);
-                const float w2 = __ldg(pr.w + s + 64), w3 = __ldg(pr.w + s + 96);
-                atomicAdd(pr.acc + t0, w0);
-                atomicAdd(pr.acc + t1, w1);
-                atomicAdd(pr.acc + t2, w2);
-                atomicAdd(pr.acc + t3, w3);
+        // 8 synapses per lane per pass: all loads issued before the
+        // reductions, so each lane keeps 16 independent loads in flight.
+        for (long long base = s0; base < s1; base += 256) {
+            uint32_t t[8];
+            float w[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const long long s = base + lane + 32 * u;
+                if (s < s1) {
+                    t[u] = __ldg(pr.tgt + s);
+                    w[u] = __ldg(pr.w + s);
+                    if (pr.mod != nullptr) w[u] = w[u] * __ldg(pr.mod + s);
+                }
             }
-            for (; s < s1; s += 32) atomicAdd(pr.acc + __ldg(pr.tgt + s), __ldg(pr.w + s));
-        } else {
-            for (long long s = s0 + lane; s < s1; s += 32)
-                atomicAdd(pr.acc + __ldg(pr.tgt + s), __ldg(pr.w + s) * __ldg(pr.mod + s));
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const long long s = base + lane + 32 * u;
+                if (s < s1) atomicAdd(pr.acc + t[u], w[u]);
+            }
         }
     }
     if (P.events && lane == 0 && my_events) atomicAdd(&blk_events, my_events);
@@ -163,10 +166,10 @@ __global__ void stdp_trace_kernel(const __grid_constant__ nrn_stdp_t s, long lon
     }
 }
 
-__device__ __forceinline__ float stdp_apply(const nrn_stdp_t& s, long long syn, float dw) {
+__device__ __forceinline__ float stdp_apply(const nrn_stdp_t& s, long long syn, float w_old, float dw) {
     float upd = (dw * s.lr) * 1.0f;
     if (s.proj.mod) upd = upd * s.proj.mod[syn];
-    float w = s.w_mut[syn] + upd;
+    float w = w_old + upd;
     w = fmaxf(w, s.w_min);
     w = fminf(w, s.w_max);
     return w;
@@ -191,22 +194,67 @@ __global__ void __launch_bounds__(kThreads) stdp_update_kernel(const __grid_cons
             const float ltp = s.a_plus * s.x_pre[j];
             const long long b0 = s.proj.seg_ptr[static_cast<long long>(j) * nd];
             const long long b1 = s.proj.seg_ptr[static_cast<long long>(j + 1) * nd];
-            for (long long syn = b0 + lane; syn < b1; syn += 32) {
-                const uint32_t i = s.proj.tgt[syn];
-                const float dw = ltp * s.spike_tgt[i] - (s.a_minus * s.x_post[i]) * 1.0f;
-                s.w_mut[syn] = stdp_apply(s, syn, dw);
+            for (long long base = b0; base < b1; base += 128) {
+                uint32_t t[4];
+                float w[4], post[4], xp[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const long long syn = base + lane + 32 * u;
+                    if (syn < b1) {
+                        t[u] = s.proj.tgt[syn];
+                        w[u] = s.w_mut[syn];
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const long long syn = base + lane + 32 * u;
+                    if (syn < b1) {
+                        post[u] = s.spike_tgt[t[u]];
+                        xp[u] = s.x_post[t[u]];
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const long long syn = base + lane + 32 * u;
+                    if (syn < b1) {
+                        const float dw = ltp * post[u] - (s.a_minus * xp[u]) * 1.0f;
+                        s.w_mut[syn] = stdp_apply(s, syn, w[u], dw);
+                    }
+                }
             }
         } else {
             // target i spiked: in-synapses from sources that did not spike get +A+ x_pre
             const int i = s.hist_tgt.ids[static_cast<long long>(slot_t) * s.hist_tgt.cap + (it - n_pre)];
             const float ltd = (s.a_minus * s.x_post[i]) * 0.0f;
             const long long b0 = s.in_ptr[i], b1 = s.in_ptr[i + 1];
-            for (long long k = b0 + lane; k < b1; k += 32) {
-                const uint32_t j = s.in_src[k];
-                if (s.spike_src[j] != 0.0f) continue;   // handled with the source's row
-                const long long syn = s.in_syn[k];
-                const float dw = (s.a_plus * s.x_pre[j]) * 1.0f - ltd;
-                s.w_mut[syn] = stdp_apply(s, syn, dw);
+            for (long long base = b0; base < b1; base += 128) {
+                uint32_t j[4], syn[4];
+                float pre[4], xp[4], w[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const long long k = base + lane + 32 * u;
+                    if (k < b1) {
+                        j[u] = s.in_src[k];
+                        syn[u] = s.in_syn[k];
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const long long k = base + lane + 32 * u;
+                    if (k < b1) {
+                        pre[u] = s.spike_src[j[u]];
+                        xp[u] = s.x_pre[j[u]];
+                        w[u] = s.w_mut[syn[u]];
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const long long k = base + lane + 32 * u;
+                    if (k < b1 && pre[u] == 0.0f) {   // else handled with the source's row
+                        const float dw = (s.a_plus * xp[u]) * 1.0f - ltd;
+                        s.w_mut[syn[u]] = stdp_apply(s, syn[u], w[u], dw);
+                    }
+                }
             }
         }
     }
@@ -271,7 +319,7 @@ extern "C" nrn_status_t nrn_cuda_deliver_counted(const nrn_proj_t* projs, int32_
     P.step_off = step_off;
     P.step_base = reinterpret_cast<const long long*>(step_base);
     P.events = events;
-    const int blocks = 4 * sm_count();
+    const int blocks = 8 * sm_count();
     deliver_kernel<<<blocks, kThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(P);
     NRN_CUDA_TRY(cudaGetLastError());
     return NRN_OK;
@@ -291,7 +339,7 @@ extern "C" nrn_status_t nrn_cuda_stdp_step(const nrn_stdp_t* s, int64_t step_off
     const long long* base = reinterpret_cast<const long long*>(step_base);
     stdp_trace_kernel<<<trace_blocks, tb, 0, st>>>(*s, step_off, base);
     NRN_CUDA_TRY(cudaGetLastError());
-    stdp_update_kernel<<<4 * sm_count(), kThreads, 0, st>>>(*s, step_off, base);
+    stdp_update_kernel<<<8 * sm_count(), kThreads, 0, st>>>(*s, step_off, base);
     NRN_CUDA_TRY(cudaGetLastError());
     return NRN_OK;
 }

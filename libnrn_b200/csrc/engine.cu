@@ -653,6 +653,8 @@ nrn_status_t nrn_engine_raster(nrn_engine* e, int32_t* step, int32_t* gid, int64
         return fail(NRN_ERR_CAPACITY, "spike raster overflowed: read it more often (" + std::to_string(cnt) +
                                           " spikes, capacity " + std::to_string(e->raster_cap) + ")");
     if (static_cast<int64_t>(cnt) > cap) return fail(NRN_ERR_CAPACITY, "output buffer too small for the raster");
+    // order of the reference's recorder: by step, ascending ids within a step
+    NRN_TRY(sort_raster(e->raster_step, e->raster_gid, static_cast<int64_t>(cnt), e->stream));
     NRN_CUDA_TRY(cudaMemcpyAsync(step, e->raster_step, cnt * 4, cudaMemcpyDeviceToHost, e->stream));
     NRN_CUDA_TRY(cudaMemcpyAsync(gid, e->raster_gid, cnt * 4, cudaMemcpyDeviceToHost, e->stream));
     NRN_CUDA_TRY(cudaMemsetAsync(e->d_raster_count, 0, sizeof(unsigned long long), e->stream));

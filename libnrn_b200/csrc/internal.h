@@ -52,4 +52,7 @@ nrn_status_t generate(const GenArgs& g, int32_t* src, int32_t* tgt, float* w, ui
 
 int sm_count_current();
 
+// Sorts n raster entries in place by (step, global id).
+nrn_status_t sort_raster(int32_t* step, int32_t* gid, int64_t n, cudaStream_t s);
+
 }  // namespace nrn

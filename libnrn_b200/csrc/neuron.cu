@@ -128,7 +128,10 @@ __global__ void __launch_bounds__(256) pop_step_kernel(const __grid_constant__ P
             const float delta_t = par<HET>(a, 11, i), i_bg = par<HET>(a, 12, i);
             const bool active = ref <= 0.0f;
             float r = ref > 0.0f ? ref - a.dtf : ref;
-            float I_exp = (g_l * delta_t) * expf((v - v_th) / delta_t);
+            // exp in double, rounded once to float: the correctly rounded
+            // float exp in all but rare cases, as the reference's CPU exp.
+            const float ex = static_cast<float>(exp(static_cast<double>((v - v_th) / delta_t)));
+            float I_exp = (g_l * delta_t) * ex;
             float acc = (-g_l) * (v - v_rest);
             acc = acc + I_exp;
             acc = acc - w;

@@ -145,15 +145,14 @@ class Network:
         return int(self.L.nrn_engine_step(self.h))
 
     def raster(self, cap: int | None = None):
-        """Spikes recorded since the last call: (step, gid), sorted by step then id."""
+        """Spikes recorded since the last call: (step, gid), sorted by step then
+        id (the engine sorts on the device before the copy)."""
         n = C.c_int64()
         cap = cap if cap is not None else 1 << 26
         st = np.empty(cap, np.int32)
         gd = np.empty(cap, np.int32)
         N.check(self.L.nrn_engine_raster(self.h, st.ctypes.data, gd.ctypes.data, cap, C.byref(n)), "raster")
-        st, gd = st[:n.value], gd[:n.value]
-        o = np.lexsort((gd, st))
-        return st[o], gd[o]
+        return st[:n.value], gd[:n.value]   # sorted on the device
 
     def weights(self, proj: int) -> np.ndarray:
         nnz = C.c_int64()

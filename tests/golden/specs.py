@@ -34,7 +34,9 @@ def gen_args(spec: dict, q: dict):
     return args, kw
 
 
-def realize(spec: dict, *, steps=None, trace_ids=None) -> dict:
+def realize(spec: dict, *, steps=None, trace_ids=None, dyadic_bits=None) -> dict:
+    """dyadic_bits=k rounds every weight to a multiple of 2^-k, so that sums
+    of a few weights are exact in fp32 and independent of summation order."""
     net = {"steps": steps if steps is not None else spec["steps"], "dt": spec["dt"],
            "seed": spec["seed"], "slow_ratio": spec.get("slow_ratio", 1), "pops": [], "projs": []}
     for p in spec["pops"]:
@@ -45,6 +47,8 @@ def realize(spec: dict, *, steps=None, trace_ids=None) -> dict:
     for q in spec["projs"]:
         args, kw = gen_args(spec, q)
         s, t, w, d = O.gen_fixed_degree(*args, **kw)
+        if dyadic_bits is not None:
+            w = (np.round(w.astype(np.float64) * 2.0 ** dyadic_bits) / 2.0 ** dyadic_bits).astype(np.float32)
         net["projs"].append({"src": q["src"], "tgt": q["tgt"], "receptor": q["receptor"],
                              "src_idx": s, "tgt_idx": t, "w": w, "delay": d,
                              "plastic": q.get("plastic", False),
