@@ -226,6 +226,46 @@ NRN_API nrn_status_t nrn_cuda_stdp_step(const nrn_stdp_t* s, int64_t step_off,
 NRN_API nrn_status_t nrn_cuda_clamp(float* w, int64_t n, float lo, float hi, nrn_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
+/* Block-dense connectivity (the nrn:: API's ConnectivityTensor layout)     */
+/* ------------------------------------------------------------------------ */
+
+/* Dense B x B blocks, CSR over target block rows; all arrays on the device,
+ * float [n_blocks][B][B] for weights and masks.  Replaces the reference's
+ * stub block-dense launcher (src/synapse/kernels/synapse_kernels.cu:56-79). */
+typedef struct {
+    const int32_t* row_ptr;          /* [n_target_blocks + 1] */
+    const int32_t* col_idx;          /* [n_blocks]            */
+    const float* weights;
+    const float* structural_mask;
+    const float* modulatory_mask;
+    int64_t block_size;
+    int64_t n_blocks;
+    int64_t n_source;
+    int64_t n_target;
+} nrn_block_csr_t;
+
+/* i_syn[t] += sum over the blocks of t's row of ((W*Ms)*Mm)[t,:] . spikes
+ * (connection_deliver, src/connectivity/connect.cpp:36-79). */
+NRN_API nrn_status_t nrn_cuda_block_deliver(const nrn_block_csr_t* c, const float* spikes, float* i_syn,
+                                            nrn_stream_t stream);
+/* One STDP update on block-dense weights with per-synapse traces
+ * (stdp_update, src/plasticity/stdp.cpp:43-141).  params = {decay_pre,
+ * decay_post, a_plus, |a_minus|, learning_rate, w_min, w_max}. */
+NRN_API nrn_status_t nrn_cuda_block_stdp(const nrn_block_csr_t* c, float* weights, float* trace_pre,
+                                         float* trace_post, const float* pre_spikes, const float* post_spikes,
+                                         const float* params, nrn_stream_t stream);
+/* Ids of the non-zero entries of x appended to ids (order within the
+ * result unspecified); *count incremented. */
+NRN_API nrn_status_t nrn_cuda_compact(const float* x, int64_t n, int32_t* ids, int32_t* count,
+                                      nrn_stream_t stream);
+/* out[i] = ring[(write_pos - delays[i]) mod depth][i]  (SpikeBuffer::read_batch). */
+NRN_API nrn_status_t nrn_cuda_gather_ring(const float* ring, int64_t n, int64_t depth, int64_t write_pos,
+                                          const int64_t* delays, float* out, nrn_stream_t stream);
+/* dst[pos[k]] = src[k]. */
+NRN_API nrn_status_t nrn_cuda_scatter(const float* src, const int64_t* pos, int64_t n, float* dst,
+                                      nrn_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
 /* Engine: a network resident on one GPU                                   */
 /* ------------------------------------------------------------------------ */
 
@@ -299,12 +339,21 @@ NRN_API nrn_status_t nrn_engine_finalize(nrn_engine* e, int32_t init_update);
 /* Enqueues `steps` steps (CUDA graphs of `chunk` steps; 0 picks a size). */
 NRN_API nrn_status_t nrn_engine_run(nrn_engine* e, int64_t steps, int32_t chunk);
 NRN_API nrn_status_t nrn_engine_sync(nrn_engine* e);
+/* Sets the number of the next step (drive counters, slow-clock boundaries,
+ * raster step numbers); spikes already in flight keep their ring slots. */
+NRN_API nrn_status_t nrn_engine_set_step(nrn_engine* e, int64_t step);
 NRN_API nrn_status_t nrn_engine_stream(nrn_engine* e, nrn_stream_t* stream);
 NRN_API int64_t nrn_engine_step(const nrn_engine* e);
 /* Recorded spikes since the last call (host buffers), sorted by step and,
  * within a step, by ascending global id; *n receives the count
  * (if above cap, nothing is copied and NRN_ERR_CAPACITY is returned). */
 NRN_API nrn_status_t nrn_engine_raster(nrn_engine* e, int32_t* step, int32_t* gid, int64_t cap, int64_t* n);
+/* Weights of a projection in the order the synapses were given, into a
+ * device array of nnz floats (enqueued on the engine stream). */
+NRN_API nrn_status_t nrn_engine_weights_device(nrn_engine* e, int32_t proj, float* out, int64_t n);
+/* Current state pointers of a population (the caller re-allocated them). */
+NRN_API nrn_status_t nrn_engine_set_state(nrn_engine* e, int32_t pop, float* v, float* aux, float* refractory,
+                                          float* spike, float* i_syn);
 /* Weights of a projection in the order the synapses were given (host). */
 NRN_API nrn_status_t nrn_engine_weights(nrn_engine* e, int32_t proj, float* out, int64_t n);
 NRN_API nrn_status_t nrn_engine_nnz(nrn_engine* e, int32_t proj, int64_t* nnz);

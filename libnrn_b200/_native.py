@@ -29,7 +29,9 @@ EXPORTS = [
     "nrn_engine_add_projection", "nrn_engine_generate_projection", "nrn_engine_set_stdp",
     "nrn_engine_finalize", "nrn_engine_run", "nrn_engine_sync", "nrn_engine_stream", "nrn_engine_step",
     "nrn_engine_raster", "nrn_engine_weights", "nrn_engine_nnz", "nrn_engine_counters",
-    "nrn_engine_profile",
+    "nrn_engine_profile", "nrn_engine_weights_device", "nrn_engine_set_state", "nrn_engine_set_step",
+    "nrn_cuda_block_deliver", "nrn_cuda_block_stdp", "nrn_cuda_compact", "nrn_cuda_gather_ring",
+    "nrn_cuda_scatter",
 ]
 
 

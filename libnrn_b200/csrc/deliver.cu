@@ -35,6 +35,8 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kMaxPairs = 1024;   // (projection, delay) pairs per launch
+constexpr int kBatch = 8;         // items a block resolves at once
+constexpr int kUnroll = 4;        // synapses in flight per thread
 
 struct DeliverParams {
     nrn_proj_t proj[NRN_MAX_PROJ];
@@ -48,22 +50,44 @@ struct DeliverParams {
     unsigned long long* events;
 };
 
-struct PairTable {
-    long long start[kMaxPairs + 1];   // exclusive prefix of spike counts
-    short proj[kMaxPairs];
-    short k[kMaxPairs];
-    int slot[kMaxPairs];
+// Dynamic shared memory: pair table of npairs entries.
+struct PairView {
+    long long* start;   // [npairs + 1] exclusive prefix of spike counts
+    int* slot;          // [npairs]
+    short* proj;        // [npairs]
+    short* k;           // [npairs]
 };
 
+__device__ __forceinline__ PairView pair_view(void* base, int npairs) {
+    PairView v;
+    v.start = reinterpret_cast<long long*>(base);
+    v.slot = reinterpret_cast<int*>(v.start + npairs + 1);
+    v.proj = reinterpret_cast<short*>(v.slot + npairs);
+    v.k = v.proj + npairs;
+    return v;
+}
+
+size_t pair_smem(int npairs) {
+    return static_cast<size_t>(npairs + 1) * sizeof(long long) + static_cast<size_t>(npairs) * (4 + 2 + 2) + 16;
+}
+
+// Work is split in two phases per batch of kBatch items (spike, delay
+// segment): first one thread per item resolves the item's synapse range
+// into shared memory (one round of dependent loads for the whole batch),
+// then all threads of the block stride over the batch's synapses,
+// kUnroll at a time with every load issued before the reductions.
 __global__ void __launch_bounds__(kThreads) deliver_kernel(const __grid_constant__ DeliverParams P) {
-    __shared__ PairTable tab;
-    __shared__ unsigned long long blk_events;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const PairView tab = pair_view(smem_raw, P.npairs);
+    __shared__ long long item_pre[kBatch + 1];
+    __shared__ long long item_s0[kBatch];
+    __shared__ int item_q[kBatch];
     using Scan = cub::BlockScan<long long, kThreads>;
     __shared__ typename Scan::TempStorage scan_tmp;
     __shared__ long long carry;
 
     const long long step = P.step_off + (P.step_base ? *P.step_base : 0);
-    if (threadIdx.x == 0) { blk_events = 0; carry = 0; }
+    if (threadIdx.x == 0) carry = 0;
     if (blockIdx.x == 0 && threadIdx.x < P.nhist) {
         const nrn_spike_hist_t& h = P.hist[threadIdx.x];
         h.count[step % h.depth] = 0;   // this step's slot, filled by the updates that follow
@@ -82,13 +106,12 @@ __global__ void __launch_bounds__(kThreads) deliver_kernel(const __grid_constant
             const long long src_step = step - (pr.dmin + k);
             tab.proj[pi] = static_cast<short>(q);
             tab.k[pi] = static_cast<short>(k);
+            tab.slot[pi] = 0;
             if (src_step >= 0) {
                 const nrn_spike_hist_t& h = P.hist[pr.src_hist];
                 const int slot = static_cast<int>(src_step % h.depth);
                 tab.slot[pi] = slot;
                 cnt = h.count[slot];
-            } else {
-                tab.slot[pi] = 0;
             }
         }
         long long excl, total;
@@ -102,47 +125,71 @@ __global__ void __launch_bounds__(kThreads) deliver_kernel(const __grid_constant
     __syncthreads();
     const long long n_items = tab.start[P.npairs];
 
-    const int lane = threadIdx.x & 31;
-    const long long warp = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
-    const long long n_warps = (static_cast<long long>(gridDim.x) * kThreads) >> 5;
     unsigned long long my_events = 0;
-    for (long long it = warp; it < n_items; it += n_warps) {
-        // pair containing item `it` (binary search over the prefix)
-        int lo = 0, hi = P.npairs - 1;
-        while (lo < hi) {
-            const int mid = (lo + hi + 1) >> 1;
-            if (tab.start[mid] <= it) lo = mid; else hi = mid - 1;
-        }
-        const nrn_proj_t& pr = P.proj[tab.proj[lo]];
-        const nrn_spike_hist_t& h = P.hist[pr.src_hist];
-        const int j = h.ids[static_cast<long long>(tab.slot[lo]) * h.cap + (it - tab.start[lo])];
-        const long long seg = static_cast<long long>(j) * pr.nd + tab.k[lo];
-        const long long s0 = pr.seg_ptr[seg], s1 = pr.seg_ptr[seg + 1];
-        if (lane == 0) my_events += static_cast<unsigned long long>(s1 - s0);
-        // 8 synapses per lane per pass: all loads issued before the
-        // reductions, so each lane keeps 16 independent loads in flight.
-        for (long long base = s0; base < s1; base += 256) {
-            uint32_t t[8];
-            float w[8];
+    for (long long b0 = static_cast<long long>(blockIdx.x) * kBatch; b0 < n_items;
+         b0 += static_cast<long long>(gridDim.x) * kBatch) {
+        // phase A: synapse range of each item of the batch
+        if (threadIdx.x < kBatch) {
+            const long long it = b0 + threadIdx.x;
+            long long len = 0, s0 = 0;
+            int q = 0;
+            if (it < n_items) {
+                int lo = 0, hi = P.npairs - 1;
+                while (lo < hi) {
+                    const int mid = (lo + hi + 1) >> 1;
+                    if (tab.start[mid] <= it) lo = mid; else hi = mid - 1;
+                }
+                q = tab.proj[lo];
+                const nrn_proj_t& pr = P.proj[q];
+                const nrn_spike_hist_t& h = P.hist[pr.src_hist];
+                const int j = h.ids[static_cast<long long>(tab.slot[lo]) * h.cap + (it - tab.start[lo])];
+                const long long seg = static_cast<long long>(j) * pr.nd + tab.k[lo];
+                s0 = pr.seg_ptr[seg];
+                len = pr.seg_ptr[seg + 1] - s0;
+            }
+            item_s0[threadIdx.x] = s0;
+            item_q[threadIdx.x] = q;
+            // inclusive prefix over the batch within warp 0
+            long long incl = len;
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const long long s = base + lane + 32 * u;
-                if (s < s1) {
-                    t[u] = __ldg(pr.tgt + s);
-                    w[u] = __ldg(pr.w + s);
-                    if (pr.mod != nullptr) w[u] = w[u] * __ldg(pr.mod + s);
+            for (int o = 1; o < kBatch; o <<= 1) {
+                const long long y = __shfl_up_sync((1u << kBatch) - 1u, incl, o, kBatch);
+                if (threadIdx.x >= o) incl += y;
+            }
+            item_pre[threadIdx.x + 1] = incl;
+            if (threadIdx.x == 0) item_pre[0] = 0;
+        }
+        __syncthreads();
+        const long long total = item_pre[kBatch];
+        if (threadIdx.x == 0) my_events += static_cast<unsigned long long>(total);
+        // phase B: every synapse of the batch
+        for (long long f0 = threadIdx.x; f0 < total; f0 += static_cast<long long>(kThreads) * kUnroll) {
+            uint32_t t[kUnroll];
+            float w[kUnroll];
+            float* acc[kUnroll];
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const long long f = f0 + static_cast<long long>(u) * kThreads;
+                acc[u] = nullptr;
+                if (f < total) {
+                    int it = 0;
+#pragma unroll
+                    for (int b = 1; b < kBatch; ++b) it += (item_pre[b] <= f);
+                    const nrn_proj_t& pr = P.proj[item_q[it]];
+                    const long long syn = item_s0[it] + (f - item_pre[it]);
+                    t[u] = __ldg(pr.tgt + syn);
+                    w[u] = __ldg(pr.w + syn);
+                    if (pr.mod != nullptr) w[u] = w[u] * __ldg(pr.mod + syn);
+                    acc[u] = pr.acc;
                 }
             }
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const long long s = base + lane + 32 * u;
-                if (s < s1) atomicAdd(pr.acc + t[u], w[u]);
-            }
+            for (int u = 0; u < kUnroll; ++u)
+                if (acc[u] != nullptr) atomicAdd(acc[u] + t[u], w[u]);
         }
+        __syncthreads();
     }
-    if (P.events && lane == 0 && my_events) atomicAdd(&blk_events, my_events);
-    __syncthreads();
-    if (P.events && threadIdx.x == 0 && blk_events) atomicAdd(P.events, blk_events);
+    if (P.events && threadIdx.x == 0 && my_events) atomicAdd(P.events, my_events);
 }
 
 // ---------------------------------------------------------------------------
@@ -175,88 +222,108 @@ __device__ __forceinline__ float stdp_apply(const nrn_stdp_t& s, long long syn, 
     return w;
 }
 
-__global__ void __launch_bounds__(kThreads) stdp_update_kernel(const __grid_constant__ nrn_stdp_t s, long long step_off,
-                                                               const long long* step_base) {
+// Items: the spiking sources (their out-rows: -A- x_post, plus +A+ x_pre
+// where the target spiked too) then the spiking targets (their in-lists:
+// +A+ x_pre where the source did not spike).  Same two-phase batching as
+// the delivery.
+__global__ void __launch_bounds__(kThreads) stdp_update_kernel(const __grid_constant__ nrn_stdp_t s,
+                                                               long long step_off, const long long* step_base) {
+    __shared__ long long item_pre[kBatch + 1];
+    __shared__ long long item_s0[kBatch];
+    __shared__ float item_f[kBatch];
+    __shared__ int item_post[kBatch];   // 1: in-list item
+
     const long long step = step_off + (step_base ? *step_base : 0);
     if (!stdp_active(s, step)) return;
     const int slot_s = static_cast<int>(step % s.hist_src.depth);
     const int slot_t = static_cast<int>(step % s.hist_tgt.depth);
-    const int n_pre = s.hist_src.count[slot_s];
-    const int n_post = s.hist_tgt.count[slot_t];
-    const int lane = threadIdx.x & 31;
-    const long long warp = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
-    const long long n_warps = (static_cast<long long>(gridDim.x) * kThreads) >> 5;
+    const long long n_pre = s.hist_src.count[slot_s];
+    const long long n_items = n_pre + s.hist_tgt.count[slot_t];
     const int nd = s.proj.nd;
-    for (long long it = warp; it < n_pre + n_post; it += n_warps) {
-        if (it < n_pre) {
-            // source j spiked: every out-synapse gets -A- x_post (+A+ x_pre if the target spiked)
-            const int j = s.hist_src.ids[static_cast<long long>(slot_s) * s.hist_src.cap + it];
-            const float ltp = s.a_plus * s.x_pre[j];
-            const long long b0 = s.proj.seg_ptr[static_cast<long long>(j) * nd];
-            const long long b1 = s.proj.seg_ptr[static_cast<long long>(j + 1) * nd];
-            for (long long base = b0; base < b1; base += 128) {
-                uint32_t t[4];
-                float w[4], post[4], xp[4];
+    for (long long b0 = static_cast<long long>(blockIdx.x) * kBatch; b0 < n_items;
+         b0 += static_cast<long long>(gridDim.x) * kBatch) {
+        if (threadIdx.x < kBatch) {
+            const long long it = b0 + threadIdx.x;
+            long long len = 0, st = 0;
+            float f = 0.0f;
+            int post = 0;
+            if (it < n_pre) {
+                const int j = s.hist_src.ids[static_cast<long long>(slot_s) * s.hist_src.cap + it];
+                st = s.proj.seg_ptr[static_cast<long long>(j) * nd];
+                len = s.proj.seg_ptr[static_cast<long long>(j + 1) * nd] - st;
+                f = s.a_plus * s.x_pre[j];                       // A+ x_pre[j]
+            } else if (it < n_items) {
+                const int i = s.hist_tgt.ids[static_cast<long long>(slot_t) * s.hist_tgt.cap + (it - n_pre)];
+                st = s.in_ptr[i];
+                len = s.in_ptr[i + 1] - st;
+                f = (s.a_minus * s.x_post[i]) * 0.0f;            // the LTD term with pre = 0
+                post = 1;
+            }
+            item_s0[threadIdx.x] = st;
+            item_f[threadIdx.x] = f;
+            item_post[threadIdx.x] = post;
+            long long incl = len;
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const long long syn = base + lane + 32 * u;
-                    if (syn < b1) {
-                        t[u] = s.proj.tgt[syn];
-                        w[u] = s.w_mut[syn];
-                    }
-                }
+            for (int o = 1; o < kBatch; o <<= 1) {
+                const long long y = __shfl_up_sync((1u << kBatch) - 1u, incl, o, kBatch);
+                if (threadIdx.x >= o) incl += y;
+            }
+            item_pre[threadIdx.x + 1] = incl;
+            if (threadIdx.x == 0) item_pre[0] = 0;
+        }
+        __syncthreads();
+        const long long total = item_pre[kBatch];
+        for (long long f0 = threadIdx.x; f0 < total; f0 += static_cast<long long>(kThreads) * kUnroll) {
+            long long syn[kUnroll];
+            uint32_t other[kUnroll];   // target (row item) or source (in-list item)
+            int it_of[kUnroll];
+            float w[kUnroll], sp[kUnroll], tr[kUnroll];
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const long long syn = base + lane + 32 * u;
-                    if (syn < b1) {
-                        post[u] = s.spike_tgt[t[u]];
-                        xp[u] = s.x_post[t[u]];
-                    }
-                }
+            for (int u = 0; u < kUnroll; ++u) {
+                const long long fi = f0 + static_cast<long long>(u) * kThreads;
+                it_of[u] = -1;
+                if (fi < total) {
+                    int it = 0;
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const long long syn = base + lane + 32 * u;
-                    if (syn < b1) {
-                        const float dw = ltp * post[u] - (s.a_minus * xp[u]) * 1.0f;
-                        s.w_mut[syn] = stdp_apply(s, syn, w[u], dw);
+                    for (int b = 1; b < kBatch; ++b) it += (item_pre[b] <= fi);
+                    it_of[u] = it;
+                    const long long k = item_s0[it] + (fi - item_pre[it]);
+                    if (item_post[it]) {
+                        other[u] = s.in_src[k];
+                        syn[u] = s.in_syn[k];
+                    } else {
+                        other[u] = s.proj.tgt[k];
+                        syn[u] = k;
                     }
                 }
             }
-        } else {
-            // target i spiked: in-synapses from sources that did not spike get +A+ x_pre
-            const int i = s.hist_tgt.ids[static_cast<long long>(slot_t) * s.hist_tgt.cap + (it - n_pre)];
-            const float ltd = (s.a_minus * s.x_post[i]) * 0.0f;
-            const long long b0 = s.in_ptr[i], b1 = s.in_ptr[i + 1];
-            for (long long base = b0; base < b1; base += 128) {
-                uint32_t j[4], syn[4];
-                float pre[4], xp[4], w[4];
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const long long k = base + lane + 32 * u;
-                    if (k < b1) {
-                        j[u] = s.in_src[k];
-                        syn[u] = s.in_syn[k];
-                    }
+            for (int u = 0; u < kUnroll; ++u) {
+                if (it_of[u] < 0) continue;
+                w[u] = s.w_mut[syn[u]];
+                if (item_post[it_of[u]]) {
+                    sp[u] = s.spike_src[other[u]];
+                    tr[u] = s.x_pre[other[u]];
+                } else {
+                    sp[u] = s.spike_tgt[other[u]];
+                    tr[u] = s.x_post[other[u]];
                 }
+            }
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const long long k = base + lane + 32 * u;
-                    if (k < b1) {
-                        pre[u] = s.spike_src[j[u]];
-                        xp[u] = s.x_pre[j[u]];
-                        w[u] = s.w_mut[syn[u]];
-                    }
-                }
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const long long k = base + lane + 32 * u;
-                    if (k < b1 && pre[u] == 0.0f) {   // else handled with the source's row
-                        const float dw = (s.a_plus * xp[u]) * 1.0f - ltd;
-                        s.w_mut[syn[u]] = stdp_apply(s, syn[u], w[u], dw);
-                    }
+            for (int u = 0; u < kUnroll; ++u) {
+                const int it = it_of[u];
+                if (it < 0) continue;
+                if (item_post[it]) {
+                    if (sp[u] != 0.0f) continue;   // handled with the source's row
+                    const float dw = (s.a_plus * tr[u]) * 1.0f - item_f[it];
+                    s.w_mut[syn[u]] = stdp_apply(s, syn[u], w[u], dw);
+                } else {
+                    const float dw = item_f[it] * sp[u] - (s.a_minus * tr[u]) * 1.0f;
+                    s.w_mut[syn[u]] = stdp_apply(s, syn[u], w[u], dw);
                 }
             }
         }
+        __syncthreads();
     }
 }
 
@@ -319,8 +386,11 @@ extern "C" nrn_status_t nrn_cuda_deliver_counted(const nrn_proj_t* projs, int32_
     P.step_off = step_off;
     P.step_base = reinterpret_cast<const long long*>(step_base);
     P.events = events;
-    const int blocks = 8 * sm_count();
-    deliver_kernel<<<blocks, kThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(P);
+    const size_t smem = pair_smem(pairs);
+    int per_sm = 0;
+    NRN_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, deliver_kernel, kThreads, smem));
+    const int blocks = std::max(1, per_sm) * sm_count();   // one full wave
+    deliver_kernel<<<blocks, kThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(P);
     NRN_CUDA_TRY(cudaGetLastError());
     return NRN_OK;
 }
@@ -339,7 +409,9 @@ extern "C" nrn_status_t nrn_cuda_stdp_step(const nrn_stdp_t* s, int64_t step_off
     const long long* base = reinterpret_cast<const long long*>(step_base);
     stdp_trace_kernel<<<trace_blocks, tb, 0, st>>>(*s, step_off, base);
     NRN_CUDA_TRY(cudaGetLastError());
-    stdp_update_kernel<<<8 * sm_count(), kThreads, 0, st>>>(*s, step_off, base);
+    int per_sm = 0;
+    NRN_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, stdp_update_kernel, kThreads, 0));
+    stdp_update_kernel<<<std::max(1, per_sm) * sm_count(), kThreads, 0, st>>>(*s, step_off, base);
     NRN_CUDA_TRY(cudaGetLastError());
     return NRN_OK;
 }

@@ -635,6 +635,16 @@ nrn_status_t nrn_engine_profile(nrn_engine* e, int64_t steps, double* ms) {
     return st;
 }
 
+nrn_status_t nrn_engine_set_step(nrn_engine* e, int64_t step) {
+    ENGINE_GUARD(e);
+    NRN_CHECK_ARG(step >= 0, "step must be >= 0");
+    const long long s = step;
+    NRN_CUDA_TRY(cudaMemcpyAsync(e->d_step, &s, sizeof(s), cudaMemcpyHostToDevice, e->stream));
+    NRN_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    e->step = step;
+    return NRN_OK;
+}
+
 nrn_status_t nrn_engine_sync(nrn_engine* e) {
     ENGINE_GUARD(e);
     NRN_CUDA_TRY(cudaStreamSynchronize(e->stream));
@@ -685,6 +695,43 @@ nrn_status_t nrn_engine_weights(nrn_engine* e, int32_t proj, float* out, int64_t
     } else {
         std::memcpy(out, w.data(), c.nnz * 4);
     }
+    return NRN_OK;
+}
+
+nrn_status_t nrn_engine_weights_device(nrn_engine* e, int32_t proj, float* out, int64_t n) {
+    ENGINE_GUARD(e);
+    NRN_CHECK_ARG(proj >= 0 && proj < static_cast<int32_t>(e->projs.size()), "bad projection index");
+    const auto& c = e->projs[proj].csr;
+    NRN_CHECK_ARG(n == c.nnz && (n == 0 || out != nullptr), "weights: output size must equal the synapse count");
+    if (n == 0) return NRN_OK;
+    if (c.orig) {
+        // out[orig[k]] = w[k]
+        return nrn_cuda_scatter(c.w, c.orig, n, out, reinterpret_cast<nrn_stream_t>(e->stream));
+    }
+    NRN_CUDA_TRY(cudaMemcpyAsync(out, c.w, n * sizeof(float), cudaMemcpyDeviceToDevice, e->stream));
+    return NRN_OK;
+}
+
+nrn_status_t nrn_engine_set_state(nrn_engine* e, int32_t pop, float* v, float* aux, float* refractory, float* spike,
+                                  float* i_syn) {
+    ENGINE_GUARD(e);
+    NRN_CHECK_ARG(pop >= 0 && pop < static_cast<int32_t>(e->pops.size()), "bad population index");
+    auto& p = e->pops[pop];
+    NRN_CHECK_ARG(v && spike, "population needs v and spike arrays");
+    NRN_CHECK_ARG(p.d.model == NRN_MODEL_LIF || aux, "population needs aux (w/u)");
+    NRN_CHECK_ARG(p.d.model == NRN_MODEL_IZH || refractory, "population needs refractory");
+    bool changed = v != p.d.v || aux != p.d.aux || refractory != p.d.refractory || spike != p.d.spike;
+    p.d.v = v;
+    p.d.aux = aux;
+    p.d.refractory = refractory;
+    p.d.spike = spike;
+    if (i_syn != nullptr && i_syn != p.d.i_syn) {
+        if (p.owns_isyn) cudaFree(p.d.i_syn);
+        p.owns_isyn = false;
+        p.d.i_syn = i_syn;
+        changed = true;
+    }
+    if (changed) e->drop_graphs();
     return NRN_OK;
 }
 

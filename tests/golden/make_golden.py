@@ -151,6 +151,22 @@ def main() -> None:
                                                        "weight_scale": 500e-12, "seed": 42}).encode(),
                                            np.uint8))
 
+    # --- a user program of the nrn:: API, built against the reference
+    #     (oracle/Makefile) and run on its CPU path
+    exe = os.path.join(os.path.dirname(O.HERE), "oracle", "_ref", "dropin_brunel_ref")
+    import subprocess
+    import tempfile
+    with tempfile.TemporaryDirectory() as td:
+        out = os.path.join(td, "ref.bin")
+        subprocess.run([exe, out, "cpu", "300"], check=True, stdout=subprocess.DEVNULL)
+        raw = open(out, "rb").read()
+    hdr = np.frombuffer(raw[:12], np.int32)
+    body = np.frombuffer(raw[12:], np.float32)
+    ne, ni, nw = (int(x) for x in hdr)
+    np.savez_compressed(os.path.join(HERE, "dropin_brunel.npz"), exc=body[:2 * ne].reshape(-1, 2),
+                        inh=body[2 * ne:2 * (ne + ni)].reshape(-1, 2), w_ee=body[2 * (ne + ni):])
+    print("dropin_brunel", ne, ni)
+
     # --- Philox known answers
     np.savez_compressed(os.path.join(HERE, "philox_kat.npz"),
                         kat=np.array([list(c) + list(k) + list(o) for c, k, o in PHILOX_KAT], np.uint64))
