@@ -144,7 +144,15 @@ typedef struct {
     int32_t* raster_gid;
     unsigned long long* raster_count;
     int64_t raster_cap;
+    /* Plasticity traces of this population, x <- x * decay + spike, updated
+     * in the same pass at slow-clock steps (step % trace_slow_ratio == 0). */
+    int32_t n_traces;          /* 0..NRN_MAX_TRACES                          */
+    int32_t trace_slow_ratio;
+    float* trace[4];
+    float trace_decay[4];
 } nrn_pop_step_t;
+
+#define NRN_MAX_TRACES 4
 
 NRN_API nrn_status_t nrn_cuda_pop_step(const nrn_pop_step_t* a, nrn_stream_t stream);
 
@@ -169,7 +177,7 @@ typedef struct {
     int32_t dmin;              /* smallest delay, steps (>= 1)              */
     int32_t nd;                /* number of delay values dmin .. dmin+nd-1  */
     int32_t src_hist;          /* index of the source's nrn_spike_hist_t    */
-    int32_t pad0;
+    int32_t max_seg;           /* longest (source, delay) segment           */
     const int64_t* seg_ptr;    /* [n_src*nd + 1]                            */
     const uint32_t* tgt;       /* [nnz] local target index                  */
     const float* w;            /* [nnz] weight                              */
@@ -205,6 +213,8 @@ typedef struct {
     const int64_t* in_ptr;     /* [n_tgt+1] target-major index              */
     const uint32_t* in_syn;    /* [nnz] synapse position of each in-synapse */
     const uint32_t* in_src;    /* [nnz] its source                          */
+    int32_t max_in;            /* longest in-list (max in-degree)           */
+    int32_t max_row;           /* longest out-row (all delays of a source)  */
     float* x_pre;              /* [n_src] presynaptic trace                 */
     float* x_post;             /* [n_tgt] postsynaptic trace                */
     const float* spike_src;    /* [n_src] this step's 0/1 spikes            */
@@ -215,6 +225,7 @@ typedef struct {
     float a_plus, a_minus;            /* a_minus as |A-|                    */
     float lr, w_min, w_max;
     int32_t slow_ratio;        /* update only when step % slow_ratio == 0   */
+    int32_t traces_updated;    /* 1: the neuron updates already advanced x_pre/x_post */
 } nrn_stdp_t;
 
 /* Trace decay and increment, then the weight update of every synapse whose

@@ -58,7 +58,8 @@ class PopStep(C.Structure):
         ("drive", Drive), ("step", C.c_int64), ("step_base", C.c_void_p), ("spike_ids", C.c_void_p),
         ("spike_count", C.c_void_p), ("hist_depth", C.c_int32), ("hist_cap", C.c_int32),
         ("raster_step", C.c_void_p), ("raster_gid", C.c_void_p), ("raster_count", C.c_void_p),
-        ("raster_cap", C.c_int64),
+        ("raster_cap", C.c_int64), ("n_traces", C.c_int32), ("trace_slow_ratio", C.c_int32),
+        ("trace", C.c_void_p * 4), ("trace_decay", C.c_float * 4),
     ]
 
 
@@ -69,7 +70,7 @@ class SpikeHist(C.Structure):
 class Proj(C.Structure):
     _fields_ = [
         ("n_src", C.c_int32), ("n_tgt", C.c_int32), ("dmin", C.c_int32), ("nd", C.c_int32),
-        ("src_hist", C.c_int32), ("pad0", C.c_int32), ("seg_ptr", C.c_void_p), ("tgt", C.c_void_p),
+        ("src_hist", C.c_int32), ("max_seg", C.c_int32), ("seg_ptr", C.c_void_p), ("tgt", C.c_void_p),
         ("w", C.c_void_p), ("mod", C.c_void_p), ("acc", C.c_void_p),
     ]
 

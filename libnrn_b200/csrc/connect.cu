@@ -68,6 +68,22 @@ __global__ void count_keys(const uint32_t* keys, int64_t n, uint32_t nkeys, int6
     }
 }
 
+__global__ void max_count(const int64_t* counts, int64_t n, unsigned long long* out) {
+    unsigned long long m = 0;
+    for (int64_t k = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; k < n;
+         k += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        m = max(m, static_cast<unsigned long long>(counts[k]));
+    atomicMax(out, m);
+}
+
+__global__ void max_row_len(const int64_t* seg_ptr, int32_t n_src, int32_t nd, unsigned long long* out) {
+    unsigned long long m = 0;
+    for (int64_t j = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; j < n_src;
+         j += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        m = max(m, static_cast<unsigned long long>(seg_ptr[(j + 1) * nd] - seg_ptr[j * nd]));
+    atomicMax(out, m);
+}
+
 __global__ void gather_syn(const uint32_t* perm, int64_t n, const int32_t* tgt, const float* w, const float* mod,
                            uint32_t* tgt_o, float* w_o, float* mod_o, int64_t* orig_o) {
     for (int64_t k = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; k < n;
@@ -228,11 +244,33 @@ nrn_status_t build_csr(DevCsr& c, int32_t n_src, int32_t n_tgt, const int32_t* s
         count_keys<<<grid_for(n_in), 256, 0, s>>>(keys, n_in, nkeys, counts);
         CSTEP(cudaGetLastError());
     }
+    {
+        unsigned long long* dm = nullptr;
+        unsigned long long hm = 0;
+        STEP(dalloc(&dm, 1));
+        CSTEP(cudaMemsetAsync(dm, 0, sizeof(*dm), s));
+        max_count<<<grid_for(nkeys), 256, 0, s>>>(counts, nkeys, dm);
+        CSTEP(cudaMemcpyAsync(&hm, dm, sizeof(hm), cudaMemcpyDeviceToHost, s));
+        CSTEP(cudaStreamSynchronize(s));
+        dfree(dm);
+        c.max_seg = static_cast<int32_t>(hm);
+    }
     STEP(dalloc(&c.seg_ptr, static_cast<size_t>(nkeys) + 1));
     tmp_bytes = 0;
     CSTEP(cub::DeviceScan::ExclusiveSum(nullptr, tmp_bytes, counts, c.seg_ptr, static_cast<int64_t>(nkeys) + 1, s));
     CSTEP(cudaMalloc(&tmp, tmp_bytes));
     CSTEP(cub::DeviceScan::ExclusiveSum(tmp, tmp_bytes, counts, c.seg_ptr, static_cast<int64_t>(nkeys) + 1, s));
+    {
+        unsigned long long* dm = nullptr;
+        unsigned long long hm = 0;
+        STEP(dalloc(&dm, 1));
+        CSTEP(cudaMemsetAsync(dm, 0, sizeof(*dm), s));
+        max_row_len<<<grid_for(n_src), 256, 0, s>>>(c.seg_ptr, n_src, c.nd, dm);
+        CSTEP(cudaMemcpyAsync(&hm, dm, sizeof(hm), cudaMemcpyDeviceToHost, s));
+        CSTEP(cudaStreamSynchronize(s));
+        dfree(dm);
+        c.max_row = static_cast<int32_t>(hm);
+    }
     int64_t nnz = 0;
     CSTEP(cudaMemcpyAsync(&nnz, c.seg_ptr + nkeys, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
     CSTEP(cudaStreamSynchronize(s));
@@ -300,6 +338,17 @@ nrn_status_t build_transpose(DevCsr& c, cudaStream_t s) {
     if (n > 0) {
         count_keys<<<grid_for(n), 256, 0, s>>>(keys, n, static_cast<uint32_t>(c.n_tgt), counts);
         CSTEP(cudaGetLastError());
+    }
+    {
+        unsigned long long* dm = nullptr;
+        unsigned long long hm = 0;
+        STEP(dalloc(&dm, 1));
+        CSTEP(cudaMemsetAsync(dm, 0, sizeof(*dm), s));
+        max_count<<<grid_for(c.n_tgt), 256, 0, s>>>(counts, c.n_tgt, dm);
+        CSTEP(cudaMemcpyAsync(&hm, dm, sizeof(hm), cudaMemcpyDeviceToHost, s));
+        CSTEP(cudaStreamSynchronize(s));
+        dfree(dm);
+        c.max_in = static_cast<int32_t>(hm);
     }
     STEP(dalloc(&c.in_ptr, static_cast<size_t>(c.n_tgt) + 1));
     tmp_bytes = 0;

@@ -35,8 +35,7 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kMaxPairs = 1024;   // (projection, delay) pairs per launch
-constexpr int kBatch = 8;         // items a block resolves at once
-constexpr int kUnroll = 4;        // synapses in flight per thread
+constexpr int kChunk = 128;       // synapses per warp work unit (4 per lane)
 
 struct DeliverParams {
     nrn_proj_t proj[NRN_MAX_PROJ];
@@ -52,8 +51,9 @@ struct DeliverParams {
 
 // Dynamic shared memory: pair table of npairs entries.
 struct PairView {
-    long long* start;   // [npairs + 1] exclusive prefix of spike counts
+    long long* start;   // [npairs + 1] exclusive prefix of work units
     int* slot;          // [npairs]
+    int* chunks;        // [npairs] units per spike (ceil(max segment / kChunk))
     short* proj;        // [npairs]
     short* k;           // [npairs]
 };
@@ -62,26 +62,24 @@ __device__ __forceinline__ PairView pair_view(void* base, int npairs) {
     PairView v;
     v.start = reinterpret_cast<long long*>(base);
     v.slot = reinterpret_cast<int*>(v.start + npairs + 1);
-    v.proj = reinterpret_cast<short*>(v.slot + npairs);
+    v.chunks = v.slot + npairs;
+    v.proj = reinterpret_cast<short*>(v.chunks + npairs);
     v.k = v.proj + npairs;
     return v;
 }
 
 size_t pair_smem(int npairs) {
-    return static_cast<size_t>(npairs + 1) * sizeof(long long) + static_cast<size_t>(npairs) * (4 + 2 + 2) + 16;
+    return static_cast<size_t>(npairs + 1) * sizeof(long long) + static_cast<size_t>(npairs) * (4 + 4 + 2 + 2) + 16;
 }
 
-// Work is split in two phases per batch of kBatch items (spike, delay
-// segment): first one thread per item resolves the item's synapse range
-// into shared memory (one round of dependent loads for the whole batch),
-// then all threads of the block stride over the batch's synapses,
-// kUnroll at a time with every load issued before the reductions.
+// Work unit = (spike, delay segment, chunk of kChunk synapses), one warp
+// each.  Every segment of a projection is given ceil(max segment length /
+// kChunk) units (units past the segment's end are empty), so the units of
+// one step are numbered without a prefix over segment lengths and spread
+// evenly over a full-occupancy grid.
 __global__ void __launch_bounds__(kThreads) deliver_kernel(const __grid_constant__ DeliverParams P) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const PairView tab = pair_view(smem_raw, P.npairs);
-    __shared__ long long item_pre[kBatch + 1];
-    __shared__ long long item_s0[kBatch];
-    __shared__ int item_q[kBatch];
     using Scan = cub::BlockScan<long long, kThreads>;
     __shared__ typename Scan::TempStorage scan_tmp;
     __shared__ long long carry;
@@ -94,28 +92,29 @@ __global__ void __launch_bounds__(kThreads) deliver_kernel(const __grid_constant
     }
     __syncthreads();
 
-    // Spike counts of every (projection, delay) pair, then their prefix.
     for (int base = 0; base < P.npairs; base += kThreads) {
         const int pi = base + threadIdx.x;
-        long long cnt = 0;
+        long long units = 0;
         if (pi < P.npairs) {
             int q = 0, acc = 0;
             while (q < P.nproj && pi >= acc + P.proj[q].nd) { acc += P.proj[q].nd; ++q; }
             const int k = pi - acc;
             const nrn_proj_t& pr = P.proj[q];
             const long long src_step = step - (pr.dmin + k);
+            const int chunks = (pr.max_seg + kChunk - 1) / kChunk;
             tab.proj[pi] = static_cast<short>(q);
             tab.k[pi] = static_cast<short>(k);
+            tab.chunks[pi] = chunks > 0 ? chunks : 1;
             tab.slot[pi] = 0;
-            if (src_step >= 0) {
+            if (src_step >= 0 && chunks > 0) {
                 const nrn_spike_hist_t& h = P.hist[pr.src_hist];
                 const int slot = static_cast<int>(src_step % h.depth);
                 tab.slot[pi] = slot;
-                cnt = h.count[slot];
+                units = static_cast<long long>(h.count[slot]) * chunks;
             }
         }
         long long excl, total;
-        Scan(scan_tmp).ExclusiveSum(cnt, excl, total);
+        Scan(scan_tmp).ExclusiveSum(units, excl, total);
         if (pi < P.npairs) tab.start[pi] = carry + excl;
         __syncthreads();
         if (threadIdx.x == 0) carry += total;
@@ -123,73 +122,47 @@ __global__ void __launch_bounds__(kThreads) deliver_kernel(const __grid_constant
     }
     if (threadIdx.x == 0) tab.start[P.npairs] = carry;
     __syncthreads();
-    const long long n_items = tab.start[P.npairs];
+    const long long n_units = tab.start[P.npairs];
 
+    const int lane = threadIdx.x & 31;
+    const long long warp = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
+    const long long n_warps = (static_cast<long long>(gridDim.x) * kThreads) >> 5;
     unsigned long long my_events = 0;
-    for (long long b0 = static_cast<long long>(blockIdx.x) * kBatch; b0 < n_items;
-         b0 += static_cast<long long>(gridDim.x) * kBatch) {
-        // phase A: synapse range of each item of the batch
-        if (threadIdx.x < kBatch) {
-            const long long it = b0 + threadIdx.x;
-            long long len = 0, s0 = 0;
-            int q = 0;
-            if (it < n_items) {
-                int lo = 0, hi = P.npairs - 1;
-                while (lo < hi) {
-                    const int mid = (lo + hi + 1) >> 1;
-                    if (tab.start[mid] <= it) lo = mid; else hi = mid - 1;
-                }
-                q = tab.proj[lo];
-                const nrn_proj_t& pr = P.proj[q];
-                const nrn_spike_hist_t& h = P.hist[pr.src_hist];
-                const int j = h.ids[static_cast<long long>(tab.slot[lo]) * h.cap + (it - tab.start[lo])];
-                const long long seg = static_cast<long long>(j) * pr.nd + tab.k[lo];
-                s0 = pr.seg_ptr[seg];
-                len = pr.seg_ptr[seg + 1] - s0;
-            }
-            item_s0[threadIdx.x] = s0;
-            item_q[threadIdx.x] = q;
-            // inclusive prefix over the batch within warp 0
-            long long incl = len;
-#pragma unroll
-            for (int o = 1; o < kBatch; o <<= 1) {
-                const long long y = __shfl_up_sync((1u << kBatch) - 1u, incl, o, kBatch);
-                if (threadIdx.x >= o) incl += y;
-            }
-            item_pre[threadIdx.x + 1] = incl;
-            if (threadIdx.x == 0) item_pre[0] = 0;
+    for (long long u = warp; u < n_units; u += n_warps) {
+        int lo = 0, hi = P.npairs - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (tab.start[mid] <= u) lo = mid; else hi = mid - 1;
         }
-        __syncthreads();
-        const long long total = item_pre[kBatch];
-        if (threadIdx.x == 0) my_events += static_cast<unsigned long long>(total);
-        // phase B: every synapse of the batch
-        for (long long f0 = threadIdx.x; f0 < total; f0 += static_cast<long long>(kThreads) * kUnroll) {
-            uint32_t t[kUnroll];
-            float w[kUnroll];
-            float* acc[kUnroll];
+        const long long local = u - tab.start[lo];
+        const int chunks = tab.chunks[lo];
+        const long long spike = local / chunks;
+        const int chunk = static_cast<int>(local - spike * chunks);
+        const nrn_proj_t& pr = P.proj[tab.proj[lo]];
+        const nrn_spike_hist_t& h = P.hist[pr.src_hist];
+        const int j = h.ids[static_cast<long long>(tab.slot[lo]) * h.cap + spike];
+        const long long seg = static_cast<long long>(j) * pr.nd + tab.k[lo];
+        const long long e0 = pr.seg_ptr[seg + 1];
+        const long long s0 = pr.seg_ptr[seg] + static_cast<long long>(chunk) * kChunk;
+        const long long s1 = s0 + kChunk < e0 ? s0 + kChunk : e0;
+        if (s0 >= s1) continue;
+        if (lane == 0) my_events += static_cast<unsigned long long>(s1 - s0);
+        uint32_t t[4];
+        float w[4];
 #pragma unroll
-            for (int u = 0; u < kUnroll; ++u) {
-                const long long f = f0 + static_cast<long long>(u) * kThreads;
-                acc[u] = nullptr;
-                if (f < total) {
-                    int it = 0;
-#pragma unroll
-                    for (int b = 1; b < kBatch; ++b) it += (item_pre[b] <= f);
-                    const nrn_proj_t& pr = P.proj[item_q[it]];
-                    const long long syn = item_s0[it] + (f - item_pre[it]);
-                    t[u] = __ldg(pr.tgt + syn);
-                    w[u] = __ldg(pr.w + syn);
-                    if (pr.mod != nullptr) w[u] = w[u] * __ldg(pr.mod + syn);
-                    acc[u] = pr.acc;
-                }
+        for (int v = 0; v < 4; ++v) {
+            const long long syn = s0 + lane + 32 * v;
+            if (syn < s1) {
+                t[v] = __ldg(pr.tgt + syn);
+                w[v] = __ldg(pr.w + syn);
+                if (pr.mod != nullptr) w[v] = w[v] * __ldg(pr.mod + syn);
             }
-#pragma unroll
-            for (int u = 0; u < kUnroll; ++u)
-                if (acc[u] != nullptr) atomicAdd(acc[u] + t[u], w[u]);
         }
-        __syncthreads();
+#pragma unroll
+        for (int v = 0; v < 4; ++v)
+            if (s0 + lane + 32 * v < s1) atomicAdd(pr.acc + t[v], w[v]);
     }
-    if (P.events && threadIdx.x == 0 && my_events) atomicAdd(P.events, my_events);
+    if (P.events && lane == 0 && my_events) atomicAdd(P.events, my_events);
 }
 
 // ---------------------------------------------------------------------------
@@ -222,108 +195,93 @@ __device__ __forceinline__ float stdp_apply(const nrn_stdp_t& s, long long syn, 
     return w;
 }
 
-// Items: the spiking sources (their out-rows: -A- x_post, plus +A+ x_pre
-// where the target spiked too) then the spiking targets (their in-lists:
-// +A+ x_pre where the source did not spike).  Same two-phase batching as
-// the delivery.
+// Work units of one warp: (spiking source, chunk of its out-row) -- the
+// -A- x_post term, plus +A+ x_pre where the target spiked too -- then
+// (spiking target, chunk of its in-list) -- +A+ x_pre where the source did
+// not spike.  Chunk counts come from the longest row / in-list.
 __global__ void __launch_bounds__(kThreads) stdp_update_kernel(const __grid_constant__ nrn_stdp_t s,
                                                                long long step_off, const long long* step_base) {
-    __shared__ long long item_pre[kBatch + 1];
-    __shared__ long long item_s0[kBatch];
-    __shared__ float item_f[kBatch];
-    __shared__ int item_post[kBatch];   // 1: in-list item
-
     const long long step = step_off + (step_base ? *step_base : 0);
     if (!stdp_active(s, step)) return;
     const int slot_s = static_cast<int>(step % s.hist_src.depth);
     const int slot_t = static_cast<int>(step % s.hist_tgt.depth);
-    const long long n_pre = s.hist_src.count[slot_s];
-    const long long n_items = n_pre + s.hist_tgt.count[slot_t];
+    const int c_pre = s.max_row > 0 ? (s.max_row + kChunk - 1) / kChunk : 1;
+    const int c_post = s.max_in > 0 ? (s.max_in + kChunk - 1) / kChunk : 1;
+    const long long u_pre = static_cast<long long>(s.hist_src.count[slot_s]) * c_pre;
+    const long long n_units = u_pre + static_cast<long long>(s.hist_tgt.count[slot_t]) * c_post;
     const int nd = s.proj.nd;
-    for (long long b0 = static_cast<long long>(blockIdx.x) * kBatch; b0 < n_items;
-         b0 += static_cast<long long>(gridDim.x) * kBatch) {
-        if (threadIdx.x < kBatch) {
-            const long long it = b0 + threadIdx.x;
-            long long len = 0, st = 0;
-            float f = 0.0f;
-            int post = 0;
-            if (it < n_pre) {
-                const int j = s.hist_src.ids[static_cast<long long>(slot_s) * s.hist_src.cap + it];
-                st = s.proj.seg_ptr[static_cast<long long>(j) * nd];
-                len = s.proj.seg_ptr[static_cast<long long>(j + 1) * nd] - st;
-                f = s.a_plus * s.x_pre[j];                       // A+ x_pre[j]
-            } else if (it < n_items) {
-                const int i = s.hist_tgt.ids[static_cast<long long>(slot_t) * s.hist_tgt.cap + (it - n_pre)];
-                st = s.in_ptr[i];
-                len = s.in_ptr[i + 1] - st;
-                f = (s.a_minus * s.x_post[i]) * 0.0f;            // the LTD term with pre = 0
-                post = 1;
-            }
-            item_s0[threadIdx.x] = st;
-            item_f[threadIdx.x] = f;
-            item_post[threadIdx.x] = post;
-            long long incl = len;
+    const int lane = threadIdx.x & 31;
+    const long long warp = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
+    const long long n_warps = (static_cast<long long>(gridDim.x) * kThreads) >> 5;
+    for (long long u = warp; u < n_units; u += n_warps) {
+        if (u < u_pre) {
+            const long long it = u / c_pre;
+            const int chunk = static_cast<int>(u - it * c_pre);
+            const int j = s.hist_src.ids[static_cast<long long>(slot_s) * s.hist_src.cap + it];
+            const long long e0 = s.proj.seg_ptr[static_cast<long long>(j + 1) * nd];
+            const long long b0 = s.proj.seg_ptr[static_cast<long long>(j) * nd] + static_cast<long long>(chunk) * kChunk;
+            const long long b1 = b0 + kChunk < e0 ? b0 + kChunk : e0;
+            if (b0 >= b1) continue;
+            const float ltp = s.a_plus * s.x_pre[j];
+            uint32_t t[4];
+            float w[4], post[4], xp[4];
 #pragma unroll
-            for (int o = 1; o < kBatch; o <<= 1) {
-                const long long y = __shfl_up_sync((1u << kBatch) - 1u, incl, o, kBatch);
-                if (threadIdx.x >= o) incl += y;
-            }
-            item_pre[threadIdx.x + 1] = incl;
-            if (threadIdx.x == 0) item_pre[0] = 0;
-        }
-        __syncthreads();
-        const long long total = item_pre[kBatch];
-        for (long long f0 = threadIdx.x; f0 < total; f0 += static_cast<long long>(kThreads) * kUnroll) {
-            long long syn[kUnroll];
-            uint32_t other[kUnroll];   // target (row item) or source (in-list item)
-            int it_of[kUnroll];
-            float w[kUnroll], sp[kUnroll], tr[kUnroll];
-#pragma unroll
-            for (int u = 0; u < kUnroll; ++u) {
-                const long long fi = f0 + static_cast<long long>(u) * kThreads;
-                it_of[u] = -1;
-                if (fi < total) {
-                    int it = 0;
-#pragma unroll
-                    for (int b = 1; b < kBatch; ++b) it += (item_pre[b] <= fi);
-                    it_of[u] = it;
-                    const long long k = item_s0[it] + (fi - item_pre[it]);
-                    if (item_post[it]) {
-                        other[u] = s.in_src[k];
-                        syn[u] = s.in_syn[k];
-                    } else {
-                        other[u] = s.proj.tgt[k];
-                        syn[u] = k;
-                    }
+            for (int v = 0; v < 4; ++v) {
+                const long long syn = b0 + lane + 32 * v;
+                if (syn < b1) {
+                    t[v] = s.proj.tgt[syn];
+                    w[v] = s.w_mut[syn];
                 }
             }
 #pragma unroll
-            for (int u = 0; u < kUnroll; ++u) {
-                if (it_of[u] < 0) continue;
-                w[u] = s.w_mut[syn[u]];
-                if (item_post[it_of[u]]) {
-                    sp[u] = s.spike_src[other[u]];
-                    tr[u] = s.x_pre[other[u]];
-                } else {
-                    sp[u] = s.spike_tgt[other[u]];
-                    tr[u] = s.x_post[other[u]];
+            for (int v = 0; v < 4; ++v)
+                if (b0 + lane + 32 * v < b1) {
+                    post[v] = s.spike_tgt[t[v]];
+                    xp[v] = s.x_post[t[v]];
+                }
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+                const long long syn = b0 + lane + 32 * v;
+                if (syn < b1) {
+                    const float dw = ltp * post[v] - (s.a_minus * xp[v]) * 1.0f;
+                    s.w_mut[syn] = stdp_apply(s, syn, w[v], dw);
+                }
+            }
+        } else {
+            const long long it = (u - u_pre) / c_post;
+            const int chunk = static_cast<int>((u - u_pre) - it * c_post);
+            const int i = s.hist_tgt.ids[static_cast<long long>(slot_t) * s.hist_tgt.cap + it];
+            const long long e0 = s.in_ptr[i + 1];
+            const long long b0 = s.in_ptr[i] + static_cast<long long>(chunk) * kChunk;
+            const long long b1 = b0 + kChunk < e0 ? b0 + kChunk : e0;
+            if (b0 >= b1) continue;
+            const float ltd = (s.a_minus * s.x_post[i]) * 0.0f;   // the LTD term with pre = 0
+            uint32_t j[4];
+            long long syn[4];
+            float pre[4], xq[4], w[4];
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+                const long long k = b0 + lane + 32 * v;
+                if (k < b1) {
+                    j[v] = s.in_src[k];
+                    syn[v] = s.in_syn[k];
                 }
             }
 #pragma unroll
-            for (int u = 0; u < kUnroll; ++u) {
-                const int it = it_of[u];
-                if (it < 0) continue;
-                if (item_post[it]) {
-                    if (sp[u] != 0.0f) continue;   // handled with the source's row
-                    const float dw = (s.a_plus * tr[u]) * 1.0f - item_f[it];
-                    s.w_mut[syn[u]] = stdp_apply(s, syn[u], w[u], dw);
-                } else {
-                    const float dw = item_f[it] * sp[u] - (s.a_minus * tr[u]) * 1.0f;
-                    s.w_mut[syn[u]] = stdp_apply(s, syn[u], w[u], dw);
+            for (int v = 0; v < 4; ++v)
+                if (b0 + lane + 32 * v < b1) {
+                    pre[v] = s.spike_src[j[v]];
+                    xq[v] = s.x_pre[j[v]];
+                    w[v] = s.w_mut[syn[v]];
+                }
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+                if (b0 + lane + 32 * v < b1 && pre[v] == 0.0f) {   // else handled with the source's row
+                    const float dw = (s.a_plus * xq[v]) * 1.0f - ltd;
+                    s.w_mut[syn[v]] = stdp_apply(s, syn[v], w[v], dw);
                 }
             }
         }
-        __syncthreads();
     }
 }
 
@@ -407,8 +365,10 @@ extern "C" nrn_status_t nrn_cuda_stdp_step(const nrn_stdp_t* s, int64_t step_off
     const int tb = 256;
     const int trace_blocks = std::max(1, std::min((n + tb - 1) / tb, 8 * sm_count()));
     const long long* base = reinterpret_cast<const long long*>(step_base);
-    stdp_trace_kernel<<<trace_blocks, tb, 0, st>>>(*s, step_off, base);
-    NRN_CUDA_TRY(cudaGetLastError());
+    if (!s->traces_updated) {
+        stdp_trace_kernel<<<trace_blocks, tb, 0, st>>>(*s, step_off, base);
+        NRN_CUDA_TRY(cudaGetLastError());
+    }
     int per_sm = 0;
     NRN_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, stdp_update_kernel, kThreads, 0));
     stdp_update_kernel<<<std::max(1, per_sm) * sm_count(), kThreads, 0, st>>>(*s, step_off, base);

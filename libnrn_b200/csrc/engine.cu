@@ -85,6 +85,7 @@ struct EngineProj {
     double stdp[7] = {0};
     float* x_pre = nullptr;
     float* x_post = nullptr;
+    bool traces_fused = false;   // both traces advanced by the neuron updates
 };
 
 struct nrn_engine {
@@ -136,6 +137,7 @@ struct nrn_engine {
         p.dmin = q.csr.dmin;
         p.nd = q.csr.nd;
         p.src_hist = q.src_pop;
+        p.max_seg = q.csr.max_seg;
         p.seg_ptr = q.csr.seg_ptr;
         p.tgt = q.csr.tgt;
         p.w = q.csr.w;
@@ -188,6 +190,19 @@ struct nrn_engine {
                 a.raster_count = d_raster_count;
                 a.raster_cap = raster_cap;
             }
+            // plasticity traces of the projections this population feeds or receives
+            a.trace_slow_ratio = slow_ratio;
+            for (const auto& q : projs) {
+                if (!q.plastic || !q.traces_fused) continue;
+                if (q.src_pop == i) {
+                    a.trace[a.n_traces] = q.x_pre;
+                    a.trace_decay[a.n_traces++] = static_cast<float>(std::exp(-dt / q.stdp[0]));
+                }
+                if (q.tgt_pop == i) {
+                    a.trace[a.n_traces] = q.x_post;
+                    a.trace_decay[a.n_traces++] = static_cast<float>(std::exp(-dt / q.stdp[1]));
+                }
+            }
         }
         return a;
     }
@@ -199,6 +214,8 @@ struct nrn_engine {
         s.in_ptr = q.csr.in_ptr;
         s.in_syn = q.csr.in_syn;
         s.in_src = q.csr.in_src;
+        s.max_in = q.csr.max_in;
+        s.max_row = q.csr.max_row;
         s.x_pre = q.x_pre;
         s.x_post = q.x_post;
         s.spike_src = pops[q.src_pop].d.spike;
@@ -213,7 +230,31 @@ struct nrn_engine {
         s.w_max = static_cast<float>(q.stdp[5]);
         s.lr = static_cast<float>(q.stdp[6]);
         s.slow_ratio = slow_ratio;
+        s.traces_updated = q.traces_fused ? 1 : 0;
         return s;
+    }
+
+    // Decides, per plastic projection, whether the neuron updates of its
+    // source and target advance its traces (both or neither: a projection
+    // that does not fit in the NRN_MAX_TRACES slots of both populations
+    // keeps the separate trace kernel).
+    void assign_trace_slots() {
+        std::vector<int> used(pops.size(), 0);
+        for (auto& q : projs) {
+            q.traces_fused = false;
+            if (!q.plastic) continue;
+            const int need_src = 1 + (q.src_pop == q.tgt_pop ? 1 : 0);
+            if (q.src_pop == q.tgt_pop) {
+                if (used[q.src_pop] + need_src <= NRN_MAX_TRACES) {
+                    used[q.src_pop] += 2;
+                    q.traces_fused = true;
+                }
+            } else if (used[q.src_pop] < NRN_MAX_TRACES && used[q.tgt_pop] < NRN_MAX_TRACES) {
+                used[q.src_pop] += 1;
+                used[q.tgt_pop] += 1;
+                q.traces_fused = true;
+            }
+        }
     }
 
     // Enqueues one step at offset `off` from *d_step; with `ev` non-null,
@@ -529,6 +570,7 @@ nrn_status_t nrn_engine_set_stdp(nrn_engine* e, int32_t proj, const double* p) {
     NRN_CHECK_ARG(p != nullptr, "null STDP parameters");
     NRN_CHECK_ARG(p[0] > 0 && p[1] > 0, "STDP time constants must be positive");
     NRN_CHECK_ARG(p[4] <= p[5], "STDP needs w_min <= w_max");
+    NRN_CHECK_ARG(!e->finalized, "nrn_engine_set_stdp: set plasticity before nrn_engine_finalize");
     auto& q = e->projs[proj];
     std::memcpy(q.stdp, p, sizeof(q.stdp));
     q.plastic = true;
@@ -560,6 +602,7 @@ nrn_status_t nrn_engine_finalize(nrn_engine* e, int32_t init_update) {
         NRN_TRY(dalloc0(&q.x_pre, e->pops[q.src_pop].d.n, e->stream));
         NRN_TRY(dalloc0(&q.x_post, e->pops[q.tgt_pop].d.n, e->stream));
     }
+    e->assign_trace_slots();
     if (init_update) {
         for (size_t i = 0; i < e->pops.size(); ++i) {
             nrn_pop_step_t a = e->pop_args(static_cast<int>(i), 0.0, 0, false);

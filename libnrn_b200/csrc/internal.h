@@ -18,6 +18,9 @@ struct DevCsr {
     float* w = nullptr;           // [nnz]
     float* mod = nullptr;         // [nnz] or null
     int64_t* orig = nullptr;      // [nnz] index in the caller's list, or null
+    int32_t max_seg = 0;          // longest (source, delay) segment
+    int32_t max_row = 0;          // longest row (all delays of one source)
+    int32_t max_in = 0;           // longest in-list
     // target-major index (plasticity)
     int64_t* in_ptr = nullptr;    // [n_tgt+1]
     uint32_t* in_syn = nullptr;   // [nnz]

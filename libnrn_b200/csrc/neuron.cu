@@ -54,6 +54,10 @@ struct PopArgs {
     int* raster_gid;
     unsigned long long* raster_count;
     long long raster_cap;
+    int n_traces;
+    int trace_slow_ratio;
+    float* trace[NRN_MAX_TRACES];
+    float trace_decay[NRN_MAX_TRACES];
 };
 
 template <bool HET>
@@ -163,6 +167,11 @@ __global__ void __launch_bounds__(256) pop_step_kernel(const __grid_constant__ P
             a.aux[i] = u;
         }
         if (a.spike) a.spike[i] = spiked ? 1.0f : 0.0f;
+        if (a.n_traces > 0 && (a.trace_slow_ratio <= 1 || step % a.trace_slow_ratio == 0)) {
+            // pair-STDP traces (src/plasticity/stdp.cpp:118-128): decay, then + spike
+            const float sp = spiked ? 1.0f : 0.0f;
+            for (int k = 0; k < a.n_traces; ++k) a.trace[k][i] = a.trace[k][i] * a.trace_decay[k] + sp;
+        }
         if (a.i_syn) a.i_syn[i] = 0.0f;
         if (COND) {
             a.gin_exc[i] = 0.0f;
@@ -281,6 +290,14 @@ extern "C" nrn_status_t nrn_cuda_pop_step(const nrn_pop_step_t* in, nrn_stream_t
     a.raster_gid = d.raster_gid;
     a.raster_count = d.raster_count;
     a.raster_cap = d.raster_cap;
+    NRN_CHECK_ARG(d.n_traces >= 0 && d.n_traces <= NRN_MAX_TRACES, "nrn_cuda_pop_step: too many traces");
+    a.n_traces = d.n_traces;
+    a.trace_slow_ratio = d.trace_slow_ratio;
+    for (int k = 0; k < d.n_traces; ++k) {
+        NRN_CHECK_ARG(d.trace[k] != nullptr, "nrn_cuda_pop_step: null trace array");
+        a.trace[k] = d.trace[k];
+        a.trace_decay[k] = d.trace_decay[k];
+    }
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     switch (d.model) {
         case NRN_MODEL_LIF: launch_model<NRN_MODEL_LIF>(a, het, false, s); break;
