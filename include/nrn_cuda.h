@@ -359,6 +359,18 @@ NRN_API int64_t nrn_engine_step(const nrn_engine* e);
  * within a step, by ascending global id; *n receives the count
  * (if above cap, nothing is copied and NRN_ERR_CAPACITY is returned). */
 NRN_API nrn_status_t nrn_engine_raster(nrn_engine* e, int32_t* step, int32_t* gid, int64_t cap, int64_t* n);
+/* As nrn_engine_raster, but allocates no device memory, for callers that
+ * cannot call cudaMalloc/cudaFree (a real-time loop draining spikes while
+ * the simulation runs: allocation and free can stall the device; a process
+ * whose device memory is spoken for).  No counterpart in the reference.
+ * The sort runs in one fixed 4 MiB scratch array inside the library, one
+ * per GPU, kept until the library is unloaded and shared by all engines on
+ * that GPU: calls that overlap on the GPU race.  At most 131,072 spikes per
+ * call; beyond that NRN_ERR_CAPACITY is returned and the raster is left for
+ * nrn_engine_raster.  The first call on a device sets up the scratch
+ * address (cudaGetSymbolAddress) and should come before any stream capture. */
+NRN_API nrn_status_t nrn_engine_raster_noalloc(nrn_engine* e, int32_t* step, int32_t* gid, int64_t cap,
+                                               int64_t* n);
 /* Weights of a projection in the order the synapses were given, into a
  * device array of nnz floats (enqueued on the engine stream). */
 NRN_API nrn_status_t nrn_engine_weights_device(nrn_engine* e, int32_t proj, float* out, int64_t n);

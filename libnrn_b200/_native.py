@@ -31,7 +31,7 @@ EXPORTS = [
     "nrn_engine_raster", "nrn_engine_weights", "nrn_engine_nnz", "nrn_engine_counters",
     "nrn_engine_profile", "nrn_engine_weights_device", "nrn_engine_set_state", "nrn_engine_set_step",
     "nrn_cuda_block_deliver", "nrn_cuda_block_stdp", "nrn_cuda_compact", "nrn_cuda_gather_ring",
-    "nrn_cuda_scatter",
+    "nrn_cuda_scatter", "nrn_engine_raster_noalloc",
 ]
 
 
@@ -137,6 +137,7 @@ def lib() -> C.CDLL:
             "nrn_engine_sync": [vp],
             "nrn_engine_stream": [vp, C.POINTER(vp)],
             "nrn_engine_raster": [vp, vp, vp, i64, C.POINTER(i64)],
+            "nrn_engine_raster_noalloc": [vp, vp, vp, i64, C.POINTER(i64)],
             "nrn_engine_weights": [vp, i32, vp, i64],
             "nrn_engine_nnz": [vp, i32, C.POINTER(i64)],
             "nrn_engine_counters": [vp, C.POINTER(i64), C.POINTER(i64)],

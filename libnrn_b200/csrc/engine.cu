@@ -327,6 +327,22 @@ struct nrn_engine {
         if (ce_ != cudaSuccess) return cuda_fail(ce_, "cudaSetDevice");          \
     } while (0)
 
+namespace nrn {
+
+nrn_status_t engine_raster_view(nrn_engine* e, EngineRasterView* v) {
+    NRN_CHECK_ARG(e != nullptr && v != nullptr, "null engine");
+    v->device = e->device;
+    v->stream = e->stream;
+    v->step = e->raster_step;
+    v->gid = e->raster_gid;
+    v->count = e->d_raster_count;
+    v->cap = e->raster_cap;
+    v->flushed = &e->spikes_flushed;
+    return NRN_OK;
+}
+
+}  // namespace nrn
+
 extern "C" {
 
 const char* nrn_status_string(nrn_status_t s) {

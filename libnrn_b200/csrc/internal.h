@@ -55,6 +55,18 @@ nrn_status_t generate(const GenArgs& g, int32_t* src, int32_t* tgt, float* w, ui
 
 int sm_count_current();
 
+// The engine's spike raster buffers (for entry points outside engine.cu).
+struct EngineRasterView {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int32_t* step = nullptr;
+    int32_t* gid = nullptr;
+    unsigned long long* count = nullptr;
+    int64_t cap = 0;
+    int64_t* flushed = nullptr;   // host counter of spikes already read
+};
+nrn_status_t engine_raster_view(nrn_engine* e, EngineRasterView* v);
+
 // Sorts n raster entries in place by (step, global id).
 nrn_status_t sort_raster(int32_t* step, int32_t* gid, int64_t n, cudaStream_t s);
 
