@@ -150,6 +150,22 @@ typedef struct {
     int32_t trace_slow_ratio;
     float* trace[4];
     float trace_decay[4];
+    /* Spike-time history (for deferred plasticity on the projections this
+     * population receives): on a spike at step t, post_recent[i] (int4:
+     * latest four spike steps, newest first) shifts in t and t is appended
+     * to post_ring[i*post_ring_k + post_cnt[i] % post_ring_k]. */
+    int32_t* post_recent;      /* [n][4] or NULL                            */
+    int32_t* post_ring;        /* [n][post_ring_k]                          */
+    int32_t* post_cnt;         /* [n]                                       */
+    int32_t post_ring_k;
+    /* Snapshot of trace slot snap_trace every snap_period steps: at the end
+     * of step t with (t+1) % snap_period == 0 the trace is copied into row
+     * ((t+1)/snap_period) % snap_depth of snap_buf [snap_depth][n]. */
+    int32_t snap_trace;        /* -1: none                                  */
+    int32_t snap_period;
+    int32_t snap_depth;
+    int32_t pad2;
+    float* snap_buf;
 } nrn_pop_step_t;
 
 #define NRN_MAX_TRACES 4

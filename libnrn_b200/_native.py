@@ -60,6 +60,9 @@ class PopStep(C.Structure):
         ("raster_step", C.c_void_p), ("raster_gid", C.c_void_p), ("raster_count", C.c_void_p),
         ("raster_cap", C.c_int64), ("n_traces", C.c_int32), ("trace_slow_ratio", C.c_int32),
         ("trace", C.c_void_p * 4), ("trace_decay", C.c_float * 4),
+        ("post_recent", C.c_void_p), ("post_ring", C.c_void_p), ("post_cnt", C.c_void_p),
+        ("post_ring_k", C.c_int32), ("snap_trace", C.c_int32), ("snap_period", C.c_int32),
+        ("snap_depth", C.c_int32), ("pad2", C.c_int32), ("snap_buf", C.c_void_p),
     ]
 
 

@@ -75,6 +75,10 @@ struct EnginePop {
     float* gin_inh = nullptr;
     int32_t* hist_ids = nullptr;
     int32_t* hist_count = nullptr;
+    // spike-time history for deferred plasticity (target of a deferred projection)
+    int32_t* post_recent = nullptr;   // [n][4]
+    int32_t* post_ring = nullptr;     // [n][kPostRing]
+    int32_t* post_cnt = nullptr;      // [n]
 };
 
 struct EngineProj {
@@ -86,7 +90,16 @@ struct EngineProj {
     float* x_pre = nullptr;
     float* x_post = nullptr;
     bool traces_fused = false;   // both traces advanced by the neuron updates
+    bool deferred = false;       // potentiation deferred to row passes (plastic.cu)
+    int32_t* seg_last = nullptr;
+    float* seg_x = nullptr;
+    float* x_snap = nullptr;
 };
+
+constexpr int kPostRing = 64;       // target spike steps kept per neuron
+constexpr int kSnapPeriod = 16;     // steps between x_pre snapshots
+constexpr int kSnapDepth = 64;      // snapshots kept
+constexpr int kSweepPeriod = 960;   // every row is walked at least this often (< (depth-1)*period)
 
 struct nrn_engine {
     int device = 0;
@@ -106,6 +119,7 @@ struct nrn_engine {
     int64_t raster_cap = 0;
     int64_t spikes_flushed = 0;
     std::map<int, cudaGraphExec_t> graphs;
+    int* d_err = nullptr;                 // deferred-plasticity history overflow
 
     ~nrn_engine() {
         if (device >= 0) cudaSetDevice(device);
@@ -114,13 +128,15 @@ struct nrn_engine {
             if (p.owns_isyn) cudaFree(p.d.i_syn);
             cudaFree(p.g_exc); cudaFree(p.g_inh); cudaFree(p.gin_exc); cudaFree(p.gin_inh);
             cudaFree(p.hist_ids); cudaFree(p.hist_count);
+            cudaFree(p.post_recent); cudaFree(p.post_ring); cudaFree(p.post_cnt);
         }
         for (auto& q : projs) {
             free_csr(q.csr);
             cudaFree(q.x_pre);
             cudaFree(q.x_post);
+            cudaFree(q.seg_last); cudaFree(q.seg_x); cudaFree(q.x_snap);
         }
-        cudaFree(d_step); cudaFree(d_events); cudaFree(d_raster_count);
+        cudaFree(d_step); cudaFree(d_events); cudaFree(d_raster_count); cudaFree(d_err);
         cudaFree(raster_step); cudaFree(raster_gid);
         if (stream) cudaStreamDestroy(stream);
     }
@@ -192,9 +208,16 @@ struct nrn_engine {
             }
             // plasticity traces of the projections this population feeds or receives
             a.trace_slow_ratio = slow_ratio;
+            a.snap_trace = -1;
             for (const auto& q : projs) {
                 if (!q.plastic || !q.traces_fused) continue;
                 if (q.src_pop == i) {
+                    if (q.deferred) {
+                        a.snap_trace = a.n_traces;
+                        a.snap_buf = q.x_snap;
+                        a.snap_period = kSnapPeriod;
+                        a.snap_depth = kSnapDepth;
+                    }
                     a.trace[a.n_traces] = q.x_pre;
                     a.trace_decay[a.n_traces++] = static_cast<float>(std::exp(-dt / q.stdp[0]));
                 }
@@ -202,6 +225,12 @@ struct nrn_engine {
                     a.trace[a.n_traces] = q.x_post;
                     a.trace_decay[a.n_traces++] = static_cast<float>(std::exp(-dt / q.stdp[1]));
                 }
+            }
+            if (p.post_recent) {
+                a.post_recent = p.post_recent;
+                a.post_ring = p.post_ring;
+                a.post_cnt = p.post_cnt;
+                a.post_ring_k = kPostRing;
             }
         }
         return a;
@@ -234,6 +263,62 @@ struct nrn_engine {
         return s;
     }
 
+    PlasticArgs plastic_args(const EngineProj& q) const {
+        PlasticArgs a;
+        a.n_src = q.csr.n_src;
+        a.nd = q.csr.nd;
+        a.dmin = q.csr.dmin;
+        a.seg_ptr = q.csr.seg_ptr;
+        a.tgt = q.csr.tgt;
+        a.w = q.csr.w;
+        a.mod = q.csr.mod;
+        a.acc = acc_of(q);
+        a.x_pre = q.x_pre;
+        a.x_post = q.x_post;
+        a.spike_src = pops[q.src_pop].d.spike;
+        a.spike_tgt = pops[q.tgt_pop].d.spike;
+        a.hist_src = hist(q.src_pop);
+        a.a_plus = static_cast<float>(q.stdp[2]);
+        a.a_minus = static_cast<float>(std::fabs(q.stdp[3]));
+        a.lr = static_cast<float>(q.stdp[6]);
+        a.w_min = static_cast<float>(q.stdp[4]);
+        a.w_max = static_cast<float>(q.stdp[5]);
+        a.decay_pre = static_cast<float>(std::exp(-dt / q.stdp[0]));
+        a.seg_last = q.seg_last;
+        a.seg_x = q.seg_x;
+        a.x_snap = q.x_snap;
+        a.snap_period = kSnapPeriod;
+        a.snap_depth = kSnapDepth;
+        const EnginePop& t = pops[q.tgt_pop];
+        a.post_recent = reinterpret_cast<const int4*>(t.post_recent);
+        a.post_ring = t.post_ring;
+        a.post_cnt = t.post_cnt;
+        a.post_ring_k = kPostRing;
+        a.sweep_period = kSweepPeriod;
+        a.sweep_rows = (q.csr.n_src + kSweepPeriod - 1) / kSweepPeriod;
+        a.err = d_err;
+        a.events = d_events;
+        return a;
+    }
+
+    // Walks every row of the deferred projections so that their weights are
+    // up to date through the last step run (before weights are read).
+    nrn_status_t flush_deferred() {
+        if (step <= 0) return NRN_OK;
+        for (auto& q : projs)
+            if (q.deferred) NRN_TRY(plastic_rows(plastic_args(q), PLASTIC_FLUSH, step - 1, nullptr, stream));
+        return NRN_OK;
+    }
+
+    nrn_status_t check_err() {
+        int h = 0;
+        NRN_CUDA_TRY(cudaMemcpyAsync(&h, d_err, sizeof(int), cudaMemcpyDeviceToHost, stream));
+        NRN_CUDA_TRY(cudaStreamSynchronize(stream));
+        if (h == 1) return fail(NRN_ERR_CAPACITY, "STDP: a target spiked more often than its spike history holds");
+        if (h == 2) return fail(NRN_ERR_STATE, "STDP: a row was not refreshed within the trace snapshot window");
+        return NRN_OK;
+    }
+
     // Decides, per plastic projection, whether the neuron updates of its
     // source and target advance its traces (both or neither: a projection
     // that does not fit in the NRN_MAX_TRACES slots of both populations
@@ -255,13 +340,25 @@ struct nrn_engine {
                 q.traces_fused = true;
             }
         }
+        // Deferred potentiation needs STDP on every step, fused traces and one
+        // snapshot slot per source population.
+        std::vector<char> snap_used(pops.size(), 0);
+        for (auto& q : projs) {
+            q.deferred = false;
+            if (!q.plastic || !q.traces_fused || slow_ratio != 1 || q.csr.nd > 256) continue;
+            if (snap_used[q.src_pop]) continue;
+            snap_used[q.src_pop] = 1;
+            q.deferred = true;
+        }
     }
 
     // Enqueues one step at offset `off` from *d_step; with `ev` non-null,
     // records events around the three phases (ev[0..3]).
     nrn_status_t enqueue_step(int64_t off, cudaEvent_t* ev = nullptr) {
         std::vector<nrn_proj_t> dp;
-        for (auto& q : projs) dp.push_back(dev_proj(q));
+        std::vector<int> src_map;
+        for (auto& q : projs)
+            if (!q.deferred) dp.push_back(dev_proj(q));
         std::vector<nrn_spike_hist_t> hs;
         for (size_t i = 0; i < pops.size(); ++i) hs.push_back(hist(static_cast<int>(i)));
         if (ev) NRN_CUDA_TRY(cudaEventRecord(ev[0], stream));
@@ -269,6 +366,8 @@ struct nrn_engine {
                                          static_cast<int32_t>(hs.size()), off,
                                          reinterpret_cast<const int64_t*>(d_step), d_events,
                                          reinterpret_cast<nrn_stream_t>(stream)));
+        for (auto& q : projs)
+            if (q.deferred) NRN_TRY(plastic_rows(plastic_args(q), PLASTIC_DELIVER, off, d_step, stream));
         if (ev) NRN_CUDA_TRY(cudaEventRecord(ev[1], stream));
         for (size_t i = 0; i < pops.size(); ++i) {
             nrn_pop_step_t a = pop_args(static_cast<int>(i), dt, off, true);
@@ -277,6 +376,10 @@ struct nrn_engine {
         if (ev) NRN_CUDA_TRY(cudaEventRecord(ev[2], stream));
         for (auto& q : projs) {
             if (!q.plastic) continue;
+            if (q.deferred) {
+                NRN_TRY(plastic_rows(plastic_args(q), PLASTIC_LTD, off, d_step, stream));
+                continue;
+            }
             nrn_stdp_t s = stdp_args(q);
             NRN_TRY(nrn_cuda_stdp_step(&s, off, reinterpret_cast<const int64_t*>(d_step),
                                         reinterpret_cast<nrn_stream_t>(stream)));
@@ -387,6 +490,7 @@ nrn_status_t nrn_engine_create(nrn_engine** out, int device, double dt, int32_t 
     NRN_TRY(dalloc0(&e->d_step, 1, e->stream));
     NRN_TRY(dalloc0(&e->d_events, 1, e->stream));
     NRN_TRY(dalloc0(&e->d_raster_count, 1, e->stream));
+    NRN_TRY(dalloc0(&e->d_err, 1, e->stream));
     *out = e.release();
     return NRN_OK;
 }
@@ -619,6 +723,21 @@ nrn_status_t nrn_engine_finalize(nrn_engine* e, int32_t init_update) {
         NRN_TRY(dalloc0(&q.x_post, e->pops[q.tgt_pop].d.n, e->stream));
     }
     e->assign_trace_slots();
+    for (auto& q : e->projs) {
+        if (!q.deferred) continue;
+        const size_t nseg = static_cast<size_t>(q.csr.n_src) * q.csr.nd;
+        NRN_TRY(dalloc0(&q.seg_last, nseg, e->stream));
+        NRN_CUDA_TRY(cudaMemsetAsync(q.seg_last, 0xFF, nseg * sizeof(int32_t), e->stream));   // -1: nothing applied
+        NRN_TRY(dalloc0(&q.seg_x, nseg, e->stream));
+        NRN_TRY(dalloc0(&q.x_snap, static_cast<size_t>(kSnapDepth) * q.csr.n_src, e->stream));
+        auto& t = e->pops[q.tgt_pop];
+        if (!t.post_recent) {
+            NRN_TRY(dalloc0(&t.post_recent, static_cast<size_t>(t.d.n) * 4, e->stream));
+            NRN_CUDA_TRY(cudaMemsetAsync(t.post_recent, 0xFF, static_cast<size_t>(t.d.n) * 16, e->stream));
+            NRN_TRY(dalloc0(&t.post_ring, static_cast<size_t>(t.d.n) * kPostRing, e->stream));
+            NRN_TRY(dalloc0(&t.post_cnt, static_cast<size_t>(t.d.n), e->stream));
+        }
+    }
     if (init_update) {
         for (size_t i = 0; i < e->pops.size(); ++i) {
             nrn_pop_step_t a = e->pop_args(static_cast<int>(i), 0.0, 0, false);
@@ -707,7 +826,7 @@ nrn_status_t nrn_engine_set_step(nrn_engine* e, int64_t step) {
 nrn_status_t nrn_engine_sync(nrn_engine* e) {
     ENGINE_GUARD(e);
     NRN_CUDA_TRY(cudaStreamSynchronize(e->stream));
-    return NRN_OK;
+    return e->check_err();
 }
 
 nrn_status_t nrn_engine_raster(nrn_engine* e, int32_t* step, int32_t* gid, int64_t cap, int64_t* n) {
@@ -744,6 +863,8 @@ nrn_status_t nrn_engine_weights(nrn_engine* e, int32_t proj, float* out, int64_t
     NRN_CHECK_ARG(proj >= 0 && proj < static_cast<int32_t>(e->projs.size()), "bad projection index");
     const auto& c = e->projs[proj].csr;
     NRN_CHECK_ARG(n == c.nnz && out != nullptr, "weights: output size must equal the synapse count");
+    NRN_TRY(e->flush_deferred());
+    NRN_TRY(e->check_err());
     std::vector<float> w(static_cast<size_t>(c.nnz));
     NRN_CUDA_TRY(cudaStreamSynchronize(e->stream));
     if (c.nnz) NRN_CUDA_TRY(cudaMemcpy(w.data(), c.w, c.nnz * 4, cudaMemcpyDeviceToHost));
@@ -763,6 +884,8 @@ nrn_status_t nrn_engine_weights_device(nrn_engine* e, int32_t proj, float* out, 
     const auto& c = e->projs[proj].csr;
     NRN_CHECK_ARG(n == c.nnz && (n == 0 || out != nullptr), "weights: output size must equal the synapse count");
     if (n == 0) return NRN_OK;
+    NRN_TRY(e->flush_deferred());
+    NRN_TRY(e->check_err());
     if (c.orig) {
         // out[orig[k]] = w[k]
         return nrn_cuda_scatter(c.w, c.orig, n, out, reinterpret_cast<nrn_stream_t>(e->stream));

@@ -55,6 +55,37 @@ nrn_status_t generate(const GenArgs& g, int32_t* src, int32_t* tgt, float* w, ui
 
 int sm_count_current();
 
+// Deferred-potentiation STDP (plastic.cu).
+enum { PLASTIC_DELIVER = 0, PLASTIC_LTD = 1, PLASTIC_FLUSH = 2 };
+struct PlasticArgs {
+    int32_t n_src = 0, nd = 1, dmin = 1;
+    const int64_t* seg_ptr = nullptr;
+    const uint32_t* tgt = nullptr;
+    float* w = nullptr;
+    const float* mod = nullptr;
+    float* acc = nullptr;
+    const float* x_pre = nullptr;
+    const float* x_post = nullptr;
+    const float* spike_src = nullptr;
+    const float* spike_tgt = nullptr;
+    nrn_spike_hist_t hist_src{};
+    float a_plus = 0, a_minus = 0, lr = 0, w_min = 0, w_max = 0, decay_pre = 1;
+    int32_t* seg_last = nullptr;      // [n_src*nd] weights applied through this step
+    float* seg_x = nullptr;           // [n_src*nd] x_pre at that step
+    const float* x_snap = nullptr;    // [snap_depth][n_src]
+    int32_t snap_period = 16, snap_depth = 64;
+    const int4* post_recent = nullptr;
+    const int32_t* post_ring = nullptr;
+    const int32_t* post_cnt = nullptr;
+    int32_t post_ring_k = 64;
+    int64_t sweep_rows = 0;           // rows refreshed per step by the sweep
+    int64_t sweep_period = 1;         // steps for the sweep to cover every row
+    int* err = nullptr;
+    unsigned long long* events = nullptr;
+};
+nrn_status_t plastic_rows(const PlasticArgs& a, int mode, long long step_off, const long long* step_base,
+                          cudaStream_t s);
+
 // The engine's spike raster buffers (for entry points outside engine.cu).
 struct EngineRasterView {
     int device = 0;

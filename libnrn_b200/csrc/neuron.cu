@@ -58,6 +58,14 @@ struct PopArgs {
     int trace_slow_ratio;
     float* trace[NRN_MAX_TRACES];
     float trace_decay[NRN_MAX_TRACES];
+    int4* post_recent;
+    int* post_ring;
+    int* post_cnt;
+    int post_ring_k;
+    int snap_trace;
+    int snap_period;
+    int snap_depth;
+    float* snap_buf;
 };
 
 template <bool HET>
@@ -170,7 +178,20 @@ __global__ void __launch_bounds__(256) pop_step_kernel(const __grid_constant__ P
         if (a.n_traces > 0 && (a.trace_slow_ratio <= 1 || step % a.trace_slow_ratio == 0)) {
             // pair-STDP traces (src/plasticity/stdp.cpp:118-128): decay, then + spike
             const float sp = spiked ? 1.0f : 0.0f;
-            for (int k = 0; k < a.n_traces; ++k) a.trace[k][i] = a.trace[k][i] * a.trace_decay[k] + sp;
+            for (int k = 0; k < a.n_traces; ++k) {
+                const float x = a.trace[k][i] * a.trace_decay[k] + sp;
+                a.trace[k][i] = x;
+                if (k == a.snap_trace && (step + 1) % a.snap_period == 0)
+                    a.snap_buf[(((step + 1) / a.snap_period) % a.snap_depth) * static_cast<long long>(a.n) + i] = x;
+            }
+        }
+        if (spiked && a.post_recent != nullptr) {
+            const int t = static_cast<int>(step);
+            int4 r = a.post_recent[i];
+            a.post_recent[i] = make_int4(t, r.x, r.y, r.z);
+            const int c = a.post_cnt[i];
+            a.post_ring[static_cast<long long>(i) * a.post_ring_k + (c % a.post_ring_k)] = t;
+            a.post_cnt[i] = c + 1;
         }
         if (a.i_syn) a.i_syn[i] = 0.0f;
         if (COND) {
@@ -298,6 +319,20 @@ extern "C" nrn_status_t nrn_cuda_pop_step(const nrn_pop_step_t* in, nrn_stream_t
         a.trace[k] = d.trace[k];
         a.trace_decay[k] = d.trace_decay[k];
     }
+    a.post_recent = reinterpret_cast<int4*>(d.post_recent);
+    a.post_ring = d.post_ring;
+    a.post_cnt = d.post_cnt;
+    a.post_ring_k = d.post_ring_k;
+    NRN_CHECK_ARG(d.post_recent == nullptr || (d.post_ring && d.post_cnt && d.post_ring_k > 0),
+                  "nrn_cuda_pop_step: spike history needs ring, count and depth");
+    NRN_CHECK_ARG(d.post_recent == nullptr || (reinterpret_cast<uintptr_t>(d.post_recent) % 16) == 0,
+                  "nrn_cuda_pop_step: post_recent must be 16-byte aligned");
+    a.snap_trace = d.snap_buf ? d.snap_trace : -1;
+    a.snap_period = d.snap_period > 0 ? d.snap_period : 1;
+    a.snap_depth = d.snap_depth > 0 ? d.snap_depth : 1;
+    a.snap_buf = d.snap_buf;
+    NRN_CHECK_ARG(d.snap_buf == nullptr || (d.snap_trace >= 0 && d.snap_trace < d.n_traces),
+                  "nrn_cuda_pop_step: snapshot of a trace slot that does not exist");
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     switch (d.model) {
         case NRN_MODEL_LIF: launch_model<NRN_MODEL_LIF>(a, het, false, s); break;
