@@ -185,6 +185,8 @@ def main():
     ap.add_argument("--chunk", type=int, default=0)
     ap.add_argument("--profile-steps", type=int, default=300)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--max-rate", type=float, default=200.0,
+                    help="mean firing rate bound (Hz) that sizes the multi-GPU spike exchange buffers")
     ap.add_argument("--scale", type=float, default=1.0,
                     help="network size factor (profiling of small cases only; the bench line uses 1)")
     args = ap.parse_args()
@@ -196,22 +198,44 @@ def main():
     if args.impl == "reference":
         run_reference_arm(args, rank)
         return
-    if world > 1:
-        raise SystemExit("multi-GPU runs are launched through torchrun; see the partitioned engine")
 
     import numpy as np
     import torch
 
     from libnrn_b200.engine import Network
+    from libnrn_b200.partition import share_unique_id
 
     peaks, peaks_kind = load_peaks()
     torch.cuda.set_device(local)
-    spec = workload_spec(args.workload, 1, args.steps, args.scale)
+    dist = None
+    partition = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                timeout=datetime.timedelta(seconds=600))
+        partition = (rank, world, share_unique_id(), args.max_rate)
+
+    def all_reduce(x: float, op: str) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
+        return float(t.item())
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    spec = workload_spec(args.workload, world, args.steps, args.scale)
     t_setup = time.perf_counter()
-    nw = Network.from_spec(spec, device=local, record=True)
+    nw = Network.from_spec(spec, device=local, record=True, partition=partition)
     torch.cuda.synchronize()
-    setup_s = time.perf_counter() - t_setup
-    nnz = sum(p["nnz"] for p in nw.projs)
+    setup_s = all_reduce(time.perf_counter() - t_setup, "max")
+    nnz = all_reduce(float(sum(p["nnz"] for p in nw.projs)), "sum")
     n_total = spec["n_total"]
     stream = torch.cuda.ExternalStream(nw.stream())
 
@@ -219,40 +243,40 @@ def main():
     nw.sync()
     nw.raster()
     s0, e0 = nw.counters()
+    barrier()
     with ClockSampler(local) as clk:
         ev_a = torch.cuda.Event(enable_timing=True)
         ev_b = torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
         ev_a.record(stream)
         nw.run(args.steps, args.chunk)
         ev_b.record(stream)
         torch.cuda.synchronize()
-    ms = ev_a.elapsed_time(ev_b)
+    ms = all_reduce(ev_a.elapsed_time(ev_b), "max")
+    barrier()
+    nw.sync()
     s1, e1 = nw.counters()
-    st, gid = nw.raster()
-    events = e1 - e0
-    spikes = s1 - s0
+    nw.raster()
+    events = all_reduce(float(e1 - e0), "sum")
+    spikes = all_reduce(float(s1 - s0), "sum")
     sec = ms / 1e3
     value = events / sec
 
-    # Per-kernel device times (eager launches, events around each phase).
+    # Per-phase device times (eager launches, events around each phase).
     ps0, pe0 = nw.counters()
     prof = nw.profile(args.profile_steps)
     ps1, pe1 = nw.counters()
     nw.raster()
     ev_p, sp_p = pe1 - pe0, ps1 - ps0
     phases = {"deliver": prof[0], "neuron": prof[1], "stdp": prof[2]}
-    # algorithmic bytes: delivery 8 B per event (target + weight)
-    # + 16 B per (spike, delay) segment; neuron update 28 B per LIF neuron
-    # (+ drive computed in-kernel); STDP per step: traces 12 B per neuron,
-    # pre rows 12 B per synapse, post in-lists 16 B per synapse.
+    # algorithmic bytes: delivery 8 B per event (target + weight) + 16 B per
+    # (spike, delay) segment for its offsets
     deliver_bytes = 8.0 * ev_p + 16.0 * sp_p * 4
     dom = max(phases, key=phases.get)
-    alg = {"deliver": deliver_bytes, "neuron": 28.0 * n_total * args.profile_steps}
-    achieved = alg.get("deliver") / (phases["deliver"] / 1e3) / 1e9 if phases["deliver"] > 0 else 0.0
+    achieved = deliver_bytes / (phases["deliver"] / 1e3) / 1e9 if phases["deliver"] > 0 else 0.0
 
-    # e2e: initial state from pinned host, run, raster to host, all timed.
-    # The copies run on torch's stream; the engine stream starts after them.
+    # e2e: this rank's initial state from pinned host, run, raster to host,
+    # all timed (wall clock, max over ranks).  The copies run on torch's
+    # stream; the engine stream starts after them.
     host_state = []
     for p in nw.pops:
         for k in ("v", "ref"):
@@ -260,7 +284,7 @@ def main():
             if t is not None:
                 host_state.append((t, t.cpu().pin_memory()))
     h2d = sum(h.numel() * 4 for _, h in host_state)
-    torch.cuda.synchronize()
+    barrier()
     t0 = time.perf_counter()
     for dev_t, h in host_state:
         dev_t.copy_(h, non_blocking=True)
@@ -270,34 +294,41 @@ def main():
     st2, gid2 = nw.raster()
     e_s1, e_e1 = nw.counters()
     t1 = time.perf_counter()
-    d2h = len(gid2) * 8
-    e2e = (e_e1 - e_e0) / (t1 - t0)
+    e2e_s = all_reduce(t1 - t0, "max")
+    e2e = all_reduce(float(e_e1 - e_e0), "sum") / e2e_s
+    d2h = all_reduce(float(len(gid2) * 8), "sum")
+    h2d = all_reduce(float(h2d), "sum")
     del host_state
     torch.cuda.synchronize()
 
     cpu = None
-    if not args.no_cpu:
+    if not args.no_cpu and rank == 0:
         try:
             cpu = cpu_reference(args)
         except Exception as ex:  # report, do not fail the GPU line
             cpu = {"error": str(ex)[:200]}
 
     clocks = clk.summary()
-    kernels_per_step = 1 + len(nw.pops) + 2 * sum(1 for q in spec["projs"] if q.get("plastic"))
-    chunk = args.chunk if args.chunk > 0 else min(args.steps, 50)
+    n_walk = sum(1 for q in spec["projs"] if q.get("plastic"))
+    windows = args.steps // 15 if (world > 1 or n_walk) else 0
+    kernels_per_step = 1 + n_walk + len(nw.pops)
+    chunk = args.chunk if args.chunk > 0 else 45
     line = {
-        "metric": "synaptic_events_per_s", "value": value, "unit": "events/s", "n_gpus": 1,
+        "metric": "synaptic_events_per_s", "value": value, "unit": "events/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (Philox-generated connectivity and drive)",
-        "config": {"workload": args.workload, "neurons": n_total, "synapses": nnz,
+        "config": {"workload": args.workload, "neurons": n_total, "synapses": int(nnz),
                    "dt_ms": spec["dt"] * 1e3, "l2": "inputs larger than L2 (synapse store "
-                   f"{nnz * 8 / 1e9:.1f} GB)", "parallelism": "single GPU"},
+                   f"{nnz * 8 / 1e9:.1f} GB)",
+                   "parallelism": "single GPU" if world == 1 else
+                   f"partitioned by neuron over {world} GPUs, NCCL all-gather of spike ids per 15-step window"},
         "neuron_updates_per_s": n_total * args.steps / sec,
         "rtf": sec / (args.steps * spec["dt"]),
         "spikes": int(spikes), "rate_hz": spikes / n_total / (args.steps * spec["dt"]),
         "setup_s": setup_s,
-        "gpu_launches": kernels_per_step * args.steps + (args.steps + chunk - 1) // chunk,
+        "gpu_launches": kernels_per_step * args.steps + windows * (1 + len(nw.pops) * (2 if world > 1 else 0))
+        + (args.steps + chunk - 1) // chunk,
         "phase_ms_per_step": {k: v / args.profile_steps for k, v in phases.items()},
         "roofline": {"kernel": "deliver", "dominant_phase": dom, "bound": "hbm", "achieved": achieved,
                      "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
@@ -316,7 +347,11 @@ def main():
     del stream
     torch.cuda.synchronize()
     nw.close()
-    print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
 
 
 if __name__ == "__main__":

@@ -150,22 +150,37 @@ typedef struct {
     int32_t trace_slow_ratio;
     float* trace[4];
     float trace_decay[4];
-    /* Spike-time history (for deferred plasticity on the projections this
-     * population receives): on a spike at step t, post_recent[i] (int4:
+    /* A trace slot k with trace_ring[k] non-NULL keeps every step's value:
+     * x(t) in row t % trace_ring_depth of trace_ring[k] [depth][n], read
+     * back from row (t-1) % depth (trace[k] is then unused). */
+    float* trace_ring[4];
+    int32_t trace_ring_depth;
+    int32_t pad1;
+    /* Spike-time history (for plasticity applied by segment walks): on a
+     * spike at step t, post_recent[i] (int4:
      * latest four spike steps, newest first) shifts in t and t is appended
      * to post_ring[i*post_ring_k + post_cnt[i] % post_ring_k]. */
     int32_t* post_recent;      /* [n][4] or NULL                            */
     int32_t* post_ring;        /* [n][post_ring_k]                          */
     int32_t* post_cnt;         /* [n]                                       */
     int32_t post_ring_k;
-    /* Snapshot of trace slot snap_trace every snap_period steps: at the end
-     * of step t with (t+1) % snap_period == 0 the trace is copied into row
-     * ((t+1)/snap_period) % snap_depth of snap_buf [snap_depth][n]. */
-    int32_t snap_trace;        /* -1: none                                  */
-    int32_t snap_period;
-    int32_t snap_depth;
+    /* Spike exchange between the GPUs a network is partitioned over
+     * (population split by neuron index).  id_offset is added to every
+     * compacted id, so that ids index the whole population.  win > 0 marks
+     * windows of win steps (win <= 32), window u = step % win:
+     *   win_mask[i] |= 1 << u for each spike (window trace snapshots);
+     *   with send_hdr non-NULL, the ids go to the window send buffer instead
+     *   of the history ring: send_hdr[u] counts the ids of window step u,
+     *   which follow those of steps 0..u-1 in send_ids[0 .. send_cap);
+     *   overflow sets *err to 4. */
+    int32_t id_offset;
+    int32_t win;
+    uint32_t* win_mask;        /* [n] or NULL                               */
+    int32_t* send_hdr;         /* [win] or NULL                             */
+    int32_t* send_ids;         /* [send_cap]                                */
+    int32_t send_cap;
     int32_t pad2;
-    float* snap_buf;
+    int32_t* err;              /* device error flag, or NULL                */
 } nrn_pop_step_t;
 
 #define NRN_MAX_TRACES 4
@@ -300,10 +315,16 @@ typedef struct nrn_engine nrn_engine;
 
 typedef struct {
     int32_t model;
-    int32_t n;
-    int32_t gid_offset;
+    int32_t n;                 /* neurons on this GPU                        */
+    int32_t gid_offset;        /* global id of the population's neuron 0    */
     int32_t record;            /* 1: keep every spike in the raster          */
-    /* state, caller-owned device arrays (the reference's state tensors) */
+    /* Partitioned network (nrn_engine_set_partition): this GPU holds neurons
+     * [local_offset, local_offset + n) of a population of n_global neurons.
+     * 0, 0: the whole population (n_global = n). */
+    int32_t n_global;
+    int32_t local_offset;
+    /* state of this GPU's neurons, caller-owned device arrays (the
+     * reference's state tensors) */
     float* v;
     float* aux;
     float* refractory;
@@ -326,8 +347,8 @@ typedef struct {
     int32_t receptor;
     int32_t on_device;         /* 1: the arrays below are device pointers   */
     int64_t nnz;
-    const int32_t* src;        /* [nnz] local source index                  */
-    const int32_t* tgt;        /* [nnz] local target index                  */
+    const int32_t* src;        /* [nnz] source index in the whole population */
+    const int32_t* tgt;        /* [nnz] target index on this GPU            */
     const float* w;            /* [nnz]                                     */
     const uint8_t* delay;      /* [nnz] steps, >= 1                         */
     const float* mod;          /* [nnz] modulatory gain, or NULL            */
@@ -351,6 +372,19 @@ typedef struct {
 
 NRN_API nrn_status_t nrn_engine_create(nrn_engine** out, int device, double dt, int32_t slow_ratio);
 NRN_API nrn_status_t nrn_engine_destroy(nrn_engine* e);
+/* Multi-GPU: the network is partitioned by neuron index over `world` GPUs,
+ * one engine (and process or thread) per GPU, each built with the same
+ * calls on its slice of every population.  Spikes are exchanged with one
+ * NCCL all-gather per window of min(smallest delay, 32) steps; `id` is an
+ * NCCL unique id from nrn_comm_unique_id on one rank, passed to all (the
+ * call blocks until every rank has made it).  max_rate_hz bounds the mean
+ * firing rate of a population over a window (exchange buffer size); above
+ * it the run fails with NRN_ERR_CAPACITY.  Call before adding populations.
+ * Every rank must run the same step counts.  No counterpart in the
+ * reference (its runner is single-device, src/simulation/runner.cpp). */
+NRN_API nrn_status_t nrn_comm_unique_id(uint8_t id[128]);
+NRN_API nrn_status_t nrn_engine_set_partition(nrn_engine* e, int32_t rank, int32_t world, const uint8_t id[128],
+                                              double max_rate_hz);
 NRN_API nrn_status_t nrn_engine_add_population(nrn_engine* e, const nrn_pop_desc_t* d, int32_t* id);
 /* Update the uniform/per-neuron parameters of a population (between runs). */
 NRN_API nrn_status_t nrn_engine_set_params(nrn_engine* e, int32_t pop, const float* const* param,

@@ -31,7 +31,7 @@ EXPORTS = [
     "nrn_engine_raster", "nrn_engine_weights", "nrn_engine_nnz", "nrn_engine_counters",
     "nrn_engine_profile", "nrn_engine_weights_device", "nrn_engine_set_state", "nrn_engine_set_step",
     "nrn_cuda_block_deliver", "nrn_cuda_block_stdp", "nrn_cuda_compact", "nrn_cuda_gather_ring",
-    "nrn_cuda_scatter", "nrn_engine_raster_noalloc",
+    "nrn_cuda_scatter", "nrn_engine_raster_noalloc", "nrn_comm_unique_id", "nrn_engine_set_partition",
 ]
 
 
@@ -60,9 +60,11 @@ class PopStep(C.Structure):
         ("raster_step", C.c_void_p), ("raster_gid", C.c_void_p), ("raster_count", C.c_void_p),
         ("raster_cap", C.c_int64), ("n_traces", C.c_int32), ("trace_slow_ratio", C.c_int32),
         ("trace", C.c_void_p * 4), ("trace_decay", C.c_float * 4),
+        ("trace_ring", C.c_void_p * 4), ("trace_ring_depth", C.c_int32), ("pad1", C.c_int32),
         ("post_recent", C.c_void_p), ("post_ring", C.c_void_p), ("post_cnt", C.c_void_p),
-        ("post_ring_k", C.c_int32), ("snap_trace", C.c_int32), ("snap_period", C.c_int32),
-        ("snap_depth", C.c_int32), ("pad2", C.c_int32), ("snap_buf", C.c_void_p),
+        ("post_ring_k", C.c_int32), ("id_offset", C.c_int32), ("win", C.c_int32),
+        ("win_mask", C.c_void_p), ("send_hdr", C.c_void_p), ("send_ids", C.c_void_p),
+        ("send_cap", C.c_int32), ("pad2", C.c_int32), ("err", C.c_void_p),
     ]
 
 
@@ -81,7 +83,7 @@ class Proj(C.Structure):
 class PopDesc(C.Structure):
     _fields_ = [
         ("model", C.c_int32), ("n", C.c_int32), ("gid_offset", C.c_int32), ("record", C.c_int32),
-        ("v", C.c_void_p), ("aux", C.c_void_p), ("refractory", C.c_void_p), ("spike", C.c_void_p),
+        ("n_global", C.c_int32), ("local_offset", C.c_int32), ("v", C.c_void_p), ("aux", C.c_void_p), ("refractory", C.c_void_p), ("spike", C.c_void_p),
         ("i_syn", C.c_void_p), ("tau_syn_exc", C.c_float), ("tau_syn_inh", C.c_float),
         ("e_exc", C.c_float), ("e_inh", C.c_float), ("param", C.c_void_p * NRN_MAX_PARAMS),
         ("uniform", C.c_float * NRN_MAX_PARAMS), ("drive", Drive),
@@ -136,6 +138,8 @@ def lib() -> C.CDLL:
             "nrn_engine_generate_projection": [vp, C.POINTER(GenDesc), C.POINTER(i32), C.POINTER(i64)],
             "nrn_engine_set_stdp": [vp, i32, C.POINTER(C.c_double)],
             "nrn_engine_finalize": [vp, i32],
+            "nrn_comm_unique_id": [C.POINTER(C.c_uint8 * 128)],
+            "nrn_engine_set_partition": [vp, i32, i32, C.POINTER(C.c_uint8 * 128), C.c_double],
             "nrn_engine_run": [vp, i64, i32],
             "nrn_engine_sync": [vp],
             "nrn_engine_stream": [vp, C.POINTER(vp)],

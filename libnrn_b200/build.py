@@ -25,7 +25,24 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-std=c++17", "-O3", "-lineinfo", "-fmad=false", "-cudart=shared", "-Xcompiler", "-fPIC", "-Xcompiler",
          "-fvisibility=hidden", f"-I{os.path.join(ROOT, 'include')}", f"-I{CSRC}"]
-SOURCES = ["neuron.cu", "deliver.cu", "connect.cu", "engine.cu", "blockdense.cu", "raster_noalloc.cu", "plastic.cu"]
+SOURCES = ["neuron.cu", "deliver.cu", "connect.cu", "engine.cu", "blockdense.cu", "raster_noalloc.cu", "plastic.cu",
+           "exchange.cu"]
+
+
+def _nccl_dir():
+    """NCCL of the installed PyTorch wheel (the library torch.distributed
+    loads, so one NCCL per process)."""
+    import importlib.util
+    spec = importlib.util.find_spec("nvidia")
+    for base in (spec.submodule_search_locations or []) if spec else []:
+        d = os.path.join(base, "nccl")
+        if os.path.exists(os.path.join(d, "include", "nccl.h")):
+            return d
+    raise RuntimeError("NCCL headers not found (nvidia-nccl wheel)")
+
+
+NCCL = _nccl_dir()
+FLAGS.append(f"-I{os.path.join(NCCL, 'include')}")
 
 
 def _headers():
@@ -148,8 +165,9 @@ def build(force: bool = False, verbose: bool = False) -> str:
     if _stale(LIB, objs):
         # one CUDA runtime per process: link the shared runtime (in a torch
         # process the runtime torch loaded is reused)
-        cmd = [NVCC, *ARCH, "-shared", "-cudart=shared", "-o", LIB, *objs, "-Xlinker", "--no-undefined",
-               "-Xlinker", "-rpath,/usr/local/cuda/lib64"]
+        nlib = os.path.join(NCCL, "lib")
+        cmd = [NVCC, *ARCH, "-shared", "-cudart=shared", "-o", LIB, *objs, f"-L{nlib}", "-l:libnccl.so.2",
+               "-Xlinker", "--no-undefined", "-Xlinker", "-rpath,/usr/local/cuda/lib64", "-Xlinker", f"-rpath,{nlib}"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stderr[-4000:]}")

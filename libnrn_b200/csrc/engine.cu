@@ -19,11 +19,14 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <memory>
 #include <string>
 #include <vector>
+
+#include <nccl.h>
 
 #include "common.cuh"
 #include "internal.h"
@@ -67,18 +70,26 @@ using namespace nrn;
 
 struct EnginePop {
     nrn_pop_desc_t d{};
+    int32_t n_global = 0;            // population size over all ranks
+    int32_t lo = 0;                  // index of this rank's first neuron
     bool cond = false;
     bool owns_isyn = false;
     float* g_exc = nullptr;
     float* g_inh = nullptr;
     float* gin_exc = nullptr;
     float* gin_inh = nullptr;
+    // spike history ring of the whole population: [depth][hist_cap]
     int32_t* hist_ids = nullptr;
     int32_t* hist_count = nullptr;
-    // spike-time history for deferred plasticity (target of a deferred projection)
-    int32_t* post_recent = nullptr;   // [n][4]
-    int32_t* post_ring = nullptr;     // [n][kPostRing]
-    int32_t* post_cnt = nullptr;      // [n]
+    int32_t hist_cap = 0;
+    // send block of this population inside a rank's exchange buffer
+    int64_t send_off = 0;
+    int32_t send_cap = 0;
+    // for projections with walk plasticity: window spike masks and spike steps
+    uint32_t* mask = nullptr;        // [n_global]
+    int32_t* recent = nullptr;       // [n_global][4] newest four spike steps
+    int32_t* ring = nullptr;         // [n][kRing] spike steps of this rank's neurons
+    int32_t* cnt = nullptr;          // [n]
 };
 
 struct EngineProj {
@@ -90,16 +101,18 @@ struct EngineProj {
     float* x_pre = nullptr;
     float* x_post = nullptr;
     bool traces_fused = false;   // both traces advanced by the neuron updates
-    bool deferred = false;       // potentiation deferred to row passes (plastic.cu)
+    bool walk = false;           // updates applied by segment walks (plastic.cu)
     int32_t* seg_last = nullptr;
     float* seg_x = nullptr;
-    float* x_snap = nullptr;
+    int32_t* seg_done = nullptr;
+    float* pre_snap = nullptr;   // [pre_depth][n_src] source trace at window ends
+    float* post_ring = nullptr;  // [ring_depth][n_tgt] target trace at every step
+    int32_t pre_depth = 1;
 };
 
-constexpr int kPostRing = 64;       // target spike steps kept per neuron
-constexpr int kSnapPeriod = 16;     // steps between x_pre snapshots
-constexpr int kSnapDepth = 64;      // snapshots kept
-constexpr int kSweepPeriod = 960;   // every row is walked at least this often (< (depth-1)*period)
+constexpr int kRing = 64;           // spike steps kept per neuron
+constexpr int kSweepPeriod = 640;   // the sweep looks at every row this often
+constexpr int kStale = 320;         // and walks segments not walked for this many steps
 
 struct nrn_engine {
     int device = 0;
@@ -119,7 +132,19 @@ struct nrn_engine {
     int64_t raster_cap = 0;
     int64_t spikes_flushed = 0;
     std::map<int, cudaGraphExec_t> graphs;
-    int* d_err = nullptr;                 // deferred-plasticity history overflow
+    int* d_err = nullptr;                 // device error flag (plasticity, exchange)
+    bool use_graphs = true;
+    // partition over GPUs
+    int32_t rank = 0, world = 1;
+    ncclComm_t comm = nullptr;
+    double max_rate_hz = 200.0;           // sizes the exchange buffers
+    // windows (exchange of spikes, STDP trace snapshots)
+    bool windows = false;
+    int32_t win = 1;
+    int32_t* send = nullptr;              // [rank_block]
+    int32_t* recv = nullptr;              // [world][rank_block]
+    int64_t rank_block = 0;
+    int32_t ring_depth = 1;               // steps of target trace kept (walk projections)
 
     ~nrn_engine() {
         if (device >= 0) cudaSetDevice(device);
@@ -128,16 +153,19 @@ struct nrn_engine {
             if (p.owns_isyn) cudaFree(p.d.i_syn);
             cudaFree(p.g_exc); cudaFree(p.g_inh); cudaFree(p.gin_exc); cudaFree(p.gin_inh);
             cudaFree(p.hist_ids); cudaFree(p.hist_count);
-            cudaFree(p.post_recent); cudaFree(p.post_ring); cudaFree(p.post_cnt);
+            cudaFree(p.mask); cudaFree(p.recent); cudaFree(p.ring); cudaFree(p.cnt);
         }
         for (auto& q : projs) {
             free_csr(q.csr);
             cudaFree(q.x_pre);
             cudaFree(q.x_post);
-            cudaFree(q.seg_last); cudaFree(q.seg_x); cudaFree(q.x_snap);
+            cudaFree(q.seg_last); cudaFree(q.seg_x); cudaFree(q.seg_done);
+            cudaFree(q.pre_snap); cudaFree(q.post_ring);
         }
         cudaFree(d_step); cudaFree(d_events); cudaFree(d_raster_count); cudaFree(d_err);
         cudaFree(raster_step); cudaFree(raster_gid);
+        cudaFree(send); cudaFree(recv);
+        if (comm) ncclCommDestroy(comm);
         if (stream) cudaStreamDestroy(stream);
     }
 
@@ -166,17 +194,19 @@ struct nrn_engine {
         nrn_spike_hist_t h{};
         h.ids = pops[i].hist_ids;
         h.count = pops[i].hist_count;
-        h.cap = pops[i].d.n > 0 ? pops[i].d.n : 1;
+        h.cap = pops[i].hist_cap > 0 ? pops[i].hist_cap : 1;
         h.depth = depth;
         return h;
     }
+
+    bool window_end(int64_t abs_step) const { return windows && (abs_step + 1) % win == 0; }
 
     nrn_pop_step_t pop_args(int i, double dt_step, int64_t step_off, bool in_run) const {
         const EnginePop& p = pops[i];
         nrn_pop_step_t a{};
         a.model = p.d.model;
         a.n = p.d.n;
-        a.gid_offset = p.d.gid_offset;
+        a.gid_offset = p.d.gid_offset + p.lo;
         a.dt = dt_step;
         a.v = p.d.v;
         a.aux = p.d.aux;
@@ -196,28 +226,40 @@ struct nrn_engine {
             a.drive = p.d.drive;
             a.step = step_off;
             a.step_base = reinterpret_cast<const int64_t*>(d_step);
-            a.spike_ids = p.hist_ids;
-            a.spike_count = p.hist_count;
-            a.hist_depth = depth;
-            a.hist_cap = p.d.n > 0 ? p.d.n : 1;
+            a.id_offset = p.lo;
+            a.err = d_err;
+            if (world > 1) {
+                // ids go to the window send buffer; the ring is filled by the exchange
+                a.win = win;
+                a.send_hdr = send + p.send_off;
+                a.send_ids = send + p.send_off + win;
+                a.send_cap = p.send_cap;
+            } else {
+                a.spike_ids = p.hist_ids;
+                a.spike_count = p.hist_count;
+                a.hist_depth = depth;
+                a.hist_cap = p.hist_cap;
+            }
+            if (p.mask) {
+                a.win = win;
+                a.win_mask = p.mask + p.lo;
+            }
             if (p.d.record) {
                 a.raster_step = raster_step;
                 a.raster_gid = raster_gid;
                 a.raster_count = d_raster_count;
                 a.raster_cap = raster_cap;
             }
-            // plasticity traces of the projections this population feeds or receives
+            // traces of the plastic projections updated at every step
             a.trace_slow_ratio = slow_ratio;
-            a.snap_trace = -1;
             for (const auto& q : projs) {
+                if (q.walk && q.tgt_pop == i) {
+                    a.trace_ring[a.n_traces] = q.post_ring;
+                    a.trace_ring_depth = ring_depth;
+                    a.trace_decay[a.n_traces++] = static_cast<float>(std::exp(-dt / q.stdp[1]));
+                }
                 if (!q.plastic || !q.traces_fused) continue;
                 if (q.src_pop == i) {
-                    if (q.deferred) {
-                        a.snap_trace = a.n_traces;
-                        a.snap_buf = q.x_snap;
-                        a.snap_period = kSnapPeriod;
-                        a.snap_depth = kSnapDepth;
-                    }
                     a.trace[a.n_traces] = q.x_pre;
                     a.trace_decay[a.n_traces++] = static_cast<float>(std::exp(-dt / q.stdp[0]));
                 }
@@ -226,11 +268,11 @@ struct nrn_engine {
                     a.trace_decay[a.n_traces++] = static_cast<float>(std::exp(-dt / q.stdp[1]));
                 }
             }
-            if (p.post_recent) {
-                a.post_recent = p.post_recent;
-                a.post_ring = p.post_ring;
-                a.post_cnt = p.post_cnt;
-                a.post_ring_k = kPostRing;
+            if (p.recent) {
+                a.post_recent = p.recent + static_cast<int64_t>(p.lo) * 4;
+                a.post_ring = p.ring;
+                a.post_cnt = p.cnt;
+                a.post_ring_k = kRing;
             }
         }
         return a;
@@ -263,50 +305,92 @@ struct nrn_engine {
         return s;
     }
 
-    PlasticArgs plastic_args(const EngineProj& q) const {
-        PlasticArgs a;
+    WalkArgs walk_args(const EngineProj& q) const {
+        const EnginePop& ps = pops[q.src_pop];
+        const EnginePop& pt = pops[q.tgt_pop];
+        WalkArgs a;
         a.n_src = q.csr.n_src;
         a.nd = q.csr.nd;
         a.dmin = q.csr.dmin;
+        a.max_seg = q.csr.max_seg;
         a.seg_ptr = q.csr.seg_ptr;
         a.tgt = q.csr.tgt;
         a.w = q.csr.w;
         a.mod = q.csr.mod;
         a.acc = acc_of(q);
-        a.x_pre = q.x_pre;
-        a.x_post = q.x_post;
-        a.spike_src = pops[q.src_pop].d.spike;
-        a.spike_tgt = pops[q.tgt_pop].d.spike;
         a.hist_src = hist(q.src_pop);
+        a.seg_last = q.seg_last;
+        a.seg_x = q.seg_x;
+        a.seg_done = q.seg_done;
+        a.src_recent = reinterpret_cast<const int4*>(ps.recent);
+        a.src_ring = ps.ring;
+        a.src_cnt = ps.cnt;
+        a.src_lo = ps.lo;
+        a.src_hi = ps.lo + ps.d.n;
+        a.tgt_recent = reinterpret_cast<const int4*>(pt.recent + static_cast<int64_t>(pt.lo) * 4);
+        a.tgt_ring = pt.ring;
+        a.tgt_cnt = pt.cnt;
+        a.ring_k = kRing;
+        a.pre_snap = q.pre_snap;
+        a.pre_stride = q.csr.n_src;
+        a.pre_depth = q.pre_depth;
+        a.post_ring = q.post_ring;
+        a.post_depth = ring_depth;
+        a.n_tgt = q.csr.n_tgt;
+        a.win = win;
+        a.decay_pre = static_cast<float>(std::exp(-dt / q.stdp[0]));
+        a.decay_post = static_cast<float>(std::exp(-dt / q.stdp[1]));
         a.a_plus = static_cast<float>(q.stdp[2]);
         a.a_minus = static_cast<float>(std::fabs(q.stdp[3]));
         a.lr = static_cast<float>(q.stdp[6]);
         a.w_min = static_cast<float>(q.stdp[4]);
         a.w_max = static_cast<float>(q.stdp[5]);
-        a.decay_pre = static_cast<float>(std::exp(-dt / q.stdp[0]));
-        a.seg_last = q.seg_last;
-        a.seg_x = q.seg_x;
-        a.x_snap = q.x_snap;
-        a.snap_period = kSnapPeriod;
-        a.snap_depth = kSnapDepth;
-        const EnginePop& t = pops[q.tgt_pop];
-        a.post_recent = reinterpret_cast<const int4*>(t.post_recent);
-        a.post_ring = t.post_ring;
-        a.post_cnt = t.post_cnt;
-        a.post_ring_k = kPostRing;
         a.sweep_period = kSweepPeriod;
         a.sweep_rows = (q.csr.n_src + kSweepPeriod - 1) / kSweepPeriod;
+        a.stale = kStale;
         a.err = d_err;
         a.events = d_events;
         return a;
     }
 
-    // Walks every row of the deferred projections so that their weights are
-    // up to date through the last step run (before weights are read).
-    nrn_status_t flush_deferred() {
+    WindowArgs window_args(int i) const {
+        const EnginePop& p = pops[i];
+        WindowArgs a;
+        a.n = p.n_global;
+        a.mask = p.mask;
+        a.win = win;
+        a.err = d_err;
+        a.own_lo = p.lo;
+        a.own_hi = p.lo + p.d.n;
+        for (const auto& q : projs) {
+            if (!q.walk) continue;
+            if (q.src_pop == i && a.n_task < 4) {
+                SnapTask& t = a.task[a.n_task++];
+                t.snap = q.pre_snap;
+                t.stride = q.csr.n_src;
+                t.depth = q.pre_depth;
+                t.lo = 0;
+                t.hi = p.n_global;
+                t.decay = static_cast<float>(std::exp(-dt / q.stdp[0]));
+                a.recent = reinterpret_cast<int4*>(p.recent);
+                a.seg_last = q.seg_last;
+                a.seg_nd = q.csr.nd;
+            }
+        }
+        return a;
+    }
+
+    // Applies every pending update of the walk projections (weights are then
+    // those after the last step run).
+    nrn_status_t flush_walks() {
         if (step <= 0) return NRN_OK;
-        for (auto& q : projs)
-            if (q.deferred) NRN_TRY(plastic_rows(plastic_args(q), PLASTIC_FLUSH, step - 1, nullptr, stream));
+        for (auto& q : projs) {
+            if (!q.walk) continue;
+            if (world > 1 && step % win != 0)
+                return fail(NRN_ERR_STATE, "partitioned network: read plastic weights at a window boundary (step " +
+                                               std::to_string(step) + ", window " + std::to_string(win) + ")");
+            NRN_TRY(walk_launch(walk_args(q), WALK_FLUSH, step, nullptr, stream));
+        }
         return NRN_OK;
     }
 
@@ -314,23 +398,38 @@ struct nrn_engine {
         int h = 0;
         NRN_CUDA_TRY(cudaMemcpyAsync(&h, d_err, sizeof(int), cudaMemcpyDeviceToHost, stream));
         NRN_CUDA_TRY(cudaStreamSynchronize(stream));
-        if (h == 1) return fail(NRN_ERR_CAPACITY, "STDP: a target spiked more often than its spike history holds");
-        if (h == 2) return fail(NRN_ERR_STATE, "STDP: a row was not refreshed within the trace snapshot window");
+        if (h == 1) return fail(NRN_ERR_CAPACITY, "STDP: a neuron spiked more often than its spike history holds");
+        if (h == 2) return fail(NRN_ERR_STATE, "STDP: a segment was not walked within the trace snapshot window");
+        if (h == 3)
+            return fail(NRN_ERR_STATE,
+                        "STDP: a source on another GPU spiked twice within one synaptic delay; the partitioned "
+                        "engine needs inter-spike intervals of plastic sources longer than their delays");
+        if (h == 4)
+            return fail(NRN_ERR_CAPACITY, "spike exchange buffer overflowed: raise max_rate_hz of the partition");
         return NRN_OK;
     }
 
-    // Decides, per plastic projection, whether the neuron updates of its
-    // source and target advance its traces (both or neither: a projection
-    // that does not fit in the NRN_MAX_TRACES slots of both populations
-    // keeps the separate trace kernel).
-    void assign_trace_slots() {
+    // Decides how each plastic projection is updated: by segment walks
+    // (STDP at every step, at most 256 delays, one per source population),
+    // else by the per-step kernels with the traces advanced in the neuron
+    // updates where trace slots are free.
+    void assign_plasticity() {
+        std::vector<char> walk_src(pops.size(), 0);
         std::vector<int> used(pops.size(), 0);
         for (auto& q : projs) {
+            q.walk = false;
+            if (!q.plastic || slow_ratio != 1 || q.csr.nd > 256 || walk_src[q.src_pop] ||
+                used[q.tgt_pop] >= NRN_MAX_TRACES)
+                continue;
+            walk_src[q.src_pop] = 1;
+            used[q.tgt_pop] += 1;   // the target trace ring
+            q.walk = true;
+        }
+        for (auto& q : projs) {
             q.traces_fused = false;
-            if (!q.plastic) continue;
-            const int need_src = 1 + (q.src_pop == q.tgt_pop ? 1 : 0);
+            if (!q.plastic || q.walk) continue;
             if (q.src_pop == q.tgt_pop) {
-                if (used[q.src_pop] + need_src <= NRN_MAX_TRACES) {
+                if (used[q.src_pop] + 2 <= NRN_MAX_TRACES) {
                     used[q.src_pop] += 2;
                     q.traces_fused = true;
                 }
@@ -340,25 +439,43 @@ struct nrn_engine {
                 q.traces_fused = true;
             }
         }
-        // Deferred potentiation needs STDP on every step, fused traces and one
-        // snapshot slot per source population.
-        std::vector<char> snap_used(pops.size(), 0);
-        for (auto& q : projs) {
-            q.deferred = false;
-            if (!q.plastic || !q.traces_fused || slow_ratio != 1 || q.csr.nd > 256) continue;
-            if (snap_used[q.src_pop]) continue;
-            snap_used[q.src_pop] = 1;
-            q.deferred = true;
+    }
+
+    // Window end (after the last step's updates): spike exchange, then trace
+    // snapshots.
+    nrn_status_t enqueue_window_end(int64_t off) {
+        if (world > 1) {
+            ncclResult_t r = ncclAllGather(send, recv, static_cast<size_t>(rank_block), ncclInt32, comm, stream);
+            if (r != ncclSuccess) return fail(NRN_ERR_COMM, std::string("ncclAllGather: ") + ncclGetErrorString(r));
+            for (size_t i = 0; i < pops.size(); ++i) {
+                const EnginePop& p = pops[i];
+                UnpackArgs u;
+                u.recv = recv;
+                u.rank_stride = rank_block;
+                u.pop_off = p.send_off;
+                u.cap = p.send_cap;
+                u.world = world;
+                u.rank = rank;
+                u.win = win;
+                u.hist = hist(static_cast<int>(i));
+                u.mask = p.mask;
+                u.err = d_err;
+                NRN_TRY(unpack_launch(u, off, d_step, stream));
+            }
+            for (const auto& p : pops)
+                NRN_CUDA_TRY(cudaMemsetAsync(send + p.send_off, 0, static_cast<size_t>(win) * sizeof(int32_t), stream));
         }
+        for (size_t i = 0; i < pops.size(); ++i)
+            if (pops[i].mask) NRN_TRY(window_launch(window_args(static_cast<int>(i)), off, d_step, stream));
+        return NRN_OK;
     }
 
     // Enqueues one step at offset `off` from *d_step; with `ev` non-null,
     // records events around the three phases (ev[0..3]).
-    nrn_status_t enqueue_step(int64_t off, cudaEvent_t* ev = nullptr) {
+    nrn_status_t enqueue_step(int64_t off, bool win_end, cudaEvent_t* ev = nullptr) {
         std::vector<nrn_proj_t> dp;
-        std::vector<int> src_map;
         for (auto& q : projs)
-            if (!q.deferred) dp.push_back(dev_proj(q));
+            if (!q.walk) dp.push_back(dev_proj(q));
         std::vector<nrn_spike_hist_t> hs;
         for (size_t i = 0; i < pops.size(); ++i) hs.push_back(hist(static_cast<int>(i)));
         if (ev) NRN_CUDA_TRY(cudaEventRecord(ev[0], stream));
@@ -367,7 +484,7 @@ struct nrn_engine {
                                          reinterpret_cast<const int64_t*>(d_step), d_events,
                                          reinterpret_cast<nrn_stream_t>(stream)));
         for (auto& q : projs)
-            if (q.deferred) NRN_TRY(plastic_rows(plastic_args(q), PLASTIC_DELIVER, off, d_step, stream));
+            if (q.walk) NRN_TRY(walk_launch(walk_args(q), WALK_STEP, off, d_step, stream));
         if (ev) NRN_CUDA_TRY(cudaEventRecord(ev[1], stream));
         for (size_t i = 0; i < pops.size(); ++i) {
             nrn_pop_step_t a = pop_args(static_cast<int>(i), dt, off, true);
@@ -375,19 +492,17 @@ struct nrn_engine {
         }
         if (ev) NRN_CUDA_TRY(cudaEventRecord(ev[2], stream));
         for (auto& q : projs) {
-            if (!q.plastic) continue;
-            if (q.deferred) {
-                NRN_TRY(plastic_rows(plastic_args(q), PLASTIC_LTD, off, d_step, stream));
-                continue;
-            }
+            if (!q.plastic || q.walk) continue;
             nrn_stdp_t s = stdp_args(q);
             NRN_TRY(nrn_cuda_stdp_step(&s, off, reinterpret_cast<const int64_t*>(d_step),
                                         reinterpret_cast<nrn_stream_t>(stream)));
         }
+        if (win_end) NRN_TRY(enqueue_window_end(off));
         if (ev) NRN_CUDA_TRY(cudaEventRecord(ev[3], stream));
         return NRN_OK;
     }
 
+    // A graph of `chunk` steps starting at a window start (when windows are on).
     nrn_status_t graph_for(int chunk, cudaGraphExec_t* out) {
         auto it = graphs.find(chunk);
         if (it != graphs.end()) {
@@ -397,7 +512,7 @@ struct nrn_engine {
         cudaGraph_t g = nullptr;
         NRN_CUDA_TRY(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
         nrn_status_t st = NRN_OK;
-        for (int k = 0; k < chunk && st == NRN_OK; ++k) st = enqueue_step(k);
+        for (int k = 0; k < chunk && st == NRN_OK; ++k) st = enqueue_step(k, window_end(k));
         if (st == NRN_OK) {
             advance_kernel<<<1, 1, 0, stream>>>(d_step, chunk);
             if (cudaGetLastError() != cudaSuccess) st = fail(NRN_ERR_CUDA, "advance_kernel launch failed");
@@ -414,6 +529,35 @@ struct nrn_engine {
         if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
         graphs[chunk] = ex;
         *out = ex;
+        return NRN_OK;
+    }
+
+    // One step launched directly (absolute step `abs`, = *d_step).
+    nrn_status_t eager_step(int64_t abs) {
+        NRN_TRY(enqueue_step(0, window_end(abs)));
+        advance_kernel<<<1, 1, 0, stream>>>(d_step, 1);
+        NRN_CUDA_TRY(cudaGetLastError());
+        return NRN_OK;
+    }
+
+    // First run: weights clamped, walk state starting at the current step.
+    nrn_status_t prepare_plastic() {
+        for (auto& q : projs) {
+            if (!q.plastic || q.clamped) continue;
+            // The reference clamps every weight of a plastic connection on
+            // each update (stdp.cpp:139); one clamp of all weights before the
+            // first update, then of each changed weight, is the same.
+            NRN_TRY(nrn_cuda_clamp(q.csr.w, q.csr.nnz, static_cast<float>(q.stdp[4]), static_cast<float>(q.stdp[5]),
+                                   reinterpret_cast<nrn_stream_t>(stream)));
+            if (q.walk) {
+                const std::vector<int32_t> last(static_cast<size_t>(q.csr.n_src) * q.csr.nd,
+                                                static_cast<int32_t>(step - 1));
+                NRN_CUDA_TRY(cudaMemcpyAsync(q.seg_last, last.data(), last.size() * sizeof(int32_t),
+                                             cudaMemcpyHostToDevice, stream));
+                NRN_CUDA_TRY(cudaStreamSynchronize(stream));
+            }
+            q.clamped = true;
+        }
         return NRN_OK;
     }
 
@@ -486,6 +630,8 @@ nrn_status_t nrn_engine_create(nrn_engine** out, int device, double dt, int32_t 
     e->device = device;
     e->dt = dt;
     e->slow_ratio = slow_ratio;
+    const char* ng = std::getenv("NRN_NO_GRAPHS");
+    e->use_graphs = !(ng && ng[0] == '1');
     NRN_CUDA_TRY(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
     NRN_TRY(dalloc0(&e->d_step, 1, e->stream));
     NRN_TRY(dalloc0(&e->d_events, 1, e->stream));
@@ -500,6 +646,40 @@ nrn_status_t nrn_engine_destroy(nrn_engine* e) {
     cudaSetDevice(e->device);
     cudaStreamSynchronize(e->stream);
     delete e;
+    return NRN_OK;
+}
+
+nrn_status_t nrn_comm_unique_id(uint8_t id[128]) {
+    NRN_CHECK_ARG(id != nullptr, "nrn_comm_unique_id: null output");
+    static_assert(sizeof(ncclUniqueId) == 128, "NCCL unique id size");
+    ncclUniqueId u;
+    ncclResult_t r = ncclGetUniqueId(&u);
+    if (r != ncclSuccess) return fail(NRN_ERR_COMM, std::string("ncclGetUniqueId: ") + ncclGetErrorString(r));
+    std::memcpy(id, &u, sizeof(u));
+    return NRN_OK;
+}
+
+nrn_status_t nrn_engine_set_partition(nrn_engine* e, int32_t rank, int32_t world, const uint8_t id[128],
+                                      double max_rate_hz) {
+    ENGINE_GUARD(e);
+    NRN_CHECK_ARG(e->pops.empty() && !e->finalized, "nrn_engine_set_partition: call before adding populations");
+    NRN_CHECK_ARG(world >= 1 && rank >= 0 && rank < world, "nrn_engine_set_partition: bad rank or world size");
+    NRN_CHECK_ARG(max_rate_hz > 0.0, "nrn_engine_set_partition: max_rate_hz must be positive");
+    NRN_CHECK_ARG(e->comm == nullptr, "nrn_engine_set_partition: already partitioned");
+    e->max_rate_hz = max_rate_hz;
+    e->rank = rank;
+    e->world = world;
+    if (world == 1) return NRN_OK;
+    NRN_CHECK_ARG(id != nullptr, "nrn_engine_set_partition: null NCCL id");
+    ncclUniqueId u;
+    std::memcpy(&u, id, sizeof(u));
+    ncclResult_t r = ncclCommInitRank(&e->comm, world, u, rank);
+    if (r != ncclSuccess) {
+        e->comm = nullptr;
+        e->world = 1;
+        e->rank = 0;
+        return fail(NRN_ERR_COMM, std::string("ncclCommInitRank: ") + ncclGetErrorString(r));
+    }
     return NRN_OK;
 }
 
@@ -524,6 +704,11 @@ nrn_status_t nrn_engine_add_population(nrn_engine* e, const nrn_pop_desc_t* d, i
     NRN_CHECK_ARG(d->model == NRN_MODEL_IZH || d->refractory, "population needs refractory");
     EnginePop p;
     p.d = *d;
+    p.n_global = d->n_global > 0 ? d->n_global : d->n;
+    p.lo = d->local_offset;
+    NRN_CHECK_ARG(p.lo >= 0 && p.lo + d->n <= p.n_global, "population slice outside the population");
+    NRN_CHECK_ARG(e->world > 1 || (p.lo == 0 && p.n_global == d->n),
+                  "a population slice (n_global, local_offset) needs nrn_engine_set_partition");
     p.cond = d->tau_syn_exc > 0.0f;
     NRN_CHECK_ARG(!p.cond || d->model == NRN_MODEL_ADEX, "conductance input is supported for AdEx");
     NRN_CHECK_ARG(d->drive.kind != NRN_DRIVE_POISSON_GEXC || p.cond, "conductance drive needs conductance input");
@@ -568,7 +753,7 @@ static nrn_status_t add_projection_dev(nrn_engine* e, int32_t src_pop, int32_t t
     q.receptor = receptor;
     q.csr.dmin = dmin;
     q.csr.nd = dmax - dmin + 1;
-    NRN_TRY(build_csr(q.csr, e->pops[src_pop].d.n, e->pops[tgt_pop].d.n, src, tgt, w, delay, mod, n, keep_orig,
+    NRN_TRY(build_csr(q.csr, e->pops[src_pop].n_global, e->pops[tgt_pop].d.n, src, tgt, w, delay, mod, n, keep_orig,
                       e->stream));
     e->projs.push_back(q);
     e->drop_graphs();
@@ -644,20 +829,22 @@ nrn_status_t nrn_engine_generate_projection(nrn_engine* e, const nrn_gen_desc_t*
     NRN_CHECK_ARG(g->degree >= 0 && g->dmin >= 1 && g->dmax >= g->dmin && g->dmax <= 255, "bad generator range");
     NRN_CHECK_ARG(g->receptor == NRN_RECV_CURRENT || e->pops[g->tgt_pop].cond,
                   "conductance receptor on a population without conductance input");
-    const auto& ps = e->pops[g->src_pop].d;
-    const auto& pt = e->pops[g->tgt_pop].d;
+    const EnginePop& ps = e->pops[g->src_pop];
+    const EnginePop& pt = e->pops[g->tgt_pop];
+    // sources over the whole population, targets on this rank
+    const int32_t src_gid = ps.d.gid_offset, tgt_gid = pt.d.gid_offset;
     GenArgs a{};
     a.out_degree = g->out_degree;
     a.degree = g->degree;
     a.gen_id = static_cast<uint32_t>(g->gen_id);
-    a.n_src = ps.n;
-    a.src_offset = ps.gid_offset;
-    a.col_offset = g->col_n > 0 ? g->col_offset : (g->out_degree ? pt.gid_offset : ps.gid_offset);
-    a.col_n = g->col_n > 0 ? g->col_n : (g->out_degree ? pt.n : ps.n);
-    a.row_offset = g->out_degree ? ps.gid_offset : pt.gid_offset;
-    a.n_rows = g->out_degree ? ps.n : pt.n;
-    a.keep_lo = pt.gid_offset;
-    a.keep_hi = pt.gid_offset + pt.n;
+    a.n_src = ps.n_global;
+    a.src_offset = src_gid;
+    a.col_offset = g->col_n > 0 ? g->col_offset : (g->out_degree ? tgt_gid : src_gid);
+    a.col_n = g->col_n > 0 ? g->col_n : (g->out_degree ? pt.n_global : ps.n_global);
+    a.row_offset = g->out_degree ? src_gid : tgt_gid + pt.lo;
+    a.n_rows = g->out_degree ? ps.n_global : pt.d.n;
+    a.keep_lo = tgt_gid + pt.lo;
+    a.keep_hi = tgt_gid + pt.lo + pt.d.n;
     a.dmin = g->dmin;
     a.dmax = g->dmax;
     a.w_lo = g->w_lo;
@@ -701,12 +888,52 @@ nrn_status_t nrn_engine_set_stdp(nrn_engine* e, int32_t proj, const double* p) {
 nrn_status_t nrn_engine_finalize(nrn_engine* e, int32_t init_update) {
     ENGINE_GUARD(e);
     NRN_CHECK_ARG(!e->finalized, "engine already finalized");
-    int maxd = 1;
-    for (auto& q : e->projs) maxd = std::max(maxd, q.csr.dmin + q.csr.nd - 1);
-    e->depth = maxd + 1;
+    int maxd = 1, mind = 255;
+    for (auto& q : e->projs) {
+        maxd = std::max(maxd, q.csr.dmin + q.csr.nd - 1);
+        mind = std::min(mind, q.csr.dmin);
+    }
+    if (e->projs.empty()) mind = 1;
+    for (auto& q : e->projs)
+        if (q.plastic) NRN_TRY(build_transpose(q.csr, e->stream));
+    e->assign_plasticity();
+    bool any_walk = false;
+    for (auto& q : e->projs) {
+        if (q.plastic && !q.walk && e->world > 1)
+            return fail(NRN_ERR_UNSUPPORTED,
+                        "partitioned network: plasticity needs STDP at every step (slow_ratio 1), at most 256 delays "
+                        "and one plastic projection per source population");
+        any_walk = any_walk || q.walk;
+    }
+    // Windows: spikes cross GPUs once per window, and STDP traces are kept at
+    // window ends.  A window is at most the smallest delay, so every spike
+    // arrives in a later window than the one it was emitted in.
+    e->windows = e->world > 1 || any_walk;
+    e->win = std::max(1, std::min(mind, 32));
+    e->depth = maxd + 1 + (e->world > 1 ? e->win : 0);
     for (auto& p : e->pops) {
-        NRN_TRY(dalloc0(&p.hist_ids, static_cast<size_t>(e->depth) * p.d.n, e->stream));
+        // ring capacity per step: every neuron (one rank), or what all ranks can send
+        if (e->world > 1) {
+            const double per_window = std::ceil(static_cast<double>(p.d.n) * e->win * e->max_rate_hz * e->dt);
+            p.send_cap = static_cast<int32_t>(std::min<double>(static_cast<double>(p.d.n) * e->win,
+                                                               std::max(4096.0, per_window)));
+            p.hist_cap = static_cast<int32_t>(std::min<int64_t>(p.n_global,
+                                                                static_cast<int64_t>(p.send_cap) * e->world));
+        } else {
+            p.hist_cap = p.d.n;
+        }
+        NRN_TRY(dalloc0(&p.hist_ids, static_cast<size_t>(e->depth) * p.hist_cap, e->stream));
         NRN_TRY(dalloc0(&p.hist_count, static_cast<size_t>(e->depth), e->stream));
+    }
+    if (e->world > 1) {
+        e->rank_block = 0;
+        for (auto& p : e->pops) {
+            p.send_off = e->rank_block;
+            e->rank_block += e->win + p.send_cap;
+            e->rank_block = (e->rank_block + 3) / 4 * 4;   // 16-byte aligned blocks
+        }
+        NRN_TRY(dalloc0(&e->send, static_cast<size_t>(e->rank_block), e->stream));
+        NRN_TRY(dalloc0(&e->recv, static_cast<size_t>(e->rank_block) * e->world, e->stream));
     }
     int64_t rec_n = 0;
     for (auto& p : e->pops)
@@ -717,26 +944,38 @@ nrn_status_t nrn_engine_finalize(nrn_engine* e, int32_t init_update) {
         NRN_TRY(dalloc0(&e->raster_gid, e->raster_cap, e->stream));
     }
     for (auto& q : e->projs) {
-        if (!q.plastic) continue;
-        NRN_TRY(build_transpose(q.csr, e->stream));
+        if (!q.plastic || q.walk) continue;
         NRN_TRY(dalloc0(&q.x_pre, e->pops[q.src_pop].d.n, e->stream));
         NRN_TRY(dalloc0(&q.x_post, e->pops[q.tgt_pop].d.n, e->stream));
     }
-    e->assign_trace_slots();
+    // Walk state.  A segment's T lags the current step by at most about
+    // kSweepPeriod + kStale + the window and the delays (the sweep), and a
+    // source spike being applied is at most the longest delay old: the
+    // snapshot rings are sized for that.
+    auto need_history = [&](EnginePop& p) -> nrn_status_t {
+        if (p.mask) return NRN_OK;
+        NRN_TRY(dalloc0(&p.mask, static_cast<size_t>(p.n_global), e->stream));
+        NRN_TRY(dalloc0(&p.recent, static_cast<size_t>(p.n_global) * 4, e->stream));
+        NRN_CUDA_TRY(cudaMemsetAsync(p.recent, 0xFF, static_cast<size_t>(p.n_global) * 16, e->stream));   // -1: none
+        NRN_TRY(dalloc0(&p.ring, static_cast<size_t>(p.d.n) * kRing, e->stream));
+        NRN_TRY(dalloc0(&p.cnt, static_cast<size_t>(p.d.n), e->stream));
+        return NRN_OK;
+    };
+    // target traces: a source spike being applied is at most the longest
+    // delay (+1) older than the walk
+    e->ring_depth = maxd + 2;
     for (auto& q : e->projs) {
-        if (!q.deferred) continue;
+        if (!q.walk) continue;
         const size_t nseg = static_cast<size_t>(q.csr.n_src) * q.csr.nd;
         NRN_TRY(dalloc0(&q.seg_last, nseg, e->stream));
-        NRN_CUDA_TRY(cudaMemsetAsync(q.seg_last, 0xFF, nseg * sizeof(int32_t), e->stream));   // -1: nothing applied
         NRN_TRY(dalloc0(&q.seg_x, nseg, e->stream));
-        NRN_TRY(dalloc0(&q.x_snap, static_cast<size_t>(kSnapDepth) * q.csr.n_src, e->stream));
-        auto& t = e->pops[q.tgt_pop];
-        if (!t.post_recent) {
-            NRN_TRY(dalloc0(&t.post_recent, static_cast<size_t>(t.d.n) * 4, e->stream));
-            NRN_CUDA_TRY(cudaMemsetAsync(t.post_recent, 0xFF, static_cast<size_t>(t.d.n) * 16, e->stream));
-            NRN_TRY(dalloc0(&t.post_ring, static_cast<size_t>(t.d.n) * kPostRing, e->stream));
-            NRN_TRY(dalloc0(&t.post_cnt, static_cast<size_t>(t.d.n), e->stream));
-        }
+        NRN_TRY(dalloc0(&q.seg_done, nseg, e->stream));
+        const int dmax = q.csr.dmin + q.csr.nd - 1;
+        q.pre_depth = (kSweepPeriod + kStale + e->win + dmax) / e->win + 4;
+        NRN_TRY(dalloc0(&q.pre_snap, static_cast<size_t>(q.pre_depth) * q.csr.n_src, e->stream));
+        NRN_TRY(dalloc0(&q.post_ring, static_cast<size_t>(e->ring_depth) * q.csr.n_tgt, e->stream));
+        NRN_TRY(need_history(e->pops[q.src_pop]));
+        NRN_TRY(need_history(e->pops[q.tgt_pop]));
     }
     if (init_update) {
         for (size_t i = 0; i < e->pops.size(); ++i) {
@@ -754,25 +993,27 @@ nrn_status_t nrn_engine_run(nrn_engine* e, int64_t steps, int32_t chunk) {
     NRN_CHECK_ARG(e->finalized, "nrn_engine_run: finalize first");
     NRN_CHECK_ARG(steps >= 0, "negative step count");
     if (steps == 0) return NRN_OK;
-    // The reference clamps every weight of a plastic connection on each
-    // update (stdp.cpp:139); one clamp of all weights before the first
-    // update, then of each changed weight, is the same.
-    for (auto& q : e->projs) {
-        if (q.plastic && !q.clamped) {
-            NRN_TRY(nrn_cuda_clamp(q.csr.w, q.csr.nnz, static_cast<float>(q.stdp[4]), static_cast<float>(q.stdp[5]),
-                                   reinterpret_cast<nrn_stream_t>(e->stream)));
-            q.clamped = true;
-        }
-    }
-    if (chunk <= 0) chunk = static_cast<int32_t>(std::min<int64_t>(steps, 50));
-    int64_t done = 0;
-    while (done < steps) {
-        const int c = static_cast<int>(std::min<int64_t>(chunk, steps - done));
+    NRN_TRY(e->prepare_plastic());
+    if (chunk <= 0) chunk = 50;
+    int64_t s = e->step, left = steps;
+    auto graph_run = [&](int c) -> nrn_status_t {
         cudaGraphExec_t g = nullptr;
         NRN_TRY(e->graph_for(c, &g));
         NRN_CUDA_TRY(cudaGraphLaunch(g, e->stream));
-        done += c;
+        s += c;
+        left -= c;
+        return NRN_OK;
+    };
+    if (e->use_graphs && e->windows) {
+        // graphs hold whole windows and start at a window start
+        chunk = std::max(e->win, chunk / e->win * e->win);
+        for (; left > 0 && s % e->win != 0; ++s, --left) NRN_TRY(e->eager_step(s));
+        while (left >= e->win)
+            NRN_TRY(graph_run(static_cast<int>(std::min<int64_t>(chunk, left / e->win * e->win))));
+    } else if (e->use_graphs) {
+        while (left > 0) NRN_TRY(graph_run(static_cast<int>(std::min<int64_t>(chunk, left))));
     }
+    for (; left > 0; ++s, --left) NRN_TRY(e->eager_step(s));
     e->step += steps;
     return NRN_OK;
 }
@@ -783,18 +1024,12 @@ nrn_status_t nrn_engine_profile(nrn_engine* e, int64_t steps, double* ms) {
     NRN_CHECK_ARG(steps >= 0 && ms != nullptr, "bad arguments");
     ms[0] = ms[1] = ms[2] = 0.0;
     if (steps == 0) return NRN_OK;
-    for (auto& q : e->projs) {
-        if (q.plastic && !q.clamped) {
-            NRN_TRY(nrn_cuda_clamp(q.csr.w, q.csr.nnz, static_cast<float>(q.stdp[4]), static_cast<float>(q.stdp[5]),
-                                   reinterpret_cast<nrn_stream_t>(e->stream)));
-            q.clamped = true;
-        }
-    }
+    NRN_TRY(e->prepare_plastic());
     cudaEvent_t ev[4];
     for (auto& x : ev) NRN_CUDA_TRY(cudaEventCreate(&x));
     nrn_status_t st = NRN_OK;
     for (int64_t k = 0; k < steps && st == NRN_OK; ++k) {
-        st = e->enqueue_step(0, ev);
+        st = e->enqueue_step(0, e->window_end(e->step + k), ev);
         if (st != NRN_OK) break;
         advance_kernel<<<1, 1, 0, e->stream>>>(e->d_step, 1);
         cudaError_t ce = cudaEventSynchronize(ev[3]);
@@ -863,7 +1098,7 @@ nrn_status_t nrn_engine_weights(nrn_engine* e, int32_t proj, float* out, int64_t
     NRN_CHECK_ARG(proj >= 0 && proj < static_cast<int32_t>(e->projs.size()), "bad projection index");
     const auto& c = e->projs[proj].csr;
     NRN_CHECK_ARG(n == c.nnz && out != nullptr, "weights: output size must equal the synapse count");
-    NRN_TRY(e->flush_deferred());
+    NRN_TRY(e->flush_walks());
     NRN_TRY(e->check_err());
     std::vector<float> w(static_cast<size_t>(c.nnz));
     NRN_CUDA_TRY(cudaStreamSynchronize(e->stream));
@@ -884,7 +1119,7 @@ nrn_status_t nrn_engine_weights_device(nrn_engine* e, int32_t proj, float* out, 
     const auto& c = e->projs[proj].csr;
     NRN_CHECK_ARG(n == c.nnz && (n == 0 || out != nullptr), "weights: output size must equal the synapse count");
     if (n == 0) return NRN_OK;
-    NRN_TRY(e->flush_deferred());
+    NRN_TRY(e->flush_walks());
     NRN_TRY(e->check_err());
     if (c.orig) {
         // out[orig[k]] = w[k]

@@ -55,36 +55,88 @@ nrn_status_t generate(const GenArgs& g, int32_t* src, int32_t* tgt, float* w, ui
 
 int sm_count_current();
 
-// Deferred-potentiation STDP (plastic.cu).
-enum { PLASTIC_DELIVER = 0, PLASTIC_LTD = 1, PLASTIC_FLUSH = 2 };
-struct PlasticArgs {
-    int32_t n_src = 0, nd = 1, dmin = 1;
+// Pair STDP applied by segment walks (plastic.cu).  Steps are int32.
+enum { WALK_STEP = 0, WALK_FLUSH = 1 };
+struct WalkArgs {
+    int32_t n_src = 0, nd = 1, dmin = 1, max_seg = 0;
     const int64_t* seg_ptr = nullptr;
     const uint32_t* tgt = nullptr;
     float* w = nullptr;
     const float* mod = nullptr;
     float* acc = nullptr;
-    const float* x_pre = nullptr;
-    const float* x_post = nullptr;
-    const float* spike_src = nullptr;
-    const float* spike_tgt = nullptr;
-    nrn_spike_hist_t hist_src{};
-    float a_plus = 0, a_minus = 0, lr = 0, w_min = 0, w_max = 0, decay_pre = 1;
-    int32_t* seg_last = nullptr;      // [n_src*nd] weights applied through this step
+    nrn_spike_hist_t hist_src{};      // spike history of the (whole) source population
+    int32_t* seg_last = nullptr;      // [n_src*nd] events applied through this step
     float* seg_x = nullptr;           // [n_src*nd] x_pre at that step
-    const float* x_snap = nullptr;    // [snap_depth][n_src]
-    int32_t snap_period = 16, snap_depth = 64;
-    const int4* post_recent = nullptr;
-    const int32_t* post_ring = nullptr;
-    const int32_t* post_cnt = nullptr;
-    int32_t post_ring_k = 64;
-    int64_t sweep_rows = 0;           // rows refreshed per step by the sweep
-    int64_t sweep_period = 1;         // steps for the sweep to cover every row
+    int32_t* seg_done = nullptr;      // [n_src*nd] chunk counter of the walk in flight
+    // spike steps of the sources (index in the source population): newest
+    // four in src_recent; older ones in src_ring/src_cnt for [src_lo, src_hi)
+    const int4* src_recent = nullptr;
+    const int32_t* src_ring = nullptr;
+    const int32_t* src_cnt = nullptr;
+    int32_t src_lo = 0, src_hi = 0;
+    // spike steps of the targets (local index)
+    const int4* tgt_recent = nullptr;
+    const int32_t* tgt_ring = nullptr;
+    const int32_t* tgt_cnt = nullptr;
+    int32_t ring_k = 64;
+    // source trace at window ends: x(m*win - 1) in row m % pre_depth
+    const float* pre_snap = nullptr;
+    int64_t pre_stride = 0;
+    int32_t pre_depth = 1;
+    // target trace at every step: x(t) in row t % post_depth ([depth][n_tgt])
+    const float* post_ring = nullptr;
+    int32_t post_depth = 1;
+    int32_t n_tgt = 0;
+    int32_t win = 1;
+    float decay_pre = 1, decay_post = 1, a_plus = 0, a_minus = 0, lr = 0, w_min = 0, w_max = 0;
+    int64_t sweep_rows = 0;           // rows looked at per step by the sweep
+    int32_t sweep_period = 1;         // steps for the sweep to pass every row
+    int32_t stale = 1;                // the sweep walks a segment not walked for this many steps
     int* err = nullptr;
     unsigned long long* events = nullptr;
 };
-nrn_status_t plastic_rows(const PlasticArgs& a, int mode, long long step_off, const long long* step_base,
-                          cudaStream_t s);
+nrn_status_t walk_launch(const WalkArgs& a, int mode, long long step_off, const long long* step_base,
+                         cudaStream_t s);
+
+// Window-end bookkeeping of one population (exchange.cu): trace snapshots
+// from the window's spike masks, spike steps of the sources other ranks
+// own, mask reset.
+struct SnapTask {
+    float* snap = nullptr;            // row m % depth holds x(m*win - 1)
+    int64_t stride = 0;
+    int32_t depth = 1;
+    int32_t lo = 0, hi = 0;           // population indices covered (snap column = j - lo)
+    float decay = 1;
+};
+struct WindowArgs {
+    int32_t n = 0;                    // population size (all ranks)
+    uint32_t* mask = nullptr;         // [n] bit u: spiked at window step u
+    SnapTask task[4];
+    int32_t n_task = 0;
+    int4* recent = nullptr;           // [n] or null; updated outside [own_lo, own_hi)
+    int32_t own_lo = 0, own_hi = 0;
+    const int32_t* seg_last = nullptr;   // segments of a walk projection from this population
+    int32_t seg_nd = 0;
+    int32_t win = 1;
+    int* err = nullptr;
+};
+nrn_status_t window_launch(const WindowArgs& a, long long step_off, const long long* step_base, cudaStream_t s);
+
+// Spike exchange: unpacks the gathered per-rank window buffers of one
+// population into its spike history ring (and the masks of the spikes of
+// other ranks).
+struct UnpackArgs {
+    const int32_t* recv = nullptr;    // rank r's block at recv + r * rank_stride
+    int64_t rank_stride = 0;
+    int64_t pop_off = 0;              // this population's block offset inside a rank block
+    int32_t cap = 0;                  // id capacity of a block (after win counts)
+    int32_t world = 1, rank = 0;
+    int32_t win = 1;
+    nrn_spike_hist_t hist{};
+    uint32_t* mask = nullptr;         // or null
+    int* err = nullptr;
+};
+nrn_status_t unpack_launch(const UnpackArgs& a, long long step_off, const long long* step_base, cudaStream_t s);
 
 // The engine's spike raster buffers (for entry points outside engine.cu).
 struct EngineRasterView {

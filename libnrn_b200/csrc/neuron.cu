@@ -58,14 +58,19 @@ struct PopArgs {
     int trace_slow_ratio;
     float* trace[NRN_MAX_TRACES];
     float trace_decay[NRN_MAX_TRACES];
+    float* trace_ring[NRN_MAX_TRACES];
+    int trace_ring_depth;
     int4* post_recent;
     int* post_ring;
     int* post_cnt;
     int post_ring_k;
-    int snap_trace;
-    int snap_period;
-    int snap_depth;
-    float* snap_buf;
+    int id_offset;
+    int win;
+    uint32_t* win_mask;
+    int* send_hdr;
+    int* send_ids;
+    int send_cap;
+    int* err;
 };
 
 template <bool HET>
@@ -179,10 +184,13 @@ __global__ void __launch_bounds__(256) pop_step_kernel(const __grid_constant__ P
             // pair-STDP traces (src/plasticity/stdp.cpp:118-128): decay, then + spike
             const float sp = spiked ? 1.0f : 0.0f;
             for (int k = 0; k < a.n_traces; ++k) {
-                const float x = a.trace[k][i] * a.trace_decay[k] + sp;
-                a.trace[k][i] = x;
-                if (k == a.snap_trace && (step + 1) % a.snap_period == 0)
-                    a.snap_buf[(((step + 1) / a.snap_period) % a.snap_depth) * static_cast<long long>(a.n) + i] = x;
+                if (a.trace_ring[k] != nullptr) {
+                    const long long D = a.trace_ring_depth;
+                    const float prev = a.trace_ring[k][((step + D - 1) % D) * a.n + i];
+                    a.trace_ring[k][(step % D) * a.n + i] = prev * a.trace_decay[k] + sp;
+                } else {
+                    a.trace[k][i] = a.trace[k][i] * a.trace_decay[k] + sp;
+                }
             }
         }
         if (spiked && a.post_recent != nullptr) {
@@ -193,6 +201,7 @@ __global__ void __launch_bounds__(256) pop_step_kernel(const __grid_constant__ P
             a.post_ring[static_cast<long long>(i) * a.post_ring_k + (c % a.post_ring_k)] = t;
             a.post_cnt[i] = c + 1;
         }
+        if (spiked && a.win_mask != nullptr) a.win_mask[i] |= 1u << static_cast<int>(step % a.win);
         if (a.i_syn) a.i_syn[i] = 0.0f;
         if (COND) {
             a.gin_exc[i] = 0.0f;
@@ -200,14 +209,28 @@ __global__ void __launch_bounds__(256) pop_step_kernel(const __grid_constant__ P
         }
     }
     // Warp-ballot compaction: ascending ids within a warp, one atomic per warp.
-    if (a.spike_ids != nullptr || a.raster_gid != nullptr) {
+    if (a.spike_ids != nullptr || a.send_hdr != nullptr || a.raster_gid != nullptr) {
         const unsigned mask = __ballot_sync(0xffffffffu, spiked);
         if (mask) {
             const int lane = threadIdx.x & 31;
             const int leader = __ffs(mask) - 1;
             const int cnt = __popc(mask);
             const int rank = __popc(mask & ((1u << lane) - 1u));
-            if (a.spike_ids) {
+            if (a.send_hdr) {
+                // window send buffer: ids of window step u follow those of steps 0..u-1
+                const int u = static_cast<int>(step % a.win);
+                int base = 0;
+                if (lane == leader) {
+                    int before = 0;
+                    for (int q = 0; q < u; ++q) before += __ldcg(a.send_hdr + q);
+                    base = before + atomicAdd(a.send_hdr + u, cnt);
+                }
+                base = __shfl_sync(0xffffffffu, base, leader);
+                if (spiked) {
+                    if (base + rank < a.send_cap) a.send_ids[base + rank] = a.id_offset + i;
+                    else if (a.err) atomicCAS(a.err, 0, 4);
+                }
+            } else if (a.spike_ids) {
                 int* ids = a.spike_ids;
                 int* count = a.spike_count;
                 if (a.hist_depth > 0) {
@@ -218,7 +241,7 @@ __global__ void __launch_bounds__(256) pop_step_kernel(const __grid_constant__ P
                 int base = 0;
                 if (lane == leader) base = atomicAdd(count, cnt);
                 base = __shfl_sync(0xffffffffu, base, leader);
-                if (spiked) ids[base + rank] = i;
+                if (spiked) ids[base + rank] = a.id_offset + i;
             }
             if (a.raster_gid) {
                 unsigned long long rb = 0;
@@ -314,9 +337,12 @@ extern "C" nrn_status_t nrn_cuda_pop_step(const nrn_pop_step_t* in, nrn_stream_t
     NRN_CHECK_ARG(d.n_traces >= 0 && d.n_traces <= NRN_MAX_TRACES, "nrn_cuda_pop_step: too many traces");
     a.n_traces = d.n_traces;
     a.trace_slow_ratio = d.trace_slow_ratio;
+    a.trace_ring_depth = d.trace_ring_depth;
     for (int k = 0; k < d.n_traces; ++k) {
-        NRN_CHECK_ARG(d.trace[k] != nullptr, "nrn_cuda_pop_step: null trace array");
+        NRN_CHECK_ARG(d.trace[k] != nullptr || (d.trace_ring[k] != nullptr && d.trace_ring_depth > 0),
+                      "nrn_cuda_pop_step: null trace array");
         a.trace[k] = d.trace[k];
+        a.trace_ring[k] = d.trace_ring[k];
         a.trace_decay[k] = d.trace_decay[k];
     }
     a.post_recent = reinterpret_cast<int4*>(d.post_recent);
@@ -327,12 +353,16 @@ extern "C" nrn_status_t nrn_cuda_pop_step(const nrn_pop_step_t* in, nrn_stream_t
                   "nrn_cuda_pop_step: spike history needs ring, count and depth");
     NRN_CHECK_ARG(d.post_recent == nullptr || (reinterpret_cast<uintptr_t>(d.post_recent) % 16) == 0,
                   "nrn_cuda_pop_step: post_recent must be 16-byte aligned");
-    a.snap_trace = d.snap_buf ? d.snap_trace : -1;
-    a.snap_period = d.snap_period > 0 ? d.snap_period : 1;
-    a.snap_depth = d.snap_depth > 0 ? d.snap_depth : 1;
-    a.snap_buf = d.snap_buf;
-    NRN_CHECK_ARG(d.snap_buf == nullptr || (d.snap_trace >= 0 && d.snap_trace < d.n_traces),
-                  "nrn_cuda_pop_step: snapshot of a trace slot that does not exist");
+    a.id_offset = d.id_offset;
+    a.win = d.win > 0 ? d.win : 1;
+    NRN_CHECK_ARG(a.win <= 32, "nrn_cuda_pop_step: windows are at most 32 steps");
+    a.win_mask = d.win > 0 ? d.win_mask : nullptr;
+    a.send_hdr = d.win > 0 ? d.send_hdr : nullptr;
+    a.send_ids = d.send_ids;
+    a.send_cap = d.send_cap;
+    a.err = d.err;
+    NRN_CHECK_ARG(a.send_hdr == nullptr || (d.send_ids != nullptr && d.send_cap >= 0),
+                  "nrn_cuda_pop_step: send buffer without ids");
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     switch (d.model) {
         case NRN_MODEL_LIF: launch_model<NRN_MODEL_LIF>(a, het, false, s); break;

@@ -1,35 +1,41 @@
-// plastic.cu -- pair STDP with the potentiation deferred to row passes.
+// plastic.cu -- pair STDP applied by walks over (source, delay) segments.
 //
-// The reference's rule (src/plasticity/stdp.cpp:43-141), applied every step
-// (slow_ratio 1), changes a weight when its source spikes (-A- x_post, plus
-// +A+ x_pre if the target spiked in the same step) or when its target spikes
-// (+A+ x_pre).  Applying the target-spike term immediately means one random
-// read-modify-write per synapse of every spiking target, the slowest memory
-// operation a GPU has.  Here that term is deferred: each (source, delay)
-// segment of the source-major CSR records the step T through which its
-// weights are up to date, and whenever the segment is walked -- at delivery
-// of one of its source's spikes, at the source's own spike, or by a rolling
-// sweep that reaches every row once per ~1000 steps -- the potentiations of
-// every target spike in (T, now] are replayed first, oldest first, with the
-// same float operations in the same order as the immediate update.  The
-// weights are therefore the same, bit for bit, as applying the rule every
-// step, but every weight access is a contiguous row access.
+// The reference's rule (src/plasticity/stdp.cpp:43-141), applied at every
+// step (slow_ratio 1), changes a weight at each step where its source or its
+// target spiked:
+//     dw = (A+ x_pre) * post - (A- x_post) * pre,   w <- clamp(w + dw*lr*mod)
+// with x_pre, x_post the traces after this step's decay and increment.  A
+// synapse's weight is read only when one of its source's spikes is
+// delivered through it, so its updates need not be applied when they
+// happen: each (source, delay) segment of the source-major CSR records the
+// step T through which its weights are up to date, and a walk of the
+// segment applies, synapse by synapse and in time order, the updates of
+// every source or target spike in (T, end] -- the same float operations in
+// the same order as updating at every step, hence the same weights bit for
+// bit.  Walks happen
+//   * when a spike arrives through the segment (end = the previous step),
+//     followed by the delivery of the updated weight: one contiguous pass
+//     over the segment per delivered spike, no random read-modify-write;
+//   * in a rolling sweep that looks at every row once per sweep_period
+//     steps and walks the segments not walked for `stale` steps, so the
+//     spike histories and trace snapshots a walk reads stay short;
+//   * over all segments before weights are read (flush).
 //
-// What the replay needs:
-//   * the target's spike steps after T: the last four are kept in one int4
-//     per target (L2-resident), older ones in a ring of post_ring_k steps;
-//   * x_pre of the source at each of those steps: the neuron update copies
-//     x_pre to a snapshot every `period` steps; x_pre(t) is the latest
-//     snapshot at or before t (or the value stored at T, if later) multiplied
-//     by the decay once per step in between -- the same sequence of float
-//     multiplications as the step-by-step trace, as the source does not
-//     spike between T and the pass.
-// A target that spiked more often than the ring holds, or a snapshot that
-// was overwritten, sets the error flag (the sweep keeps both from happening
-// for firing rates below ~1 kHz).
+// The traces at a past step t are rebuilt from snapshots: the trace value at
+// the end of every window of `win` steps is kept (exchange.cu), and x(t) is
+// that value advanced step by step -- x <- x*decay + spike -- through t,
+// the same operations as the per-step update.  A walk needs the spike steps
+// of the source (newest four per neuron, older ones in a ring for the
+// neurons of this GPU) and of each target.
+//
+// Work unit: one warp per (arriving spike, segment chunk of 128 synapses);
+// the last chunk of a segment to finish advances the segment's T.
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <climits>
+
+#include <cub/block/block_scan.cuh>
 
 #include "common.cuh"
 #include "internal.h"
@@ -38,178 +44,409 @@ namespace nrn {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kMaxReplay = 32;
+constexpr int kWarps = kThreads / 32;
+constexpr int kChunk = 128;      // synapses per warp unit (4 per lane)
+constexpr int kMaxPost = 64;     // target spike steps one walk may need (the ring depth)
+constexpr int kMaxPre = 8;       // source spike steps one walk may need
+constexpr int kMaxSpan = 1280;   // steps one walk may cover (x_pre table per warp)
+
+enum { ERR_HISTORY = 1, ERR_SNAPSHOT = 2 };
+
+__device__ __forceinline__ void set_err(int* err, int code) {
+    if (err) atomicCAS(err, 0, code);
+}
 
 __device__ __forceinline__ float clampw(float w, float lo, float hi) { return fminf(fmaxf(w, lo), hi); }
 
-// x_pre of source j at step t, T < t, no spike of j in (T, t].
-__device__ __forceinline__ float x_at(const PlasticArgs& a, int j, int t, int T, float xT) {
-    const int s_star = ((t + 1) / a.snap_period) * a.snap_period - 1;
-    float x;
-    int base;
-    if (s_star > T) {
-        x = a.x_snap[static_cast<long long>(((s_star + 1) / a.snap_period) % a.snap_depth) * a.n_src + j];
-        base = s_star;
-    } else {
-        x = xT;
-        base = T;
+// Ascending spike steps: up to four in registers (the common case) ...
+struct Steps4 {
+    int v0 = 0, v1 = 0, v2 = 0, v3 = 0;
+    int n = 0;
+    __device__ __forceinline__ int operator[](int k) const { return k == 0 ? v0 : k == 1 ? v1 : k == 2 ? v2 : v3; }
+    __device__ __forceinline__ void push(int t) {
+        v0 = n == 0 ? t : v0;
+        v1 = n == 1 ? t : v1;
+        v2 = n == 2 ? t : v2;
+        v3 = n == 3 ? t : v3;
+        ++n;
     }
-    for (int u = base + 1; u <= t; ++u) x = x * a.decay_pre;
-    return x;
+};
+// ... or in memory (shared, or local for long histories).
+struct StepsPtr {
+    const int* p = nullptr;
+    int n = 0;
+    __device__ __forceinline__ int operator[](int k) const { return p[k]; }
+};
+
+// The steps in (lo, hi] of a newest-first int4 that holds all of them (its
+// oldest entry is at or before lo), ascending.
+__device__ __forceinline__ Steps4 steps_from4(int4 r, int lo, int hi) {
+    Steps4 s;
+    if (r.w > lo && r.w <= hi) s.push(r.w);
+    if (r.z > lo && r.z <= hi) s.push(r.z);
+    if (r.y > lo && r.y <= hi) s.push(r.y);
+    if (r.x > lo && r.x <= hi) s.push(r.x);
+    return s;
 }
 
-// Potentiation of one synapse for the target spikes in (T, end], oldest first.
-__device__ __forceinline__ float replay(const PlasticArgs& a, int j, uint32_t i, int T, float xT, int end, float w,
-                                        float mod) {
-    const int4 r = a.post_recent[i];
-    if (r.x <= T) return w;   // no target spike since T (the common case)
-    int steps[kMaxReplay];
+// Spike steps of neuron `idx` in (lo, hi], ascending, into out[0..cap).
+// r: newest four steps (newest first, -1 = none); ring/cnt: all steps, if
+// kept for this neuron.  Returns the count, or -1 if the kept history does
+// not reach back to lo or holds more than cap steps in the range.
+__device__ int spikes_in(int4 r, const int32_t* ring, const int32_t* cnt, long long idx, int ring_k, int lo, int hi,
+                         int* out, int cap) {
     int n = 0;
-    const int cand[4] = {r.x, r.y, r.z, r.w};
+    const int c4[4] = {r.x, r.y, r.z, r.w};
     bool more = true;
+#pragma unroll
     for (int q = 0; q < 4; ++q) {
-        if (cand[q] <= T) { more = false; break; }
-        if (cand[q] <= end) steps[n++] = cand[q];
-    }
-    if (more) {
-        // older spikes from the ring (entries cnt-5, cnt-6, ...)
-        const int cnt = a.post_cnt[i];
-        int idx = cnt - 5;
-        const int oldest = cnt - a.post_ring_k;
-        for (; idx >= 0; --idx) {
-            if (idx < oldest || n >= kMaxReplay) {
-                atomicExch(a.err, 1);   // history too short for this gap
-                break;
-            }
-            const int t = a.post_ring[static_cast<long long>(i) * a.post_ring_k + (idx % a.post_ring_k)];
-            if (t <= T) break;
-            if (t <= end) steps[n++] = t;
+        const int t = c4[q];
+        if (!more || t <= lo) {
+            more = false;
+            continue;
+        }
+        if (t <= hi) {
+            if (n == cap) return -1;
+            out[n++] = t;
         }
     }
-    for (int q = n - 1; q >= 0; --q) {
-        const float x = x_at(a, j, steps[q], T, xT);
-        const float dw = a.a_plus * x;   // (A+ x_pre) * post(=1) - (A- x_post) * pre(=0)
+    if (more) {
+        // all four newest steps are after lo: older ones from the ring
+        if (ring == nullptr) return -1;
+        const int c = cnt[idx];
+        const int oldest = c - ring_k;
+        for (int e = c - 5; e >= 0; --e) {
+            if (e < oldest) return -1;
+            const int t = ring[idx * ring_k + (e % ring_k)];
+            if (t <= lo) break;
+            if (t <= hi) {
+                if (n == cap) return -1;
+                out[n++] = t;
+            }
+        }
+    }
+    for (int q = 0; q < n / 2; ++q) {
+        const int x = out[q];
+        out[q] = out[n - 1 - q];
+        out[n - 1 - q] = x;
+    }
+    return n;
+}
+
+struct Seg {
+    int j;            // source
+    long long seg;    // j * nd + k
+    long long s0, s1; // synapse range
+    int T;            // events applied through T
+    int e;            // apply through e
+    StepsPtr P;       // source spikes in (T, e] (per-warp shared memory)
+    const float* X;   // x_pre(T + 1 + u) at X[u], u < e - T (per-warp shared memory)
+};
+
+// One synapse: every update in (T, e], oldest first.
+template <class L>
+__device__ __forceinline__ float apply_events(const WalkArgs& a, const Seg& g, const L& Q, uint32_t i, float w,
+                                              float mod, int now) {
+    int p = 0, q = 0;
+    while (p < g.P.n || q < Q.n) {
+        const int tp = p < g.P.n ? g.P[p] : INT_MAX;
+        const int tq = q < Q.n ? Q[q] : INT_MAX;
+        const int t = tp < tq ? tp : tq;
+        const bool pre = tp == t, post = tq == t;
+        const float xpre = post ? g.X[t - g.T - 1] : 0.0f;
+        float xpost = 0.0f;
+        if (pre) {
+            if (now - t >= a.post_depth) set_err(a.err, ERR_SNAPSHOT);
+            xpost = a.post_ring[static_cast<long long>(t % a.post_depth) * a.n_tgt + i];
+        }
+        const float dw = (a.a_plus * xpre) * (post ? 1.0f : 0.0f) - (a.a_minus * xpost) * (pre ? 1.0f : 0.0f);
         float upd = (dw * a.lr) * 1.0f;
         if (a.mod) upd = upd * mod;
         w = clampw(w + upd, a.w_min, a.w_max);
+        if (pre) ++p;
+        if (post) ++q;
     }
     return w;
 }
 
-// One segment (source j, delay index k) walked by the whole block.
-__device__ void walk_segment(const PlasticArgs& a, int mode, int j, int k, long long step) {
-    __shared__ int sh_T;
-    __shared__ float sh_xT;
-    const long long seg = static_cast<long long>(j) * a.nd + k;
-    if (threadIdx.x == 0) {
-        sh_T = a.seg_last[seg];
-        sh_xT = a.seg_x[seg];
+__device__ __noinline__ float walk_syn_long(const WalkArgs& a, const Seg& g, uint32_t i, int4 r, float w, float mod,
+                                            int now) {
+    int buf[kMaxPost];
+    StepsPtr Q;
+    Q.p = buf;
+    Q.n = spikes_in(r, a.tgt_ring, a.tgt_cnt, i, a.ring_k, g.T, g.e, buf, kMaxPost);
+    if (Q.n < 0) {
+        set_err(a.err, ERR_HISTORY);
+        return w;
     }
-    __syncthreads();
-    const int T = sh_T;
-    const float xT = sh_xT;
-    // Pending potentiation through `end`; the delivery runs before this
-    // step's update (end = step - 1), the source-spike update and the sweep
-    // after it (the source-spike step itself is handled below).
-    const int now = static_cast<int>(step);
-    const int end = mode == PLASTIC_FLUSH ? now : now - 1;
-    const long long s0 = a.seg_ptr[seg], s1 = a.seg_ptr[seg + 1];
-    if (threadIdx.x == 0 && T < now - (a.snap_depth - 1) * a.snap_period)
-        atomicExch(a.err, 2);   // segment not visited within the snapshot window
-    const float ltp_now = a.a_plus * a.x_pre[j];
-    unsigned long long events = 0;
-    for (long long syn = s0 + threadIdx.x; syn < s1; syn += kThreads) {
-        const uint32_t i = a.tgt[syn];
-        const float mod = a.mod ? a.mod[syn] : 1.0f;
-        const float w0 = a.w[syn];
-        float w = T < end ? replay(a, j, i, T, xT, end, w0, mod) : w0;
-        if (mode == PLASTIC_LTD) {
-            // the source spiked now: -A- x_post, plus +A+ x_pre if the target did too
-            const float dw = ltp_now * a.spike_tgt[i] - (a.a_minus * a.x_post[i]) * 1.0f;
-            float upd = (dw * a.lr) * 1.0f;
-            if (a.mod) upd = upd * mod;
-            w = clampw(w + upd, a.w_min, a.w_max);
-        }
-        if (__float_as_uint(w) != __float_as_uint(w0)) a.w[syn] = w;
-        if (mode == PLASTIC_DELIVER) {
-            atomicAdd(a.acc + i, a.mod ? w * mod : w);
-            ++events;
-        }
-    }
-    if (mode == PLASTIC_DELIVER && a.events) {
-        __shared__ unsigned long long sh_ev;
-        if (threadIdx.x == 0) sh_ev = 0;
-        __syncthreads();
-        if (events) atomicAdd(&sh_ev, events);
-        __syncthreads();
-        if (threadIdx.x == 0 && sh_ev) atomicAdd(a.events, sh_ev);
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        a.seg_last[seg] = mode == PLASTIC_DELIVER ? now - 1 : now;
-        a.seg_x[seg] = a.x_pre[j];   // x_pre at the new T (the trace as it is now)
-    }
-    __syncthreads();
+    return apply_events(a, g, Q, i, w, mod, now);
 }
 
-__global__ void __launch_bounds__(kThreads) plastic_rows_kernel(const __grid_constant__ PlasticArgs a, int mode,
-                                                                long long step_off, const long long* step_base) {
-    const long long step = step_off + (step_base ? *step_base : 0);
-    __shared__ long long pre[257];
-    __shared__ int slots[256];
-    long long n_items = 0;
-    if (mode == PLASTIC_DELIVER) {
-        // spikes of step - (dmin + k) through the delay-k segments
-        if (threadIdx.x == 0) {
-            long long acc = 0;
-            for (int k = 0; k < a.nd; ++k) {
-                pre[k] = acc;
-                const long long src_step = step - (a.dmin + k);
-                slots[k] = src_step >= 0 ? static_cast<int>(src_step % a.hist_src.depth) : -1;
-                if (src_step >= 0) acc += a.hist_src.count[slots[k]];
-            }
-            pre[a.nd] = acc;
-        }
-        __syncthreads();
-        n_items = pre[a.nd];
-    } else {
-        const int slot = static_cast<int>(step % a.hist_src.depth);
-        const long long n_spk = mode == PLASTIC_LTD ? a.hist_src.count[slot] : 0;
-        const long long r0 = static_cast<long long>(step % a.sweep_period) * a.sweep_rows;
-        const long long left = a.n_src - r0;
-        const long long n_sweep = left <= 0 ? 0 : (a.sweep_rows < left ? a.sweep_rows : left);
-        n_items = n_spk + (mode == PLASTIC_LTD ? n_sweep : a.n_src);
-        for (long long it = blockIdx.x; it < n_items; it += gridDim.x) {
-            if (mode == PLASTIC_LTD && it < n_spk) {
-                const int j = a.hist_src.ids[static_cast<long long>(slot) * a.hist_src.cap + it];
-                for (int k = 0; k < a.nd; ++k) walk_segment(a, PLASTIC_LTD, j, k, step);
+__device__ __forceinline__ float walk_syn(const WalkArgs& a, const Seg& g, uint32_t i, int4 r, float w, float mod,
+                                          int now) {
+    if (g.P.n == 0 && r.x <= g.T) return w;   // nothing happened to this synapse
+    if (r.w <= g.T) return apply_events(a, g, steps_from4(r, g.T, g.e), i, w, mod, now);
+    return walk_syn_long(a, g, i, r, w, mod, now);
+}
+
+// Loads the segment's state, the source's spikes in (T, e] and the source
+// trace over (T, e] into the warp's shared slots.  The trace is rebuilt
+// window by window (one window per lane) from the snapshot at the window's
+// start -- or, for the first, from x_pre(T) -- with the same operations as
+// the per-step update.
+__device__ __forceinline__ bool load_seg(const WalkArgs& a, Seg& g, int* sP, float* sX, int j, int k, int e,
+                                         int m_new, int lane) {
+    __syncwarp();   // the warp is done with the previous segment's lists
+    g.j = j;
+    g.seg = static_cast<long long>(j) * a.nd + k;
+    g.e = e;
+    long long s0 = 0, s1 = 0;
+    int T = 0, n = 0;
+    float xT = 0.0f;
+    if (lane == 0) {
+        s0 = a.seg_ptr[g.seg];
+        s1 = a.seg_ptr[g.seg + 1];
+        T = a.seg_last[g.seg];
+        xT = a.seg_x[g.seg];
+        if (s0 < s1 && T < e) {
+            if (e - T > kMaxSpan) {
+                set_err(a.err, ERR_SNAPSHOT);
+                n = -1;
             } else {
-                const long long r = mode == PLASTIC_LTD ? r0 + (it - n_spk) : it;
-                const int j = static_cast<int>(r);
-                // a row whose source spiked this step was just updated above
-                if (mode == PLASTIC_LTD && a.spike_src[j] != 0.0f) continue;
-                for (int k = 0; k < a.nd; ++k) walk_segment(a, PLASTIC_FLUSH, j, k, step);
+                const bool own = j >= a.src_lo && j < a.src_hi;
+                n = spikes_in(a.src_recent[j], own ? a.src_ring : nullptr, a.src_cnt, j - a.src_lo, a.ring_k, T, e,
+                              sP, kMaxPre);
+                if (n < 0) set_err(a.err, ERR_HISTORY);
             }
+        }
+    }
+    __syncwarp();
+    g.s0 = __shfl_sync(0xffffffffu, s0, 0);
+    g.s1 = __shfl_sync(0xffffffffu, s1, 0);
+    g.T = __shfl_sync(0xffffffffu, T, 0);
+    xT = __shfl_sync(0xffffffffu, xT, 0);
+    n = __shfl_sync(0xffffffffu, n, 0);
+    g.P.p = sP;
+    g.P.n = n < 0 ? 0 : n;
+    g.X = sX;
+    if (!(g.s0 < g.s1 && g.T < e && n >= 0)) return false;
+    // window ends b = m*win - 1 in (T, e): m = m0, m0+1, ...
+    const int W = a.win;
+    const int m0 = (g.T + 1) / W + 1;
+    const int n_pieces = 1 + (m0 * W - 1 < e ? (e - (m0 * W - 1) + W - 1) / W : 0);
+    for (int pc = lane; pc < n_pieces; pc += 32) {
+        int start;
+        float x;
+        if (pc == 0) {
+            start = g.T;
+            x = xT;
+        } else {
+            const int m = m0 + pc - 1;
+            start = m * W - 1;
+            if (m_new - m >= a.pre_depth) set_err(a.err, ERR_SNAPSHOT);
+            x = a.pre_snap[static_cast<long long>(m % a.pre_depth) * a.pre_stride + j];
+        }
+        const int stop = pc == 0 ? (m0 * W - 1 < e ? m0 * W - 1 : e) : (start + W < e ? start + W : e);
+        int q = 0;
+        while (q < g.P.n && g.P[q] <= start) ++q;
+        int next = q < g.P.n ? g.P[q] : INT_MAX;
+        for (int u = start + 1; u <= stop; ++u) {
+            float s = 0.0f;
+            if (next == u) {
+                s = 1.0f;
+                ++q;
+                next = q < g.P.n ? g.P[q] : INT_MAX;
+            }
+            x = x * a.decay_pre + s;
+            sX[u - g.T - 1] = x;
+        }
+    }
+    __syncwarp();
+    return true;
+}
+
+// Walks synapses [c0, c1) of the segment, one per lane and round (the next
+// round's loads issued before this round's work); with deliver, adds the
+// updated weights into the target accumulators.
+__device__ __forceinline__ unsigned walk_chunk(const WalkArgs& a, const Seg& g, long long c0, long long c1,
+                                               bool deliver, int now, int lane) {
+    struct Syn {
+        uint32_t t;
+        float w, md;
+        int4 r;
+    };
+    auto load = [&](long long syn) {
+        Syn x;
+        x.t = __ldcs(a.tgt + syn);
+        x.w = a.w[syn];
+        x.md = a.mod ? __ldcs(a.mod + syn) : 1.0f;
+        x.r = a.tgt_recent[x.t];
+        return x;
+    };
+    unsigned n = 0;
+    long long syn = c0 + lane;
+    Syn cur{};
+    if (syn < c1) cur = load(syn);
+#pragma unroll 1
+    for (; syn < c1; syn += 32) {
+        Syn nxt{};
+        if (syn + 32 < c1) nxt = load(syn + 32);
+        const float w1 = walk_syn(a, g, cur.t, cur.r, cur.w, cur.md, now);
+        if (__float_as_uint(w1) != __float_as_uint(cur.w)) a.w[syn] = w1;
+        if (deliver) {
+            atomicAdd(a.acc + cur.t, a.mod ? w1 * cur.md : w1);
+            ++n;
+        }
+        cur = nxt;
+    }
+    return n;
+}
+
+// New segment state after a walk through g.e.
+__device__ __forceinline__ void finish_seg(const WalkArgs& a, const Seg& g) {
+    a.seg_x[g.seg] = g.X[g.e - g.T - 1];
+    a.seg_last[g.seg] = g.e;
+}
+
+// Walks a whole segment with one warp (sweep, flush).
+__device__ void walk_whole(const WalkArgs& a, const Seg& g, int now, int lane) {
+    for (long long c0 = g.s0; c0 < g.s1; c0 += kChunk) {
+        const long long c1 = c0 + kChunk < g.s1 ? c0 + kChunk : g.s1;
+        walk_chunk(a, g, c0, c1, false, now, lane);
+    }
+    __syncwarp();
+    if (lane == 0) finish_seg(a, g);
+    __syncwarp();
+}
+
+__global__ void __launch_bounds__(kThreads) walk_kernel(const __grid_constant__ WalkArgs a, int mode,
+                                                        long long step_off, const long long* step_base) {
+    using Scan = cub::BlockScan<long long, kThreads>;
+    __shared__ typename Scan::TempStorage scan_tmp;
+    __shared__ long long start[257];
+    __shared__ int slot[256];
+    __shared__ int sP_all[kWarps][kMaxPre];
+    __shared__ float sX_all[kWarps][kMaxSpan];
+    int* sP = sP_all[threadIdx.x >> 5];
+    float* sX = sX_all[threadIdx.x >> 5];
+
+    const long long step = step_off + (step_base ? *step_base : 0);
+    const int now = static_cast<int>(step);
+    const int m_new = static_cast<int>(step / a.win);   // newest snapshot written
+    const int lane = threadIdx.x & 31;
+    const long long warp = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
+    const long long n_warps = (static_cast<long long>(gridDim.x) * kThreads) >> 5;
+
+    if (mode == WALK_FLUSH) {
+        // every segment through step - 1
+        const long long nseg = static_cast<long long>(a.n_src) * a.nd;
+        for (long long s = warp; s < nseg; s += n_warps) {
+            Seg g;
+            if (!load_seg(a, g, sP, sX, static_cast<int>(s / a.nd), static_cast<int>(s % a.nd), now - 1, m_new, lane)) continue;
+            walk_whole(a, g, now, lane);
         }
         return;
     }
-    for (long long it = blockIdx.x; it < n_items; it += gridDim.x) {
-        int k = 0;
-        while (k + 1 < a.nd && pre[k + 1] <= it) ++k;
-        const int j = a.hist_src.ids[static_cast<long long>(slots[k]) * a.hist_src.cap + (it - pre[k])];
-        walk_segment(a, PLASTIC_DELIVER, j, k, step);
+
+    // Arrivals: spikes of step - (dmin + k) through the delay-k segments,
+    // ceil(max_seg / kChunk) units each.
+    const int chunks = (a.max_seg + kChunk - 1) / kChunk > 0 ? (a.max_seg + kChunk - 1) / kChunk : 1;
+    long long units = 0;
+    if (threadIdx.x < a.nd) {
+        const long long src_step = step - (a.dmin + threadIdx.x);
+        slot[threadIdx.x] = src_step >= 0 ? static_cast<int>(src_step % a.hist_src.depth) : 0;
+        if (src_step >= 0) units = static_cast<long long>(a.hist_src.count[slot[threadIdx.x]]) * chunks;
     }
+    long long excl, n_arr;
+    Scan(scan_tmp).ExclusiveSum(units, excl, n_arr);
+    if (threadIdx.x < a.nd) start[threadIdx.x] = excl;
+    if (threadIdx.x == 0) start[a.nd] = n_arr;
+    __syncthreads();
+
+    // Sweep: rows [r0, r0 + rows), one warp per segment.
+    const long long r0 = (step % a.sweep_period) * a.sweep_rows;
+    const long long left = a.n_src - r0;
+    const long long rows = left <= 0 ? 0 : (a.sweep_rows < left ? a.sweep_rows : left);
+    const long long n_units = n_arr + rows * a.nd;
+    const int win_end = static_cast<int>((step / a.win) * a.win) - 1;   // spikes of all ranks known through here
+    const int dmax = a.dmin + a.nd - 1;
+
+    unsigned long long my_events = 0;
+    for (long long u = warp; u < n_units; u += n_warps) {
+        if (u < n_arr) {
+            int lo = 0, hi = a.nd - 1;
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (start[mid] <= u) lo = mid; else hi = mid - 1;
+            }
+            const int k = lo;
+            const long long local = u - start[k];
+            const long long spike = local / chunks;
+            const int chunk = static_cast<int>(local - spike * chunks);
+            const int j = a.hist_src.ids[static_cast<long long>(slot[k]) * a.hist_src.cap + spike];
+            const long long seg = static_cast<long long>(j) * a.nd + k;
+            const long long s0 = a.seg_ptr[seg], s1 = a.seg_ptr[seg + 1];
+            const long long c0 = s0 + static_cast<long long>(chunk) * kChunk;
+            if (c0 >= s1) continue;
+            const long long c1 = c0 + kChunk < s1 ? c0 + kChunk : s1;
+            Seg g;
+            const bool pending = load_seg(a, g, sP, sX, j, k, now - 1, m_new, lane);
+            unsigned n;
+            if (pending) {
+                n = walk_chunk(a, g, c0, c1, true, now, lane);
+            } else {
+                // nothing to apply (already walked through now - 1): deliver only
+                n = 0;
+                for (long long syn = c0 + lane; syn < c1; syn += 32) {
+                    const float wv = a.w[syn];
+                    atomicAdd(a.acc + __ldg(a.tgt + syn), a.mod ? wv * __ldg(a.mod + syn) : wv);
+                    ++n;
+                }
+            }
+            my_events += n;
+            if (pending) {
+                // the last chunk of the segment to finish records the new T
+                __syncwarp();
+                if (lane == 0) {
+                    const int n_chunks = static_cast<int>((s1 - s0 + kChunk - 1) / kChunk);
+                    __threadfence();
+                    const int done = atomicAdd(a.seg_done + seg, 1);
+                    if (done == n_chunks - 1) {
+                        __threadfence();
+                        a.seg_done[seg] = 0;
+                        finish_seg(a, g);
+                    }
+                }
+            }
+        } else {
+            const long long q = u - n_arr;
+            const int j = static_cast<int>(r0 + q / a.nd);
+            const int k = static_cast<int>(q % a.nd);
+            // rows with spikes still to arrive are walked by those arrivals
+            if (a.src_recent[j].x >= now - dmax) continue;
+            const long long seg = static_cast<long long>(j) * a.nd + k;
+            if (a.seg_last[seg] >= now - a.stale) continue;
+            Seg g;
+            if (!load_seg(a, g, sP, sX, j, k, win_end, m_new, lane)) continue;
+            walk_whole(a, g, now, lane);
+        }
+    }
+    // lane sums -> one atomic per warp
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) my_events += __shfl_down_sync(0xffffffffu, my_events, o);
+    if (a.events && lane == 0 && my_events) atomicAdd(a.events, my_events);
 }
 
 }  // namespace
 
-nrn_status_t plastic_rows(const PlasticArgs& a, int mode, long long step_off, const long long* step_base,
-                          cudaStream_t s) {
+nrn_status_t walk_launch(const WalkArgs& a, int mode, long long step_off, const long long* step_base,
+                         cudaStream_t s) {
     NRN_CHECK_ARG(a.nd >= 1 && a.nd <= 256, "plastic projection: at most 256 delay values");
+    NRN_CHECK_ARG(a.win >= 1 && a.sweep_period >= 1, "plastic projection: bad window or sweep period");
     int per_sm = 0;
-    NRN_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, plastic_rows_kernel, kThreads, 0));
+    NRN_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, walk_kernel, kThreads, 0));
     const int blocks = std::max(1, per_sm) * sm_count_current();
-    plastic_rows_kernel<<<blocks, kThreads, 0, s>>>(a, mode, step_off, step_base);
+    walk_kernel<<<blocks, kThreads, 0, s>>>(a, mode, step_off, step_base);
     NRN_CUDA_TRY(cudaGetLastError());
     return NRN_OK;
 }

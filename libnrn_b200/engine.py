@@ -24,7 +24,12 @@ def _ptr(t):
 
 
 class Network:
-    def __init__(self, dt: float, slow_ratio: int = 1, device: int = 0):
+    """A network on one GPU, or this rank's part of a network partitioned
+    over GPUs: ``partition=(rank, world, nccl_unique_id, max_rate_hz)``
+    (libnrn_b200.partition); populations are then added with their whole
+    size ``n_global`` and this rank's slice."""
+
+    def __init__(self, dt: float, slow_ratio: int = 1, device: int = 0, partition=None):
         self.L = N.lib()
         self.device = device
         self.dt = float(dt)
@@ -32,6 +37,13 @@ class Network:
         h = C.c_void_p()
         N.check(self.L.nrn_engine_create(C.byref(h), device, self.dt, int(slow_ratio)), "nrn_engine_create")
         self.h = h
+        self.rank, self.world = 0, 1
+        if partition is not None:
+            rank, world, uid, max_rate = partition
+            buf = (C.c_uint8 * 128)(*bytes(uid))
+            N.check(self.L.nrn_engine_set_partition(self.h, int(rank), int(world), C.byref(buf), float(max_rate)),
+                    "nrn_engine_set_partition")
+            self.rank, self.world = int(rank), int(world)
         self.pops: list[dict] = []
         self.projs: list[dict] = []
         self._keep: list = []
@@ -39,9 +51,14 @@ class Network:
 
     # -- construction -------------------------------------------------------
     def add_population(self, model: str, n: int, params, *, hp=None, drive=None, cond=None,
-                       init_v=None, init_aux=None, record: bool = True, seed: int = 0) -> int:
+                       init_v=None, init_aux=None, record: bool = True, seed: int = 0,
+                       n_global: int | None = None, local_offset: int = 0) -> int:
+        """n neurons on this GPU: neurons [local_offset, local_offset + n) of a
+        population of n_global (default n); per-neuron arrays are this
+        slice's."""
         f32 = dict(dtype=torch.float32, device=self.dev)
-        off = sum(p["n"] for p in self.pops)
+        off = sum(p["n_global"] for p in self.pops)
+        n_global = n if n_global is None else int(n_global)
         if init_v is None:
             v = torch.full((n,), -65.0 if model == "izh" else float(params[0]), **f32)
         else:
@@ -62,6 +79,9 @@ class Network:
         d.n = n
         d.gid_offset = off
         d.record = int(record)
+        if n_global != n or local_offset:
+            d.n_global = n_global
+            d.local_offset = int(local_offset)
         d.v, d.aux, d.refractory, d.spike, d.i_syn = (_ptr(t) for t in (v, aux, ref, spike, i_syn))
         if cond is not None:
             d.tau_syn_exc, d.tau_syn_inh, d.e_exc, d.e_inh = (float(x) for x in cond)
@@ -79,7 +99,8 @@ class Network:
             d.drive.seed = int(seed)
         pid = C.c_int32()
         N.check(self.L.nrn_engine_add_population(self.h, C.byref(d), C.byref(pid)), "add_population")
-        self.pops.append({"model": model, "n": n, "offset": off, "v": v, "aux": aux, "ref": ref,
+        self.pops.append({"model": model, "n": n, "n_global": n_global, "lo": int(local_offset),
+                          "offset": off, "v": v, "aux": aux, "ref": ref,
                           "spike": spike, "i_syn": i_syn, "hp": hpt, "record": record})
         return pid.value
 
@@ -205,17 +226,26 @@ class Network:
         return nw
 
     @classmethod
-    def from_spec(cls, spec: dict, device: int = 0, record: bool = True) -> "Network":
+    def from_spec(cls, spec: dict, device: int = 0, record: bool = True, partition=None) -> "Network":
         """From a workload spec (libnrn_b200.workloads), connectivity
-        generated on the device."""
+        generated on the device; with ``partition``, this rank's slice."""
         from . import workloads as W
+        from .partition import partition_range
 
-        nw = cls(spec["dt"], spec.get("slow_ratio", 1), device)
+        nw = cls(spec["dt"], spec.get("slow_ratio", 1), device, partition=partition)
         for p in spec["pops"]:
             arr = W.population_arrays(spec, p)
-            nw.add_population(p["model"], p["n"], p["params"], hp=arr["hp"], drive=p.get("drive"),
-                              cond=p.get("cond"), init_v=arr["init_v"], init_aux=arr["init_aux"],
-                              record=record, seed=spec["seed"])
+            lo, n = partition_range(p["n"], nw.rank, nw.world)
+
+            def cut(a):
+                if a is None:
+                    return None
+                a = np.asarray(a)
+                return a[..., lo:lo + n]
+
+            nw.add_population(p["model"], n, p["params"], hp=cut(arr["hp"]), drive=p.get("drive"),
+                              cond=p.get("cond"), init_v=cut(arr["init_v"]), init_aux=cut(arr["init_aux"]),
+                              record=record, seed=spec["seed"], n_global=p["n"], local_offset=lo)
         for q in spec["projs"]:
             g = q["gen"]
             cols = (0, spec["n_total"]) if g.get("cols") == "all" else None
