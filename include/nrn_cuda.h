@@ -308,6 +308,44 @@ NRN_API nrn_status_t nrn_cuda_scatter(const float* src, const int64_t* pos, int6
                                       nrn_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
+/* Batched block-sparse propagation (tensor cores)                          */
+/* ------------------------------------------------------------------------ */
+
+/* Block-sparse weights of 64x64 bf16 blocks, block-row CSR.  Each block is
+ * stored as one 4096-element tile in the tensor core's K-major canonical
+ * order (nrn_cuda_bsr_pack makes it from row-major [post][pre] blocks). */
+typedef struct {
+    int32_t n_post_blocks;     /* block rows: post neurons / 64             */
+    int32_t n_pre_blocks;      /* block columns: pre neurons / 64           */
+    int64_t n_blocks;
+    const int32_t* row_ptr;    /* [n_post_blocks + 1]                       */
+    const int32_t* col_idx;    /* [n_blocks]                                */
+    const uint16_t* tiles;     /* [n_blocks][4096] bf16, 16-byte aligned    */
+} nrn_bsr_t;
+
+/* I[post][trial] += sum over blocks (r,c): W[r,c] . S[pre in c][trial], for
+ * 64 trials at once: bf16 x bf16 products accumulated in fp32 (tcgen05).
+ * i_syn is [n_post_blocks*64][64] fp32; spike_tiles holds one tile per pre
+ * block (nrn_cuda_bsr_spikes / nrn_cuda_bsr_pack_spikes).  Replaces the
+ * reference's block-dense kernel, launch_synaptic_current_block_dense
+ * (src/synapse/kernels/synapse_kernels.cu:30-79, a stub there), for the
+ * batched-trial case.  A device-side wait that times out sets *err to 5. */
+NRN_API nrn_status_t nrn_cuda_bsr_propagate(const nrn_bsr_t* w, const uint16_t* spike_tiles, float* i_syn,
+                                            int32_t* err, nrn_stream_t stream);
+/* Row-major bf16 blocks [n_blocks][64 post][64 pre] -> tiles. */
+NRN_API nrn_status_t nrn_cuda_bsr_pack(const uint16_t* blocks, int64_t n_blocks, uint16_t* tiles,
+                                       nrn_stream_t stream);
+/* 0/1 spikes [n_pre_blocks*64][64 trials] (float) <-> spike tiles. */
+NRN_API nrn_status_t nrn_cuda_bsr_pack_spikes(const float* spikes, int32_t n_pre_blocks, uint16_t* tiles,
+                                              nrn_stream_t stream);
+NRN_API nrn_status_t nrn_cuda_bsr_unpack_spikes(const uint16_t* tiles, int32_t n_pre_blocks, float* spikes,
+                                                nrn_stream_t stream);
+/* Bernoulli(p) spikes of step `step` for 64 trials, Philox keyed by (pre
+ * neuron, trial group, step) -- the same spikes for any launch shape. */
+NRN_API nrn_status_t nrn_cuda_bsr_spikes(uint64_t seed, int64_t step, float p, int32_t n_pre_blocks,
+                                         uint16_t* tiles, nrn_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
 /* Engine: a network resident on one GPU                                   */
 /* ------------------------------------------------------------------------ */
 

@@ -32,6 +32,8 @@ EXPORTS = [
     "nrn_engine_profile", "nrn_engine_weights_device", "nrn_engine_set_state", "nrn_engine_set_step",
     "nrn_cuda_block_deliver", "nrn_cuda_block_stdp", "nrn_cuda_compact", "nrn_cuda_gather_ring",
     "nrn_cuda_scatter", "nrn_engine_raster_noalloc", "nrn_comm_unique_id", "nrn_engine_set_partition",
+    "nrn_cuda_bsr_propagate", "nrn_cuda_bsr_pack", "nrn_cuda_bsr_pack_spikes", "nrn_cuda_bsr_unpack_spikes",
+    "nrn_cuda_bsr_spikes",
 ]
 
 
@@ -90,6 +92,13 @@ class PopDesc(C.Structure):
     ]
 
 
+class Bsr(C.Structure):
+    _fields_ = [
+        ("n_post_blocks", C.c_int32), ("n_pre_blocks", C.c_int32), ("n_blocks", C.c_int64),
+        ("row_ptr", C.c_void_p), ("col_idx", C.c_void_p), ("tiles", C.c_void_p),
+    ]
+
+
 class ProjDesc(C.Structure):
     _fields_ = [
         ("src_pop", C.c_int32), ("tgt_pop", C.c_int32), ("receptor", C.c_int32), ("on_device", C.c_int32),
@@ -139,6 +148,11 @@ def lib() -> C.CDLL:
             "nrn_engine_set_stdp": [vp, i32, C.POINTER(C.c_double)],
             "nrn_engine_finalize": [vp, i32],
             "nrn_comm_unique_id": [C.POINTER(C.c_uint8 * 128)],
+            "nrn_cuda_bsr_propagate": [C.POINTER(Bsr), vp, vp, vp, vp],
+            "nrn_cuda_bsr_pack": [vp, i64, vp, vp],
+            "nrn_cuda_bsr_pack_spikes": [vp, i32, vp, vp],
+            "nrn_cuda_bsr_unpack_spikes": [vp, i32, vp, vp],
+            "nrn_cuda_bsr_spikes": [C.c_uint64, i64, C.c_float, i32, vp, vp],
             "nrn_engine_set_partition": [vp, i32, i32, C.POINTER(C.c_uint8 * 128), C.c_double],
             "nrn_engine_run": [vp, i64, i32],
             "nrn_engine_sync": [vp],
