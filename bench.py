@@ -8,7 +8,10 @@ Workload (default): the Brunel balanced LIF network with pair STDP on E->E,
 from Philox (synthetic, seeded).  One bench step = one simulation timestep.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload brunel_stdp|brunel|adex|izh]
+                  [--workload brunel_stdp|brunel|adex|izh|bsr]
+
+`--workload bsr` is the batched-trial block-sparse product (64 trials, 262,144
+neurons, 2% of 64x64 bf16 blocks) with its own metric line.
 
 Prints one JSON line (rank 0).  `value` is delivered synaptic events per
 second over the timed steps with the network resident in HBM; `e2e` is the
@@ -118,6 +121,8 @@ def cpu_reference(args, world_steps_hint=None):
     import specs as S
 
     threads = os.cpu_count() or 1
+    if args.workload == "bsr":
+        return cpu_bsr_sample(threads)
     steps = int(os.environ.get("NRN_CPU_SAMPLE_STEPS", "30"))
     if args.workload in ("brunel_stdp", "brunel"):
         spec = W.brunel(10_000, 2_500, 1_000, 250, steps=steps, stdp=args.workload == "brunel_stdp")
@@ -157,10 +162,163 @@ def cpu_reference(args, world_steps_hint=None):
     }
 
 
+BSR_N = 262_144          # pre = post neurons of the batched block-sparse workload
+BSR_DENSITY = 0.02       # fraction of the 64x64 block slots present
+BSR_P = 0.01             # spike probability per neuron, trial and step
+
+
+def cpu_bsr_sample(threads: int) -> dict:
+    """The batched block-sparse product on the host cores (torch fp32, all
+    threads) for a sample of 64 block rows of the full-size workload (82
+    blocks of 64x64 per row on average, 64 trials), scaled to one step of
+    all 4,096 block rows."""
+    import torch
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(4)
+    nb_rows, nc, rows = BSR_N // 64, BSR_N // 64, 64
+    per_row = int(round(BSR_DENSITY * nc))
+    w = torch.randn(rows * per_row, 64, 64, generator=g) * 0.02
+    cols = torch.randint(0, nc, (rows * per_row,), generator=g)
+    s = (torch.rand(BSR_N, 64, generator=g) < BSR_P).float().view(nc, 64, 64)
+    out = torch.zeros(rows, 64, 64)
+    reps = 3
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        prod = torch.bmm(w, s[cols])
+        out.index_add_(0, torch.arange(rows).repeat_interleave(per_row), prod)
+    dt = (time.perf_counter() - t0) / reps * (nb_rows / rows)
+    n_blocks = int(round(BSR_DENSITY * nb_rows * nc))
+    return {"updates_per_s": n_blocks * 64 * 64 * 64 / dt, "step_s": dt, "cores": threads, "kind": "port",
+            "sample": f"torch fp32 block product, 64 of 4,096 block rows ({per_row} blocks each, 64 trials), "
+                      f"{reps} repetitions, scaled to all rows"}
+
+
+def run_bsr(args, rank: int, world: int, local: int) -> None:
+    """C4: 64 trials of a 262,144 x 262,144 network of 64x64 bf16 blocks at
+    2% block density; Bernoulli(0.01) spikes per step.  The workload does not
+    shard: at N GPUs each rank runs its own replica (`value` sums them)."""
+    import torch
+
+    from libnrn_b200 import bsr as B
+
+    peaks, peaks_kind = load_peaks()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                timeout=datetime.timedelta(seconds=600))
+
+    def reduce(x: float, op: str) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
+        return float(t.item())
+
+    n = max(64, int(BSR_N * args.scale) // 64 * 64)
+    w = B.BlockSparse.random(n, n, BSR_DENSITY, seed=4)
+    tiles = B.spike_tiles(w.n_pre_blocks)
+    cur = torch.zeros(n, 64, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def step(s: int) -> None:
+        B.bernoulli_spikes(tiles, 5, s, BSR_P, stream)
+        w.propagate(tiles, cur, stream)
+
+    for s in range(args.warmup):
+        step(s)
+    torch.cuda.synchronize()
+    w.check()
+    if dist is not None:
+        dist.barrier()
+    with ClockSampler(local) as clk:
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for s in range(args.steps):
+            step(args.warmup + s)
+        b.record(stream)
+        torch.cuda.synchronize()
+    w.check()
+    ms = reduce(a.elapsed_time(b), "max")
+    updates = w.n_blocks * 64 * 64 * 64   # (synapse, trial) pairs per step
+    value = reduce(updates * args.steps / (ms / 1e3), "sum")
+    # the dominant kernel alone (propagation), CUDA events on the same stream
+    kp = max(10, args.steps // 10)
+    a.record(stream)
+    for _ in range(kp):
+        w.propagate(tiles, cur, stream)
+    b.record(stream)
+    torch.cuda.synchronize()
+    w.check()
+    k_ms = a.elapsed_time(b) / kp
+    alg_bytes = w.n_blocks * 8192 + n * 64 * 8 + n * 64 * 2   # weights, currents r/w, spikes once
+    flops = 2.0 * 64 ** 3 * w.n_blocks
+    achieved = alg_bytes / (k_ms / 1e3) / 1e9
+    # e2e: each step's spike tiles from pinned host memory, the currents back at the end
+    host_tiles = tiles.cpu().pin_memory()
+    host_cur = torch.empty(cur.shape, dtype=cur.dtype).pin_memory()
+    torch.cuda.synchronize()
+    k_e2e = max(5, min(args.steps, 50))
+    t0 = time.perf_counter()
+    for _ in range(k_e2e):
+        tiles.copy_(host_tiles, non_blocking=True)
+        w.propagate(tiles, cur, stream)
+    host_cur.copy_(cur, non_blocking=True)
+    torch.cuda.synchronize()
+    e2e_s = reduce(time.perf_counter() - t0, "max")
+    e2e = reduce(updates * k_e2e, "sum") / e2e_s
+    cpu = None
+    if not args.no_cpu and rank == 0:
+        try:
+            cpu = cpu_bsr_sample(os.cpu_count() or 1)
+        except Exception as ex:
+            cpu = {"error": str(ex)[:200]}
+    line = {
+        "metric": "synapse_trial_updates_per_s", "value": value, "unit": "updates/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16 x bf16 -> f32",
+        "data": "synthetic (seeded block positions, N(0, 0.02) weights, Bernoulli spikes)",
+        "config": {"workload": "bsr", "neurons": n, "trials": 64, "blocks": w.n_blocks, "block": 64,
+                   "density": BSR_DENSITY, "p_spike": BSR_P,
+                   "l2": f"inputs larger than L2 (weights {w.n_blocks * 8192 / 1e9:.2f} GB)",
+                   "parallelism": "single GPU" if world == 1 else f"{world} independent replicas"},
+        "kernel_ms": k_ms, "tflops": flops / (k_ms / 1e3) / 1e12,
+        "gpu_launches": 2 * args.steps,
+        "roofline": {"kernel": "bsr_kernel", "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "peak_kind": peaks_kind,
+                     "traffic": None, "tensor_frac": flops / (k_ms / 1e3) / 1e12 / peaks.get("bf16_tflops", 1590.0)},
+        "e2e": {"value": e2e, "unit": "updates/s", "h2d_bytes_per_step": tiles.numel() * 2,
+                "d2h_bytes_per_step": cur.numel() * 4 / k_e2e},
+        "clocks": clk.summary(),
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu if "error" in cpu else {
+            "value": cpu["updates_per_s"], "unit": "updates/s", "cores": cpu["cores"], "kind": cpu["kind"],
+            "sample": cpu["sample"]}
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def run_reference_arm(args, rank: int):
     if rank != 0:
         return
     r = cpu_reference(args)
+    if args.workload == "bsr":
+        line = {"impl": "reference", "metric": "synapse_trial_updates_per_s", "value": r["updates_per_s"],
+                "unit": "updates/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                "higher_is_better": True, "dtype": "f32", "data": "synthetic", "config": {"workload": "bsr"},
+                "cpu_baseline": {"value": r["updates_per_s"], "unit": "updates/s", "cores": r["cores"],
+                                 "kind": r["kind"], "sample": r["sample"]},
+                "e2e": {"value": r["updates_per_s"], "unit": "updates/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
     line = {
         "impl": "reference", "metric": "synaptic_events_per_s", "value": r["events_per_s"],
         "unit": "events/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -181,7 +339,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10_000)
     ap.add_argument("--warmup", type=int, default=200)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="brunel_stdp", choices=["brunel_stdp", "brunel", "adex", "izh"])
+    ap.add_argument("--workload", default="brunel_stdp", choices=["brunel_stdp", "brunel", "adex", "izh", "bsr"])
     ap.add_argument("--chunk", type=int, default=0)
     ap.add_argument("--profile-steps", type=int, default=300)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
@@ -197,6 +355,9 @@ def main():
 
     if args.impl == "reference":
         run_reference_arm(args, rank)
+        return
+    if args.workload == "bsr":
+        run_bsr(args, rank, world, local)
         return
 
     import numpy as np

@@ -45,7 +45,7 @@
 namespace nrn {
 namespace {
 
-constexpr int kStages = 8;
+constexpr int kStages = 13;   // 13 x 16 KB in flight per SM: enough bytes to cover HBM latency at ~45 GB/s per SM
 constexpr int kTileElems = 4096;
 constexpr int kTileBytes = 8192;
 constexpr int kBsrThreads = 192;
@@ -200,28 +200,42 @@ __global__ void __launch_bounds__(kBsrThreads, 1) bsr_kernel(const __grid_consta
     };
 
     if (warp == 0) {
-        if (lane == 0) {
-            long long it = 0;
-            bool ok = true;
-            for (int r = blockIdx.x; r < a.n_rows && ok; r += gridDim.x) {
-                const int b1 = a.row_ptr[r + 1];
-                for (int b = a.row_ptr[r]; b < b1; ++b, ++it) {
-                    const int s = static_cast<int>(it % kStages);
-                    const uint32_t ph = static_cast<uint32_t>((it / kStages) & 1);
-                    if (!mbar_wait(&S.empty[s], ph ^ 1u, abort)) {
-                        fail();
+        // The warp reads 32 column indices per coalesced load; lane 0 issues
+        // the copies (no dependent global load per block).
+        long long it = 0;
+        bool ok = true;
+        for (int r = blockIdx.x; r < a.n_rows && ok; r += gridDim.x) {
+            const int b0 = a.row_ptr[r], b1 = a.row_ptr[r + 1];
+            for (int base = b0; base < b1 && ok; base += 32) {
+                const int my_col = base + lane < b1 ? a.col_idx[base + lane] : 0;
+                const int cnt = b1 - base < 32 ? b1 - base : 32;
+                for (int q = 0; q < cnt; ++q, ++it) {
+                    const int c = __shfl_sync(0xffffffffu, my_col, q);
+                    bool got = true;
+                    if (lane == 0) {
+                        const int s = static_cast<int>(it % kStages);
+                        const uint32_t ph = static_cast<uint32_t>((it / kStages) & 1);
+                        got = mbar_wait(&S.empty[s], ph ^ 1u, abort);
+                        if (got) {
+                            mbar_expect_tx(&S.full[s], 2 * kTileBytes);
+                            bulk_load(stA + s * kTileBytes, a.tiles + static_cast<long long>(base + q) * kTileElems,
+                                      kTileBytes, &S.full[s]);
+                            bulk_load(stB + s * kTileBytes, a.spikes + static_cast<long long>(c) * kTileElems,
+                                      kTileBytes, &S.full[s]);
+                        } else {
+                            fail();
+                        }
+                    }
+                    if (!__shfl_sync(0xffffffffu, got, 0)) {
                         ok = false;
                         break;
                     }
-                    mbar_expect_tx(&S.full[s], 2 * kTileBytes);
-                    bulk_load(stA + s * kTileBytes, a.tiles + static_cast<long long>(b) * kTileElems, kTileBytes,
-                              &S.full[s]);
-                    bulk_load(stB + s * kTileBytes, a.spikes + static_cast<long long>(a.col_idx[b]) * kTileElems,
-                              kTileBytes, &S.full[s]);
                 }
             }
-            // the copies still in flight land before the CTA exits
-            for (long long q = it - 1; q >= 0 && q >= it - kStages; --q)
+        }
+        // the copies still in flight land before the CTA exits
+        if (lane == 0) {
+            for (long long q = it - 1; q >= 0 && q >= it - kStages; --q)   // `it` counts issued stages
                 mbar_wait(&S.full[q % kStages], static_cast<uint32_t>((q / kStages) & 1), nullptr);
         }
     } else if (warp == 1) {

@@ -308,15 +308,44 @@ __device__ __forceinline__ void finish_seg(const WalkArgs& a, const Seg& g) {
     a.seg_last[g.seg] = g.e;
 }
 
-// Walks a whole segment with one warp (sweep, flush).
-__device__ void walk_whole(const WalkArgs& a, const Seg& g, int now, int lane) {
-    for (long long c0 = g.s0; c0 < g.s1; c0 += kChunk) {
-        const long long c1 = c0 + kChunk < g.s1 ? c0 + kChunk : g.s1;
-        walk_chunk(a, g, c0, c1, false, now, lane);
+// One chunk of kChunk synapses of segment (j, k): applies the updates
+// through e (and, with deliver, delivers the updated weights); the last
+// chunk of the segment to finish records the segment's new state.  Every
+// chunk of a segment reads the same state (the write happens only after
+// all of them have counted themselves) and so makes the same decision.
+// Returns the number of delivered events of this lane.
+__device__ unsigned segment_chunk(const WalkArgs& a, int* sP, float* sX, int j, int k, int chunk, int e,
+                                  bool deliver, int now, int m_new, int lane) {
+    const long long seg = static_cast<long long>(j) * a.nd + k;
+    const long long s0 = a.seg_ptr[seg], s1 = a.seg_ptr[seg + 1];
+    const long long c0 = s0 + static_cast<long long>(chunk) * kChunk;
+    if (c0 >= s1) return 0;
+    const long long c1 = c0 + kChunk < s1 ? c0 + kChunk : s1;
+    Seg g;
+    const bool pending = load_seg(a, g, sP, sX, j, k, e, m_new, lane);
+    unsigned n = 0;
+    if (pending) {
+        n = walk_chunk(a, g, c0, c1, deliver, now, lane);
+        __syncwarp();
+        if (lane == 0) {
+            const int n_chunks = static_cast<int>((s1 - s0 + kChunk - 1) / kChunk);
+            __threadfence();
+            const int done = atomicAdd(a.seg_done + seg, 1);
+            if (done == n_chunks - 1) {
+                __threadfence();
+                a.seg_done[seg] = 0;
+                finish_seg(a, g);
+            }
+        }
+    } else if (deliver) {
+        // nothing to apply (already walked through e): deliver only
+        for (long long syn = c0 + lane; syn < c1; syn += 32) {
+            const float wv = a.w[syn];
+            atomicAdd(a.acc + __ldg(a.tgt + syn), a.mod ? wv * __ldg(a.mod + syn) : wv);
+            ++n;
+        }
     }
-    __syncwarp();
-    if (lane == 0) finish_seg(a, g);
-    __syncwarp();
+    return n;
 }
 
 __global__ void __launch_bounds__(kThreads) walk_kernel(const __grid_constant__ WalkArgs a, int mode,
@@ -337,20 +366,23 @@ __global__ void __launch_bounds__(kThreads) walk_kernel(const __grid_constant__ 
     const long long warp = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
     const long long n_warps = (static_cast<long long>(gridDim.x) * kThreads) >> 5;
 
+    const int chunks = (a.max_seg + kChunk - 1) / kChunk > 0 ? (a.max_seg + kChunk - 1) / kChunk : 1;
+    const long long per_row = static_cast<long long>(a.nd) * chunks;   // units of one source row
+
     if (mode == WALK_FLUSH) {
         // every segment through step - 1
-        const long long nseg = static_cast<long long>(a.n_src) * a.nd;
-        for (long long s = warp; s < nseg; s += n_warps) {
-            Seg g;
-            if (!load_seg(a, g, sP, sX, static_cast<int>(s / a.nd), static_cast<int>(s % a.nd), now - 1, m_new, lane)) continue;
-            walk_whole(a, g, now, lane);
+        const long long n_units = static_cast<long long>(a.n_src) * per_row;
+        for (long long u = warp; u < n_units; u += n_warps) {
+            const long long row = u / per_row;
+            const int rem = static_cast<int>(u - row * per_row);
+            segment_chunk(a, sP, sX, static_cast<int>(row), rem / chunks, rem % chunks, now - 1, false, now, m_new,
+                          lane);
         }
         return;
     }
 
     // Arrivals: spikes of step - (dmin + k) through the delay-k segments,
-    // ceil(max_seg / kChunk) units each.
-    const int chunks = (a.max_seg + kChunk - 1) / kChunk > 0 ? (a.max_seg + kChunk - 1) / kChunk : 1;
+    // `chunks` units each.
     long long units = 0;
     if (threadIdx.x < a.nd) {
         const long long src_step = step - (a.dmin + threadIdx.x);
@@ -363,11 +395,11 @@ __global__ void __launch_bounds__(kThreads) walk_kernel(const __grid_constant__ 
     if (threadIdx.x == 0) start[a.nd] = n_arr;
     __syncthreads();
 
-    // Sweep: rows [r0, r0 + rows), one warp per segment.
+    // Sweep: rows [r0, r0 + rows), `chunks` units per segment.
     const long long r0 = (step % a.sweep_period) * a.sweep_rows;
     const long long left = a.n_src - r0;
     const long long rows = left <= 0 ? 0 : (a.sweep_rows < left ? a.sweep_rows : left);
-    const long long n_units = n_arr + rows * a.nd;
+    const long long n_units = n_arr + rows * per_row;
     const int win_end = static_cast<int>((step / a.win) * a.win) - 1;   // spikes of all ranks known through here
     const int dmax = a.dmin + a.nd - 1;
 
@@ -384,51 +416,18 @@ __global__ void __launch_bounds__(kThreads) walk_kernel(const __grid_constant__ 
             const long long spike = local / chunks;
             const int chunk = static_cast<int>(local - spike * chunks);
             const int j = a.hist_src.ids[static_cast<long long>(slot[k]) * a.hist_src.cap + spike];
-            const long long seg = static_cast<long long>(j) * a.nd + k;
-            const long long s0 = a.seg_ptr[seg], s1 = a.seg_ptr[seg + 1];
-            const long long c0 = s0 + static_cast<long long>(chunk) * kChunk;
-            if (c0 >= s1) continue;
-            const long long c1 = c0 + kChunk < s1 ? c0 + kChunk : s1;
-            Seg g;
-            const bool pending = load_seg(a, g, sP, sX, j, k, now - 1, m_new, lane);
-            unsigned n;
-            if (pending) {
-                n = walk_chunk(a, g, c0, c1, true, now, lane);
-            } else {
-                // nothing to apply (already walked through now - 1): deliver only
-                n = 0;
-                for (long long syn = c0 + lane; syn < c1; syn += 32) {
-                    const float wv = a.w[syn];
-                    atomicAdd(a.acc + __ldg(a.tgt + syn), a.mod ? wv * __ldg(a.mod + syn) : wv);
-                    ++n;
-                }
-            }
-            my_events += n;
-            if (pending) {
-                // the last chunk of the segment to finish records the new T
-                __syncwarp();
-                if (lane == 0) {
-                    const int n_chunks = static_cast<int>((s1 - s0 + kChunk - 1) / kChunk);
-                    __threadfence();
-                    const int done = atomicAdd(a.seg_done + seg, 1);
-                    if (done == n_chunks - 1) {
-                        __threadfence();
-                        a.seg_done[seg] = 0;
-                        finish_seg(a, g);
-                    }
-                }
-            }
+            my_events += segment_chunk(a, sP, sX, j, k, chunk, now - 1, true, now, m_new, lane);
         } else {
             const long long q = u - n_arr;
-            const int j = static_cast<int>(r0 + q / a.nd);
-            const int k = static_cast<int>(q % a.nd);
-            // rows with spikes still to arrive are walked by those arrivals
+            const long long row = q / per_row;
+            const int rem = static_cast<int>(q - row * per_row);
+            const int j = static_cast<int>(r0 + row);
+            const int k = rem / chunks;
+            // rows with spikes still to arrive are walked by those arrivals;
+            // segments walked recently are left for later
             if (a.src_recent[j].x >= now - dmax) continue;
-            const long long seg = static_cast<long long>(j) * a.nd + k;
-            if (a.seg_last[seg] >= now - a.stale) continue;
-            Seg g;
-            if (!load_seg(a, g, sP, sX, j, k, win_end, m_new, lane)) continue;
-            walk_whole(a, g, now, lane);
+            if (a.seg_last[static_cast<long long>(j) * a.nd + k] >= now - a.stale) continue;
+            segment_chunk(a, sP, sX, j, k, rem % chunks, win_end, false, now, m_new, lane);
         }
     }
     // lane sums -> one atomic per warp
