@@ -37,6 +37,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "internal.h"
@@ -45,7 +46,7 @@
 namespace nrn {
 namespace {
 
-constexpr int kStages = 13;   // 13 x 16 KB in flight per SM: enough bytes to cover HBM latency at ~45 GB/s per SM
+constexpr int kMaxStages = 13;   // 13 x 16 KB: the most one CTA's shared memory holds
 constexpr int kTileElems = 4096;
 constexpr int kTileBytes = 8192;
 constexpr int kBsrThreads = 192;
@@ -56,6 +57,7 @@ enum { ERR_BSR_TIMEOUT = 5 };
 
 struct BsrArgs {
     int32_t n_rows;
+    int32_t stages;   // pipeline stages of 16 KB (weights + spikes), <= kMaxStages
     const int32_t* row_ptr;
     const int32_t* col_idx;
     const uint16_t* tiles;
@@ -102,12 +104,27 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
                  : "memory");
 }
 
+// L2 policies: the weights stream through once per step (evict first); the
+// spike tiles are read by every block of their column (evict last).
+__device__ __forceinline__ uint64_t policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
 // Plain (untiled, no multicast) bulk copy global -> this CTA's shared memory.
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     smem_u32(dst)),
-                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
-                 : "memory");
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                          uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::
+            "r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
 }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -152,8 +169,8 @@ __device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t* v) {
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 struct Smem {
-    uint64_t full[kStages];
-    uint64_t empty[kStages];
+    uint64_t full[kMaxStages];
+    uint64_t empty[kMaxStages];
     uint64_t tfull[2];
     uint64_t tempty[2];
     uint64_t drain;
@@ -161,11 +178,15 @@ struct Smem {
     int abort;
 };
 
-__global__ void __launch_bounds__(kBsrThreads, 1) bsr_kernel(const __grid_constant__ BsrArgs a) {
+constexpr int kSmemHead = 1024;   // Smem, padded so that the tiles start 1 KB aligned
+static_assert(sizeof(Smem) <= kSmemHead, "barrier block too large");
+
+__global__ void __launch_bounds__(kBsrThreads, 2) bsr_kernel(const __grid_constant__ BsrArgs a) {
     extern __shared__ __align__(1024) unsigned char smem[];
-    unsigned char* stA = smem;                              // [kStages][8 KB] weight tiles
-    unsigned char* stB = smem + kStages * kTileBytes;       // [kStages][8 KB] spike tiles
-    Smem& S = *reinterpret_cast<Smem*>(smem + 2 * kStages * kTileBytes);
+    const int kStages = a.stages;
+    Smem& S = *reinterpret_cast<Smem*>(smem);               // barriers first, then the tiles
+    unsigned char* stA = smem + kSmemHead;                  // [stages][8 KB] weight tiles
+    unsigned char* stB = stA + kStages * kTileBytes;        // [stages][8 KB] spike tiles
     volatile int* abort = &S.abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -203,7 +224,10 @@ __global__ void __launch_bounds__(kBsrThreads, 1) bsr_kernel(const __grid_consta
         // The warp reads 32 column indices per coalesced load; lane 0 issues
         // the copies (no dependent global load per block).
         long long it = 0;
+        int stage = 0;          // it % stages
+        uint32_t phase = 0;     // (it / stages) & 1
         bool ok = true;
+        const uint64_t stream_once = policy_evict_first(), keep = policy_evict_last();
         for (int r = blockIdx.x; r < a.n_rows && ok; r += gridDim.x) {
             const int b0 = a.row_ptr[r], b1 = a.row_ptr[r + 1];
             for (int base = b0; base < b1 && ok; base += 32) {
@@ -213,15 +237,19 @@ __global__ void __launch_bounds__(kBsrThreads, 1) bsr_kernel(const __grid_consta
                     const int c = __shfl_sync(0xffffffffu, my_col, q);
                     bool got = true;
                     if (lane == 0) {
-                        const int s = static_cast<int>(it % kStages);
-                        const uint32_t ph = static_cast<uint32_t>((it / kStages) & 1);
+                        const int s = stage;
+                        const uint32_t ph = phase;
+                        if (++stage == kStages) {
+                            stage = 0;
+                            phase ^= 1u;
+                        }
                         got = mbar_wait(&S.empty[s], ph ^ 1u, abort);
                         if (got) {
                             mbar_expect_tx(&S.full[s], 2 * kTileBytes);
                             bulk_load(stA + s * kTileBytes, a.tiles + static_cast<long long>(base + q) * kTileElems,
-                                      kTileBytes, &S.full[s]);
+                                      kTileBytes, &S.full[s], stream_once);
                             bulk_load(stB + s * kTileBytes, a.spikes + static_cast<long long>(c) * kTileElems,
-                                      kTileBytes, &S.full[s]);
+                                      kTileBytes, &S.full[s], keep);
                         } else {
                             fail();
                         }
@@ -241,6 +269,8 @@ __global__ void __launch_bounds__(kBsrThreads, 1) bsr_kernel(const __grid_consta
     } else if (warp == 1) {
         if (lane == 0) {
             long long it = 0, rr = 0;
+            int stage = 0;
+            uint32_t phase = 0;
             bool ok = true;
             for (int r = blockIdx.x; r < a.n_rows && ok; r += gridDim.x) {
                 const int b0 = a.row_ptr[r], b1 = a.row_ptr[r + 1];
@@ -253,8 +283,13 @@ __global__ void __launch_bounds__(kBsrThreads, 1) bsr_kernel(const __grid_consta
                 tc_fence_after();
                 const uint32_t d = tmem + static_cast<uint32_t>(acc * 64);
                 for (int b = b0; b < b1; ++b, ++it) {
-                    const int s = static_cast<int>(it % kStages);
-                    if (!mbar_wait(&S.full[s], static_cast<uint32_t>((it / kStages) & 1), abort)) {
+                    const int s = stage;
+                    const uint32_t ph = phase;
+                    if (++stage == kStages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                    if (!mbar_wait(&S.full[s], ph, abort)) {
                         fail();
                         ok = false;
                         break;
@@ -472,9 +507,19 @@ extern "C" nrn_status_t nrn_cuda_bsr_propagate(const nrn_bsr_t* w, const uint16_
     a.spikes = spike_tiles;
     a.i_syn = i_syn;
     a.err = err;
-    const size_t smem = 2 * kStages * kTileBytes + sizeof(Smem);
+    // Pipeline shape: CTAs per SM and stages per CTA (defaults measured on
+    // B200; NRN_BSR_CTAS / NRN_BSR_STAGES override them for tuning).
+    // Two CTAs per SM, 6 stages each (2 independent pipelines): 89% of the
+    // measured HBM bandwidth at 262,144^2 neurons, against 46-61% for one.
+    int ctas = 2, stages = 6;
+    if (const char* v = std::getenv("NRN_BSR_CTAS")) ctas = std::max(1, std::min(2, std::atoi(v)));
+    if (ctas == 1) stages = kMaxStages;
+    if (const char* v = std::getenv("NRN_BSR_STAGES")) stages = std::max(2, std::min(kMaxStages, std::atoi(v)));
+    if (ctas == 2 && stages > 6) stages = 6;   // two CTAs share one SM's shared memory
+    a.stages = stages;
+    const size_t smem = kSmemHead + 2 * static_cast<size_t>(stages) * kTileBytes;
     NRN_CUDA_TRY(cudaFuncSetAttribute(bsr_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-    const int grid = std::min(a.n_rows, sm_count_current());
+    const int grid = std::min(a.n_rows, ctas * sm_count_current());
     bsr_kernel<<<grid, kBsrThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(a);
     NRN_CUDA_TRY(cudaGetLastError());
     return NRN_OK;

@@ -119,6 +119,8 @@ struct nrn_engine {
     double dt = 1e-4;
     int32_t slow_ratio = 1;
     cudaStream_t stream = nullptr;
+    cudaStream_t side = nullptr;          // static delivery, concurrent with the STDP walks
+    cudaEvent_t fork_ev = nullptr, join_ev = nullptr;
     std::vector<EnginePop> pops;
     std::vector<EngineProj> projs;
     bool finalized = false;
@@ -134,6 +136,7 @@ struct nrn_engine {
     std::map<int, cudaGraphExec_t> graphs;
     int* d_err = nullptr;                 // device error flag (plasticity, exchange)
     bool use_graphs = true;
+    int32_t walk_chunk = 128;             // synapses per warp unit of the STDP walks
     // partition over GPUs
     int32_t rank = 0, world = 1;
     ncclComm_t comm = nullptr;
@@ -166,6 +169,9 @@ struct nrn_engine {
         cudaFree(raster_step); cudaFree(raster_gid);
         cudaFree(send); cudaFree(recv);
         if (comm) ncclCommDestroy(comm);
+        if (fork_ev) cudaEventDestroy(fork_ev);
+        if (join_ev) cudaEventDestroy(join_ev);
+        if (side) cudaStreamDestroy(side);
         if (stream) cudaStreamDestroy(stream);
     }
 
@@ -348,6 +354,7 @@ struct nrn_engine {
         a.sweep_period = kSweepPeriod;
         a.sweep_rows = (q.csr.n_src + kSweepPeriod - 1) / kSweepPeriod;
         a.stale = kStale;
+        a.chunk = walk_chunk;
         a.err = d_err;
         a.events = d_events;
         return a;
@@ -479,17 +486,30 @@ struct nrn_engine {
         std::vector<nrn_spike_hist_t> hs;
         for (size_t i = 0; i < pops.size(); ++i) hs.push_back(hist(static_cast<int>(i)));
         if (ev) NRN_CUDA_TRY(cudaEventRecord(ev[0], stream));
+        bool any_walk = false;
+        for (auto& q : projs) any_walk = any_walk || q.walk;
+        // Static delivery (which also clears this step's history slots) and the
+        // STDP walks touch different history slots and only add into the
+        // accumulators: with walks, the delivery runs on the side stream.
+        cudaStream_t ds = any_walk ? side : stream;
+        if (any_walk) {
+            NRN_CUDA_TRY(cudaEventRecord(fork_ev, stream));
+            NRN_CUDA_TRY(cudaStreamWaitEvent(side, fork_ev, 0));
+        }
         NRN_TRY(nrn_cuda_deliver_counted(dp.data(), static_cast<int32_t>(dp.size()), hs.data(),
                                          static_cast<int32_t>(hs.size()), off,
                                          reinterpret_cast<const int64_t*>(d_step), d_events,
-                                         reinterpret_cast<nrn_stream_t>(stream)));
+                                         reinterpret_cast<nrn_stream_t>(ds)));
         for (auto& q : projs)
             if (q.walk) NRN_TRY(walk_launch(walk_args(q), WALK_STEP, off, d_step, stream));
-        if (ev) NRN_CUDA_TRY(cudaEventRecord(ev[1], stream));
-        for (size_t i = 0; i < pops.size(); ++i) {
-            nrn_pop_step_t a = pop_args(static_cast<int>(i), dt, off, true);
-            NRN_TRY(nrn_cuda_pop_step(&a, reinterpret_cast<nrn_stream_t>(stream)));
+        if (any_walk) {
+            NRN_CUDA_TRY(cudaEventRecord(join_ev, side));
+            NRN_CUDA_TRY(cudaStreamWaitEvent(stream, join_ev, 0));
         }
+        if (ev) NRN_CUDA_TRY(cudaEventRecord(ev[1], stream));
+        std::vector<nrn_pop_step_t> pa;
+        for (size_t i = 0; i < pops.size(); ++i) pa.push_back(pop_args(static_cast<int>(i), dt, off, true));
+        NRN_TRY(pop_step_group(pa.data(), static_cast<int>(pa.size()), stream));
         if (ev) NRN_CUDA_TRY(cudaEventRecord(ev[2], stream));
         for (auto& q : projs) {
             if (!q.plastic || q.walk) continue;
@@ -632,7 +652,14 @@ nrn_status_t nrn_engine_create(nrn_engine** out, int device, double dt, int32_t 
     e->slow_ratio = slow_ratio;
     const char* ng = std::getenv("NRN_NO_GRAPHS");
     e->use_graphs = !(ng && ng[0] == '1');
+    if (const char* wc = std::getenv("NRN_WALK_CHUNK")) {
+        const int c = std::atoi(wc);
+        if (c >= 32 && c % 32 == 0 && c <= 4096) e->walk_chunk = c;
+    }
     NRN_CUDA_TRY(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
+    NRN_CUDA_TRY(cudaStreamCreateWithFlags(&e->side, cudaStreamNonBlocking));
+    NRN_CUDA_TRY(cudaEventCreateWithFlags(&e->fork_ev, cudaEventDisableTiming));
+    NRN_CUDA_TRY(cudaEventCreateWithFlags(&e->join_ev, cudaEventDisableTiming));
     NRN_TRY(dalloc0(&e->d_step, 1, e->stream));
     NRN_TRY(dalloc0(&e->d_events, 1, e->stream));
     NRN_TRY(dalloc0(&e->d_raster_count, 1, e->stream));
@@ -963,7 +990,12 @@ nrn_status_t nrn_engine_finalize(nrn_engine* e, int32_t init_update) {
     };
     // target traces: a source spike being applied is at most the longest
     // delay (+1) older than the walk
-    e->ring_depth = maxd + 2;
+    auto pow2 = [](int x) {
+        int p = 1;
+        while (p < x) p <<= 1;
+        return p;
+    };
+    e->ring_depth = pow2(maxd + 2);
     for (auto& q : e->projs) {
         if (!q.walk) continue;
         const size_t nseg = static_cast<size_t>(q.csr.n_src) * q.csr.nd;
@@ -971,7 +1003,7 @@ nrn_status_t nrn_engine_finalize(nrn_engine* e, int32_t init_update) {
         NRN_TRY(dalloc0(&q.seg_x, nseg, e->stream));
         NRN_TRY(dalloc0(&q.seg_done, nseg, e->stream));
         const int dmax = q.csr.dmin + q.csr.nd - 1;
-        q.pre_depth = (kSweepPeriod + kStale + e->win + dmax) / e->win + 4;
+        q.pre_depth = pow2((kSweepPeriod + kStale + e->win + dmax) / e->win + 4);
         NRN_TRY(dalloc0(&q.pre_snap, static_cast<size_t>(q.pre_depth) * q.csr.n_src, e->stream));
         NRN_TRY(dalloc0(&q.post_ring, static_cast<size_t>(e->ring_depth) * q.csr.n_tgt, e->stream));
         NRN_TRY(need_history(e->pops[q.src_pop]));

@@ -43,9 +43,9 @@ __global__ void __launch_bounds__(kThreads) window_kernel(const __grid_constant_
             const SnapTask& t = a.task[k];
             if (j < t.lo || j >= t.hi) continue;
             const long long col = j - t.lo;
-            float x = t.snap[static_cast<long long>((m - 1) % t.depth) * t.stride + col];
+            float x = t.snap[static_cast<long long>((m - 1) & (t.depth - 1)) * t.stride + col];
             for (int u = 0; u < a.win; ++u) x = x * t.decay + (((bits >> u) & 1u) ? 1.0f : 0.0f);
-            t.snap[static_cast<long long>(m % t.depth) * t.stride + col] = x;
+            t.snap[static_cast<long long>(m & (t.depth - 1)) * t.stride + col] = x;
         }
         if (bits == 0) continue;
         a.mask[j] = 0;
@@ -109,6 +109,9 @@ __global__ void __launch_bounds__(kThreads) unpack_kernel(const __grid_constant_
 
 nrn_status_t window_launch(const WindowArgs& a, long long step_off, const long long* step_base, cudaStream_t s) {
     NRN_CHECK_ARG(a.win >= 1 && a.win <= 32 && a.n_task >= 0 && a.n_task <= 4, "window: bad arguments");
+    for (int k = 0; k < a.n_task; ++k)
+        NRN_CHECK_ARG(a.task[k].depth > 0 && (a.task[k].depth & (a.task[k].depth - 1)) == 0,
+                      "window: snapshot depth must be a power of two");
     if (a.n <= 0) return NRN_OK;
     const int blocks = static_cast<int>(std::min<long long>((a.n + kThreads - 1) / kThreads, 16LL * sm_count_current()));
     window_kernel<<<blocks, kThreads, 0, s>>>(a, step_off, step_base);

@@ -55,6 +55,10 @@ nrn_status_t generate(const GenArgs& g, int32_t* src, int32_t* tgt, float* w, ui
 
 int sm_count_current();
 
+// Neuron updates of several populations; populations of the same model and
+// kind share one launch (neuron.cu).
+nrn_status_t pop_step_group(const nrn_pop_step_t* list, int n, cudaStream_t s);
+
 // Pair STDP applied by segment walks (plastic.cu).  Steps are int32.
 enum { WALK_STEP = 0, WALK_FLUSH = 1 };
 struct WalkArgs {
@@ -92,6 +96,7 @@ struct WalkArgs {
     int64_t sweep_rows = 0;           // rows looked at per step by the sweep
     int32_t sweep_period = 1;         // steps for the sweep to pass every row
     int32_t stale = 1;                // the sweep walks a segment not walked for this many steps
+    int32_t chunk = 128;              // synapses per warp work unit (multiple of 32)
     int* err = nullptr;
     unsigned long long* events = nullptr;
 };

@@ -16,8 +16,10 @@
 #include <cuda_runtime.h>
 
 #include <cmath>
+#include <vector>
 
 #include "common.cuh"
+#include "internal.h"
 #include "rng.cuh"
 
 namespace nrn {
@@ -92,9 +94,10 @@ __device__ __forceinline__ float drive_value(const PopArgs& a, uint32_t gid, uin
     return a.d1 * static_cast<float>(k);
 }
 
+// One neuron of one population: every thread of a warp belongs to the same
+// population (the compaction below is warp-wide).
 template <int MODEL, bool HET, bool COND>
-__global__ void __launch_bounds__(256) pop_step_kernel(const __grid_constant__ PopArgs a) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+__device__ __forceinline__ void pop_body(const PopArgs& a, const int i) {
     const bool valid = i < a.n;
     int spiked = 0;
     long long step = a.step;
@@ -185,9 +188,9 @@ __global__ void __launch_bounds__(256) pop_step_kernel(const __grid_constant__ P
             const float sp = spiked ? 1.0f : 0.0f;
             for (int k = 0; k < a.n_traces; ++k) {
                 if (a.trace_ring[k] != nullptr) {
-                    const long long D = a.trace_ring_depth;
-                    const float prev = a.trace_ring[k][((step + D - 1) % D) * a.n + i];
-                    a.trace_ring[k][(step % D) * a.n + i] = prev * a.trace_decay[k] + sp;
+                    const long long mask = a.trace_ring_depth - 1;   // depth is a power of two
+                    const float prev = a.trace_ring[k][((step - 1) & mask) * a.n + i];
+                    a.trace_ring[k][(step & mask) * a.n + i] = prev * a.trace_decay[k] + sp;
                 } else {
                     a.trace[k][i] = a.trace[k][i] * a.trace_decay[k] + sp;
                 }
@@ -257,26 +260,58 @@ __global__ void __launch_bounds__(256) pop_step_kernel(const __grid_constant__ P
     }
 }
 
-template <int MODEL>
-void launch_model(const PopArgs& a, bool het, bool cond, cudaStream_t s) {
-    const int threads = 256;
-    const int blocks = (a.n + threads - 1) / threads;
-    if (het) {
-        if (cond) pop_step_kernel<MODEL, true, true><<<blocks, threads, 0, s>>>(a);
-        else pop_step_kernel<MODEL, true, false><<<blocks, threads, 0, s>>>(a);
-    } else {
-        if (cond) pop_step_kernel<MODEL, false, true><<<blocks, threads, 0, s>>>(a);
-        else pop_step_kernel<MODEL, false, false><<<blocks, threads, 0, s>>>(a);
+template <int MODEL, bool HET, bool COND>
+__global__ void __launch_bounds__(256) pop_step_kernel(const __grid_constant__ PopArgs a) {
+    pop_body<MODEL, HET, COND>(a, blockIdx.x * blockDim.x + threadIdx.x);
+}
+
+// Several populations of the same kind in one launch, block ranges
+// [start[q], start[q+1]) for population q.
+constexpr int kMaxGroup = 4;
+struct PopGroup {
+    PopArgs p[kMaxGroup];
+    int start[kMaxGroup + 1];
+    int n;
+};
+
+template <int MODEL, bool HET, bool COND>
+__global__ void __launch_bounds__(256) pop_group_kernel(const __grid_constant__ PopGroup g) {
+    int q = 0;
+    while (q + 1 < g.n && static_cast<int>(blockIdx.x) >= g.start[q + 1]) ++q;
+    pop_body<MODEL, HET, COND>(g.p[q], (static_cast<int>(blockIdx.x) - g.start[q]) * blockDim.x + threadIdx.x);
+}
+
+constexpr int kPopThreads = 256;
+
+template <int MODEL, bool HET, bool COND>
+void launch_kind(const PopGroup& g, cudaStream_t s) {
+    if (g.n == 1) pop_step_kernel<MODEL, HET, COND><<<g.start[1], kPopThreads, 0, s>>>(g.p[0]);
+    else pop_group_kernel<MODEL, HET, COND><<<g.start[g.n], kPopThreads, 0, s>>>(g);
+}
+
+void launch_group(const PopGroup& g, int model, bool het, bool cond, cudaStream_t s) {
+    switch (model) {
+        case NRN_MODEL_LIF:
+            het ? launch_kind<NRN_MODEL_LIF, true, false>(g, s) : launch_kind<NRN_MODEL_LIF, false, false>(g, s);
+            break;
+        case NRN_MODEL_ADEX:
+            if (het) cond ? launch_kind<NRN_MODEL_ADEX, true, true>(g, s) : launch_kind<NRN_MODEL_ADEX, true, false>(g, s);
+            else cond ? launch_kind<NRN_MODEL_ADEX, false, true>(g, s) : launch_kind<NRN_MODEL_ADEX, false, false>(g, s);
+            break;
+        default:
+            het ? launch_kind<NRN_MODEL_IZH, true, false>(g, s) : launch_kind<NRN_MODEL_IZH, false, false>(g, s);
+            break;
     }
 }
 
 }  // namespace
 }  // namespace nrn
 
-extern "C" nrn_status_t nrn_cuda_pop_step(const nrn_pop_step_t* in, nrn_stream_t stream) {
-    using namespace nrn;
-    NRN_CHECK_ARG(in != nullptr, "nrn_cuda_pop_step: null arguments");
-    const nrn_pop_step_t& d = *in;
+namespace nrn {
+namespace {
+
+// Checks one population's arguments and converts them for the kernel.
+nrn_status_t make_args(const nrn_pop_step_t& d, PopArgs& a, bool& het, bool& cond) {
     NRN_CHECK_ARG(d.model >= NRN_MODEL_LIF && d.model <= NRN_MODEL_IZH, "nrn_cuda_pop_step: unknown model");
     NRN_CHECK_ARG(d.n >= 0, "nrn_cuda_pop_step: neuron count must be >= 0");
     if (d.n == 0) return NRN_OK;
@@ -291,12 +326,12 @@ extern "C" nrn_status_t nrn_cuda_pop_step(const nrn_pop_step_t* in, nrn_stream_t
                   "nrn_cuda_pop_step: raster needs step and count arrays");
     NRN_CHECK_ARG(d.drive.kind >= NRN_DRIVE_NONE && d.drive.kind <= NRN_DRIVE_POISSON_GEXC,
                   "nrn_cuda_pop_step: unknown drive kind");
-    const bool cond = d.gin_exc != nullptr;
+    cond = d.gin_exc != nullptr;
     NRN_CHECK_ARG(!cond || (d.model == NRN_MODEL_ADEX && d.g_exc && d.g_inh && d.gin_inh),
                   "nrn_cuda_pop_step: conductance input needs an AdEx population and all four arrays");
     NRN_CHECK_ARG(d.drive.kind != NRN_DRIVE_POISSON_GEXC || cond,
                   "nrn_cuda_pop_step: conductance drive needs conductance input");
-    PopArgs a{};
+    a = PopArgs{};
     a.n = d.n;
     a.gid_offset = d.gid_offset;
     a.dtf = static_cast<float>(d.dt);
@@ -312,7 +347,7 @@ extern "C" nrn_status_t nrn_cuda_pop_step(const nrn_pop_step_t* in, nrn_stream_t
     a.e_inh = d.e_inh;
     a.v = d.v; a.aux = d.aux; a.ref = d.refractory; a.spike = d.spike; a.i_syn = d.i_syn;
     a.g_exc = d.g_exc; a.g_inh = d.g_inh; a.gin_exc = d.gin_exc; a.gin_inh = d.gin_inh;
-    bool het = false;
+    het = false;
     for (int k = 0; k < NRN_MAX_PARAMS; ++k) {
         a.param[k] = d.param[k];
         a.uniform[k] = d.uniform[k];
@@ -338,6 +373,8 @@ extern "C" nrn_status_t nrn_cuda_pop_step(const nrn_pop_step_t* in, nrn_stream_t
     a.n_traces = d.n_traces;
     a.trace_slow_ratio = d.trace_slow_ratio;
     a.trace_ring_depth = d.trace_ring_depth;
+    NRN_CHECK_ARG(d.trace_ring_depth <= 0 || (d.trace_ring_depth & (d.trace_ring_depth - 1)) == 0,
+                  "nrn_cuda_pop_step: trace ring depth must be a power of two");
     for (int k = 0; k < d.n_traces; ++k) {
         NRN_CHECK_ARG(d.trace[k] != nullptr || (d.trace_ring[k] != nullptr && d.trace_ring_depth > 0),
                       "nrn_cuda_pop_step: null trace array");
@@ -363,12 +400,45 @@ extern "C" nrn_status_t nrn_cuda_pop_step(const nrn_pop_step_t* in, nrn_stream_t
     a.err = d.err;
     NRN_CHECK_ARG(a.send_hdr == nullptr || (d.send_ids != nullptr && d.send_cap >= 0),
                   "nrn_cuda_pop_step: send buffer without ids");
-    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    switch (d.model) {
-        case NRN_MODEL_LIF: launch_model<NRN_MODEL_LIF>(a, het, false, s); break;
-        case NRN_MODEL_ADEX: launch_model<NRN_MODEL_ADEX>(a, het, cond, s); break;
-        default: launch_model<NRN_MODEL_IZH>(a, het, false, s); break;
-    }
-    NRN_CUDA_TRY(cudaGetLastError());
+    if (d.model != NRN_MODEL_ADEX) cond = false;
     return NRN_OK;
+}
+
+}  // namespace
+
+nrn_status_t pop_step_group(const nrn_pop_step_t* list, int n, cudaStream_t s) {
+    NRN_CHECK_ARG(n >= 0 && (n == 0 || list != nullptr), "pop_step_group: bad arguments");
+    std::vector<char> done(static_cast<size_t>(n), 0);
+    for (int q = 0; q < n; ++q) {
+        if (done[q]) continue;
+        PopGroup g{};
+        bool het = false, cond = false;
+        NRN_TRY(make_args(list[q], g.p[0], het, cond));
+        done[q] = 1;
+        if (list[q].n == 0) continue;
+        g.n = 1;
+        g.start[1] = (list[q].n + kPopThreads - 1) / kPopThreads;
+        // later populations of the same kind join this launch
+        for (int r = q + 1; r < n && g.n < kMaxGroup; ++r) {
+            if (done[r] || list[r].n == 0 || list[r].model != list[q].model) continue;
+            PopArgs x;
+            bool h2 = false, c2 = false;
+            NRN_TRY(make_args(list[r], x, h2, c2));
+            if (h2 != het || c2 != cond) continue;
+            g.p[g.n] = x;
+            g.start[g.n + 1] = g.start[g.n] + (list[r].n + kPopThreads - 1) / kPopThreads;
+            ++g.n;
+            done[r] = 1;
+        }
+        launch_group(g, list[q].model, het, cond, s);
+        NRN_CUDA_TRY(cudaGetLastError());
+    }
+    return NRN_OK;
+}
+
+}  // namespace nrn
+
+extern "C" nrn_status_t nrn_cuda_pop_step(const nrn_pop_step_t* in, nrn_stream_t stream) {
+    NRN_CHECK_ARG(in != nullptr, "nrn_cuda_pop_step: null arguments");
+    return nrn::pop_step_group(in, 1, reinterpret_cast<cudaStream_t>(stream));
 }

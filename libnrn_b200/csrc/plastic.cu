@@ -28,7 +28,7 @@
 // of the source (newest four per neuron, older ones in a ring for the
 // neurons of this GPU) and of each target.
 //
-// Work unit: one warp per (arriving spike, segment chunk of 128 synapses);
+// Work unit: one warp per (arriving spike, segment chunk of `chunk` synapses);
 // the last chunk of a segment to finish advances the segment's T.
 #include <cuda_runtime.h>
 
@@ -45,7 +45,6 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kChunk = 128;      // synapses per warp unit (4 per lane)
 constexpr int kMaxPost = 64;     // target spike steps one walk may need (the ring depth)
 constexpr int kMaxPre = 8;       // source spike steps one walk may need
 constexpr int kMaxSpan = 1280;   // steps one walk may cover (x_pre table per warp)
@@ -143,10 +142,17 @@ struct Seg {
     const float* X;   // x_pre(T + 1 + u) at X[u], u < e - T (per-warp shared memory)
 };
 
+// Target trace at source spike t (xp0: already loaded for the first one).
+__device__ __forceinline__ float x_post_at(const WalkArgs& a, const Seg& g, uint32_t i, int t, int now, float xp0) {
+    if (t == g.P[0]) return xp0;
+    if (now - t >= a.post_depth) set_err(a.err, ERR_SNAPSHOT);
+    return a.post_ring[static_cast<long long>(t & (a.post_depth - 1)) * a.n_tgt + i];
+}
+
 // One synapse: every update in (T, e], oldest first.
 template <class L>
 __device__ __forceinline__ float apply_events(const WalkArgs& a, const Seg& g, const L& Q, uint32_t i, float w,
-                                              float mod, int now) {
+                                              float mod, int now, float xp0) {
     int p = 0, q = 0;
     while (p < g.P.n || q < Q.n) {
         const int tp = p < g.P.n ? g.P[p] : INT_MAX;
@@ -154,11 +160,7 @@ __device__ __forceinline__ float apply_events(const WalkArgs& a, const Seg& g, c
         const int t = tp < tq ? tp : tq;
         const bool pre = tp == t, post = tq == t;
         const float xpre = post ? g.X[t - g.T - 1] : 0.0f;
-        float xpost = 0.0f;
-        if (pre) {
-            if (now - t >= a.post_depth) set_err(a.err, ERR_SNAPSHOT);
-            xpost = a.post_ring[static_cast<long long>(t % a.post_depth) * a.n_tgt + i];
-        }
+        const float xpost = pre ? x_post_at(a, g, i, t, now, xp0) : 0.0f;
         const float dw = (a.a_plus * xpre) * (post ? 1.0f : 0.0f) - (a.a_minus * xpost) * (pre ? 1.0f : 0.0f);
         float upd = (dw * a.lr) * 1.0f;
         if (a.mod) upd = upd * mod;
@@ -170,7 +172,7 @@ __device__ __forceinline__ float apply_events(const WalkArgs& a, const Seg& g, c
 }
 
 __device__ __noinline__ float walk_syn_long(const WalkArgs& a, const Seg& g, uint32_t i, int4 r, float w, float mod,
-                                            int now) {
+                                            int now, float xp0) {
     int buf[kMaxPost];
     StepsPtr Q;
     Q.p = buf;
@@ -179,14 +181,48 @@ __device__ __noinline__ float walk_syn_long(const WalkArgs& a, const Seg& g, uin
         set_err(a.err, ERR_HISTORY);
         return w;
     }
-    return apply_events(a, g, Q, i, w, mod, now);
+    return apply_events(a, g, Q, i, w, mod, now, xp0);
 }
 
-__device__ __forceinline__ float walk_syn(const WalkArgs& a, const Seg& g, uint32_t i, int4 r, float w, float mod,
-                                          int now) {
+// w after one update of the reference's rule with the given spike flags and
+// traces (stdp.cpp:130-139): dw = (A+ x_pre) post - (A- x_post) pre.
+__device__ __forceinline__ float stdp_apply1(const WalkArgs& a, float w, float mod, float xpre, float post, float xpost,
+                                             float pre) {
+    const float dw = (a.a_plus * xpre) * post - (a.a_minus * xpost) * pre;
+    float upd = (dw * a.lr) * 1.0f;
+    if (a.mod) upd = upd * mod;
+    return clampw(w + upd, a.w_min, a.w_max);
+}
+
+// The common case, straight-line: one source spike t1 in (T, e] and the
+// target's spikes in (T, e] among its newest four (r, newest first).
+// Target spikes before t1, then t1 (with the target's own spike at t1 if
+// any), then target spikes after t1 -- the order of apply_events.
+__device__ __forceinline__ float walk_one_pre(const WalkArgs& a, const Seg& g, int t1, int4 r, float w, float mod,
+                                              float xp0) {
+    const int q4[4] = {r.w, r.z, r.y, r.x};   // oldest first
+    bool coincide = false;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int q = q4[k];
+        if (q > g.T && q < t1) w = stdp_apply1(a, w, mod, g.X[q - g.T - 1], 1.0f, 0.0f, 0.0f);
+        coincide = coincide || q == t1;
+    }
+    w = stdp_apply1(a, w, mod, coincide ? g.X[t1 - g.T - 1] : 0.0f, coincide ? 1.0f : 0.0f, xp0, 1.0f);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int q = q4[k];
+        if (q > t1 && q <= g.e) w = stdp_apply1(a, w, mod, g.X[q - g.T - 1], 1.0f, 0.0f, 0.0f);
+    }
+    return w;
+}
+
+__device__ __forceinline__ float walk_syn(const WalkArgs& a, const Seg& g, int t1, uint32_t i, int4 r, float w,
+                                          float mod, int now, float xp0) {
+    if (g.P.n == 1 && r.w <= g.T) return walk_one_pre(a, g, t1, r, w, mod, xp0);
     if (g.P.n == 0 && r.x <= g.T) return w;   // nothing happened to this synapse
-    if (r.w <= g.T) return apply_events(a, g, steps_from4(r, g.T, g.e), i, w, mod, now);
-    return walk_syn_long(a, g, i, r, w, mod, now);
+    if (r.w <= g.T) return apply_events(a, g, steps_from4(r, g.T, g.e), i, w, mod, now, xp0);
+    return walk_syn_long(a, g, i, r, w, mod, now, xp0);
 }
 
 // Loads the segment's state, the source's spikes in (T, e] and the source
@@ -244,7 +280,7 @@ __device__ __forceinline__ bool load_seg(const WalkArgs& a, Seg& g, int* sP, flo
             const int m = m0 + pc - 1;
             start = m * W - 1;
             if (m_new - m >= a.pre_depth) set_err(a.err, ERR_SNAPSHOT);
-            x = a.pre_snap[static_cast<long long>(m % a.pre_depth) * a.pre_stride + j];
+            x = a.pre_snap[static_cast<long long>(m & (a.pre_depth - 1)) * a.pre_stride + j];
         }
         const int stop = pc == 0 ? (m0 * W - 1 < e ? m0 * W - 1 : e) : (start + W < e ? start + W : e);
         int q = 0;
@@ -272,15 +308,21 @@ __device__ __forceinline__ unsigned walk_chunk(const WalkArgs& a, const Seg& g, 
                                                bool deliver, int now, int lane) {
     struct Syn {
         uint32_t t;
-        float w, md;
+        float w, md, xp0;
         int4 r;
     };
+    // the target trace at the first source spike is loaded with the target's spike steps
+    const bool has_pre = g.P.n > 0;
+    const int t0 = has_pre ? g.P[0] : 0;
+    if (has_pre && now - t0 >= a.post_depth) set_err(a.err, ERR_SNAPSHOT);
+    const float* ring0 = a.post_ring + static_cast<long long>(t0 & (a.post_depth - 1)) * a.n_tgt;
     auto load = [&](long long syn) {
         Syn x;
         x.t = __ldcs(a.tgt + syn);
         x.w = a.w[syn];
         x.md = a.mod ? __ldcs(a.mod + syn) : 1.0f;
         x.r = a.tgt_recent[x.t];
+        x.xp0 = has_pre ? ring0[x.t] : 0.0f;
         return x;
     };
     unsigned n = 0;
@@ -291,7 +333,7 @@ __device__ __forceinline__ unsigned walk_chunk(const WalkArgs& a, const Seg& g, 
     for (; syn < c1; syn += 32) {
         Syn nxt{};
         if (syn + 32 < c1) nxt = load(syn + 32);
-        const float w1 = walk_syn(a, g, cur.t, cur.r, cur.w, cur.md, now);
+        const float w1 = walk_syn(a, g, t0, cur.t, cur.r, cur.w, cur.md, now, cur.xp0);
         if (__float_as_uint(w1) != __float_as_uint(cur.w)) a.w[syn] = w1;
         if (deliver) {
             atomicAdd(a.acc + cur.t, a.mod ? w1 * cur.md : w1);
@@ -308,7 +350,7 @@ __device__ __forceinline__ void finish_seg(const WalkArgs& a, const Seg& g) {
     a.seg_last[g.seg] = g.e;
 }
 
-// One chunk of kChunk synapses of segment (j, k): applies the updates
+// One chunk of a.chunk synapses of segment (j, k): applies the updates
 // through e (and, with deliver, delivers the updated weights); the last
 // chunk of the segment to finish records the segment's new state.  Every
 // chunk of a segment reads the same state (the write happens only after
@@ -318,9 +360,9 @@ __device__ unsigned segment_chunk(const WalkArgs& a, int* sP, float* sX, int j, 
                                   bool deliver, int now, int m_new, int lane) {
     const long long seg = static_cast<long long>(j) * a.nd + k;
     const long long s0 = a.seg_ptr[seg], s1 = a.seg_ptr[seg + 1];
-    const long long c0 = s0 + static_cast<long long>(chunk) * kChunk;
+    const long long c0 = s0 + static_cast<long long>(chunk) * a.chunk;
     if (c0 >= s1) return 0;
-    const long long c1 = c0 + kChunk < s1 ? c0 + kChunk : s1;
+    const long long c1 = c0 + a.chunk < s1 ? c0 + a.chunk : s1;
     Seg g;
     const bool pending = load_seg(a, g, sP, sX, j, k, e, m_new, lane);
     unsigned n = 0;
@@ -328,7 +370,7 @@ __device__ unsigned segment_chunk(const WalkArgs& a, int* sP, float* sX, int j, 
         n = walk_chunk(a, g, c0, c1, deliver, now, lane);
         __syncwarp();
         if (lane == 0) {
-            const int n_chunks = static_cast<int>((s1 - s0 + kChunk - 1) / kChunk);
+            const int n_chunks = static_cast<int>((s1 - s0 + a.chunk - 1) / a.chunk);
             __threadfence();
             const int done = atomicAdd(a.seg_done + seg, 1);
             if (done == n_chunks - 1) {
@@ -348,7 +390,7 @@ __device__ unsigned segment_chunk(const WalkArgs& a, int* sP, float* sX, int j, 
     return n;
 }
 
-__global__ void __launch_bounds__(kThreads) walk_kernel(const __grid_constant__ WalkArgs a, int mode,
+__global__ void __launch_bounds__(kThreads, 4) walk_kernel(const __grid_constant__ WalkArgs a, int mode,
                                                         long long step_off, const long long* step_base) {
     using Scan = cub::BlockScan<long long, kThreads>;
     __shared__ typename Scan::TempStorage scan_tmp;
@@ -366,7 +408,7 @@ __global__ void __launch_bounds__(kThreads) walk_kernel(const __grid_constant__ 
     const long long warp = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
     const long long n_warps = (static_cast<long long>(gridDim.x) * kThreads) >> 5;
 
-    const int chunks = (a.max_seg + kChunk - 1) / kChunk > 0 ? (a.max_seg + kChunk - 1) / kChunk : 1;
+    const int chunks = (a.max_seg + a.chunk - 1) / a.chunk > 0 ? (a.max_seg + a.chunk - 1) / a.chunk : 1;
     const long long per_row = static_cast<long long>(a.nd) * chunks;   // units of one source row
 
     if (mode == WALK_FLUSH) {
@@ -412,15 +454,15 @@ __global__ void __launch_bounds__(kThreads) walk_kernel(const __grid_constant__ 
                 if (start[mid] <= u) lo = mid; else hi = mid - 1;
             }
             const int k = lo;
-            const long long local = u - start[k];
-            const long long spike = local / chunks;
-            const int chunk = static_cast<int>(local - spike * chunks);
+            const int local = static_cast<int>(u - start[k]);   // < spikes * chunks of one slot
+            const int spike = local / chunks;
+            const int chunk = local - spike * chunks;
             const int j = a.hist_src.ids[static_cast<long long>(slot[k]) * a.hist_src.cap + spike];
             my_events += segment_chunk(a, sP, sX, j, k, chunk, now - 1, true, now, m_new, lane);
         } else {
-            const long long q = u - n_arr;
-            const long long row = q / per_row;
-            const int rem = static_cast<int>(q - row * per_row);
+            const int q = static_cast<int>(u - n_arr);   // < sweep rows * per_row
+            const int row = q / static_cast<int>(per_row);
+            const int rem = q - row * static_cast<int>(per_row);
             const int j = static_cast<int>(r0 + row);
             const int k = rem / chunks;
             // rows with spikes still to arrive are walked by those arrivals;
@@ -442,6 +484,10 @@ nrn_status_t walk_launch(const WalkArgs& a, int mode, long long step_off, const 
                          cudaStream_t s) {
     NRN_CHECK_ARG(a.nd >= 1 && a.nd <= 256, "plastic projection: at most 256 delay values");
     NRN_CHECK_ARG(a.win >= 1 && a.sweep_period >= 1, "plastic projection: bad window or sweep period");
+    NRN_CHECK_ARG(a.chunk >= 32 && a.chunk % 32 == 0, "plastic projection: chunk must be a multiple of 32");
+    NRN_CHECK_ARG(a.pre_depth > 0 && (a.pre_depth & (a.pre_depth - 1)) == 0 && a.post_depth > 0 &&
+                      (a.post_depth & (a.post_depth - 1)) == 0,
+                  "plastic projection: trace ring depths must be powers of two");
     int per_sm = 0;
     NRN_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, walk_kernel, kThreads, 0));
     const int blocks = std::max(1, per_sm) * sm_count_current();
