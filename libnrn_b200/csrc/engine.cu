@@ -112,7 +112,7 @@ struct EngineProj {
 
 constexpr int kRing = 64;           // spike steps kept per neuron
 constexpr int kSweepPeriod = 640;   // the sweep looks at every row this often
-constexpr int kStale = 320;         // and walks segments not walked for this many steps
+constexpr int kStale = 480;         // and walks segments not walked for this many steps
 
 struct nrn_engine {
     int device = 0;

@@ -45,6 +45,10 @@ struct PopArgs {
     float uniform[NRN_MAX_PARAMS];
     int drive_kind;
     float d0, d1, d_exp;       // drive parameters, expf(-lambda)
+    // Poisson CDF F_0..F_{n_cdf-1} of the drive, built on the host with the
+    // sampler's own float operations (p_k = p_{k-1}*lambda/k, F_k = F_{k-1}+p_k)
+    float cdf[32];
+    int n_cdf;
     uint64_t seed;
     int64_t step;
     const int64_t* step_base;
@@ -90,7 +94,12 @@ __device__ __forceinline__ float drive_value(const PopArgs& a, uint32_t gid, uin
         float z = normal_bm(u01(w.x), u01(w.y));
         return a.d0 + a.d1 * z;
     }
-    int k = poisson_inv(u01(w.x), a.d0, a.d_exp);
+    // the first k with u <= F_k, from the table (the same values the loop of
+    // poisson_inv adds up); past the table, the loop itself
+    const float u = u01(w.x);
+    int k = 0;
+    while (k < a.n_cdf && u > a.cdf[k]) ++k;
+    if (k == a.n_cdf) k = poisson_inv(u, a.d0, a.d_exp);
     return a.d1 * static_cast<float>(k);
 }
 
@@ -357,6 +366,21 @@ nrn_status_t make_args(const nrn_pop_step_t& d, PopArgs& a, bool& het, bool& con
     a.d0 = d.drive.p0;
     a.d1 = d.drive.p1;
     a.d_exp = static_cast<float>(std::exp(-static_cast<double>(d.drive.p0)));
+    a.n_cdf = 0;
+    if (d.drive.kind == NRN_DRIVE_POISSON_CURRENT || d.drive.kind == NRN_DRIVE_POISSON_GEXC) {
+        // host float arithmetic, one rounding per operation (no contraction
+        // is possible: a product then a quotient, and separate sums)
+        volatile float p = a.d_exp, F = p;
+        a.cdf[0] = F;
+        a.n_cdf = 1;
+        for (int k = 1; k < 32; ++k) {
+            const float pl = p * a.d0;
+            p = pl / static_cast<float>(k);
+            F = F + p;
+            a.cdf[k] = F;
+            a.n_cdf = k + 1;
+        }
+    }
     a.seed = d.drive.seed;
     a.step = d.step;
     a.step_base = d.step_base;

@@ -150,7 +150,7 @@ __device__ __forceinline__ float x_post_at(const WalkArgs& a, const Seg& g, uint
 }
 
 // One synapse: every update in (T, e], oldest first.
-template <class L>
+template <bool MOD, class L>
 __device__ __forceinline__ float apply_events(const WalkArgs& a, const Seg& g, const L& Q, uint32_t i, float w,
                                               float mod, int now, float xp0) {
     int p = 0, q = 0;
@@ -163,7 +163,7 @@ __device__ __forceinline__ float apply_events(const WalkArgs& a, const Seg& g, c
         const float xpost = pre ? x_post_at(a, g, i, t, now, xp0) : 0.0f;
         const float dw = (a.a_plus * xpre) * (post ? 1.0f : 0.0f) - (a.a_minus * xpost) * (pre ? 1.0f : 0.0f);
         float upd = (dw * a.lr) * 1.0f;
-        if (a.mod) upd = upd * mod;
+        if (MOD) upd = upd * mod;
         w = clampw(w + upd, a.w_min, a.w_max);
         if (pre) ++p;
         if (post) ++q;
@@ -171,6 +171,7 @@ __device__ __forceinline__ float apply_events(const WalkArgs& a, const Seg& g, c
     return w;
 }
 
+template <bool MOD>
 __device__ __noinline__ float walk_syn_long(const WalkArgs& a, const Seg& g, uint32_t i, int4 r, float w, float mod,
                                             int now, float xp0) {
     int buf[kMaxPost];
@@ -181,16 +182,17 @@ __device__ __noinline__ float walk_syn_long(const WalkArgs& a, const Seg& g, uin
         set_err(a.err, ERR_HISTORY);
         return w;
     }
-    return apply_events(a, g, Q, i, w, mod, now, xp0);
+    return apply_events<MOD>(a, g, Q, i, w, mod, now, xp0);
 }
 
 // w after one update of the reference's rule with the given spike flags and
 // traces (stdp.cpp:130-139): dw = (A+ x_pre) post - (A- x_post) pre.
+template <bool MOD>
 __device__ __forceinline__ float stdp_apply1(const WalkArgs& a, float w, float mod, float xpre, float post, float xpost,
                                              float pre) {
     const float dw = (a.a_plus * xpre) * post - (a.a_minus * xpost) * pre;
     float upd = (dw * a.lr) * 1.0f;
-    if (a.mod) upd = upd * mod;
+    if (MOD) upd = upd * mod;
     return clampw(w + upd, a.w_min, a.w_max);
 }
 
@@ -198,6 +200,7 @@ __device__ __forceinline__ float stdp_apply1(const WalkArgs& a, float w, float m
 // target's spikes in (T, e] among its newest four (r, newest first).
 // Target spikes before t1, then t1 (with the target's own spike at t1 if
 // any), then target spikes after t1 -- the order of apply_events.
+template <bool MOD>
 __device__ __forceinline__ float walk_one_pre(const WalkArgs& a, const Seg& g, int t1, int4 r, float w, float mod,
                                               float xp0) {
     const int q4[4] = {r.w, r.z, r.y, r.x};   // oldest first
@@ -205,24 +208,25 @@ __device__ __forceinline__ float walk_one_pre(const WalkArgs& a, const Seg& g, i
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         const int q = q4[k];
-        if (q > g.T && q < t1) w = stdp_apply1(a, w, mod, g.X[q - g.T - 1], 1.0f, 0.0f, 0.0f);
+        if (q > g.T && q < t1) w = stdp_apply1<MOD>(a, w, mod, g.X[q - g.T - 1], 1.0f, 0.0f, 0.0f);
         coincide = coincide || q == t1;
     }
-    w = stdp_apply1(a, w, mod, coincide ? g.X[t1 - g.T - 1] : 0.0f, coincide ? 1.0f : 0.0f, xp0, 1.0f);
+    w = stdp_apply1<MOD>(a, w, mod, coincide ? g.X[t1 - g.T - 1] : 0.0f, coincide ? 1.0f : 0.0f, xp0, 1.0f);
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         const int q = q4[k];
-        if (q > t1 && q <= g.e) w = stdp_apply1(a, w, mod, g.X[q - g.T - 1], 1.0f, 0.0f, 0.0f);
+        if (q > t1 && q <= g.e) w = stdp_apply1<MOD>(a, w, mod, g.X[q - g.T - 1], 1.0f, 0.0f, 0.0f);
     }
     return w;
 }
 
+template <bool MOD>
 __device__ __forceinline__ float walk_syn(const WalkArgs& a, const Seg& g, int t1, uint32_t i, int4 r, float w,
                                           float mod, int now, float xp0) {
-    if (g.P.n == 1 && r.w <= g.T) return walk_one_pre(a, g, t1, r, w, mod, xp0);
+    if (g.P.n == 1 && r.w <= g.T) return walk_one_pre<MOD>(a, g, t1, r, w, mod, xp0);
     if (g.P.n == 0 && r.x <= g.T) return w;   // nothing happened to this synapse
-    if (r.w <= g.T) return apply_events(a, g, steps_from4(r, g.T, g.e), i, w, mod, now, xp0);
-    return walk_syn_long(a, g, i, r, w, mod, now, xp0);
+    if (r.w <= g.T) return apply_events<MOD>(a, g, steps_from4(r, g.T, g.e), i, w, mod, now, xp0);
+    return walk_syn_long<MOD>(a, g, i, r, w, mod, now, xp0);
 }
 
 // Loads the segment's state, the source's spikes in (T, e] and the source
@@ -304,6 +308,7 @@ __device__ __forceinline__ bool load_seg(const WalkArgs& a, Seg& g, int* sP, flo
 // Walks synapses [c0, c1) of the segment, one per lane and round (the next
 // round's loads issued before this round's work); with deliver, adds the
 // updated weights into the target accumulators.
+template <bool MOD>
 __device__ __forceinline__ unsigned walk_chunk(const WalkArgs& a, const Seg& g, long long c0, long long c1,
                                                bool deliver, int now, int lane) {
     struct Syn {
@@ -320,7 +325,7 @@ __device__ __forceinline__ unsigned walk_chunk(const WalkArgs& a, const Seg& g, 
         Syn x;
         x.t = __ldcs(a.tgt + syn);
         x.w = a.w[syn];
-        x.md = a.mod ? __ldcs(a.mod + syn) : 1.0f;
+        x.md = MOD ? __ldcs(a.mod + syn) : 1.0f;
         x.r = a.tgt_recent[x.t];
         x.xp0 = has_pre ? ring0[x.t] : 0.0f;
         return x;
@@ -333,10 +338,10 @@ __device__ __forceinline__ unsigned walk_chunk(const WalkArgs& a, const Seg& g, 
     for (; syn < c1; syn += 32) {
         Syn nxt{};
         if (syn + 32 < c1) nxt = load(syn + 32);
-        const float w1 = walk_syn(a, g, t0, cur.t, cur.r, cur.w, cur.md, now, cur.xp0);
+        const float w1 = walk_syn<MOD>(a, g, t0, cur.t, cur.r, cur.w, cur.md, now, cur.xp0);
         if (__float_as_uint(w1) != __float_as_uint(cur.w)) a.w[syn] = w1;
         if (deliver) {
-            atomicAdd(a.acc + cur.t, a.mod ? w1 * cur.md : w1);
+            atomicAdd(a.acc + cur.t, MOD ? w1 * cur.md : w1);
             ++n;
         }
         cur = nxt;
@@ -356,6 +361,7 @@ __device__ __forceinline__ void finish_seg(const WalkArgs& a, const Seg& g) {
 // chunk of a segment reads the same state (the write happens only after
 // all of them have counted themselves) and so makes the same decision.
 // Returns the number of delivered events of this lane.
+template <bool MOD>
 __device__ unsigned segment_chunk(const WalkArgs& a, int* sP, float* sX, int j, int k, int chunk, int e,
                                   bool deliver, int now, int m_new, int lane) {
     const long long seg = static_cast<long long>(j) * a.nd + k;
@@ -367,7 +373,7 @@ __device__ unsigned segment_chunk(const WalkArgs& a, int* sP, float* sX, int j, 
     const bool pending = load_seg(a, g, sP, sX, j, k, e, m_new, lane);
     unsigned n = 0;
     if (pending) {
-        n = walk_chunk(a, g, c0, c1, deliver, now, lane);
+        n = walk_chunk<MOD>(a, g, c0, c1, deliver, now, lane);
         __syncwarp();
         if (lane == 0) {
             const int n_chunks = static_cast<int>((s1 - s0 + a.chunk - 1) / a.chunk);
@@ -383,13 +389,14 @@ __device__ unsigned segment_chunk(const WalkArgs& a, int* sP, float* sX, int j, 
         // nothing to apply (already walked through e): deliver only
         for (long long syn = c0 + lane; syn < c1; syn += 32) {
             const float wv = a.w[syn];
-            atomicAdd(a.acc + __ldg(a.tgt + syn), a.mod ? wv * __ldg(a.mod + syn) : wv);
+            atomicAdd(a.acc + __ldg(a.tgt + syn), MOD ? wv * __ldg(a.mod + syn) : wv);
             ++n;
         }
     }
     return n;
 }
 
+template <bool MOD>
 __global__ void __launch_bounds__(kThreads, 4) walk_kernel(const __grid_constant__ WalkArgs a, int mode,
                                                         long long step_off, const long long* step_base) {
     using Scan = cub::BlockScan<long long, kThreads>;
@@ -417,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, 4) walk_kernel(const __grid_constant
         for (long long u = warp; u < n_units; u += n_warps) {
             const long long row = u / per_row;
             const int rem = static_cast<int>(u - row * per_row);
-            segment_chunk(a, sP, sX, static_cast<int>(row), rem / chunks, rem % chunks, now - 1, false, now, m_new,
+            segment_chunk<MOD>(a, sP, sX, static_cast<int>(row), rem / chunks, rem % chunks, now - 1, false, now, m_new,
                           lane);
         }
         return;
@@ -458,7 +465,7 @@ __global__ void __launch_bounds__(kThreads, 4) walk_kernel(const __grid_constant
             const int spike = local / chunks;
             const int chunk = local - spike * chunks;
             const int j = a.hist_src.ids[static_cast<long long>(slot[k]) * a.hist_src.cap + spike];
-            my_events += segment_chunk(a, sP, sX, j, k, chunk, now - 1, true, now, m_new, lane);
+            my_events += segment_chunk<MOD>(a, sP, sX, j, k, chunk, now - 1, true, now, m_new, lane);
         } else {
             const int q = static_cast<int>(u - n_arr);   // < sweep rows * per_row
             const int row = q / static_cast<int>(per_row);
@@ -469,7 +476,7 @@ __global__ void __launch_bounds__(kThreads, 4) walk_kernel(const __grid_constant
             // segments walked recently are left for later
             if (a.src_recent[j].x >= now - dmax) continue;
             if (a.seg_last[static_cast<long long>(j) * a.nd + k] >= now - a.stale) continue;
-            segment_chunk(a, sP, sX, j, k, rem % chunks, win_end, false, now, m_new, lane);
+            segment_chunk<MOD>(a, sP, sX, j, k, rem % chunks, win_end, false, now, m_new, lane);
         }
     }
     // lane sums -> one atomic per warp
@@ -489,9 +496,13 @@ nrn_status_t walk_launch(const WalkArgs& a, int mode, long long step_off, const 
                       (a.post_depth & (a.post_depth - 1)) == 0,
                   "plastic projection: trace ring depths must be powers of two");
     int per_sm = 0;
-    NRN_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, walk_kernel, kThreads, 0));
-    const int blocks = std::max(1, per_sm) * sm_count_current();
-    walk_kernel<<<blocks, kThreads, 0, s>>>(a, mode, step_off, step_base);
+    if (a.mod) {
+        NRN_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, walk_kernel<true>, kThreads, 0));
+        walk_kernel<true><<<std::max(1, per_sm) * sm_count_current(), kThreads, 0, s>>>(a, mode, step_off, step_base);
+    } else {
+        NRN_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, walk_kernel<false>, kThreads, 0));
+        walk_kernel<false><<<std::max(1, per_sm) * sm_count_current(), kThreads, 0, s>>>(a, mode, step_off, step_base);
+    }
     NRN_CUDA_TRY(cudaGetLastError());
     return NRN_OK;
 }
