@@ -423,9 +423,11 @@ struct nrn_engine {
     void assign_plasticity() {
         std::vector<char> walk_src(pops.size(), 0);
         std::vector<int> used(pops.size(), 0);
+        const char* eager = std::getenv("NRN_STDP_EAGER");   // per-step STDP kernels only (comparisons)
+        const bool no_walk = eager && eager[0] == '1' && world == 1;
         for (auto& q : projs) {
             q.walk = false;
-            if (!q.plastic || slow_ratio != 1 || q.csr.nd > 256 || walk_src[q.src_pop] ||
+            if (no_walk || !q.plastic || slow_ratio != 1 || q.csr.nd > 256 || walk_src[q.src_pop] ||
                 used[q.tgt_pop] >= NRN_MAX_TRACES)
                 continue;
             walk_src[q.src_pop] = 1;

@@ -305,9 +305,8 @@ __device__ __forceinline__ bool load_seg(const WalkArgs& a, Seg& g, int* sP, flo
     return true;
 }
 
-// Walks synapses [c0, c1) of the segment, one per lane and round (the next
-// round's loads issued before this round's work); with deliver, adds the
-// updated weights into the target accumulators.
+// Walks synapses [c0, c1) of the segment, one per lane and round; with
+// deliver, adds the updated weights into the target accumulators.
 template <bool MOD>
 __device__ __forceinline__ unsigned walk_chunk(const WalkArgs& a, const Seg& g, long long c0, long long c1,
                                                bool deliver, int now, int lane) {
@@ -331,20 +330,15 @@ __device__ __forceinline__ unsigned walk_chunk(const WalkArgs& a, const Seg& g, 
         return x;
     };
     unsigned n = 0;
-    long long syn = c0 + lane;
-    Syn cur{};
-    if (syn < c1) cur = load(syn);
 #pragma unroll 1
-    for (; syn < c1; syn += 32) {
-        Syn nxt{};
-        if (syn + 32 < c1) nxt = load(syn + 32);
+    for (long long syn = c0 + lane; syn < c1; syn += 32) {
+        const Syn cur = load(syn);
         const float w1 = walk_syn<MOD>(a, g, t0, cur.t, cur.r, cur.w, cur.md, now, cur.xp0);
         if (__float_as_uint(w1) != __float_as_uint(cur.w)) a.w[syn] = w1;
         if (deliver) {
             atomicAdd(a.acc + cur.t, MOD ? w1 * cur.md : w1);
             ++n;
         }
-        cur = nxt;
     }
     return n;
 }

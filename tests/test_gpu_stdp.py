@@ -96,3 +96,22 @@ def test_eager_launches_equal_graphs():
         assert np.array_equal(a, b)
     for a, b in zip(whole[2], eager[2]):
         assert np.array_equal(a, b)
+
+
+def test_modulatory_gains_walk_equals_per_step_kernels():
+    # gains on the plastic projection: the walks against the per-step STDP
+    # kernels (the oracle has no gains), same spikes and weights
+    net = S.realize(burst_spec(300))
+    rng = np.random.default_rng(3)
+    q = net["projs"][0]
+    q["mod"] = rng.uniform(0.5, 1.5, len(q["w"])).astype(np.float32)
+    walk = run(net)
+    os.environ["NRN_STDP_EAGER"] = "1"
+    try:
+        eager = run(net)
+    finally:
+        del os.environ["NRN_STDP_EAGER"]
+    for a, b in zip(walk[:2], eager[:2]):
+        assert np.array_equal(a, b)
+    for a, b in zip(walk[2], eager[2]):
+        assert np.array_equal(a, b)
