@@ -127,7 +127,8 @@ def cpu_reference(args, world_steps_hint=None):
     if args.workload in ("brunel_stdp", "brunel"):
         spec = W.brunel(10_000, 2_500, 1_000, 250, steps=steps, stdp=args.workload == "brunel_stdp")
         sample = (f"Brunel LIF 10,000 E + 2,500 I, in-degree 1,000 + 250, delay 15, "
-                  f"{'STDP on E->E, ' if args.workload == 'brunel_stdp' else ''}{steps} steps, block 256")
+                  f"{'STDP on E->E, ' if args.workload == 'brunel_stdp' else ''}{steps} steps, block 256; "
+                  f"events per step over the steps after the first delay")
     elif args.workload == "adex":
         spec = W.adex_cond(16_384, 1_000, steps=steps)
         sample = f"AdEx conductance network 16,384 neurons, in-degree 1,000, {steps} steps, block 256"
@@ -155,8 +156,14 @@ def cpu_reference(args, world_steps_hint=None):
     dmin = min(delay_of.values()) if delay_of else 1
     st, gid = res["spike_step"], res["spike_id"]
     ev = int(outdeg[gid[st + dmin < steps]].sum())
+    # No spike can arrive in the first dmin steps of the sample, but the
+    # reference spends the same time on every step (its block-dense product
+    # runs regardless of spikes): events per step are taken over the steps
+    # that deliver, time per step over all steps.
+    per_step_s = elapsed / steps
+    ev_per_step = ev / max(1, steps - dmin)
     return {
-        "events_per_s": ev / elapsed, "neuron_updates_per_s": n_total * steps / elapsed,
+        "events_per_s": ev_per_step / per_step_s, "neuron_updates_per_s": n_total * steps / elapsed,
         "rtf": elapsed / (steps * spec["dt"]), "elapsed_s": elapsed, "cores": threads, "kind": kind,
         "sample": sample,
     }
@@ -426,12 +433,28 @@ def main():
     ps0, pe0 = nw.counters()
     prof = nw.profile(args.profile_steps)
     ps1, pe1 = nw.counters()
-    nw.raster()
+    _, gid_p = nw.raster()
     ev_p, sp_p = pe1 - pe0, ps1 - ps0
     phases = {"deliver": prof[0], "neuron": prof[1], "stdp": prof[2]}
-    # algorithmic bytes: delivery 8 B per event (target + weight) + 16 B per
-    # (spike, delay) segment for its offsets
-    deliver_bytes = 8.0 * ev_p + 16.0 * sp_p * 4
+    # Algorithmic bytes of the delivery phase (static delivery and the STDP
+    # walks): 8 B per static event (target + weight), 12 B per event through
+    # a plastic segment (target, weight read and write), 16 B per synapse of
+    # a spiking target's plastic in-list (potentiation: synapse, weight r/w),
+    # and 16 B of segment offsets per spike.  The plastic events and
+    # potentiations follow from the spikes of the plastic projections'
+    # source and target populations in the profiled steps (the raster).
+    plastic_ev = ltp = 0.0
+    for q in spec["projs"]:
+        if not q.get("plastic"):
+            continue
+        ps_, pt_ = spec["pops"][q["src"]], spec["pops"][q["tgt"]]
+        deg = q["gen"]["degree"]   # in-degree of each target
+        s_src = np.count_nonzero((gid_p >= ps_["offset"]) & (gid_p < ps_["offset"] + ps_["n"]))
+        s_tgt = np.count_nonzero((gid_p >= pt_["offset"]) & (gid_p < pt_["offset"] + pt_["n"]))
+        plastic_ev += s_src * deg * pt_["n"] / ps_["n"]   # mean out-degree onto this rank's targets
+        ltp += s_tgt * deg
+    static_ev = max(0.0, ev_p - plastic_ev)
+    deliver_bytes = 8.0 * static_ev + 12.0 * plastic_ev + 16.0 * ltp + 16.0 * sp_p
     dom = max(phases, key=phases.get)
     achieved = deliver_bytes / (phases["deliver"] / 1e3) / 1e9 if phases["deliver"] > 0 else 0.0
 

@@ -171,12 +171,12 @@ typedef struct {
      *   win_mask[i] |= 1 << u for each spike (window trace snapshots);
      *   with send_hdr non-NULL, the ids go to the window send buffer instead
      *   of the history ring: send_hdr[u] counts the ids of window step u,
-     *   which follow those of steps 0..u-1 in send_ids[0 .. send_cap);
-     *   overflow sets *err to 4. */
+     *   which follow those of steps 0..u-1 in send_ids[0 .. send_cap), and
+     *   send_hdr[win] counts them all; overflow sets *err to 4. */
     int32_t id_offset;
     int32_t win;
     uint32_t* win_mask;        /* [n] or NULL                               */
-    int32_t* send_hdr;         /* [win] or NULL                             */
+    int32_t* send_hdr;         /* [win + 1] or NULL                         */
     int32_t* send_ids;         /* [send_cap]                                */
     int32_t send_cap;
     int32_t pad2;

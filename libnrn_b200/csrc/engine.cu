@@ -238,7 +238,7 @@ struct nrn_engine {
                 // ids go to the window send buffer; the ring is filled by the exchange
                 a.win = win;
                 a.send_hdr = send + p.send_off;
-                a.send_ids = send + p.send_off + win;
+                a.send_ids = send + p.send_off + win + 1;
                 a.send_cap = p.send_cap;
             } else {
                 a.spike_ids = p.hist_ids;
@@ -472,7 +472,7 @@ struct nrn_engine {
                 NRN_TRY(unpack_launch(u, off, d_step, stream));
             }
             for (const auto& p : pops)
-                NRN_CUDA_TRY(cudaMemsetAsync(send + p.send_off, 0, static_cast<size_t>(win) * sizeof(int32_t), stream));
+                NRN_CUDA_TRY(cudaMemsetAsync(send + p.send_off, 0, static_cast<size_t>(win + 1) * sizeof(int32_t), stream));
         }
         for (size_t i = 0; i < pops.size(); ++i)
             if (pops[i].mask) NRN_TRY(window_launch(window_args(static_cast<int>(i)), off, d_step, stream));
@@ -958,7 +958,7 @@ nrn_status_t nrn_engine_finalize(nrn_engine* e, int32_t init_update) {
         e->rank_block = 0;
         for (auto& p : e->pops) {
             p.send_off = e->rank_block;
-            e->rank_block += e->win + p.send_cap;
+            e->rank_block += e->win + 1 + p.send_cap;   // [win counts | total | ids]
             e->rank_block = (e->rank_block + 3) / 4 * 4;   // 16-byte aligned blocks
         }
         NRN_TRY(dalloc0(&e->send, static_cast<size_t>(e->rank_block), e->stream));

@@ -6,7 +6,7 @@
 // arrives in a later one, so each GPU only needs the other GPUs' spikes
 // once per window.  During a window, each population's update appends the
 // ids of its spiking neurons (index in the whole population) to a send
-// buffer, [win counts][ids, window step by window step].  At the window's
+// buffer, [win counts][total][ids, window step by window step].  At the window's
 // end the per-rank buffers are gathered (one all-gather over NCCL,
 // engine.cu) and unpacked here into the population's spike history ring:
 // step s in slot s % depth, the ranks' ids one after the other.
@@ -94,7 +94,7 @@ __global__ void __launch_bounds__(kThreads) unpack_kernel(const __grid_constant_
         n = room > 0 ? room : 0;
     }
     const int slot = static_cast<int>((ws + u) % a.hist.depth);
-    const int32_t* src = blk + a.win + before;
+    const int32_t* src = blk + a.win + 1 + before;   // [win counts | total | ids]
     int32_t* dst = a.hist.ids + static_cast<long long>(slot) * a.hist.cap + off;
     const bool other = r != a.rank && a.mask != nullptr;
     for (int q = threadIdx.x; q < n; q += blockDim.x) {

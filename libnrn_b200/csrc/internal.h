@@ -134,7 +134,7 @@ struct UnpackArgs {
     const int32_t* recv = nullptr;    // rank r's block at recv + r * rank_stride
     int64_t rank_stride = 0;
     int64_t pop_off = 0;              // this population's block offset inside a rank block
-    int32_t cap = 0;                  // id capacity of a block (after win counts)
+    int32_t cap = 0;                  // id capacity of a block (after win counts and the total)
     int32_t world = 1, rank = 0;
     int32_t win = 1;
     nrn_spike_hist_t hist{};

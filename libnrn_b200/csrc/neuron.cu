@@ -229,13 +229,13 @@ __device__ __forceinline__ void pop_body(const PopArgs& a, const int i) {
             const int cnt = __popc(mask);
             const int rank = __popc(mask & ((1u << lane) - 1u));
             if (a.send_hdr) {
-                // window send buffer: ids of window step u follow those of steps 0..u-1
+                // window send buffer: ids in step order (the steps of a window
+                // run one after the other), the running total in send_hdr[win]
                 const int u = static_cast<int>(step % a.win);
                 int base = 0;
                 if (lane == leader) {
-                    int before = 0;
-                    for (int q = 0; q < u; ++q) before += __ldcg(a.send_hdr + q);
-                    base = before + atomicAdd(a.send_hdr + u, cnt);
+                    base = atomicAdd(a.send_hdr + a.win, cnt);
+                    atomicAdd(a.send_hdr + u, cnt);
                 }
                 base = __shfl_sync(0xffffffffu, base, leader);
                 if (spiked) {

@@ -310,33 +310,36 @@ __device__ __forceinline__ bool load_seg(const WalkArgs& a, Seg& g, int* sP, flo
 template <bool MOD>
 __device__ __forceinline__ unsigned walk_chunk(const WalkArgs& a, const Seg& g, long long c0, long long c1,
                                                bool deliver, int now, int lane) {
-    struct Syn {
-        uint32_t t;
-        float w, md, xp0;
-        int4 r;
-    };
     // the target trace at the first source spike is loaded with the target's spike steps
     const bool has_pre = g.P.n > 0;
     const int t0 = has_pre ? g.P[0] : 0;
     if (has_pre && now - t0 >= a.post_depth) set_err(a.err, ERR_SNAPSHOT);
     const float* ring0 = a.post_ring + static_cast<long long>(t0 & (a.post_depth - 1)) * a.n_tgt;
-    auto load = [&](long long syn) {
-        Syn x;
-        x.t = __ldcs(a.tgt + syn);
-        x.w = a.w[syn];
-        x.md = MOD ? __ldcs(a.mod + syn) : 1.0f;
-        x.r = a.tgt_recent[x.t];
-        x.xp0 = has_pre ? ring0[x.t] : 0.0f;
-        return x;
-    };
+    // the next round's target and weight (the HBM stream) are loaded a round
+    // ahead; the target's spike steps and trace (L2) within the round
     unsigned n = 0;
+    long long syn = c0 + lane;
+    uint32_t t_next = 0;
+    float w_next = 0.0f;
+    if (syn < c1) {
+        t_next = __ldcs(a.tgt + syn);
+        w_next = a.w[syn];
+    }
 #pragma unroll 1
-    for (long long syn = c0 + lane; syn < c1; syn += 32) {
-        const Syn cur = load(syn);
-        const float w1 = walk_syn<MOD>(a, g, t0, cur.t, cur.r, cur.w, cur.md, now, cur.xp0);
-        if (__float_as_uint(w1) != __float_as_uint(cur.w)) a.w[syn] = w1;
+    for (; syn < c1; syn += 32) {
+        const uint32_t t = t_next;
+        const float w = w_next;
+        const int4 r = a.tgt_recent[t];
+        const float xp0 = has_pre ? ring0[t] : 0.0f;
+        const float md = MOD ? __ldcs(a.mod + syn) : 1.0f;
+        if (syn + 32 < c1) {
+            t_next = __ldcs(a.tgt + syn + 32);
+            w_next = a.w[syn + 32];
+        }
+        const float w1 = walk_syn<MOD>(a, g, t0, t, r, w, md, now, xp0);
+        if (__float_as_uint(w1) != __float_as_uint(w)) a.w[syn] = w1;
         if (deliver) {
-            atomicAdd(a.acc + cur.t, MOD ? w1 * cur.md : w1);
+            atomicAdd(a.acc + t, MOD ? w1 * md : w1);
             ++n;
         }
     }

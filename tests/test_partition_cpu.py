@@ -1,7 +1,7 @@
 """Host side of the multi-GPU partition, on CPU with world-size-2 gloo
 groups: slice ranges, distribution of the NCCL unique id made by the engine
 library, and the window exchange protocol (per-rank send blocks of
-[window counts][ids], one all-gather, unpack into the step slots of the
+[window counts][total][ids], one all-gather, unpack into the step slots of the
 spike history) checked against the unpartitioned spike list."""
 import os
 import socket
@@ -40,19 +40,20 @@ def _free_port():
 
 
 def _pack(local_ids_per_step, win, cap):
-    """Send block of one rank for one window: [win counts][ids], the ids of
-    window step u after those of steps 0..u-1 (the layout the neuron update
-    writes); ids past the capacity are dropped and reported."""
-    blk = np.zeros(win + cap, np.int32)
+    """Send block of one rank for one window: [win counts][total][ids], the
+    ids of window step u after those of steps 0..u-1 (the layout the neuron
+    update writes); ids past the capacity are dropped and reported."""
+    blk = np.zeros(win + 1 + cap, np.int32)
     pos, overflow = 0, False
     for u, ids in enumerate(local_ids_per_step):
         blk[u] = len(ids)
         for x in ids:
             if pos < cap:
-                blk[win + pos] = x
+                blk[win + 1 + pos] = x
             else:
                 overflow = True
             pos += 1
+    blk[win] = pos
     return blk, overflow
 
 
@@ -65,7 +66,7 @@ def _unpack(gathered, win, cap):
         for blk in gathered:
             before = int(blk[:u].sum())
             n = int(blk[u])
-            step_ids.extend(blk[win + before:win + before + n].tolist())
+            step_ids.extend(blk[win + 1 + before:win + 1 + before + n].tolist())
         out.append(step_ids)
     return out
 
@@ -119,4 +120,4 @@ def test_window_exchange_two_ranks():
 
 def test_pack_reports_overflow():
     blk, overflow = _pack([np.arange(10), np.arange(10)], 2, 15)
-    assert overflow and blk[0] == 10 and blk[1] == 10
+    assert overflow and blk[0] == 10 and blk[1] == 10 and blk[2] == 20
