@@ -485,6 +485,27 @@ def main():
     del host_state
     torch.cuda.synchronize()
 
+    # Partitioned runs: one all-gather of the engine's per-window exchange
+    # block size alone (same sizes, torch's communicator), for the line.
+    exch_ms = None
+    if dist is not None:
+        win = min(15, 32)
+        block = sum(win + 1 + max(4096, int(p["n"] * win * args.max_rate * spec["dt"] + 0.999999))
+                    for p in nw.pops)
+        sb = torch.zeros(block, dtype=torch.int32, device="cuda")
+        rb = torch.zeros(block * world, dtype=torch.int32, device="cuda")
+        for _ in range(3):
+            dist.all_gather_into_tensor(rb, sb)
+        torch.cuda.synchronize()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        for _ in range(20):
+            dist.all_gather_into_tensor(rb, sb)
+        a1.record()
+        torch.cuda.synchronize()
+        exch_ms = all_reduce(a0.elapsed_time(a1) / 20, "max")
+        del sb, rb
+
     cpu = None
     if not args.no_cpu and rank == 0:
         try:
@@ -514,6 +535,7 @@ def main():
         "gpu_launches": kernels_per_step * args.steps + windows * (1 + len(nw.pops) * (2 if world > 1 else 0))
         + (args.steps + chunk - 1) // chunk,
         "phase_ms_per_step": {k: v / args.profile_steps for k, v in phases.items()},
+        "exchange_ms_per_window": exch_ms,
         "roofline": {"kernel": "deliver", "dominant_phase": dom, "bound": "hbm", "achieved": achieved,
                      "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
                      "peak_kind": peaks_kind, "traffic": None},

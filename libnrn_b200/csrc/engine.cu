@@ -905,6 +905,7 @@ nrn_status_t nrn_engine_set_stdp(nrn_engine* e, int32_t proj, const double* p) {
     NRN_CHECK_ARG(proj >= 0 && proj < static_cast<int32_t>(e->projs.size()), "bad projection index");
     NRN_CHECK_ARG(p != nullptr, "null STDP parameters");
     NRN_CHECK_ARG(p[0] > 0 && p[1] > 0, "STDP time constants must be positive");
+    for (int k = 0; k < 7; ++k) NRN_CHECK_ARG(std::isfinite(p[k]), "STDP parameters must be finite");
     NRN_CHECK_ARG(p[4] <= p[5], "STDP needs w_min <= w_max");
     NRN_CHECK_ARG(!e->finalized, "nrn_engine_set_stdp: set plasticity before nrn_engine_finalize");
     auto& q = e->projs[proj];

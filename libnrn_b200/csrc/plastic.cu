@@ -196,6 +196,16 @@ __device__ __forceinline__ float stdp_apply1(const WalkArgs& a, float w, float m
     return clampw(w + upd, a.w_min, a.w_max);
 }
 
+// Potentiation by a target spike alone: the general update with post = 1,
+// pre = 0.  With finite parameters (nrn_engine_set_stdp checks) the LTD term
+// (A- * 0) * 0 is +0 and the update reduces to clamp(w + (A+ x_pre) * lr).
+template <bool MOD>
+__device__ __forceinline__ float stdp_ltp(const WalkArgs& a, float w, float mod, float xpre) {
+    float upd = (a.a_plus * xpre) * a.lr;
+    if (MOD) upd = upd * mod;
+    return clampw(w + upd, a.w_min, a.w_max);
+}
+
 // The common case, straight-line: one source spike t1 in (T, e] and the
 // target's spikes in (T, e] among its newest four (r, newest first).
 // Target spikes before t1, then t1 (with the target's own spike at t1 if
@@ -204,18 +214,19 @@ template <bool MOD>
 __device__ __forceinline__ float walk_one_pre(const WalkArgs& a, const Seg& g, int t1, int4 r, float w, float mod,
                                               float xp0) {
     const int q4[4] = {r.w, r.z, r.y, r.x};   // oldest first
+    const float* X = g.X - (g.T + 1);         // X[t] = x_pre(t)
     bool coincide = false;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         const int q = q4[k];
-        if (q > g.T && q < t1) w = stdp_apply1<MOD>(a, w, mod, g.X[q - g.T - 1], 1.0f, 0.0f, 0.0f);
+        if (q > g.T && q < t1) w = stdp_ltp<MOD>(a, w, mod, X[q]);
         coincide = coincide || q == t1;
     }
-    w = stdp_apply1<MOD>(a, w, mod, coincide ? g.X[t1 - g.T - 1] : 0.0f, coincide ? 1.0f : 0.0f, xp0, 1.0f);
+    w = stdp_apply1<MOD>(a, w, mod, coincide ? X[t1] : 0.0f, coincide ? 1.0f : 0.0f, xp0, 1.0f);
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         const int q = q4[k];
-        if (q > t1 && q <= g.e) w = stdp_apply1<MOD>(a, w, mod, g.X[q - g.T - 1], 1.0f, 0.0f, 0.0f);
+        if (q > t1 && q <= g.e) w = stdp_ltp<MOD>(a, w, mod, X[q]);
     }
     return w;
 }
