@@ -473,8 +473,11 @@ def main():
     for dev_t, h in host_state:
         dev_t.copy_(h, non_blocking=True)
     torch.cuda.current_stream().synchronize()
+    t_up = time.perf_counter()
     e_s0, e_e0 = nw.counters()
     nw.run(args.steps, args.chunk)
+    nw.sync()
+    t_run = time.perf_counter()
     st2, gid2 = nw.raster()
     e_s1, e_e1 = nw.counters()
     t1 = time.perf_counter()
@@ -540,7 +543,8 @@ def main():
                      "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
                      "peak_kind": peaks_kind, "traffic": None},
         "e2e": {"value": e2e, "unit": "events/s", "h2d_bytes_per_step": h2d / args.steps,
-                "d2h_bytes_per_step": d2h / args.steps},
+                "d2h_bytes_per_step": d2h / args.steps,
+                "seconds": {"upload": t_up - t0, "run": t_run - t_up, "raster": t1 - t_run}},
         "clocks": clocks,
     }
     if cpu is not None:

@@ -10,7 +10,8 @@ import ctypes as C
 import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "_lib", "libnrn_cuda.so")
+# NRN_CUDA_LIB: another build of the same library (for example a debug build)
+LIB_PATH = os.environ.get("NRN_CUDA_LIB") or os.path.join(HERE, "_lib", "libnrn_cuda.so")
 
 NRN_MAX_PARAMS = 13
 NRN_MAX_PROJ = 32

@@ -240,50 +240,14 @@ __device__ __forceinline__ float walk_syn(const WalkArgs& a, const Seg& g, int t
     return walk_syn_long<MOD>(a, g, i, r, w, mod, now, xp0);
 }
 
-// Loads the segment's state, the source's spikes in (T, e] and the source
-// trace over (T, e] into the warp's shared slots.  The trace is rebuilt
-// window by window (one window per lane) from the snapshot at the window's
-// start -- or, for the first, from x_pre(T) -- with the same operations as
-// the per-step update.
-__device__ __forceinline__ bool load_seg(const WalkArgs& a, Seg& g, int* sP, float* sX, int j, int k, int e,
-                                         int m_new, int lane) {
-    __syncwarp();   // the warp is done with the previous segment's lists
-    g.j = j;
-    g.seg = static_cast<long long>(j) * a.nd + k;
-    g.e = e;
-    long long s0 = 0, s1 = 0;
-    int T = 0, n = 0;
-    float xT = 0.0f;
-    if (lane == 0) {
-        s0 = a.seg_ptr[g.seg];
-        s1 = a.seg_ptr[g.seg + 1];
-        T = a.seg_last[g.seg];
-        xT = a.seg_x[g.seg];
-        if (s0 < s1 && T < e) {
-            if (e - T > kMaxSpan) {
-                set_err(a.err, ERR_SNAPSHOT);
-                n = -1;
-            } else {
-                const bool own = j >= a.src_lo && j < a.src_hi;
-                n = spikes_in(a.src_recent[j], own ? a.src_ring : nullptr, a.src_cnt, j - a.src_lo, a.ring_k, T, e,
-                              sP, kMaxPre);
-                if (n < 0) set_err(a.err, ERR_HISTORY);
-            }
-        }
-    }
-    __syncwarp();
-    g.s0 = __shfl_sync(0xffffffffu, s0, 0);
-    g.s1 = __shfl_sync(0xffffffffu, s1, 0);
-    g.T = __shfl_sync(0xffffffffu, T, 0);
-    xT = __shfl_sync(0xffffffffu, xT, 0);
-    n = __shfl_sync(0xffffffffu, n, 0);
-    g.P.p = sP;
-    g.P.n = n < 0 ? 0 : n;
-    g.X = sX;
-    if (!(g.s0 < g.s1 && g.T < e && n >= 0)) return false;
-    // window ends b = m*win - 1 in (T, e): m = m0, m0+1, ...
-    const int W = a.win;
-    const int m0 = (g.T + 1) / W + 1;
+// The source trace over (T, e] into the warp's shared table, window by
+// window (one window per lane) from the snapshot at the window's start --
+// or, for the first, from x_pre(T) -- with the same operations as the
+// per-step update.
+__device__ __forceinline__ void build_table(const WalkArgs& a, const Seg& g, float* sX, float xT, int m_new,
+                                            int lane) {
+    const int W = a.win, e = g.e;
+    const int m0 = (g.T + 1) / W + 1;   // window ends b = m*W - 1 in (T, e): m = m0, m0+1, ...
     const int n_pieces = 1 + (m0 * W - 1 < e ? (e - (m0 * W - 1) + W - 1) / W : 0);
     for (int pc = lane; pc < n_pieces; pc += 32) {
         int start;
@@ -295,32 +259,31 @@ __device__ __forceinline__ bool load_seg(const WalkArgs& a, Seg& g, int* sP, flo
             const int m = m0 + pc - 1;
             start = m * W - 1;
             if (m_new - m >= a.pre_depth) set_err(a.err, ERR_SNAPSHOT);
-            x = a.pre_snap[static_cast<long long>(m & (a.pre_depth - 1)) * a.pre_stride + j];
+            x = a.pre_snap[static_cast<long long>(m & (a.pre_depth - 1)) * a.pre_stride + g.j];
         }
         const int stop = pc == 0 ? (m0 * W - 1 < e ? m0 * W - 1 : e) : (start + W < e ? start + W : e);
         int q = 0;
         while (q < g.P.n && g.P[q] <= start) ++q;
         int next = q < g.P.n ? g.P[q] : INT_MAX;
         for (int u = start + 1; u <= stop; ++u) {
-            float s = 0.0f;
+            float sp = 0.0f;
             if (next == u) {
-                s = 1.0f;
+                sp = 1.0f;
                 ++q;
                 next = q < g.P.n ? g.P[q] : INT_MAX;
             }
-            x = x * a.decay_pre + s;
+            x = x * a.decay_pre + sp;
             sX[u - g.T - 1] = x;
         }
     }
     __syncwarp();
-    return true;
 }
 
 // Walks synapses [c0, c1) of the segment, one per lane and round; with
 // deliver, adds the updated weights into the target accumulators.
 template <bool MOD>
 __device__ __forceinline__ unsigned walk_chunk(const WalkArgs& a, const Seg& g, long long c0, long long c1,
-                                               bool deliver, int now, int lane) {
+                                               bool deliver, int now, int lane, uint32_t t_first, float w_first) {
     // the target trace at the first source spike is loaded with the target's spike steps
     const bool has_pre = g.P.n > 0;
     const int t0 = has_pre ? g.P[0] : 0;
@@ -330,12 +293,8 @@ __device__ __forceinline__ unsigned walk_chunk(const WalkArgs& a, const Seg& g, 
     // ahead; the target's spike steps and trace (L2) within the round
     unsigned n = 0;
     long long syn = c0 + lane;
-    uint32_t t_next = 0;
-    float w_next = 0.0f;
-    if (syn < c1) {
-        t_next = __ldcs(a.tgt + syn);
-        w_next = a.w[syn];
-    }
+    uint32_t t_next = t_first;
+    float w_next = w_first;
 #pragma unroll 1
     for (; syn < c1; syn += 32) {
         const uint32_t t = t_next;
@@ -368,20 +327,74 @@ __device__ __forceinline__ void finish_seg(const WalkArgs& a, const Seg& g) {
 // chunk of the segment to finish records the segment's new state.  Every
 // chunk of a segment reads the same state (the write happens only after
 // all of them have counted themselves) and so makes the same decision.
-// Returns the number of delivered events of this lane.
+// With sweep, the chunk is skipped when its source has spikes still to
+// arrive (their walks come) or the segment was walked recently.  Loads are
+// grouped so that the chain per chunk is: segment bounds, state and source
+// spike steps (one round trip); trace snapshots and the first synapses
+// (one); the targets' spike steps and trace (one).  Returns the number of
+// events this lane delivered.
 template <bool MOD>
 __device__ unsigned segment_chunk(const WalkArgs& a, int* sP, float* sX, int j, int k, int chunk, int e,
-                                  bool deliver, int now, int m_new, int lane) {
+                                  bool deliver, bool sweep, int now, int m_new, int lane) {
+    __syncwarp();   // the warp is done with the previous segment's lists
     const long long seg = static_cast<long long>(j) * a.nd + k;
-    const long long s0 = a.seg_ptr[seg], s1 = a.seg_ptr[seg + 1];
+    long long s0 = 0, s1 = 0;
+    int T = 0;
+    float xT = 0.0f;
+    int4 rj = make_int4(-1, -1, -1, -1);
+    if (lane == 0) {
+        s0 = a.seg_ptr[seg];
+        s1 = a.seg_ptr[seg + 1];
+        T = a.seg_last[seg];
+        xT = a.seg_x[seg];
+        rj = a.src_recent[j];
+    }
+    s0 = __shfl_sync(0xffffffffu, s0, 0);
+    s1 = __shfl_sync(0xffffffffu, s1, 0);
+    T = __shfl_sync(0xffffffffu, T, 0);
+    if (sweep) {
+        const int newest = __shfl_sync(0xffffffffu, rj.x, 0);
+        if (newest >= now - (a.dmin + a.nd - 1) || T >= now - a.stale) return 0;
+    }
     const long long c0 = s0 + static_cast<long long>(chunk) * a.chunk;
     if (c0 >= s1) return 0;
     const long long c1 = c0 + a.chunk < s1 ? c0 + a.chunk : s1;
-    Seg g;
-    const bool pending = load_seg(a, g, sP, sX, j, k, e, m_new, lane);
+    // the first round's synapses, independent of the segment's history
+    uint32_t t_first = 0;
+    float w_first = 0.0f;
+    if (c0 + lane < c1) {
+        t_first = __ldcs(a.tgt + c0 + lane);
+        w_first = a.w[c0 + lane];
+    }
     unsigned n = 0;
-    if (pending) {
-        n = walk_chunk<MOD>(a, g, c0, c1, deliver, now, lane);
+    int nP = -2;   // -2: nothing to apply (walked through e already)
+    if (T < e) {
+        nP = -1;
+        if (lane == 0) {
+            if (e - T > kMaxSpan) {
+                set_err(a.err, ERR_SNAPSHOT);
+            } else {
+                const bool own = j >= a.src_lo && j < a.src_hi;
+                nP = spikes_in(rj, own ? a.src_ring : nullptr, a.src_cnt, j - a.src_lo, a.ring_k, T, e, sP, kMaxPre);
+                if (nP < 0) set_err(a.err, ERR_HISTORY);
+            }
+        }
+        nP = __shfl_sync(0xffffffffu, nP, 0);
+        __syncwarp();
+    }
+    if (nP >= 0) {
+        Seg g;
+        g.j = j;
+        g.seg = seg;
+        g.s0 = s0;
+        g.s1 = s1;
+        g.T = T;
+        g.e = e;
+        g.P.p = sP;
+        g.P.n = nP;
+        g.X = sX;
+        build_table(a, g, sX, __shfl_sync(0xffffffffu, xT, 0), m_new, lane);
+        n = walk_chunk<MOD>(a, g, c0, c1, deliver, now, lane, t_first, w_first);
         __syncwarp();
         if (lane == 0) {
             const int n_chunks = static_cast<int>((s1 - s0 + a.chunk - 1) / a.chunk);
@@ -394,8 +407,13 @@ __device__ unsigned segment_chunk(const WalkArgs& a, int* sP, float* sX, int j, 
             }
         }
     } else if (deliver) {
-        // nothing to apply (already walked through e): deliver only
-        for (long long syn = c0 + lane; syn < c1; syn += 32) {
+        // nothing to apply (or a history error, flagged): deliver only
+        long long syn = c0 + lane;
+        if (syn < c1) {
+            atomicAdd(a.acc + t_first, MOD ? w_first * __ldg(a.mod + syn) : w_first);
+            ++n;
+        }
+        for (syn += 32; syn < c1; syn += 32) {
             const float wv = a.w[syn];
             atomicAdd(a.acc + __ldg(a.tgt + syn), MOD ? wv * __ldg(a.mod + syn) : wv);
             ++n;
@@ -432,8 +450,8 @@ __global__ void __launch_bounds__(kThreads, 4) walk_kernel(const __grid_constant
         for (long long u = warp; u < n_units; u += n_warps) {
             const long long row = u / per_row;
             const int rem = static_cast<int>(u - row * per_row);
-            segment_chunk<MOD>(a, sP, sX, static_cast<int>(row), rem / chunks, rem % chunks, now - 1, false, now, m_new,
-                          lane);
+            segment_chunk<MOD>(a, sP, sX, static_cast<int>(row), rem / chunks, rem % chunks, now - 1, false, false,
+                               now, m_new, lane);
         }
         return;
     }
@@ -458,7 +476,6 @@ __global__ void __launch_bounds__(kThreads, 4) walk_kernel(const __grid_constant
     const long long rows = left <= 0 ? 0 : (a.sweep_rows < left ? a.sweep_rows : left);
     const long long n_units = n_arr + rows * per_row;
     const int win_end = static_cast<int>((step / a.win) * a.win) - 1;   // spikes of all ranks known through here
-    const int dmax = a.dmin + a.nd - 1;
 
     unsigned long long my_events = 0;
     for (long long u = warp; u < n_units; u += n_warps) {
@@ -473,18 +490,14 @@ __global__ void __launch_bounds__(kThreads, 4) walk_kernel(const __grid_constant
             const int spike = local / chunks;
             const int chunk = local - spike * chunks;
             const int j = a.hist_src.ids[static_cast<long long>(slot[k]) * a.hist_src.cap + spike];
-            my_events += segment_chunk<MOD>(a, sP, sX, j, k, chunk, now - 1, true, now, m_new, lane);
+            my_events += segment_chunk<MOD>(a, sP, sX, j, k, chunk, now - 1, true, false, now, m_new, lane);
         } else {
             const int q = static_cast<int>(u - n_arr);   // < sweep rows * per_row
             const int row = q / static_cast<int>(per_row);
             const int rem = q - row * static_cast<int>(per_row);
             const int j = static_cast<int>(r0 + row);
             const int k = rem / chunks;
-            // rows with spikes still to arrive are walked by those arrivals;
-            // segments walked recently are left for later
-            if (a.src_recent[j].x >= now - dmax) continue;
-            if (a.seg_last[static_cast<long long>(j) * a.nd + k] >= now - a.stale) continue;
-            segment_chunk<MOD>(a, sP, sX, j, k, rem % chunks, win_end, false, now, m_new, lane);
+            segment_chunk<MOD>(a, sP, sX, j, k, rem % chunks, win_end, false, true, now, m_new, lane);
         }
     }
     // lane sums -> one atomic per warp
