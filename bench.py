@@ -53,6 +53,10 @@ def workload_spec(name: str, world: int, steps: int, scale: float = 1.0):
         return W.brunel_stdp_per_gpu(world, steps=steps)
     if name == "brunel":
         return W.brunel(10_000 * world, 2_500 * world, 1_000, 250, steps=steps)
+    if name == "brunel_1m":
+        # the bench network without plasticity: 1,048,576 LIF neurons and
+        # 1.31e9 static synapses per GPU
+        return W.brunel(838_860 * world, 209_716 * world, 1_000, 250, steps=steps)
     if name == "adex":
         return W.adex_cond(1_048_576 * world, 1_000, steps=steps)
     if name == "izh":
@@ -124,7 +128,7 @@ def cpu_reference(args, world_steps_hint=None):
     if args.workload == "bsr":
         return cpu_bsr_sample(threads)
     steps = int(os.environ.get("NRN_CPU_SAMPLE_STEPS", "30"))
-    if args.workload in ("brunel_stdp", "brunel"):
+    if args.workload in ("brunel_stdp", "brunel", "brunel_1m"):
         spec = W.brunel(10_000, 2_500, 1_000, 250, steps=steps, stdp=args.workload == "brunel_stdp")
         sample = (f"Brunel LIF 10,000 E + 2,500 I, in-degree 1,000 + 250, delay 15, "
                   f"{'STDP on E->E, ' if args.workload == 'brunel_stdp' else ''}{steps} steps, block 256; "
@@ -346,7 +350,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10_000)
     ap.add_argument("--warmup", type=int, default=200)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="brunel_stdp", choices=["brunel_stdp", "brunel", "adex", "izh", "bsr"])
+    ap.add_argument("--workload", default="brunel_stdp", choices=["brunel_stdp", "brunel_1m", "brunel", "adex", "izh", "bsr"])
     ap.add_argument("--chunk", type=int, default=0)
     ap.add_argument("--profile-steps", type=int, default=300)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")

@@ -105,7 +105,7 @@ struct EngineProj {
     int32_t* seg_last = nullptr;
     float* seg_x = nullptr;
     int32_t* seg_done = nullptr;
-    float* pre_snap = nullptr;   // [pre_depth][n_src] source trace at window ends
+    float* pre_snap = nullptr;   // [n_src][pre_depth] source trace at window ends
     float* post_ring = nullptr;  // [ring_depth][n_tgt] target trace at every step
     int32_t pre_depth = 1;
 };
@@ -338,7 +338,6 @@ struct nrn_engine {
         a.tgt_cnt = pt.cnt;
         a.ring_k = kRing;
         a.pre_snap = q.pre_snap;
-        a.pre_stride = q.csr.n_src;
         a.pre_depth = q.pre_depth;
         a.post_ring = q.post_ring;
         a.post_depth = ring_depth;
@@ -374,7 +373,6 @@ struct nrn_engine {
             if (q.src_pop == i && a.n_task < 4) {
                 SnapTask& t = a.task[a.n_task++];
                 t.snap = q.pre_snap;
-                t.stride = q.csr.n_src;
                 t.depth = q.pre_depth;
                 t.lo = 0;
                 t.hi = p.n_global;

@@ -43,9 +43,10 @@ __global__ void __launch_bounds__(kThreads) window_kernel(const __grid_constant_
             const SnapTask& t = a.task[k];
             if (j < t.lo || j >= t.hi) continue;
             const long long col = j - t.lo;
-            float x = t.snap[static_cast<long long>((m - 1) & (t.depth - 1)) * t.stride + col];
+            float* row = t.snap + col * t.depth;   // this neuron's snapshots, window m at m % depth
+            float x = row[(m - 1) & (t.depth - 1)];
             for (int u = 0; u < a.win; ++u) x = x * t.decay + (((bits >> u) & 1u) ? 1.0f : 0.0f);
-            t.snap[static_cast<long long>(m & (t.depth - 1)) * t.stride + col] = x;
+            row[m & (t.depth - 1)] = x;
         }
         if (bits == 0) continue;
         a.mask[j] = 0;

@@ -83,9 +83,9 @@ struct WalkArgs {
     const int32_t* tgt_ring = nullptr;
     const int32_t* tgt_cnt = nullptr;
     int32_t ring_k = 64;
-    // source trace at window ends: x(m*win - 1) in row m % pre_depth
+    // source trace at window ends: x_j(m*win - 1) at j * pre_depth + m % pre_depth
+    // (a source's snapshots are contiguous: a walk reads consecutive windows)
     const float* pre_snap = nullptr;
-    int64_t pre_stride = 0;
     int32_t pre_depth = 1;
     // target trace at every step: x(t) in row t % post_depth ([depth][n_tgt])
     const float* post_ring = nullptr;
@@ -107,8 +107,7 @@ nrn_status_t walk_launch(const WalkArgs& a, int mode, long long step_off, const 
 // from the window's spike masks, spike steps of the sources other ranks
 // own, mask reset.
 struct SnapTask {
-    float* snap = nullptr;            // row m % depth holds x(m*win - 1)
-    int64_t stride = 0;
+    float* snap = nullptr;            // x_j(m*win - 1) at (j - lo) * depth + m % depth
     int32_t depth = 1;
     int32_t lo = 0, hi = 0;           // population indices covered (snap column = j - lo)
     float decay = 1;

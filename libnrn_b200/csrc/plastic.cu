@@ -259,7 +259,7 @@ __device__ __forceinline__ void build_table(const WalkArgs& a, const Seg& g, flo
             const int m = m0 + pc - 1;
             start = m * W - 1;
             if (m_new - m >= a.pre_depth) set_err(a.err, ERR_SNAPSHOT);
-            x = a.pre_snap[static_cast<long long>(m & (a.pre_depth - 1)) * a.pre_stride + g.j];
+            x = a.pre_snap[static_cast<long long>(g.j) * a.pre_depth + (m & (a.pre_depth - 1))];
         }
         const int stop = pc == 0 ? (m0 * W - 1 < e ? m0 * W - 1 : e) : (start + W < e ? start + W : e);
         int q = 0;
