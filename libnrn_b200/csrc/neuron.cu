@@ -103,12 +103,14 @@ __device__ __forceinline__ float drive_value(const PopArgs& a, uint32_t gid, uin
     return a.d1 * static_cast<float>(k);
 }
 
-// The update of neuron i (no-op past the population's end); returns 1 if it
-// spiked.
+// One neuron of one population: every thread of a warp belongs to the same
+// population (the compaction below is warp-wide).
 template <int MODEL, bool HET, bool COND>
-__device__ __forceinline__ int pop_update(const PopArgs& a, const int i, const long long step) {
+__device__ __forceinline__ void pop_body(const PopArgs& a, const int i) {
     const bool valid = i < a.n;
     int spiked = 0;
+    long long step = a.step;
+    if (a.step_base) step += *a.step_base;
     if (valid) {
         float I = a.i_syn ? a.i_syn[i] : 0.0f;
         float in_e = 0.0f, in_i = 0.0f;
@@ -218,13 +220,7 @@ __device__ __forceinline__ int pop_update(const PopArgs& a, const int i, const l
             a.gin_inh[i] = 0.0f;
         }
     }
-    return spiked;
-}
-
-// Appends the ids of the warp's spiking neurons: warp-ballot compaction,
-// ascending ids within a warp, one atomic per warp (every thread of a warp
-// belongs to the same population).
-__device__ __forceinline__ void pop_compact(const PopArgs& a, const int i, const int spiked, const long long step) {
+    // Warp-ballot compaction: ascending ids within a warp, one atomic per warp.
     if (a.spike_ids != nullptr || a.send_hdr != nullptr || a.raster_gid != nullptr) {
         const unsigned mask = __ballot_sync(0xffffffffu, spiked);
         if (mask) {
@@ -273,28 +269,13 @@ __device__ __forceinline__ void pop_compact(const PopArgs& a, const int i, const
     }
 }
 
-// Each thread updates two neurons, i and i + blockDim.x of the block's
-// 2*blockDim.x (independent work for the scheduler to interleave), then the
-// two compactions in order.
-template <int MODEL, bool HET, bool COND>
-__device__ __forceinline__ void pop_body(const PopArgs& a, const int block) {
-    long long step = a.step;
-    if (a.step_base) step += *a.step_base;
-    const int i0 = block * 2 * blockDim.x + threadIdx.x;
-    const int i1 = i0 + blockDim.x;
-    const int s0 = pop_update<MODEL, HET, COND>(a, i0, step);
-    const int s1 = pop_update<MODEL, HET, COND>(a, i1, step);
-    pop_compact(a, i0, s0, step);
-    pop_compact(a, i1, s1, step);
-}
-
 template <int MODEL, bool HET, bool COND>
 __global__ void __launch_bounds__(256) pop_step_kernel(const __grid_constant__ PopArgs a) {
-    pop_body<MODEL, HET, COND>(a, blockIdx.x);
+    pop_body<MODEL, HET, COND>(a, blockIdx.x * blockDim.x + threadIdx.x);
 }
 
 // Several populations of the same kind in one launch, block ranges
-// [start[q], start[q+1]) for population q (2 * blockDim.x neurons a block).
+// [start[q], start[q+1]) for population q.
 constexpr int kMaxGroup = 4;
 struct PopGroup {
     PopArgs p[kMaxGroup];
@@ -306,7 +287,7 @@ template <int MODEL, bool HET, bool COND>
 __global__ void __launch_bounds__(256) pop_group_kernel(const __grid_constant__ PopGroup g) {
     int q = 0;
     while (q + 1 < g.n && static_cast<int>(blockIdx.x) >= g.start[q + 1]) ++q;
-    pop_body<MODEL, HET, COND>(g.p[q], static_cast<int>(blockIdx.x) - g.start[q]);
+    pop_body<MODEL, HET, COND>(g.p[q], (static_cast<int>(blockIdx.x) - g.start[q]) * blockDim.x + threadIdx.x);
 }
 
 constexpr int kPopThreads = 256;
@@ -460,7 +441,7 @@ nrn_status_t pop_step_group(const nrn_pop_step_t* list, int n, cudaStream_t s) {
         done[q] = 1;
         if (list[q].n == 0) continue;
         g.n = 1;
-        g.start[1] = (list[q].n + 2 * kPopThreads - 1) / (2 * kPopThreads);
+        g.start[1] = (list[q].n + kPopThreads - 1) / kPopThreads;
         // later populations of the same kind join this launch
         for (int r = q + 1; r < n && g.n < kMaxGroup; ++r) {
             if (done[r] || list[r].n == 0 || list[r].model != list[q].model) continue;
@@ -469,7 +450,7 @@ nrn_status_t pop_step_group(const nrn_pop_step_t* list, int n, cudaStream_t s) {
             NRN_TRY(make_args(list[r], x, h2, c2));
             if (h2 != het || c2 != cond) continue;
             g.p[g.n] = x;
-            g.start[g.n + 1] = g.start[g.n] + (list[r].n + 2 * kPopThreads - 1) / (2 * kPopThreads);
+            g.start[g.n + 1] = g.start[g.n] + (list[r].n + kPopThreads - 1) / kPopThreads;
             ++g.n;
             done[r] = 1;
         }
