@@ -181,11 +181,19 @@ typedef struct {
     int32_t send_cap;
     int32_t pad2;
     int32_t* err;              /* device error flag, or NULL                */
+    /* Drive values of this step computed ahead (nrn_cuda_drive_fill with the
+     * same arguments): if non-NULL, drive_values[i] replaces drawing the
+     * drive of neuron i here -- the same numbers. */
+    const float* drive_values;
 } nrn_pop_step_t;
 
 #define NRN_MAX_TRACES 4
 
 NRN_API nrn_status_t nrn_cuda_pop_step(const nrn_pop_step_t* a, nrn_stream_t stream);
+/* The external drive of the step described by a (drive, gid_offset, step,
+ * step_base) into out[0..n): the values nrn_cuda_pop_step would draw, so
+ * that they can be drawn ahead, concurrently with other work. */
+NRN_API nrn_status_t nrn_cuda_drive_fill(const nrn_pop_step_t* a, float* out, nrn_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
 /* Spike delivery                                                           */

@@ -34,7 +34,7 @@ EXPORTS = [
     "nrn_cuda_block_deliver", "nrn_cuda_block_stdp", "nrn_cuda_compact", "nrn_cuda_gather_ring",
     "nrn_cuda_scatter", "nrn_engine_raster_noalloc", "nrn_comm_unique_id", "nrn_engine_set_partition",
     "nrn_cuda_bsr_propagate", "nrn_cuda_bsr_pack", "nrn_cuda_bsr_pack_spikes", "nrn_cuda_bsr_unpack_spikes",
-    "nrn_cuda_bsr_spikes",
+    "nrn_cuda_bsr_spikes", "nrn_cuda_drive_fill",
 ]
 
 
@@ -67,7 +67,7 @@ class PopStep(C.Structure):
         ("post_recent", C.c_void_p), ("post_ring", C.c_void_p), ("post_cnt", C.c_void_p),
         ("post_ring_k", C.c_int32), ("id_offset", C.c_int32), ("win", C.c_int32),
         ("win_mask", C.c_void_p), ("send_hdr", C.c_void_p), ("send_ids", C.c_void_p),
-        ("send_cap", C.c_int32), ("pad2", C.c_int32), ("err", C.c_void_p),
+        ("send_cap", C.c_int32), ("pad2", C.c_int32), ("err", C.c_void_p), ("drive_values", C.c_void_p),
     ]
 
 
@@ -137,6 +137,7 @@ def lib() -> C.CDLL:
         L.nrn_engine_step.argtypes = [vp]
         sig = {
             "nrn_cuda_pop_step": [C.POINTER(PopStep), vp],
+            "nrn_cuda_drive_fill": [C.POINTER(PopStep), vp, vp],
             "nrn_cuda_deliver": [C.POINTER(Proj), i32, C.POINTER(SpikeHist), i32, i64, vp, vp],
             "nrn_cuda_deliver_counted": [C.POINTER(Proj), i32, C.POINTER(SpikeHist), i32, i64, vp, vp, vp],
             "nrn_cuda_clamp": [vp, i64, C.c_float, C.c_float, vp],

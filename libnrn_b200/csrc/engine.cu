@@ -90,6 +90,7 @@ struct EnginePop {
     int32_t* recent = nullptr;       // [n_global][4] newest four spike steps
     int32_t* ring = nullptr;         // [n][kRing] spike steps of this rank's neurons
     int32_t* cnt = nullptr;          // [n]
+    float* drive_buf = nullptr;      // [n] this step's drive, drawn ahead on the side stream
 };
 
 struct EngineProj {
@@ -156,7 +157,7 @@ struct nrn_engine {
             if (p.owns_isyn) cudaFree(p.d.i_syn);
             cudaFree(p.g_exc); cudaFree(p.g_inh); cudaFree(p.gin_exc); cudaFree(p.gin_inh);
             cudaFree(p.hist_ids); cudaFree(p.hist_count);
-            cudaFree(p.mask); cudaFree(p.recent); cudaFree(p.ring); cudaFree(p.cnt);
+            cudaFree(p.mask); cudaFree(p.recent); cudaFree(p.ring); cudaFree(p.cnt); cudaFree(p.drive_buf);
         }
         for (auto& q : projs) {
             free_csr(q.csr);
@@ -234,6 +235,7 @@ struct nrn_engine {
             a.step_base = reinterpret_cast<const int64_t*>(d_step);
             a.id_offset = p.lo;
             a.err = d_err;
+            a.drive_values = p.drive_buf;
             if (world > 1) {
                 // ids go to the window send buffer; the ring is filled by the exchange
                 a.win = win;
@@ -488,24 +490,27 @@ struct nrn_engine {
         if (ev) NRN_CUDA_TRY(cudaEventRecord(ev[0], stream));
         bool any_walk = false;
         for (auto& q : projs) any_walk = any_walk || q.walk;
-        // Static delivery (which also clears this step's history slots) and the
-        // STDP walks touch different history slots and only add into the
-        // accumulators: with walks, the delivery runs on the side stream.
-        cudaStream_t ds = any_walk ? side : stream;
-        if (any_walk) {
-            NRN_CUDA_TRY(cudaEventRecord(fork_ev, stream));
-            NRN_CUDA_TRY(cudaStreamWaitEvent(side, fork_ev, 0));
+        // Side stream, concurrent with the main stream's delivery work: this
+        // step's external drive for every population (drawn ahead for the
+        // neuron updates) and, with STDP walks on the main stream, the static
+        // delivery (it also clears this step's history slots; the two touch
+        // different history slots and only add into the accumulators).
+        NRN_CUDA_TRY(cudaEventRecord(fork_ev, stream));
+        NRN_CUDA_TRY(cudaStreamWaitEvent(side, fork_ev, 0));
+        for (size_t i = 0; i < pops.size(); ++i) {
+            if (!pops[i].drive_buf) continue;
+            nrn_pop_step_t pa = pop_args(static_cast<int>(i), dt, off, true);
+            NRN_TRY(nrn_cuda_drive_fill(&pa, pops[i].drive_buf, reinterpret_cast<nrn_stream_t>(side)));
         }
+        cudaStream_t ds = any_walk ? side : stream;
         NRN_TRY(nrn_cuda_deliver_counted(dp.data(), static_cast<int32_t>(dp.size()), hs.data(),
                                          static_cast<int32_t>(hs.size()), off,
                                          reinterpret_cast<const int64_t*>(d_step), d_events,
                                          reinterpret_cast<nrn_stream_t>(ds)));
         for (auto& q : projs)
             if (q.walk) NRN_TRY(walk_launch(walk_args(q), WALK_STEP, off, d_step, stream));
-        if (any_walk) {
-            NRN_CUDA_TRY(cudaEventRecord(join_ev, side));
-            NRN_CUDA_TRY(cudaStreamWaitEvent(stream, join_ev, 0));
-        }
+        NRN_CUDA_TRY(cudaEventRecord(join_ev, side));
+        NRN_CUDA_TRY(cudaStreamWaitEvent(stream, join_ev, 0));
         if (ev) NRN_CUDA_TRY(cudaEventRecord(ev[1], stream));
         std::vector<nrn_pop_step_t> pa;
         for (size_t i = 0; i < pops.size(); ++i) pa.push_back(pop_args(static_cast<int>(i), dt, off, true));
@@ -1010,6 +1015,8 @@ nrn_status_t nrn_engine_finalize(nrn_engine* e, int32_t init_update) {
         NRN_TRY(need_history(e->pops[q.src_pop]));
         NRN_TRY(need_history(e->pops[q.tgt_pop]));
     }
+    for (auto& p : e->pops)
+        if (p.d.drive.kind != NRN_DRIVE_NONE) NRN_TRY(dalloc0(&p.drive_buf, static_cast<size_t>(p.d.n), e->stream));
     if (init_update) {
         for (size_t i = 0; i < e->pops.size(); ++i) {
             nrn_pop_step_t a = e->pop_args(static_cast<int>(i), 0.0, 0, false);

@@ -15,6 +15,7 @@
 // 28 B (+20 B per-neuron a,b,c,d,v_peak), AdEx with conductances 64 B.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <vector>
 
@@ -49,6 +50,7 @@ struct PopArgs {
     // sampler's own float operations (p_k = p_{k-1}*lambda/k, F_k = F_{k-1}+p_k)
     float cdf[32];
     int n_cdf;
+    const float* drive_values;   // this step's drive drawn ahead, or null
     uint64_t seed;
     int64_t step;
     const int64_t* step_base;
@@ -119,7 +121,9 @@ __device__ __forceinline__ void pop_body(const PopArgs& a, const int i) {
             in_i = a.gin_inh[i];
         }
         if (a.drive_kind != NRN_DRIVE_NONE) {
-            float x = drive_value(a, static_cast<uint32_t>(a.gid_offset + i), static_cast<uint32_t>(step));
+            const float x = a.drive_values ? a.drive_values[i]
+                                           : drive_value(a, static_cast<uint32_t>(a.gid_offset + i),
+                                                         static_cast<uint32_t>(step));
             if (a.drive_kind == NRN_DRIVE_POISSON_GEXC) in_e = in_e + x;
             else I = I + x;
         }
@@ -292,6 +296,15 @@ __global__ void __launch_bounds__(256) pop_group_kernel(const __grid_constant__ 
 
 constexpr int kPopThreads = 256;
 
+// The drive of every neuron of one population for the step (drive_value,
+// the neuron update's own sampler).
+__global__ void __launch_bounds__(256) drive_fill_kernel(const __grid_constant__ PopArgs a, float* out) {
+    long long step = a.step;
+    if (a.step_base) step += *a.step_base;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += gridDim.x * blockDim.x)
+        out[i] = drive_value(a, static_cast<uint32_t>(a.gid_offset + i), static_cast<uint32_t>(step));
+}
+
 template <int MODEL, bool HET, bool COND>
 void launch_kind(const PopGroup& g, cudaStream_t s) {
     if (g.n == 1) pop_step_kernel<MODEL, HET, COND><<<g.start[1], kPopThreads, 0, s>>>(g.p[0]);
@@ -422,6 +435,7 @@ nrn_status_t make_args(const nrn_pop_step_t& d, PopArgs& a, bool& het, bool& con
     a.send_ids = d.send_ids;
     a.send_cap = d.send_cap;
     a.err = d.err;
+    a.drive_values = d.drive_values;
     NRN_CHECK_ARG(a.send_hdr == nullptr || (d.send_ids != nullptr && d.send_cap >= 0),
                   "nrn_cuda_pop_step: send buffer without ids");
     if (d.model != NRN_MODEL_ADEX) cond = false;
@@ -461,6 +475,19 @@ nrn_status_t pop_step_group(const nrn_pop_step_t* list, int n, cudaStream_t s) {
 }
 
 }  // namespace nrn
+
+extern "C" nrn_status_t nrn_cuda_drive_fill(const nrn_pop_step_t* in, float* out, nrn_stream_t stream) {
+    using namespace nrn;
+    NRN_CHECK_ARG(in != nullptr && (out != nullptr || in->n == 0), "nrn_cuda_drive_fill: null arguments");
+    PopArgs a;
+    bool het = false, cond = false;
+    NRN_TRY(make_args(*in, a, het, cond));
+    if (in->n == 0 || a.drive_kind == NRN_DRIVE_NONE) return NRN_OK;
+    const int blocks = std::min((in->n + 255) / 256, 8 * sm_count_current());
+    drive_fill_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a, out);
+    NRN_CUDA_TRY(cudaGetLastError());
+    return NRN_OK;
+}
 
 extern "C" nrn_status_t nrn_cuda_pop_step(const nrn_pop_step_t* in, nrn_stream_t stream) {
     NRN_CHECK_ARG(in != nullptr, "nrn_cuda_pop_step: null arguments");

@@ -135,7 +135,7 @@ __device__ int spikes_in(int4 r, const int32_t* ring, const int32_t* cnt, long l
 struct Seg {
     int j;            // source
     long long seg;    // j * nd + k
-    long long s0, s1; // synapse range
+    uint32_t s0, s1;  // synapse range (a projection holds < 2^32 synapses)
     int T;            // events applied through T
     int e;            // apply through e
     StepsPtr P;       // source spikes in (T, e] (per-warp shared memory)
@@ -282,7 +282,7 @@ __device__ __forceinline__ void build_table(const WalkArgs& a, const Seg& g, flo
 // Walks synapses [c0, c1) of the segment, one per lane and round; with
 // deliver, adds the updated weights into the target accumulators.
 template <bool MOD>
-__device__ __forceinline__ unsigned walk_chunk(const WalkArgs& a, const Seg& g, long long c0, long long c1,
+__device__ __forceinline__ unsigned walk_chunk(const WalkArgs& a, const Seg& g, uint32_t c0, uint32_t c1,
                                                bool deliver, int now, int lane, uint32_t t_first, float w_first) {
     // the target trace at the first source spike is loaded with the target's spike steps
     const bool has_pre = g.P.n > 0;
@@ -292,17 +292,18 @@ __device__ __forceinline__ unsigned walk_chunk(const WalkArgs& a, const Seg& g, 
     // the next round's target and weight (the HBM stream) are loaded a round
     // ahead; the target's spike steps and trace (L2) within the round
     unsigned n = 0;
-    long long syn = c0 + lane;
+    const uint32_t len = c1 - c0;   // at most one chunk: offsets never wrap
     uint32_t t_next = t_first;
     float w_next = w_first;
 #pragma unroll 1
-    for (; syn < c1; syn += 32) {
+    for (uint32_t o = lane; o < len; o += 32) {
+        const uint32_t syn = c0 + o;
         const uint32_t t = t_next;
         const float w = w_next;
         const int4 r = a.tgt_recent[t];
         const float xp0 = has_pre ? ring0[t] : 0.0f;
         const float md = MOD ? __ldcs(a.mod + syn) : 1.0f;
-        if (syn + 32 < c1) {
+        if (o + 32 < len) {
             t_next = __ldcs(a.tgt + syn + 32);
             w_next = a.w[syn + 32];
         }
@@ -338,13 +339,13 @@ __device__ unsigned segment_chunk(const WalkArgs& a, int* sP, float* sX, int j, 
                                   bool deliver, bool sweep, int now, int m_new, int lane) {
     __syncwarp();   // the warp is done with the previous segment's lists
     const long long seg = static_cast<long long>(j) * a.nd + k;
-    long long s0 = 0, s1 = 0;
+    uint32_t s0 = 0, s1 = 0;
     int T = 0;
     float xT = 0.0f;
     int4 rj = make_int4(-1, -1, -1, -1);
     if (lane == 0) {
-        s0 = a.seg_ptr[seg];
-        s1 = a.seg_ptr[seg + 1];
+        s0 = static_cast<uint32_t>(a.seg_ptr[seg]);
+        s1 = static_cast<uint32_t>(a.seg_ptr[seg + 1]);
         T = a.seg_last[seg];
         xT = a.seg_x[seg];
         rj = a.src_recent[j];
@@ -356,13 +357,13 @@ __device__ unsigned segment_chunk(const WalkArgs& a, int* sP, float* sX, int j, 
         const int newest = __shfl_sync(0xffffffffu, rj.x, 0);
         if (newest >= now - (a.dmin + a.nd - 1) || T >= now - a.stale) return 0;
     }
-    const long long c0 = s0 + static_cast<long long>(chunk) * a.chunk;
-    if (c0 >= s1) return 0;
-    const long long c1 = c0 + a.chunk < s1 ? c0 + a.chunk : s1;
+    if (static_cast<uint32_t>(chunk) * static_cast<uint32_t>(a.chunk) >= s1 - s0) return 0;
+    const uint32_t c0 = s0 + static_cast<uint32_t>(chunk) * static_cast<uint32_t>(a.chunk);
+    const uint32_t c1 = s1 - c0 > static_cast<uint32_t>(a.chunk) ? c0 + a.chunk : s1;
     // the first round's synapses, independent of the segment's history
     uint32_t t_first = 0;
     float w_first = 0.0f;
-    if (c0 + lane < c1) {
+    if (static_cast<uint32_t>(lane) < c1 - c0) {
         t_first = __ldcs(a.tgt + c0 + lane);
         w_first = a.w[c0 + lane];
     }
@@ -408,12 +409,13 @@ __device__ unsigned segment_chunk(const WalkArgs& a, int* sP, float* sX, int j, 
         }
     } else if (deliver) {
         // nothing to apply (or a history error, flagged): deliver only
-        long long syn = c0 + lane;
-        if (syn < c1) {
-            atomicAdd(a.acc + t_first, MOD ? w_first * __ldg(a.mod + syn) : w_first);
+        const uint32_t len = c1 - c0;
+        if (static_cast<uint32_t>(lane) < len) {
+            atomicAdd(a.acc + t_first, MOD ? w_first * __ldg(a.mod + c0 + lane) : w_first);
             ++n;
         }
-        for (syn += 32; syn < c1; syn += 32) {
+        for (uint32_t o = lane + 32; o < len; o += 32) {
+            const uint32_t syn = c0 + o;
             const float wv = a.w[syn];
             atomicAdd(a.acc + __ldg(a.tgt + syn), MOD ? wv * __ldg(a.mod + syn) : wv);
             ++n;
