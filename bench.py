@@ -173,6 +173,11 @@ def cpu_reference(args, world_steps_hint=None):
     }
 
 
+# dram__bytes_read.sum + dram__bytes_write.sum of walk_kernel (8.198 MB) and
+# deliver_kernel (2.773 MB) per launch in ncu captures of the bench network at
+# 262,144 neurons (bench.py --scale 0.25), scaled x4 to 1,048,576 neurons
+DELIVERY_TRAFFIC_PER_STEP = 4 * (8.1984e6 + 256 + 2.773248e6)
+
 BSR_N = 262_144          # pre = post neurons of the batched block-sparse workload
 BSR_DENSITY = 0.02       # fraction of the 64x64 block slots present
 BSR_P = 0.01             # spike probability per neuron, trial and step
@@ -543,9 +548,13 @@ def main():
         + (args.steps + chunk - 1) // chunk,
         "phase_ms_per_step": {k: v / args.profile_steps for k, v in phases.items()},
         "exchange_ms_per_window": exch_ms,
-        "roofline": {"kernel": "deliver", "dominant_phase": dom, "bound": "hbm", "achieved": achieved,
-                     "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
-                     "peak_kind": peaks_kind, "traffic": None},
+        "roofline": {"kernel": "walk_kernel + deliver_kernel (delivery phase)", "dominant_phase": dom,
+                     "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / peaks["hbm_gbs"], "peak_kind": peaks_kind,
+                     "traffic": DELIVERY_TRAFFIC_PER_STEP if args.workload == "brunel_stdp" and args.scale == 1.0
+                     else None,
+                     "traffic_note": "DRAM bytes per step of walk_kernel + deliver_kernel from the ncu captures "
+                                     "at 262,144 neurons, x4 to the bench size (the units scale with the network)"},
         "e2e": {"value": e2e, "unit": "events/s", "h2d_bytes_per_step": h2d / args.steps,
                 "d2h_bytes_per_step": d2h / args.steps,
                 "seconds": {"upload": t_up - t0, "run": t_run - t_up, "raster": t1 - t_run}},
