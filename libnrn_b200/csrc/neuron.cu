@@ -105,6 +105,24 @@ __device__ __forceinline__ float drive_value(const PopArgs& a, uint32_t gid, uin
     return a.d1 * static_cast<float>(k);
 }
 
+// The LIF update of one neuron (src/neuron/lif.cpp:80-97), each operation
+// rounded to fp32 in the reference's order; returns whether it spiked.
+__device__ __forceinline__ bool lif_math(float v, float ref, float I, float dtf, float v_rest, float v_th,
+                                         float v_reset, float tau_m, float tau_ref, float c_m, float i_bg, float& vn_out,
+                                         float& r_out) {
+    const bool active = ref <= 0.0f;
+    float r = ref > 0.0f ? ref - dtf : ref;
+    float lk = (-(v - v_rest)) / tau_m;
+    float in = (I + i_bg) / c_m;
+    float dv = dtf * (lk + in);
+    float vn = active ? v + dv : v;
+    const bool spiked = (vn >= v_th) && active;
+    if (spiked) { vn = v_reset; r = tau_ref; }
+    vn_out = vn;
+    r_out = r;
+    return spiked;
+}
+
 // One neuron of one population: every thread of a warp belongs to the same
 // population (the compaction below is warp-wide).
 template <int MODEL, bool HET, bool COND>
@@ -133,14 +151,8 @@ __device__ __forceinline__ void pop_body(const PopArgs& a, const int i) {
             const float v_reset = par<HET>(a, 2, i), tau_m = par<HET>(a, 3, i);
             const float tau_ref = par<HET>(a, 4, i), c_m = par<HET>(a, 5, i);
             const float i_bg = par<HET>(a, 6, i);
-            const bool active = ref <= 0.0f;
-            float r = ref > 0.0f ? ref - a.dtf : ref;
-            float lk = (-(v - v_rest)) / tau_m;
-            float in = (I + i_bg) / c_m;
-            float dv = a.dtf * (lk + in);
-            float vn = active ? v + dv : v;
-            spiked = (vn >= v_th) && active;
-            if (spiked) { vn = v_reset; r = tau_ref; }
+            float vn, r;
+            spiked = lif_math(v, ref, I, a.dtf, v_rest, v_th, v_reset, tau_m, tau_ref, c_m, i_bg, vn, r);
             a.v[i] = vn;
             a.ref[i] = r;
         } else if (MODEL == NRN_MODEL_ADEX) {
@@ -296,6 +308,151 @@ __global__ void __launch_bounds__(256) pop_group_kernel(const __grid_constant__ 
 
 constexpr int kPopThreads = 256;
 
+__device__ __forceinline__ float4 ld4(const float* p, int i) { return *reinterpret_cast<const float4*>(p + i); }
+__device__ __forceinline__ void st4(float* p, int i, float4 x) { *reinterpret_cast<float4*>(p + i) = x; }
+__device__ __forceinline__ float& at(float4& x, int k) { return k == 0 ? x.x : k == 1 ? x.y : k == 2 ? x.z : x.w; }
+
+// Appends each lane's cnt ids to a list whose length is *count: a scan of
+// the counts over the warp (every lane must call it), one atomic per warp;
+// the ids in lane order.  Returns the warp's total.
+template <class Write>
+__device__ __forceinline__ int warp_append(int cnt, int* count, Write write) {
+    const int lane = threadIdx.x & 31;
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    const int tot = __shfl_sync(0xffffffffu, incl, 31);
+    int base = 0;
+    if (lane == 31 && tot > 0) base = atomicAdd(count, tot);
+    base = __shfl_sync(0xffffffffu, base, 31);
+    if (cnt > 0) write(base + incl - cnt);
+    return tot;
+}
+
+// LIF with uniform parameters, four neurons per thread (float4 state, n a
+// multiple of 4, arrays 16-byte aligned): the same arithmetic as pop_body
+// (lif_math), with wider memory transactions.
+__global__ void __launch_bounds__(256) lif4_group_kernel(const __grid_constant__ PopGroup g) {
+    int q = 0;
+    while (q + 1 < g.n && static_cast<int>(blockIdx.x) >= g.start[q + 1]) ++q;
+    const PopArgs& a = g.p[q];
+    const int i0 = 4 * ((static_cast<int>(blockIdx.x) - g.start[q]) * blockDim.x + threadIdx.x);
+    const int lane = threadIdx.x & 31;
+    long long step = a.step;
+    if (a.step_base) step += *a.step_base;
+    int sp[4] = {0, 0, 0, 0};
+    if (i0 < a.n) {
+        float4 I = a.i_syn ? ld4(a.i_syn, i0) : make_float4(0.f, 0.f, 0.f, 0.f);
+        if (a.drive_kind != NRN_DRIVE_NONE) {
+            float4 x;
+            if (a.drive_values) {
+                x = ld4(a.drive_values, i0);
+            } else {
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    at(x, k) = drive_value(a, static_cast<uint32_t>(a.gid_offset + i0 + k), static_cast<uint32_t>(step));
+            }
+            I.x = I.x + x.x; I.y = I.y + x.y; I.z = I.z + x.z; I.w = I.w + x.w;
+        }
+        float4 v = ld4(a.v, i0), ref = ld4(a.ref, i0);
+        const float* u = a.uniform;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            float vn, r;
+            sp[k] = lif_math(at(v, k), at(ref, k), at(I, k), a.dtf, u[0], u[1], u[2], u[3], u[4], u[5], u[6], vn, r);
+            at(v, k) = vn;
+            at(ref, k) = r;
+        }
+        st4(a.v, i0, v);
+        st4(a.ref, i0, ref);
+        const float4 s4 = make_float4(sp[0] ? 1.f : 0.f, sp[1] ? 1.f : 0.f, sp[2] ? 1.f : 0.f, sp[3] ? 1.f : 0.f);
+        if (a.spike) st4(a.spike, i0, s4);
+        if (a.n_traces > 0 && (a.trace_slow_ratio <= 1 || step % a.trace_slow_ratio == 0)) {
+            for (int k = 0; k < a.n_traces; ++k) {
+                const float d = a.trace_decay[k];
+                float4 x;
+                float* dst;
+                if (a.trace_ring[k] != nullptr) {
+                    const long long mask = a.trace_ring_depth - 1;
+                    x = ld4(a.trace_ring[k] + ((step - 1) & mask) * a.n, i0);
+                    dst = a.trace_ring[k] + (step & mask) * a.n;
+                } else {
+                    x = ld4(a.trace[k], i0);
+                    dst = a.trace[k];
+                }
+                x.x = x.x * d + s4.x; x.y = x.y * d + s4.y; x.z = x.z * d + s4.z; x.w = x.w * d + s4.w;
+                st4(dst, i0, x);
+            }
+        }
+        if (a.i_syn) st4(a.i_syn, i0, make_float4(0.f, 0.f, 0.f, 0.f));
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            if (!sp[k]) continue;
+            const int i = i0 + k;
+            if (a.post_recent != nullptr) {
+                const int t = static_cast<int>(step);
+                const int4 r = a.post_recent[i];
+                a.post_recent[i] = make_int4(t, r.x, r.y, r.z);
+                const int c = a.post_cnt[i];
+                a.post_ring[static_cast<long long>(i) * a.post_ring_k + (c % a.post_ring_k)] = t;
+                a.post_cnt[i] = c + 1;
+            }
+            if (a.win_mask != nullptr) a.win_mask[i] |= 1u << static_cast<int>(step % a.win);
+        }
+    }
+    const int cnt = sp[0] + sp[1] + sp[2] + sp[3];
+    auto write_ids = [&](int* dst, int cap, int pos) {
+        for (int k = 0; k < 4; ++k) {
+            if (!sp[k]) continue;
+            if (pos < cap) dst[pos] = a.id_offset + i0 + k;
+            else if (a.err) atomicCAS(a.err, 0, 4);
+            ++pos;
+        }
+    };
+    if (a.send_hdr) {
+        // window send buffer: ids in step order, the running total in send_hdr[win]
+        const int uu = static_cast<int>(step % a.win);
+        const int tot = warp_append(cnt, a.send_hdr + a.win, [&](int pos) { write_ids(a.send_ids, a.send_cap, pos); });
+        if (lane == 0 && tot) atomicAdd(a.send_hdr + uu, tot);
+    } else if (a.spike_ids) {
+        int* ids = a.spike_ids;
+        int* count = a.spike_count;
+        if (a.hist_depth > 0) {
+            const int slot = static_cast<int>(step % a.hist_depth);
+            ids += static_cast<long long>(slot) * a.hist_cap;
+            count += slot;
+        }
+        warp_append(cnt, count, [&](int pos) { write_ids(ids, 0x7fffffff, pos); });
+    }
+    if (a.raster_gid) {
+        // one 64-bit atomic per warp on the raster count
+        int incl = cnt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        const int tot = __shfl_sync(0xffffffffu, incl, 31);
+        unsigned long long base = 0;
+        if (lane == 31 && tot > 0) base = atomicAdd(a.raster_count, static_cast<unsigned long long>(tot));
+        base = __shfl_sync(0xffffffffu, base, 31);
+        if (cnt > 0) {
+            unsigned long long pos = base + static_cast<unsigned long long>(incl - cnt);
+            for (int k = 0; k < 4; ++k) {
+                if (!sp[k]) continue;
+                if (pos < static_cast<unsigned long long>(a.raster_cap)) {
+                    a.raster_step[pos] = static_cast<int>(step);
+                    a.raster_gid[pos] = a.gid_offset + i0 + k;
+                }
+                ++pos;
+            }
+        }
+    }
+}
+
 // The drive of every neuron of one population for the step (drive_value,
 // the neuron update's own sampler).
 __global__ void __launch_bounds__(256) drive_fill_kernel(const __grid_constant__ PopArgs a, float* out) {
@@ -309,6 +466,20 @@ template <int MODEL, bool HET, bool COND>
 void launch_kind(const PopGroup& g, cudaStream_t s) {
     if (g.n == 1) pop_step_kernel<MODEL, HET, COND><<<g.start[1], kPopThreads, 0, s>>>(g.p[0]);
     else pop_group_kernel<MODEL, HET, COND><<<g.start[g.n], kPopThreads, 0, s>>>(g);
+}
+
+// The four-neurons-a-thread LIF kernel applies when every population's
+// size is a multiple of 4 and its arrays are 16-byte aligned.
+bool lif4_ok(const PopGroup& g) {
+    auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+    for (int k = 0; k < g.n; ++k) {
+        const PopArgs& a = g.p[k];
+        if (a.n % 4 != 0 || !al(a.v) || !al(a.ref) || !al(a.spike) || !al(a.i_syn) || !al(a.drive_values))
+            return false;
+        for (int t = 0; t < a.n_traces; ++t)
+            if (!al(a.trace[t]) || !al(a.trace_ring[t])) return false;
+    }
+    return true;
 }
 
 void launch_group(const PopGroup& g, int model, bool het, bool cond, cudaStream_t s) {
@@ -468,7 +639,18 @@ nrn_status_t pop_step_group(const nrn_pop_step_t* list, int n, cudaStream_t s) {
             ++g.n;
             done[r] = 1;
         }
-        launch_group(g, list[q].model, het, cond, s);
+        if (list[q].model == NRN_MODEL_LIF && !het && lif4_ok(g)) {
+            // four neurons a thread: block ranges in units of 4 * kPopThreads neurons
+            int b = 0;
+            for (int k = 0; k < g.n; ++k) {
+                g.start[k] = b;
+                b += (g.p[k].n + 4 * kPopThreads - 1) / (4 * kPopThreads);
+            }
+            g.start[g.n] = b;
+            lif4_group_kernel<<<b, kPopThreads, 0, s>>>(g);
+        } else {
+            launch_group(g, list[q].model, het, cond, s);
+        }
         NRN_CUDA_TRY(cudaGetLastError());
     }
     return NRN_OK;
