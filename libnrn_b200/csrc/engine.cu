@@ -105,7 +105,6 @@ struct EngineProj {
     bool walk = false;           // updates applied by segment walks (plastic.cu)
     int32_t* seg_last = nullptr;
     float* seg_x = nullptr;
-    int32_t* seg_done = nullptr;
     float* pre_snap = nullptr;   // [n_src][pre_depth] source trace at window ends
     float* post_ring = nullptr;  // [ring_depth][n_tgt] target trace at every step
     int32_t pre_depth = 1;
@@ -137,7 +136,6 @@ struct nrn_engine {
     std::map<int, cudaGraphExec_t> graphs;
     int* d_err = nullptr;                 // device error flag (plasticity, exchange)
     bool use_graphs = true;
-    int32_t walk_chunk = 128;             // synapses per warp unit of the STDP walks
     // partition over GPUs
     int32_t rank = 0, world = 1;
     ncclComm_t comm = nullptr;
@@ -163,7 +161,7 @@ struct nrn_engine {
             free_csr(q.csr);
             cudaFree(q.x_pre);
             cudaFree(q.x_post);
-            cudaFree(q.seg_last); cudaFree(q.seg_x); cudaFree(q.seg_done);
+            cudaFree(q.seg_last); cudaFree(q.seg_x);
             cudaFree(q.pre_snap); cudaFree(q.post_ring);
         }
         cudaFree(d_step); cudaFree(d_events); cudaFree(d_raster_count); cudaFree(d_err);
@@ -329,7 +327,6 @@ struct nrn_engine {
         a.hist_src = hist(q.src_pop);
         a.seg_last = q.seg_last;
         a.seg_x = q.seg_x;
-        a.seg_done = q.seg_done;
         a.src_recent = reinterpret_cast<const int4*>(ps.recent);
         a.src_ring = ps.ring;
         a.src_cnt = ps.cnt;
@@ -355,7 +352,6 @@ struct nrn_engine {
         a.sweep_period = kSweepPeriod;
         a.sweep_rows = (q.csr.n_src + kSweepPeriod - 1) / kSweepPeriod;
         a.stale = kStale;
-        a.chunk = walk_chunk;
         a.err = d_err;
         a.events = d_events;
         return a;
@@ -657,10 +653,6 @@ nrn_status_t nrn_engine_create(nrn_engine** out, int device, double dt, int32_t 
     e->slow_ratio = slow_ratio;
     const char* ng = std::getenv("NRN_NO_GRAPHS");
     e->use_graphs = !(ng && ng[0] == '1');
-    if (const char* wc = std::getenv("NRN_WALK_CHUNK")) {
-        const int c = std::atoi(wc);
-        if (c >= 32 && c % 32 == 0 && c <= 4096) e->walk_chunk = c;
-    }
     NRN_CUDA_TRY(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
     NRN_CUDA_TRY(cudaStreamCreateWithFlags(&e->side, cudaStreamNonBlocking));
     NRN_CUDA_TRY(cudaEventCreateWithFlags(&e->fork_ev, cudaEventDisableTiming));
@@ -1007,7 +999,6 @@ nrn_status_t nrn_engine_finalize(nrn_engine* e, int32_t init_update) {
         const size_t nseg = static_cast<size_t>(q.csr.n_src) * q.csr.nd;
         NRN_TRY(dalloc0(&q.seg_last, nseg, e->stream));
         NRN_TRY(dalloc0(&q.seg_x, nseg, e->stream));
-        NRN_TRY(dalloc0(&q.seg_done, nseg, e->stream));
         const int dmax = q.csr.dmin + q.csr.nd - 1;
         q.pre_depth = pow2((kSweepPeriod + kStale + e->win + dmax) / e->win + 4);
         NRN_TRY(dalloc0(&q.pre_snap, static_cast<size_t>(q.pre_depth) * q.csr.n_src, e->stream));

@@ -71,7 +71,6 @@ struct WalkArgs {
     nrn_spike_hist_t hist_src{};      // spike history of the (whole) source population
     int32_t* seg_last = nullptr;      // [n_src*nd] events applied through this step
     float* seg_x = nullptr;           // [n_src*nd] x_pre at that step
-    int32_t* seg_done = nullptr;      // [n_src*nd] chunk counter of the walk in flight
     // spike steps of the sources (index in the source population): newest
     // four in src_recent; older ones in src_ring/src_cnt for [src_lo, src_hi)
     const int4* src_recent = nullptr;
@@ -96,7 +95,6 @@ struct WalkArgs {
     int64_t sweep_rows = 0;           // rows looked at per step by the sweep
     int32_t sweep_period = 1;         // steps for the sweep to pass every row
     int32_t stale = 1;                // the sweep walks a segment not walked for this many steps
-    int32_t chunk = 128;              // synapses per warp work unit (multiple of 32)
     int* err = nullptr;
     unsigned long long* events = nullptr;
 };

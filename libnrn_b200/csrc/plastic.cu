@@ -28,8 +28,10 @@
 // of the source (newest four per neuron, older ones in a ring for the
 // neurons of this GPU) and of each target.
 //
-// Work unit: one warp per (arriving spike, segment chunk of `chunk` synapses);
-// the last chunk of a segment to finish advances the segment's T.
+// Work unit: one block per (arriving spike, segment), its threads striding
+// over the segment's synapses, sharing the segment's source spike steps and
+// trace table; sweep and flush units look at groups of segments and walk
+// those that need it.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -44,7 +46,7 @@ namespace nrn {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kWarps = kThreads / 32;
+constexpr int kMinBlocks = 4;    // 64 registers a thread
 constexpr int kMaxPost = 64;     // target spike steps one walk may need (the ring depth)
 constexpr int kMaxPre = 8;       // source spike steps one walk may need
 constexpr int kMaxSpan = 1280;   // steps one walk may cover (x_pre table per warp)
@@ -240,16 +242,16 @@ __device__ __forceinline__ float walk_syn(const WalkArgs& a, const Seg& g, int t
     return walk_syn_long<MOD>(a, g, i, r, w, mod, now, xp0);
 }
 
-// The source trace over (T, e] into the warp's shared table, window by
-// window (one window per lane) from the snapshot at the window's start --
+// The source trace over (T, e] into the block's shared table, window by
+// window (one window per thread) from the snapshot at the window's start --
 // or, for the first, from x_pre(T) -- with the same operations as the
 // per-step update.
 __device__ __forceinline__ void build_table(const WalkArgs& a, const Seg& g, float* sX, float xT, int m_new,
-                                            int lane) {
+                                            int tid) {
     const int W = a.win, e = g.e;
     const int m0 = (g.T + 1) / W + 1;   // window ends b = m*W - 1 in (T, e): m = m0, m0+1, ...
     const int n_pieces = 1 + (m0 * W - 1 < e ? (e - (m0 * W - 1) + W - 1) / W : 0);
-    for (int pc = lane; pc < n_pieces; pc += 32) {
+    for (int pc = tid; pc < n_pieces; pc += kThreads) {
         int start;
         float x;
         if (pc == 0) {
@@ -276,14 +278,14 @@ __device__ __forceinline__ void build_table(const WalkArgs& a, const Seg& g, flo
             sX[u - g.T - 1] = x;
         }
     }
-    __syncwarp();
 }
 
-// Walks synapses [c0, c1) of the segment, one per lane and round; with
-// deliver, adds the updated weights into the target accumulators.
+// Walks the segment's synapses, thread tid taking offsets tid, tid +
+// kThreads, ...; with deliver, adds the updated weights into the target
+// accumulators.
 template <bool MOD>
-__device__ __forceinline__ unsigned walk_chunk(const WalkArgs& a, const Seg& g, uint32_t c0, uint32_t c1,
-                                               bool deliver, int now, int lane, uint32_t t_first, float w_first) {
+__device__ __forceinline__ unsigned walk_block(const WalkArgs& a, const Seg& g, bool deliver, int now, int tid,
+                                               uint32_t t_first, float w_first) {
     // the target trace at the first source spike is loaded with the target's spike steps
     const bool has_pre = g.P.n > 0;
     const int t0 = has_pre ? g.P[0] : 0;
@@ -292,20 +294,20 @@ __device__ __forceinline__ unsigned walk_chunk(const WalkArgs& a, const Seg& g, 
     // the next round's target and weight (the HBM stream) are loaded a round
     // ahead; the target's spike steps and trace (L2) within the round
     unsigned n = 0;
-    const uint32_t len = c1 - c0;   // at most one chunk: offsets never wrap
+    const uint32_t len = g.s1 - g.s0;   // a projection holds < 2^32 synapses
     uint32_t t_next = t_first;
     float w_next = w_first;
 #pragma unroll 1
-    for (uint32_t o = lane; o < len; o += 32) {
-        const uint32_t syn = c0 + o;
+    for (uint32_t o = tid; o < len; o += kThreads) {
+        const uint32_t syn = g.s0 + o;
         const uint32_t t = t_next;
         const float w = w_next;
         const int4 r = a.tgt_recent[t];
         const float xp0 = has_pre ? ring0[t] : 0.0f;
         const float md = MOD ? __ldcs(a.mod + syn) : 1.0f;
-        if (o + 32 < len) {
-            t_next = __ldcs(a.tgt + syn + 32);
-            w_next = a.w[syn + 32];
+        if (o + kThreads < len) {
+            t_next = __ldcs(a.tgt + syn + kThreads);
+            w_next = a.w[syn + kThreads];
         }
         const float w1 = walk_syn<MOD>(a, g, t0, t, r, w, md, now, xp0);
         if (__float_as_uint(w1) != __float_as_uint(w)) a.w[syn] = w1;
@@ -323,99 +325,85 @@ __device__ __forceinline__ void finish_seg(const WalkArgs& a, const Seg& g) {
     a.seg_last[g.seg] = g.e;
 }
 
-// One chunk of a.chunk synapses of segment (j, k): applies the updates
-// through e (and, with deliver, delivers the updated weights); the last
-// chunk of the segment to finish records the segment's new state.  Every
-// chunk of a segment reads the same state (the write happens only after
-// all of them have counted themselves) and so makes the same decision.
-// With sweep, the chunk is skipped when its source has spikes still to
-// arrive (their walks come) or the segment was walked recently.  Loads are
-// grouped so that the chain per chunk is: segment bounds, state and source
-// spike steps (one round trip); trace snapshots and the first synapses
-// (one); the targets' spike steps and trace (one).  Returns the number of
-// events this lane delivered.
+// The segment state one block reads before walking (thread 0 loads it).
+struct SegHead {
+    uint32_t s0, s1;
+    int T;
+    int nP;   // source spikes in (T, e]; -2: walked through e already; -1: history error (flagged)
+    float xT;
+};
+
+// Segment (j, k) by the whole block: applies the updates through e and,
+// with deliver, delivers the updated weights.  The load chain is: segment
+// bounds, state and source spike steps (thread 0, one round trip); trace
+// snapshots and the first synapses (one); the targets' spike steps and
+// trace (one per round).  A segment is walked by one block at a time (an
+// arrival walk and a sweep walk never meet: the sweep skips sources with
+// spikes still to arrive), so the block records the new state as soon as
+// its trace table is built.  Returns the number of events this thread
+// delivered.
 template <bool MOD>
-__device__ unsigned segment_chunk(const WalkArgs& a, int* sP, float* sX, int j, int k, int chunk, int e,
-                                  bool deliver, bool sweep, int now, int m_new, int lane) {
-    __syncwarp();   // the warp is done with the previous segment's lists
+__device__ unsigned segment_walk(const WalkArgs& a, SegHead& head, int* sP, float* sX, int j, int k, int e,
+                                 bool deliver, int now, int m_new, int tid) {
+    __syncthreads();   // the block is done with the previous segment's lists
     const long long seg = static_cast<long long>(j) * a.nd + k;
-    uint32_t s0 = 0, s1 = 0;
-    int T = 0;
-    float xT = 0.0f;
-    int4 rj = make_int4(-1, -1, -1, -1);
-    if (lane == 0) {
-        s0 = static_cast<uint32_t>(a.seg_ptr[seg]);
-        s1 = static_cast<uint32_t>(a.seg_ptr[seg + 1]);
-        T = a.seg_last[seg];
-        xT = a.seg_x[seg];
-        rj = a.src_recent[j];
-    }
-    s0 = __shfl_sync(0xffffffffu, s0, 0);
-    s1 = __shfl_sync(0xffffffffu, s1, 0);
-    T = __shfl_sync(0xffffffffu, T, 0);
-    if (sweep) {
-        const int newest = __shfl_sync(0xffffffffu, rj.x, 0);
-        if (newest >= now - (a.dmin + a.nd - 1) || T >= now - a.stale) return 0;
-    }
-    if (static_cast<uint32_t>(chunk) * static_cast<uint32_t>(a.chunk) >= s1 - s0) return 0;
-    const uint32_t c0 = s0 + static_cast<uint32_t>(chunk) * static_cast<uint32_t>(a.chunk);
-    const uint32_t c1 = s1 - c0 > static_cast<uint32_t>(a.chunk) ? c0 + a.chunk : s1;
-    // the first round's synapses, independent of the segment's history
-    uint32_t t_first = 0;
-    float w_first = 0.0f;
-    if (static_cast<uint32_t>(lane) < c1 - c0) {
-        t_first = __ldcs(a.tgt + c0 + lane);
-        w_first = a.w[c0 + lane];
-    }
-    unsigned n = 0;
-    int nP = -2;   // -2: nothing to apply (walked through e already)
-    if (T < e) {
-        nP = -1;
-        if (lane == 0) {
-            if (e - T > kMaxSpan) {
+    if (tid == 0) {
+        SegHead h;
+        h.s0 = static_cast<uint32_t>(a.seg_ptr[seg]);
+        h.s1 = static_cast<uint32_t>(a.seg_ptr[seg + 1]);
+        h.T = a.seg_last[seg];
+        h.xT = a.seg_x[seg];
+        const int4 rj = a.src_recent[j];
+        h.nP = -2;
+        if (h.T < e) {
+            if (e - h.T > kMaxSpan) {
+                h.nP = -1;
                 set_err(a.err, ERR_SNAPSHOT);
             } else {
                 const bool own = j >= a.src_lo && j < a.src_hi;
-                nP = spikes_in(rj, own ? a.src_ring : nullptr, a.src_cnt, j - a.src_lo, a.ring_k, T, e, sP, kMaxPre);
-                if (nP < 0) set_err(a.err, ERR_HISTORY);
+                h.nP = spikes_in(rj, own ? a.src_ring : nullptr, a.src_cnt, j - a.src_lo, a.ring_k, h.T, e, sP, kMaxPre);
+                if (h.nP < 0) {
+                    h.nP = -1;
+                    set_err(a.err, ERR_HISTORY);
+                }
             }
         }
-        nP = __shfl_sync(0xffffffffu, nP, 0);
-        __syncwarp();
+        head = h;
     }
-    if (nP >= 0) {
+    __syncthreads();
+    const SegHead h = head;
+    const uint32_t len = h.s1 - h.s0;
+    // the first round's synapses, independent of the segment's history
+    uint32_t t_first = 0;
+    float w_first = 0.0f;
+    if (static_cast<uint32_t>(tid) < len) {
+        t_first = __ldcs(a.tgt + h.s0 + tid);
+        w_first = a.w[h.s0 + tid];
+    }
+    unsigned n = 0;
+    if (h.nP >= 0) {
         Seg g;
         g.j = j;
         g.seg = seg;
-        g.s0 = s0;
-        g.s1 = s1;
-        g.T = T;
+        g.s0 = h.s0;
+        g.s1 = h.s1;
+        g.T = h.T;
         g.e = e;
         g.P.p = sP;
-        g.P.n = nP;
+        g.P.n = h.nP;
         g.X = sX;
-        build_table(a, g, sX, __shfl_sync(0xffffffffu, xT, 0), m_new, lane);
-        n = walk_chunk<MOD>(a, g, c0, c1, deliver, now, lane, t_first, w_first);
-        __syncwarp();
-        if (lane == 0) {
-            const int n_chunks = static_cast<int>((s1 - s0 + a.chunk - 1) / a.chunk);
-            __threadfence();
-            const int done = atomicAdd(a.seg_done + seg, 1);
-            if (done == n_chunks - 1) {
-                __threadfence();
-                a.seg_done[seg] = 0;
-                finish_seg(a, g);
-            }
-        }
+        build_table(a, g, sX, h.xT, m_new, tid);
+        __syncthreads();
+        if (tid == 0) finish_seg(a, g);
+        n = walk_block<MOD>(a, g, deliver, now, tid, t_first, w_first);
     } else if (deliver) {
         // nothing to apply (or a history error, flagged): deliver only
-        const uint32_t len = c1 - c0;
-        if (static_cast<uint32_t>(lane) < len) {
-            atomicAdd(a.acc + t_first, MOD ? w_first * __ldg(a.mod + c0 + lane) : w_first);
+        if (static_cast<uint32_t>(tid) < len) {
+            atomicAdd(a.acc + t_first, MOD ? w_first * __ldg(a.mod + h.s0 + tid) : w_first);
             ++n;
         }
-        for (uint32_t o = lane + 32; o < len; o += 32) {
-            const uint32_t syn = c0 + o;
+        for (uint32_t o = tid + kThreads; o < len; o += kThreads) {
+            const uint32_t syn = h.s0 + o;
             const float wv = a.w[syn];
             atomicAdd(a.acc + __ldg(a.tgt + syn), MOD ? wv * __ldg(a.mod + syn) : wv);
             ++n;
@@ -424,63 +412,91 @@ __device__ unsigned segment_chunk(const WalkArgs& a, int* sP, float* sX, int j, 
     return n;
 }
 
+// Segments [g0, g0 + count) (count <= kThreads) through e: each thread
+// looks at one and the block walks, one after another, those with updates
+// to apply -- all of them (flush), or (sweep) those not walked for `stale`
+// steps whose source has no spike still to arrive.
 template <bool MOD>
-__global__ void __launch_bounds__(kThreads, 4) walk_kernel(const __grid_constant__ WalkArgs a, int mode,
-                                                        long long step_off, const long long* step_base) {
+__device__ void segment_group(const WalkArgs& a, SegHead& head, int* sP, float* sX, int* list, int* n_list,
+                              long long g0, int count, int e, bool sweep, int now, int m_new, int tid) {
+    __syncthreads();   // the previous group's list is read
+    if (tid == 0) *n_list = 0;
+    __syncthreads();
+    if (tid < count) {
+        const long long seg = g0 + tid;
+        const int j = static_cast<int>(seg / a.nd);
+        const int T = a.seg_last[seg];
+        bool go = T < e && a.seg_ptr[seg + 1] > a.seg_ptr[seg];
+        if (sweep) {
+            const int newest = a.src_recent[j].x;
+            go = go && newest < now - (a.dmin + a.nd - 1) && T < now - a.stale;
+        }
+        if (go) list[atomicAdd(n_list, 1)] = tid;
+    }
+    __syncthreads();
+    const int n = *n_list;
+    for (int q = 0; q < n; ++q) {
+        const long long seg = g0 + list[q];
+        segment_walk<MOD>(a, head, sP, sX, static_cast<int>(seg / a.nd), static_cast<int>(seg % a.nd), e, false, now,
+                          m_new, tid);
+    }
+}
+
+constexpr int kGroup = 8;   // segments a sweep unit looks at
+
+template <bool MOD>
+__global__ void __launch_bounds__(kThreads, kMinBlocks) walk_kernel(const __grid_constant__ WalkArgs a, int mode,
+                                                                  long long step_off, const long long* step_base) {
     using Scan = cub::BlockScan<long long, kThreads>;
     __shared__ typename Scan::TempStorage scan_tmp;
     __shared__ long long start[257];
     __shared__ int slot[256];
-    __shared__ int sP_all[kWarps][kMaxPre];
-    __shared__ float sX_all[kWarps][kMaxSpan];
-    int* sP = sP_all[threadIdx.x >> 5];
-    float* sX = sX_all[threadIdx.x >> 5];
+    __shared__ int sP[kMaxPre];
+    __shared__ float sX[kMaxSpan];
+    __shared__ SegHead head;
+    __shared__ int list[kThreads];
+    __shared__ int n_list;
 
+    const int tid = threadIdx.x;
     const long long step = step_off + (step_base ? *step_base : 0);
     const int now = static_cast<int>(step);
     const int m_new = static_cast<int>(step / a.win);   // newest snapshot written
-    const int lane = threadIdx.x & 31;
-    const long long warp = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
-    const long long n_warps = (static_cast<long long>(gridDim.x) * kThreads) >> 5;
-
-    const int chunks = (a.max_seg + a.chunk - 1) / a.chunk > 0 ? (a.max_seg + a.chunk - 1) / a.chunk : 1;
-    const long long per_row = static_cast<long long>(a.nd) * chunks;   // units of one source row
+    const long long n_seg = static_cast<long long>(a.n_src) * a.nd;
 
     if (mode == WALK_FLUSH) {
         // every segment through step - 1
-        const long long n_units = static_cast<long long>(a.n_src) * per_row;
-        for (long long u = warp; u < n_units; u += n_warps) {
-            const long long row = u / per_row;
-            const int rem = static_cast<int>(u - row * per_row);
-            segment_chunk<MOD>(a, sP, sX, static_cast<int>(row), rem / chunks, rem % chunks, now - 1, false, false,
-                               now, m_new, lane);
+        for (long long g0 = static_cast<long long>(blockIdx.x) * kThreads; g0 < n_seg;
+             g0 += static_cast<long long>(gridDim.x) * kThreads) {
+            const int count = n_seg - g0 < kThreads ? static_cast<int>(n_seg - g0) : kThreads;
+            segment_group<MOD>(a, head, sP, sX, list, &n_list, g0, count, now - 1, false, now, m_new, tid);
         }
         return;
     }
 
     // Arrivals: spikes of step - (dmin + k) through the delay-k segments,
-    // `chunks` units each.
+    // one unit each.
     long long units = 0;
-    if (threadIdx.x < a.nd) {
-        const long long src_step = step - (a.dmin + threadIdx.x);
-        slot[threadIdx.x] = src_step >= 0 ? static_cast<int>(src_step % a.hist_src.depth) : 0;
-        if (src_step >= 0) units = static_cast<long long>(a.hist_src.count[slot[threadIdx.x]]) * chunks;
+    if (tid < a.nd) {
+        const long long src_step = step - (a.dmin + tid);
+        slot[tid] = src_step >= 0 ? static_cast<int>(src_step % a.hist_src.depth) : 0;
+        if (src_step >= 0) units = a.hist_src.count[slot[tid]];
     }
     long long excl, n_arr;
     Scan(scan_tmp).ExclusiveSum(units, excl, n_arr);
-    if (threadIdx.x < a.nd) start[threadIdx.x] = excl;
-    if (threadIdx.x == 0) start[a.nd] = n_arr;
+    if (tid < a.nd) start[tid] = excl;
+    if (tid == 0) start[a.nd] = n_arr;
     __syncthreads();
 
-    // Sweep: rows [r0, r0 + rows), `chunks` units per segment.
+    // Sweep: the segments of rows [r0, r0 + rows), kGroup per unit.
     const long long r0 = (step % a.sweep_period) * a.sweep_rows;
     const long long left = a.n_src - r0;
     const long long rows = left <= 0 ? 0 : (a.sweep_rows < left ? a.sweep_rows : left);
-    const long long n_units = n_arr + rows * per_row;
+    const long long sweep_segs = rows * a.nd;
+    const long long n_units = n_arr + (sweep_segs + kGroup - 1) / kGroup;
     const int win_end = static_cast<int>((step / a.win) * a.win) - 1;   // spikes of all ranks known through here
 
     unsigned long long my_events = 0;
-    for (long long u = warp; u < n_units; u += n_warps) {
+    for (long long u = blockIdx.x; u < n_units; u += gridDim.x) {
         if (u < n_arr) {
             int lo = 0, hi = a.nd - 1;
             while (lo < hi) {
@@ -488,24 +504,19 @@ __global__ void __launch_bounds__(kThreads, 4) walk_kernel(const __grid_constant
                 if (start[mid] <= u) lo = mid; else hi = mid - 1;
             }
             const int k = lo;
-            const int local = static_cast<int>(u - start[k]);   // < spikes * chunks of one slot
-            const int spike = local / chunks;
-            const int chunk = local - spike * chunks;
+            const int spike = static_cast<int>(u - start[k]);
             const int j = a.hist_src.ids[static_cast<long long>(slot[k]) * a.hist_src.cap + spike];
-            my_events += segment_chunk<MOD>(a, sP, sX, j, k, chunk, now - 1, true, false, now, m_new, lane);
+            my_events += segment_walk<MOD>(a, head, sP, sX, j, k, now - 1, true, now, m_new, tid);
         } else {
-            const int q = static_cast<int>(u - n_arr);   // < sweep rows * per_row
-            const int row = q / static_cast<int>(per_row);
-            const int rem = q - row * static_cast<int>(per_row);
-            const int j = static_cast<int>(r0 + row);
-            const int k = rem / chunks;
-            segment_chunk<MOD>(a, sP, sX, j, k, rem % chunks, win_end, false, true, now, m_new, lane);
+            const long long q0 = (u - n_arr) * kGroup;
+            const int count = sweep_segs - q0 < kGroup ? static_cast<int>(sweep_segs - q0) : kGroup;
+            segment_group<MOD>(a, head, sP, sX, list, &n_list, r0 * a.nd + q0, count, win_end, true, now, m_new, tid);
         }
     }
-    // lane sums -> one atomic per warp
+    // thread sums -> one atomic per warp
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) my_events += __shfl_down_sync(0xffffffffu, my_events, o);
-    if (a.events && lane == 0 && my_events) atomicAdd(a.events, my_events);
+    if (a.events && (tid & 31) == 0 && my_events) atomicAdd(a.events, my_events);
 }
 
 }  // namespace
@@ -514,7 +525,6 @@ nrn_status_t walk_launch(const WalkArgs& a, int mode, long long step_off, const 
                          cudaStream_t s) {
     NRN_CHECK_ARG(a.nd >= 1 && a.nd <= 256, "plastic projection: at most 256 delay values");
     NRN_CHECK_ARG(a.win >= 1 && a.sweep_period >= 1, "plastic projection: bad window or sweep period");
-    NRN_CHECK_ARG(a.chunk >= 32 && a.chunk % 32 == 0, "plastic projection: chunk must be a multiple of 32");
     NRN_CHECK_ARG(a.pre_depth > 0 && (a.pre_depth & (a.pre_depth - 1)) == 0 && a.post_depth > 0 &&
                       (a.post_depth & (a.post_depth - 1)) == 0,
                   "plastic projection: trace ring depths must be powers of two");
