@@ -28,10 +28,13 @@
 // of the source (newest four per neuron, older ones in a ring for the
 // neurons of this GPU) and of each target.
 //
-// Work unit: one block per (arriving spike, segment), its threads striding
-// over the segment's synapses, sharing the segment's source spike steps and
-// trace table; sweep and flush units look at groups of segments and walk
-// those that need it.
+// Work: each block is a two-stage pipeline over its units.  Warp 0 (the
+// producer) prepares the next segment to walk -- state, source spike
+// steps, source trace table, new segment state, L2 prefetch of the
+// synapses -- while warps 1.. (the consumers) walk the current one, the
+// two buffers swapping at one block barrier per segment.  Units: one per
+// (arriving spike, segment); sweep and flush units are groups of segments
+// that the producer looks at one lane each.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -174,8 +177,16 @@ __device__ __forceinline__ float apply_events(const WalkArgs& a, const Seg& g, c
 }
 
 template <bool MOD>
-__device__ __noinline__ float walk_syn_long(const WalkArgs& a, const Seg& g, uint32_t i, int4 r, float w, float mod,
-                                            int now, float xp0) {
+__device__ __noinline__ float walk_syn_long(const WalkArgs& a, int j, int T, int e, const int* P, int nP,
+                                            const float* X, uint32_t i, int4 r, float w, float mod, int now,
+                                            float xp0) {
+    Seg g;
+    g.j = j;
+    g.T = T;
+    g.e = e;
+    g.P.p = P;
+    g.P.n = nP;
+    g.X = X;
     int buf[kMaxPost];
     StepsPtr Q;
     Q.p = buf;
@@ -239,19 +250,19 @@ __device__ __forceinline__ float walk_syn(const WalkArgs& a, const Seg& g, int t
     if (g.P.n == 1 && r.w <= g.T) return walk_one_pre<MOD>(a, g, t1, r, w, mod, xp0);
     if (g.P.n == 0 && r.x <= g.T) return w;   // nothing happened to this synapse
     if (r.w <= g.T) return apply_events<MOD>(a, g, steps_from4(r, g.T, g.e), i, w, mod, now, xp0);
-    return walk_syn_long<MOD>(a, g, i, r, w, mod, now, xp0);
+    return walk_syn_long<MOD>(a, g.j, g.T, g.e, g.P.p, g.P.n, g.X, i, r, w, mod, now, xp0);
 }
 
-// The source trace over (T, e] into the block's shared table, window by
-// window (one window per thread) from the snapshot at the window's start --
+// The source trace over (T, e] into a shared table by one warp, window by
+// window (one window per lane) from the snapshot at the window's start --
 // or, for the first, from x_pre(T) -- with the same operations as the
 // per-step update.
 __device__ __forceinline__ void build_table(const WalkArgs& a, const Seg& g, float* sX, float xT, int m_new,
-                                            int tid) {
+                                            int lane) {
     const int W = a.win, e = g.e;
     const int m0 = (g.T + 1) / W + 1;   // window ends b = m*W - 1 in (T, e): m = m0, m0+1, ...
     const int n_pieces = 1 + (m0 * W - 1 < e ? (e - (m0 * W - 1) + W - 1) / W : 0);
-    for (int pc = tid; pc < n_pieces; pc += kThreads) {
+    for (int pc = lane; pc < n_pieces; pc += 32) {
         int start;
         float x;
         if (pc == 0) {
@@ -280,34 +291,41 @@ __device__ __forceinline__ void build_table(const WalkArgs& a, const Seg& g, flo
     }
 }
 
-// Walks the segment's synapses, thread tid taking offsets tid, tid +
-// kThreads, ...; with deliver, adds the updated weights into the target
+constexpr int kConsumers = kThreads - 32;   // threads that walk synapses (warps 1..)
+constexpr int kGroup = 8;                    // segments a sweep or flush unit looks at
+
+__device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+
+// Walks the segment's synapses, consumer thread c taking offsets c, c +
+// kConsumers, ...; with deliver, adds the updated weights into the target
 // accumulators.
 template <bool MOD>
-__device__ __forceinline__ unsigned walk_block(const WalkArgs& a, const Seg& g, bool deliver, int now, int tid,
-                                               uint32_t t_first, float w_first) {
+__device__ __forceinline__ unsigned walk_block(const WalkArgs& a, const Seg& g, bool deliver, int now, int c) {
     // the target trace at the first source spike is loaded with the target's spike steps
     const bool has_pre = g.P.n > 0;
     const int t0 = has_pre ? g.P[0] : 0;
-    if (has_pre && now - t0 >= a.post_depth) set_err(a.err, ERR_SNAPSHOT);
     const float* ring0 = a.post_ring + static_cast<long long>(t0 & (a.post_depth - 1)) * a.n_tgt;
     // the next round's target and weight (the HBM stream) are loaded a round
     // ahead; the target's spike steps and trace (L2) within the round
     unsigned n = 0;
     const uint32_t len = g.s1 - g.s0;   // a projection holds < 2^32 synapses
-    uint32_t t_next = t_first;
-    float w_next = w_first;
+    uint32_t t_next = 0;
+    float w_next = 0.0f;
+    if (static_cast<uint32_t>(c) < len) {
+        t_next = __ldcs(a.tgt + g.s0 + c);
+        w_next = a.w[g.s0 + c];
+    }
 #pragma unroll 1
-    for (uint32_t o = tid; o < len; o += kThreads) {
+    for (uint32_t o = c; o < len; o += kConsumers) {
         const uint32_t syn = g.s0 + o;
         const uint32_t t = t_next;
         const float w = w_next;
         const int4 r = a.tgt_recent[t];
         const float xp0 = has_pre ? ring0[t] : 0.0f;
         const float md = MOD ? __ldcs(a.mod + syn) : 1.0f;
-        if (o + kThreads < len) {
-            t_next = __ldcs(a.tgt + syn + kThreads);
-            w_next = a.w[syn + kThreads];
+        if (o + kConsumers < len) {
+            t_next = __ldcs(a.tgt + syn + kConsumers);
+            w_next = a.w[syn + kConsumers];
         }
         const float w1 = walk_syn<MOD>(a, g, t0, t, r, w, md, now, xp0);
         if (__float_as_uint(w1) != __float_as_uint(w)) a.w[syn] = w1;
@@ -319,130 +337,171 @@ __device__ __forceinline__ unsigned walk_block(const WalkArgs& a, const Seg& g, 
     return n;
 }
 
+// Delivery without updates (the segment is up to date, or its history was
+// flagged as an error).
+template <bool MOD>
+__device__ __forceinline__ unsigned deliver_only(const WalkArgs& a, uint32_t s0, uint32_t s1, int c) {
+    unsigned n = 0;
+    for (uint32_t o = c; o < s1 - s0; o += kConsumers) {
+        const uint32_t syn = s0 + o;
+        const float wv = a.w[syn];
+        atomicAdd(a.acc + __ldg(a.tgt + syn), MOD ? wv * __ldg(a.mod + syn) : wv);
+        ++n;
+    }
+    return n;
+}
+
 // New segment state after a walk through g.e.
 __device__ __forceinline__ void finish_seg(const WalkArgs& a, const Seg& g) {
     a.seg_x[g.seg] = g.X[g.e - g.T - 1];
     a.seg_last[g.seg] = g.e;
 }
 
-// The segment state one block reads before walking (thread 0 loads it).
-struct SegHead {
+enum { ITEM_DONE = 0, ITEM_WALK = 1, ITEM_DELIVER = 2 };
+
+// One segment walk, prepared by the producer warp for the consumers.
+struct Item {
+    int kind;
+    int j, T, e, nP, deliver;
     uint32_t s0, s1;
-    int T;
-    int nP;   // source spikes in (T, e]; -2: walked through e already; -1: history error (flagged)
-    float xT;
 };
 
-// Segment (j, k) by the whole block: applies the updates through e and,
-// with deliver, delivers the updated weights.  The load chain is: segment
-// bounds, state and source spike steps (thread 0, one round trip); trace
-// snapshots and the first synapses (one); the targets' spike steps and
-// trace (one per round).  A segment is walked by one block at a time (an
-// arrival walk and a sweep walk never meet: the sweep skips sources with
-// spikes still to arrive), so the block records the new state as soon as
-// its trace table is built.  Returns the number of events this thread
-// delivered.
-template <bool MOD>
-__device__ unsigned segment_walk(const WalkArgs& a, SegHead& head, int* sP, float* sX, int j, int k, int e,
-                                 bool deliver, int now, int m_new, int tid) {
-    __syncthreads();   // the block is done with the previous segment's lists
+// What the producer warp needs to step through the block's units.
+struct Producer {
+    long long u;          // next unit of this block
+    long long n_units, n_arr;
+    long long base, g_end;   // group units cover segments [base, g_end), kGroup each
+    unsigned pending;     // segments g0 + bit of the current group still to look at
+    long long g0;
+    int e_group;          // groups walk through this step
+};
+
+// Segment (j, k) through e, by the producer warp: state and source spike
+// steps (lane 0, one round trip), the source trace table (all lanes, one
+// round trip for the snapshots), the segment's new state, and an L2
+// prefetch of its synapses for the consumers.  Returns false when there is
+// nothing to walk or deliver (a sweep or flush segment already up to date).
+__device__ bool prepare(const WalkArgs& a, Item& it, int* sP, float* sX, int j, int k, int e, bool deliver, int now,
+                        int m_new, int lane) {
     const long long seg = static_cast<long long>(j) * a.nd + k;
-    if (tid == 0) {
-        SegHead h;
+    Item h;
+    h.kind = ITEM_DONE;
+    h.j = j;
+    h.e = e;
+    h.deliver = deliver;
+    int nP = -2;
+    float xT = 0.0f;
+    if (lane == 0) {
         h.s0 = static_cast<uint32_t>(a.seg_ptr[seg]);
         h.s1 = static_cast<uint32_t>(a.seg_ptr[seg + 1]);
         h.T = a.seg_last[seg];
-        h.xT = a.seg_x[seg];
+        xT = a.seg_x[seg];
         const int4 rj = a.src_recent[j];
-        h.nP = -2;
         if (h.T < e) {
             if (e - h.T > kMaxSpan) {
-                h.nP = -1;
+                nP = -1;
                 set_err(a.err, ERR_SNAPSHOT);
             } else {
                 const bool own = j >= a.src_lo && j < a.src_hi;
-                h.nP = spikes_in(rj, own ? a.src_ring : nullptr, a.src_cnt, j - a.src_lo, a.ring_k, h.T, e, sP, kMaxPre);
-                if (h.nP < 0) {
-                    h.nP = -1;
+                nP = spikes_in(rj, own ? a.src_ring : nullptr, a.src_cnt, j - a.src_lo, a.ring_k, h.T, e, sP, kMaxPre);
+                if (nP < 0) {
+                    nP = -1;
                     set_err(a.err, ERR_HISTORY);
                 }
             }
         }
-        head = h;
     }
-    __syncthreads();
-    const SegHead h = head;
-    const uint32_t len = h.s1 - h.s0;
-    // the first round's synapses, independent of the segment's history
-    uint32_t t_first = 0;
-    float w_first = 0.0f;
-    if (static_cast<uint32_t>(tid) < len) {
-        t_first = __ldcs(a.tgt + h.s0 + tid);
-        w_first = a.w[h.s0 + tid];
-    }
-    unsigned n = 0;
-    if (h.nP >= 0) {
+    nP = __shfl_sync(0xffffffffu, nP, 0);
+    h.s0 = __shfl_sync(0xffffffffu, h.s0, 0);
+    h.s1 = __shfl_sync(0xffffffffu, h.s1, 0);
+    h.T = __shfl_sync(0xffffffffu, h.T, 0);
+    xT = __shfl_sync(0xffffffffu, xT, 0);
+    h.nP = nP;
+    __syncwarp();   // sP written by lane 0
+    if (nP >= 0) {
+        h.kind = ITEM_WALK;
+        if (nP > 0 && now - sP[0] >= a.post_depth) set_err(a.err, ERR_SNAPSHOT);
         Seg g;
         g.j = j;
         g.seg = seg;
-        g.s0 = h.s0;
-        g.s1 = h.s1;
         g.T = h.T;
         g.e = e;
         g.P.p = sP;
-        g.P.n = h.nP;
+        g.P.n = nP;
         g.X = sX;
-        build_table(a, g, sX, h.xT, m_new, tid);
-        __syncthreads();
-        if (tid == 0) finish_seg(a, g);
-        n = walk_block<MOD>(a, g, deliver, now, tid, t_first, w_first);
+        build_table(a, g, sX, xT, m_new, lane);
+        __syncwarp();
+        if (lane == 0) finish_seg(a, g);
     } else if (deliver) {
-        // nothing to apply (or a history error, flagged): deliver only
-        if (static_cast<uint32_t>(tid) < len) {
-            atomicAdd(a.acc + t_first, MOD ? w_first * __ldg(a.mod + h.s0 + tid) : w_first);
-            ++n;
-        }
-        for (uint32_t o = tid + kThreads; o < len; o += kThreads) {
-            const uint32_t syn = h.s0 + o;
-            const float wv = a.w[syn];
-            atomicAdd(a.acc + __ldg(a.tgt + syn), MOD ? wv * __ldg(a.mod + syn) : wv);
-            ++n;
-        }
+        h.kind = ITEM_DELIVER;
+    } else {
+        return false;
     }
-    return n;
+    // the consumers' first rounds come from L2
+    for (uint32_t o = h.s0 + 32u * lane; o < h.s1; o += 32u * 32u) {
+        prefetch_l2(a.tgt + o);
+        prefetch_l2(a.w + o);
+        if (a.mod) prefetch_l2(a.mod + o);
+    }
+    if (lane == 0) it = h;
+    return true;
 }
 
-// Segments [g0, g0 + count) (count <= kThreads) through e: each thread
-// looks at one and the block walks, one after another, those with updates
-// to apply -- all of them (flush), or (sweep) those not walked for `stale`
-// steps whose source has no spike still to arrive.
-template <bool MOD>
-__device__ void segment_group(const WalkArgs& a, SegHead& head, int* sP, float* sX, int* list, int* n_list,
-                              long long g0, int count, int e, bool sweep, int now, int m_new, int tid) {
-    __syncthreads();   // the previous group's list is read
-    if (tid == 0) *n_list = 0;
-    __syncthreads();
-    if (tid < count) {
-        const long long seg = g0 + tid;
-        const int j = static_cast<int>(seg / a.nd);
-        const int T = a.seg_last[seg];
-        bool go = T < e && a.seg_ptr[seg + 1] > a.seg_ptr[seg];
-        if (sweep) {
-            const int newest = a.src_recent[j].x;
-            go = go && newest < now - (a.dmin + a.nd - 1) && T < now - a.stale;
+// The producer's next item into `it` (kind ITEM_DONE when the block's
+// units are exhausted).  Arrival units give one item each; sweep and flush
+// units are groups of kGroup segments, looked at one lane each, whose
+// segments to walk become items one after another.  The producer's state
+// lives in shared memory (only warp 0 reads it), so the consumers' loop
+// does not carry it in registers.
+__device__ void produce(const WalkArgs& a, Producer& shared_pr, Item& it, int* sP, float* sX, const long long* start,
+                        const int* slot, bool sweep, int now, int m_new, int lane) {
+    Producer pr = shared_pr;
+    for (;;) {
+        bool got = false;
+        while (pr.pending && !got) {
+            const int b = __ffs(pr.pending) - 1;
+            pr.pending &= pr.pending - 1;
+            const long long seg = pr.g0 + b;
+            got = prepare(a, it, sP, sX, static_cast<int>(seg / a.nd), static_cast<int>(seg % a.nd), pr.e_group, false,
+                          now, m_new, lane);
         }
-        if (go) list[atomicAdd(n_list, 1)] = tid;
+        if (got) break;
+        if (pr.u >= pr.n_units) {
+            if (lane == 0) it.kind = ITEM_DONE;
+            break;
+        }
+        const long long u = pr.u;
+        pr.u += gridDim.x;
+        if (u < pr.n_arr) {
+            int lo = 0, hi = a.nd - 1;
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (start[mid] <= u) lo = mid; else hi = mid - 1;
+            }
+            const int spike = static_cast<int>(u - start[lo]);
+            const int j = a.hist_src.ids[static_cast<long long>(slot[lo]) * a.hist_src.cap + spike];
+            prepare(a, it, sP, sX, j, lo, now - 1, true, now, m_new, lane);   // always an item
+            break;
+        }
+        // a group of segments: each lane looks at one
+        pr.g0 = pr.base + (u - pr.n_arr) * kGroup;
+        const long long seg = pr.g0 + lane;
+        bool go = false;
+        if (lane < kGroup && seg < pr.g_end) {
+            const int j = static_cast<int>(seg / a.nd);
+            const int T = a.seg_last[seg];
+            go = T < pr.e_group && a.seg_ptr[seg + 1] > a.seg_ptr[seg];
+            if (sweep) {
+                const int newest = a.src_recent[j].x;
+                go = go && newest < now - (a.dmin + a.nd - 1) && T < now - a.stale;
+            }
+        }
+        pr.pending = __ballot_sync(0xffffffffu, go);
     }
-    __syncthreads();
-    const int n = *n_list;
-    for (int q = 0; q < n; ++q) {
-        const long long seg = g0 + list[q];
-        segment_walk<MOD>(a, head, sP, sX, static_cast<int>(seg / a.nd), static_cast<int>(seg % a.nd), e, false, now,
-                          m_new, tid);
-    }
+    __syncwarp();
+    if (lane == 0) shared_pr = pr;
+    __syncwarp();
 }
-
-constexpr int kGroup = 8;   // segments a sweep unit looks at
 
 template <bool MOD>
 __global__ void __launch_bounds__(kThreads, kMinBlocks) walk_kernel(const __grid_constant__ WalkArgs a, int mode,
@@ -451,72 +510,89 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) walk_kernel(const __grid
     __shared__ typename Scan::TempStorage scan_tmp;
     __shared__ long long start[257];
     __shared__ int slot[256];
-    __shared__ int sP[kMaxPre];
-    __shared__ float sX[kMaxSpan];
-    __shared__ SegHead head;
-    __shared__ int list[kThreads];
-    __shared__ int n_list;
+    __shared__ int sP[2][kMaxPre];
+    __shared__ float sX[2][kMaxSpan];
+    __shared__ Item items[2];
 
-    const int tid = threadIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const long long step = step_off + (step_base ? *step_base : 0);
     const int now = static_cast<int>(step);
     const int m_new = static_cast<int>(step / a.win);   // newest snapshot written
     const long long n_seg = static_cast<long long>(a.n_src) * a.nd;
 
+    __shared__ Producer pr;
+    bool sweep = false;
     if (mode == WALK_FLUSH) {
-        // every segment through step - 1
-        for (long long g0 = static_cast<long long>(blockIdx.x) * kThreads; g0 < n_seg;
-             g0 += static_cast<long long>(gridDim.x) * kThreads) {
-            const int count = n_seg - g0 < kThreads ? static_cast<int>(n_seg - g0) : kThreads;
-            segment_group<MOD>(a, head, sP, sX, list, &n_list, g0, count, now - 1, false, now, m_new, tid);
+        // every segment through step - 1, kGroup per unit
+        if (tid == 0) {
+            pr.n_arr = 0;
+            pr.n_units = (n_seg + kGroup - 1) / kGroup;
+            pr.base = 0;
+            pr.g_end = n_seg;
+            pr.e_group = now - 1;
         }
-        return;
+    } else {
+        // Arrivals: spikes of step - (dmin + k) through the delay-k
+        // segments, one unit each; then the sweep: the segments of rows
+        // [r0, r0 + rows), kGroup per unit.
+        long long units = 0;
+        if (tid < a.nd) {
+            const long long src_step = step - (a.dmin + tid);
+            slot[tid] = src_step >= 0 ? static_cast<int>(src_step % a.hist_src.depth) : 0;
+            if (src_step >= 0) units = a.hist_src.count[slot[tid]];
+        }
+        long long excl, n_arr;
+        Scan(scan_tmp).ExclusiveSum(units, excl, n_arr);
+        if (tid < a.nd) start[tid] = excl;
+        if (tid == 0) {
+            start[a.nd] = n_arr;
+            const long long r0 = (step % a.sweep_period) * a.sweep_rows;
+            const long long left = a.n_src - r0;
+            const long long rows = left <= 0 ? 0 : (a.sweep_rows < left ? a.sweep_rows : left);
+            pr.n_arr = n_arr;
+            pr.n_units = n_arr + (rows * a.nd + kGroup - 1) / kGroup;
+            pr.base = r0 * a.nd;
+            pr.g_end = (r0 + rows) * a.nd;
+            pr.e_group = static_cast<int>((step / a.win) * a.win) - 1;   // spikes of all ranks known through here
+        }
+        sweep = true;
     }
-
-    // Arrivals: spikes of step - (dmin + k) through the delay-k segments,
-    // one unit each.
-    long long units = 0;
-    if (tid < a.nd) {
-        const long long src_step = step - (a.dmin + tid);
-        slot[tid] = src_step >= 0 ? static_cast<int>(src_step % a.hist_src.depth) : 0;
-        if (src_step >= 0) units = a.hist_src.count[slot[tid]];
+    if (tid == 0) {
+        pr.u = blockIdx.x;
+        pr.pending = 0;
+        pr.g0 = 0;
     }
-    long long excl, n_arr;
-    Scan(scan_tmp).ExclusiveSum(units, excl, n_arr);
-    if (tid < a.nd) start[tid] = excl;
-    if (tid == 0) start[a.nd] = n_arr;
     __syncthreads();
 
-    // Sweep: the segments of rows [r0, r0 + rows), kGroup per unit.
-    const long long r0 = (step % a.sweep_period) * a.sweep_rows;
-    const long long left = a.n_src - r0;
-    const long long rows = left <= 0 ? 0 : (a.sweep_rows < left ? a.sweep_rows : left);
-    const long long sweep_segs = rows * a.nd;
-    const long long n_units = n_arr + (sweep_segs + kGroup - 1) / kGroup;
-    const int win_end = static_cast<int>((step / a.win) * a.win) - 1;   // spikes of all ranks known through here
-
+    if (warp == 0) produce(a, pr, items[0], sP[0], sX[0], start, slot, sweep, now, m_new, lane);
+    __syncthreads();
     unsigned long long my_events = 0;
-    for (long long u = blockIdx.x; u < n_units; u += gridDim.x) {
-        if (u < n_arr) {
-            int lo = 0, hi = a.nd - 1;
-            while (lo < hi) {
-                const int mid = (lo + hi + 1) >> 1;
-                if (start[mid] <= u) lo = mid; else hi = mid - 1;
-            }
-            const int k = lo;
-            const int spike = static_cast<int>(u - start[k]);
-            const int j = a.hist_src.ids[static_cast<long long>(slot[k]) * a.hist_src.cap + spike];
-            my_events += segment_walk<MOD>(a, head, sP, sX, j, k, now - 1, true, now, m_new, tid);
+    for (int q = 0;; q ^= 1) {
+        const Item cur = items[q];
+        if (cur.kind == ITEM_DONE) break;
+        if (warp == 0) {
+            produce(a, pr, items[q ^ 1], sP[q ^ 1], sX[q ^ 1], start, slot, sweep, now, m_new, lane);
+        } else if (cur.kind == ITEM_WALK) {
+            Seg g;
+            g.j = cur.j;
+            g.seg = 0;
+            g.s0 = cur.s0;
+            g.s1 = cur.s1;
+            g.T = cur.T;
+            g.e = cur.e;
+            g.P.p = sP[q];
+            g.P.n = cur.nP;
+            g.X = sX[q];
+            my_events += walk_block<MOD>(a, g, cur.deliver != 0, now, tid - 32);
         } else {
-            const long long q0 = (u - n_arr) * kGroup;
-            const int count = sweep_segs - q0 < kGroup ? static_cast<int>(sweep_segs - q0) : kGroup;
-            segment_group<MOD>(a, head, sP, sX, list, &n_list, r0 * a.nd + q0, count, win_end, true, now, m_new, tid);
+            my_events += deliver_only<MOD>(a, cur.s0, cur.s1, tid - 32);
         }
+        __syncthreads();
     }
     // thread sums -> one atomic per warp
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) my_events += __shfl_down_sync(0xffffffffu, my_events, o);
-    if (a.events && (tid & 31) == 0 && my_events) atomicAdd(a.events, my_events);
+    if (a.events && lane == 0 && my_events) atomicAdd(a.events, my_events);
 }
 
 }  // namespace
