@@ -90,19 +90,43 @@ __device__ __forceinline__ float par(const PopArgs& a, int k, int i) {
     return a.uniform[k];
 }
 
-__device__ __forceinline__ float drive_value(const PopArgs& a, uint32_t gid, uint32_t step) {
-    U4 w = philox4x32_10(U4{gid, step, 0u, kStreamDrive}, a.seed);
-    if (a.drive_kind == NRN_DRIVE_GAUSS_CURRENT) {
-        float z = normal_bm(u01(w.x), u01(w.y));
-        return a.d0 + a.d1 * z;
-    }
-    // the first k with u <= F_k, from the table (the same values the loop of
-    // poisson_inv adds up); past the table, the loop itself
-    const float u = u01(w.x);
+// Poisson count of the drive from its uniform: the first k with u <= F_k,
+// from the table (the same values the loop of poisson_inv adds up); past
+// the table, the loop itself.
+__device__ __forceinline__ float poisson_drive(const PopArgs& a, uint32_t word) {
+    const float u = u01(word);
     int k = 0;
     while (k < a.n_cdf && u > a.cdf[k]) ++k;
     if (k == a.n_cdf) k = poisson_inv(u, a.d0, a.d_exp);
     return a.d1 * static_cast<float>(k);
+}
+
+__device__ __forceinline__ uint32_t word_at(const U4& w, uint32_t q) {
+    return q == 0 ? w.x : q == 1 ? w.y : q == 2 ? w.z : w.w;
+}
+
+// The drive of neuron gid at step.  Poisson kinds: word gid % 4 of the
+// Philox block (gid / 4, step) -- four consecutive neurons share a block;
+// Gaussian: words 0 and 1 of the block (gid, step).
+__device__ __forceinline__ float drive_value(const PopArgs& a, uint32_t gid, uint32_t step) {
+    if (a.drive_kind == NRN_DRIVE_GAUSS_CURRENT) {
+        const U4 w = philox4x32_10(U4{gid, step, 0u, kStreamDrive}, a.seed);
+        float z = normal_bm(u01(w.x), u01(w.y));
+        return a.d0 + a.d1 * z;
+    }
+    const U4 w = philox4x32_10(U4{gid >> 2, step, 0u, kStreamDrive}, a.seed);
+    return poisson_drive(a, word_at(w, gid & 3u));
+}
+
+// The drive of neurons gid0 .. gid0+3 (one Philox block when gid0 is a
+// multiple of 4 and the drive is Poisson).
+__device__ __forceinline__ float4 drive_value4(const PopArgs& a, uint32_t gid0, uint32_t step) {
+    if (a.drive_kind != NRN_DRIVE_GAUSS_CURRENT && (gid0 & 3u) == 0) {
+        const U4 w = philox4x32_10(U4{gid0 >> 2, step, 0u, kStreamDrive}, a.seed);
+        return make_float4(poisson_drive(a, w.x), poisson_drive(a, w.y), poisson_drive(a, w.z), poisson_drive(a, w.w));
+    }
+    return make_float4(drive_value(a, gid0, step), drive_value(a, gid0 + 1, step), drive_value(a, gid0 + 2, step),
+                       drive_value(a, gid0 + 3, step));
 }
 
 // The LIF update of one neuron (src/neuron/lif.cpp:80-97), each operation
@@ -348,13 +372,8 @@ __global__ void __launch_bounds__(256) lif4_group_kernel(const __grid_constant__
         float4 I = a.i_syn ? ld4(a.i_syn, i0) : make_float4(0.f, 0.f, 0.f, 0.f);
         if (a.drive_kind != NRN_DRIVE_NONE) {
             float4 x;
-            if (a.drive_values) {
-                x = ld4(a.drive_values, i0);
-            } else {
-#pragma unroll
-                for (int k = 0; k < 4; ++k)
-                    at(x, k) = drive_value(a, static_cast<uint32_t>(a.gid_offset + i0 + k), static_cast<uint32_t>(step));
-            }
+            if (a.drive_values) x = ld4(a.drive_values, i0);
+            else x = drive_value4(a, static_cast<uint32_t>(a.gid_offset + i0), static_cast<uint32_t>(step));
             I.x = I.x + x.x; I.y = I.y + x.y; I.z = I.z + x.z; I.w = I.w + x.w;
         }
         float4 v = ld4(a.v, i0), ref = ld4(a.ref, i0);
@@ -453,13 +472,21 @@ __global__ void __launch_bounds__(256) lif4_group_kernel(const __grid_constant__
     }
 }
 
-// The drive of every neuron of one population for the step (drive_value,
-// the neuron update's own sampler).
+// The drive of every neuron of one population for the step (the neuron
+// update's own sampler), four neurons a thread: the group of global ids
+// 4m .. 4m+3 shares one Philox block.
 __global__ void __launch_bounds__(256) drive_fill_kernel(const __grid_constant__ PopArgs a, float* out) {
     long long step = a.step;
     if (a.step_base) step += *a.step_base;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += gridDim.x * blockDim.x)
-        out[i] = drive_value(a, static_cast<uint32_t>(a.gid_offset + i), static_cast<uint32_t>(step));
+    const long long m0 = a.gid_offset >> 2, m1 = (static_cast<long long>(a.gid_offset) + a.n + 3) >> 2;
+    for (long long m = m0 + blockIdx.x * blockDim.x + threadIdx.x; m < m1; m += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const float4 x = drive_value4(a, static_cast<uint32_t>(4 * m), static_cast<uint32_t>(step));
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const long long i = 4 * m + k - a.gid_offset;
+            if (i >= 0 && i < a.n) out[i] = k == 0 ? x.x : k == 1 ? x.y : k == 2 ? x.z : x.w;
+        }
+    }
 }
 
 template <int MODEL, bool HET, bool COND>
@@ -665,7 +692,7 @@ extern "C" nrn_status_t nrn_cuda_drive_fill(const nrn_pop_step_t* in, float* out
     bool het = false, cond = false;
     NRN_TRY(make_args(*in, a, het, cond));
     if (in->n == 0 || a.drive_kind == NRN_DRIVE_NONE) return NRN_OK;
-    const int blocks = std::min((in->n + 255) / 256, 8 * sm_count_current());
+    const int blocks = std::min((in->n / 4 + 256) / 256, 8 * sm_count_current());
     drive_fill_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a, out);
     NRN_CUDA_TRY(cudaGetLastError());
     return NRN_OK;

@@ -225,15 +225,19 @@ static inline float orc_normal(float u1, float u2) {
 }
 
 /* External drive of neuron gid at step: returns the amount added to the
- * current (kinds 1,2) or to the excitatory conductance input (kind 3). */
+ * current (kinds 1,2) or to the excitatory conductance input (kind 3).
+ * Poisson kinds draw one uniform per neuron: word gid % 4 of the Philox
+ * block (gid / 4, step), so four consecutive neurons share one block.  The
+ * Gaussian kind uses words 0 and 1 of the block (gid, step). */
 static inline float orc_drive_value(int kind, float d0, float d1, float exp_neg,
                                     uint64_t seed, uint32_t gid, uint32_t step) {
     uint32_t w[4];
-    orc_philox_words(seed, gid, step, ORC_STREAM_DRIVE, w);
     if (kind == ORC_DRIVE_POISSON_CURRENT || kind == ORC_DRIVE_POISSON_GEXC) {
-        int k = orc_poisson(orc_u01(w[0]), d0, exp_neg);
+        orc_philox_words(seed, gid >> 2, step, ORC_STREAM_DRIVE, w);
+        int k = orc_poisson(orc_u01(w[gid & 3u]), d0, exp_neg);
         return d1 * (float)k;
     }
+    orc_philox_words(seed, gid, step, ORC_STREAM_DRIVE, w);
     if (kind == ORC_DRIVE_GAUSS_CURRENT) {
         float z = orc_normal(orc_u01(w[0]), orc_u01(w[1]));
         return d0 + d1 * z;

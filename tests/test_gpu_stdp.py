@@ -17,16 +17,16 @@ pytestmark = pytest.mark.gpu
 
 
 def burst_spec(steps):
-    """Brunel network with a 0.2 ms refractory period, reset 2 mV below
-    threshold and twice the drive (about a third of the inter-spike
-    intervals are shorter than the longest delay), and delays 4..12 steps
-    on the plastic E->E projection."""
+    """Brunel network with a 0.2 ms refractory period and reset 2 mV below
+    threshold (about 175 Hz; over 1,200 steps some 1,400 inter-spike
+    intervals of E sources are shorter than the longest delay, while no
+    target spikes more than about 40 times between two walks of a segment,
+    inside the 64-step history), and delays 4..12 steps on the plastic E->E
+    projection."""
     spec = W.brunel(800, 200, 80, 20, delay=8, stdp=True, seed=21, steps=steps)
     for p in spec["pops"]:
         p["params"][4] = 2e-4
         p["params"][2] = 0.018
-        kind, lam, w = p["drive"]
-        p["drive"] = (kind, lam * 2.0, w)
     g = spec["projs"][0]["gen"]
     g["dmin"], g["dmax"] = 4, 12
     return spec
