@@ -46,17 +46,20 @@ def load_peaks():
 
 def workload_spec(name: str, world: int, steps: int, scale: float = 1.0):
     from libnrn_b200 import workloads as W
+
+    def scaled(n):   # population sizes of a scaled-down network: multiples of 4
+        return max(4, int(round(n * scale / 4)) * 4)
+
     if name == "brunel_stdp":
         if scale != 1.0:
-            return W.brunel(int(838_860 * world * scale), int(209_716 * world * scale), 1_000, 250,
-                            steps=steps, stdp=True)
+            return W.brunel(scaled(838_860 * world), scaled(209_716 * world), 1_000, 250, steps=steps, stdp=True)
         return W.brunel_stdp_per_gpu(world, steps=steps)
     if name == "brunel":
         return W.brunel(10_000 * world, 2_500 * world, 1_000, 250, steps=steps)
     if name == "brunel_1m":
         # the bench network without plasticity: 1,048,576 LIF neurons and
         # 1.31e9 static synapses per GPU
-        return W.brunel(838_860 * world, 209_716 * world, 1_000, 250, steps=steps)
+        return W.brunel(scaled(838_860 * world), scaled(209_716 * world), 1_000, 250, steps=steps)
     if name == "adex":
         return W.adex_cond(1_048_576 * world, 1_000, steps=steps)
     if name == "izh":
