@@ -499,7 +499,11 @@ __device__ void produce(const WalkArgs& a, Producer& shared_pr, Item& it, int* s
         pr.pending = __ballot_sync(0xffffffffu, go);
     }
     __syncwarp();
-    if (lane == 0) shared_pr = pr;
+    if (lane == 0) {   // the fields that change (the consumers read the others)
+        shared_pr.u = pr.u;
+        shared_pr.pending = pr.pending;
+        shared_pr.g0 = pr.g0;
+    }
     __syncwarp();
 }
 
@@ -564,7 +568,29 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) walk_kernel(const __grid
     }
     __syncthreads();
 
-    if (warp == 0) produce(a, pr, items[0], sP[0], sX[0], start, slot, sweep, now, m_new, lane);
+    if (warp == 0) {
+        produce(a, pr, items[0], sP[0], sX[0], start, slot, sweep, now, m_new, lane);
+    } else if (sweep) {
+        // Meanwhile the consumers bring into L2 what the producer will read
+        // for this block's later arrival units: segment bounds and state,
+        // source spike steps and trace snapshots.
+        const long long u = blockIdx.x + static_cast<long long>(tid - 32 + 1) * gridDim.x;
+        if (u < pr.n_arr) {
+            int lo = 0, hi = a.nd - 1;
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (start[mid] <= u) lo = mid; else hi = mid - 1;
+            }
+            const int j = a.hist_src.ids[static_cast<long long>(slot[lo]) * a.hist_src.cap + (u - start[lo])];
+            const long long seg = static_cast<long long>(j) * a.nd + lo;
+            prefetch_l2(a.seg_ptr + seg);
+            prefetch_l2(a.seg_last + seg);
+            prefetch_l2(a.seg_x + seg);
+            prefetch_l2(a.src_recent + j);
+            const float* snap = a.pre_snap + static_cast<long long>(j) * a.pre_depth;
+            for (int o = 0; o < a.pre_depth; o += 32) prefetch_l2(snap + o);
+        }
+    }
     __syncthreads();
     unsigned long long my_events = 0;
     for (int q = 0;; q ^= 1) {

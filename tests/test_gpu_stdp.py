@@ -98,10 +98,26 @@ def test_eager_launches_equal_graphs():
         assert np.array_equal(a, b)
 
 
+def sparse_burst_spec(steps):
+    """burst_spec with in-degree 1 E + 1 I: a neuron receives at most two
+    synaptic events in a step, and a float sum of two terms does not
+    depend on the order in which the reductions land, so runs with
+    non-dyadic weights are deterministic."""
+    spec = W.brunel(800, 200, 1, 1, delay=8, stdp=True, seed=21, steps=steps)
+    for p in spec["pops"]:
+        p["params"][4] = 2e-4
+        p["params"][2] = 0.018
+    g = spec["projs"][0]["gen"]
+    g["dmin"], g["dmax"] = 4, 12
+    return spec
+
+
 def test_modulatory_gains_walk_equals_per_step_kernels():
     # gains on the plastic projection: the walks against the per-step STDP
-    # kernels (the oracle has no gains), same spikes and weights
-    net = S.realize(burst_spec(300))
+    # kernels (the oracle has no gains), same spikes and weights.  Gains make
+    # the delivered values non-dyadic, so the network has at most two inputs
+    # per neuron and step (order-independent sums).
+    net = S.realize(sparse_burst_spec(300))
     rng = np.random.default_rng(3)
     q = net["projs"][0]
     q["mod"] = rng.uniform(0.5, 1.5, len(q["w"])).astype(np.float32)
