@@ -176,10 +176,10 @@ def cpu_reference(args, world_steps_hint=None):
     }
 
 
-# dram__bytes_read.sum + dram__bytes_write.sum of walk_kernel (8.198 MB) and
-# deliver_kernel (2.773 MB) per launch in ncu captures of the bench network at
+# dram__bytes_read.sum + dram__bytes_write.sum of walk_kernel (8.349 MB) and
+# deliver_kernel (2.812 MB) per launch in ncu captures of the bench network at
 # 262,144 neurons (bench.py --scale 0.25), scaled x4 to 1,048,576 neurons
-DELIVERY_TRAFFIC_PER_STEP = 4 * (8.1984e6 + 256 + 2.773248e6)
+DELIVERY_TRAFFIC_PER_STEP = 4 * (8.349184e6 + 2.811904e6)
 
 BSR_N = 262_144          # pre = post neurons of the batched block-sparse workload
 BSR_DENSITY = 0.02       # fraction of the 64x64 block slots present
