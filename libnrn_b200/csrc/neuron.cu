@@ -336,26 +336,6 @@ __device__ __forceinline__ float4 ld4(const float* p, int i) { return *reinterpr
 __device__ __forceinline__ void st4(float* p, int i, float4 x) { *reinterpret_cast<float4*>(p + i) = x; }
 __device__ __forceinline__ float& at(float4& x, int k) { return k == 0 ? x.x : k == 1 ? x.y : k == 2 ? x.z : x.w; }
 
-// Appends each lane's cnt ids to a list whose length is *count: a scan of
-// the counts over the warp (every lane must call it), one atomic per warp;
-// the ids in lane order.  Returns the warp's total.
-template <class Write>
-__device__ __forceinline__ int warp_append(int cnt, int* count, Write write) {
-    const int lane = threadIdx.x & 31;
-    int incl = cnt;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += y;
-    }
-    const int tot = __shfl_sync(0xffffffffu, incl, 31);
-    int base = 0;
-    if (lane == 31 && tot > 0) base = atomicAdd(count, tot);
-    base = __shfl_sync(0xffffffffu, base, 31);
-    if (cnt > 0) write(base + incl - cnt);
-    return tot;
-}
-
 // LIF with uniform parameters, four neurons per thread (float4 state, n a
 // multiple of 4, arrays 16-byte aligned): the same arithmetic as pop_body
 // (lif_math), with wider memory transactions.
@@ -377,6 +357,14 @@ __global__ void __launch_bounds__(256) lif4_group_kernel(const __grid_constant__
             I.x = I.x + x.x; I.y = I.y + x.y; I.z = I.z + x.z; I.w = I.w + x.w;
         }
         float4 v = ld4(a.v, i0), ref = ld4(a.ref, i0);
+        // the first trace is loaded with the state (the stores below could
+        // alias it, so it would otherwise wait for them)
+        const bool traces_now = a.n_traces > 0 && (a.trace_slow_ratio <= 1 || step % a.trace_slow_ratio == 0);
+        const long long ring_mask = a.trace_ring_depth - 1;
+        float4 x0 = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (traces_now)
+            x0 = a.trace_ring[0] != nullptr ? ld4(a.trace_ring[0] + ((step - 1) & ring_mask) * a.n, i0)
+                                            : ld4(a.trace[0], i0);
         const float* u = a.uniform;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
@@ -389,17 +377,16 @@ __global__ void __launch_bounds__(256) lif4_group_kernel(const __grid_constant__
         st4(a.ref, i0, ref);
         const float4 s4 = make_float4(sp[0] ? 1.f : 0.f, sp[1] ? 1.f : 0.f, sp[2] ? 1.f : 0.f, sp[3] ? 1.f : 0.f);
         if (a.spike) st4(a.spike, i0, s4);
-        if (a.n_traces > 0 && (a.trace_slow_ratio <= 1 || step % a.trace_slow_ratio == 0)) {
+        if (traces_now) {
             for (int k = 0; k < a.n_traces; ++k) {
                 const float d = a.trace_decay[k];
                 float4 x;
                 float* dst;
                 if (a.trace_ring[k] != nullptr) {
-                    const long long mask = a.trace_ring_depth - 1;
-                    x = ld4(a.trace_ring[k] + ((step - 1) & mask) * a.n, i0);
-                    dst = a.trace_ring[k] + (step & mask) * a.n;
+                    x = k == 0 ? x0 : ld4(a.trace_ring[k] + ((step - 1) & ring_mask) * a.n, i0);
+                    dst = a.trace_ring[k] + (step & ring_mask) * a.n;
                 } else {
-                    x = ld4(a.trace[k], i0);
+                    x = k == 0 ? x0 : ld4(a.trace[k], i0);
                     dst = a.trace[k];
                 }
                 x.x = x.x * d + s4.x; x.y = x.y * d + s4.y; x.z = x.z * d + s4.z; x.w = x.w * d + s4.w;
@@ -407,6 +394,44 @@ __global__ void __launch_bounds__(256) lif4_group_kernel(const __grid_constant__
             }
         }
         if (a.i_syn) st4(a.i_syn, i0, make_float4(0.f, 0.f, 0.f, 0.f));
+    }
+    // Spike lists: one warp scan of the spike counts serves every list, and
+    // lane 31 issues all the warp's list reservations at once, so a warp
+    // with spikes waits for one atomic round trip, overlapped with the
+    // updates of its neurons' spike records.
+    const int cnt = sp[0] + sp[1] + sp[2] + sp[3];
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    const int tot = __shfl_sync(0xffffffffu, incl, 31);
+    int* list_ids = nullptr;
+    int* list_count = nullptr;
+    int list_cap = 0x7fffffff;
+    if (a.send_hdr) {
+        // window send buffer: ids in step order, the running total in send_hdr[win]
+        list_ids = a.send_ids;
+        list_count = a.send_hdr + a.win;
+        list_cap = a.send_cap;
+    } else if (a.spike_ids) {
+        list_ids = a.spike_ids;
+        list_count = a.spike_count;
+        if (a.hist_depth > 0) {
+            const int slot = static_cast<int>(step % a.hist_depth);
+            list_ids += static_cast<long long>(slot) * a.hist_cap;
+            list_count += slot;
+        }
+    }
+    int base = 0;
+    unsigned long long rbase = 0;
+    if (lane == 31 && tot > 0) {
+        if (list_count) base = atomicAdd(list_count, tot);
+        if (a.send_hdr) atomicAdd(a.send_hdr + static_cast<int>(step % a.win), tot);
+        if (a.raster_gid) rbase = atomicAdd(a.raster_count, static_cast<unsigned long long>(tot));
+    }
+    if (cnt > 0) {
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
             if (!sp[k]) continue;
@@ -422,52 +447,24 @@ __global__ void __launch_bounds__(256) lif4_group_kernel(const __grid_constant__
             if (a.win_mask != nullptr) a.win_mask[i] |= 1u << static_cast<int>(step % a.win);
         }
     }
-    const int cnt = sp[0] + sp[1] + sp[2] + sp[3];
-    auto write_ids = [&](int* dst, int cap, int pos) {
+    base = __shfl_sync(0xffffffffu, base, 31);
+    rbase = __shfl_sync(0xffffffffu, rbase, 31);
+    if (cnt > 0) {
+        int pos = base + incl - cnt;
+        unsigned long long rpos = rbase + static_cast<unsigned long long>(incl - cnt);
         for (int k = 0; k < 4; ++k) {
             if (!sp[k]) continue;
-            if (pos < cap) dst[pos] = a.id_offset + i0 + k;
-            else if (a.err) atomicCAS(a.err, 0, 4);
-            ++pos;
-        }
-    };
-    if (a.send_hdr) {
-        // window send buffer: ids in step order, the running total in send_hdr[win]
-        const int uu = static_cast<int>(step % a.win);
-        const int tot = warp_append(cnt, a.send_hdr + a.win, [&](int pos) { write_ids(a.send_ids, a.send_cap, pos); });
-        if (lane == 0 && tot) atomicAdd(a.send_hdr + uu, tot);
-    } else if (a.spike_ids) {
-        int* ids = a.spike_ids;
-        int* count = a.spike_count;
-        if (a.hist_depth > 0) {
-            const int slot = static_cast<int>(step % a.hist_depth);
-            ids += static_cast<long long>(slot) * a.hist_cap;
-            count += slot;
-        }
-        warp_append(cnt, count, [&](int pos) { write_ids(ids, 0x7fffffff, pos); });
-    }
-    if (a.raster_gid) {
-        // one 64-bit atomic per warp on the raster count
-        int incl = cnt;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int y = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += y;
-        }
-        const int tot = __shfl_sync(0xffffffffu, incl, 31);
-        unsigned long long base = 0;
-        if (lane == 31 && tot > 0) base = atomicAdd(a.raster_count, static_cast<unsigned long long>(tot));
-        base = __shfl_sync(0xffffffffu, base, 31);
-        if (cnt > 0) {
-            unsigned long long pos = base + static_cast<unsigned long long>(incl - cnt);
-            for (int k = 0; k < 4; ++k) {
-                if (!sp[k]) continue;
-                if (pos < static_cast<unsigned long long>(a.raster_cap)) {
-                    a.raster_step[pos] = static_cast<int>(step);
-                    a.raster_gid[pos] = a.gid_offset + i0 + k;
-                }
-                ++pos;
+            const int id = i0 + k;
+            if (list_ids) {
+                if (pos < list_cap) list_ids[pos] = a.id_offset + id;
+                else if (a.err) atomicCAS(a.err, 0, 4);
             }
+            if (a.raster_gid && rpos < static_cast<unsigned long long>(a.raster_cap)) {
+                a.raster_step[rpos] = static_cast<int>(step);
+                a.raster_gid[rpos] = a.gid_offset + id;
+            }
+            ++pos;
+            ++rpos;
         }
     }
 }
