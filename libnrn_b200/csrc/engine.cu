@@ -105,7 +105,7 @@ struct EngineProj {
     bool walk = false;           // updates applied by segment walks (plastic.cu)
     int32_t* seg_last = nullptr;
     float* seg_x = nullptr;
-    float* pre_snap = nullptr;   // [n_src][pre_depth] source trace at window ends
+    float* pre_snap = nullptr;   // [pre_depth][n_src] source trace at window ends
     float* post_ring = nullptr;  // [ring_depth][n_tgt] target trace at every step
     int32_t pre_depth = 1;
 };

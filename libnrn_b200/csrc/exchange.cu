@@ -42,11 +42,11 @@ __global__ void __launch_bounds__(kThreads) window_kernel(const __grid_constant_
         for (int k = 0; k < a.n_task; ++k) {
             const SnapTask& t = a.task[k];
             if (j < t.lo || j >= t.hi) continue;
-            const long long col = j - t.lo;
-            float* row = t.snap + col * t.depth;   // this neuron's snapshots, window m at m % depth
-            float x = row[(m - 1) & (t.depth - 1)];
+            // window-major rows: consecutive neurons are adjacent (coalesced)
+            const long long col = j - t.lo, cols = t.hi - t.lo;
+            float x = t.snap[static_cast<long long>((m - 1) & (t.depth - 1)) * cols + col];
             for (int u = 0; u < a.win; ++u) x = x * t.decay + (((bits >> u) & 1u) ? 1.0f : 0.0f);
-            row[m & (t.depth - 1)] = x;
+            t.snap[static_cast<long long>(m & (t.depth - 1)) * cols + col] = x;
         }
         if (bits == 0) continue;
         a.mask[j] = 0;

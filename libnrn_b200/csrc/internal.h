@@ -82,8 +82,9 @@ struct WalkArgs {
     const int32_t* tgt_ring = nullptr;
     const int32_t* tgt_cnt = nullptr;
     int32_t ring_k = 64;
-    // source trace at window ends: x_j(m*win - 1) at j * pre_depth + m % pre_depth
-    // (a source's snapshots are contiguous: a walk reads consecutive windows)
+    // source trace at window ends: x_j(m*win - 1) at (m % pre_depth) * n_src + j
+    // (window-major: the window-end update is coalesced; a walk reads its
+    // windows one lane each)
     const float* pre_snap = nullptr;
     int32_t pre_depth = 1;
     // target trace at every step: x(t) in row t % post_depth ([depth][n_tgt])
@@ -105,7 +106,7 @@ nrn_status_t walk_launch(const WalkArgs& a, int mode, long long step_off, const 
 // from the window's spike masks, spike steps of the sources other ranks
 // own, mask reset.
 struct SnapTask {
-    float* snap = nullptr;            // x_j(m*win - 1) at (j - lo) * depth + m % depth
+    float* snap = nullptr;            // x_j(m*win - 1) at (m % depth) * (hi - lo) + (j - lo)
     int32_t depth = 1;
     int32_t lo = 0, hi = 0;           // population indices covered (snap column = j - lo)
     float decay = 1;

@@ -272,7 +272,7 @@ __device__ __forceinline__ void build_table(const WalkArgs& a, const Seg& g, flo
             const int m = m0 + pc - 1;
             start = m * W - 1;
             if (m_new - m >= a.pre_depth) set_err(a.err, ERR_SNAPSHOT);
-            x = a.pre_snap[static_cast<long long>(g.j) * a.pre_depth + (m & (a.pre_depth - 1))];
+            x = a.pre_snap[static_cast<long long>(m & (a.pre_depth - 1)) * a.n_src + g.j];
         }
         const int stop = pc == 0 ? (m0 * W - 1 < e ? m0 * W - 1 : e) : (start + W < e ? start + W : e);
         int q = 0;
@@ -573,7 +573,7 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) walk_kernel(const __grid
     } else if (sweep) {
         // Meanwhile the consumers bring into L2 what the producer will read
         // for this block's later arrival units: segment bounds and state,
-        // source spike steps and trace snapshots.
+        // and source spike steps.
         const long long u = blockIdx.x + static_cast<long long>(tid - 32 + 1) * gridDim.x;
         if (u < pr.n_arr) {
             int lo = 0, hi = a.nd - 1;
@@ -587,8 +587,6 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) walk_kernel(const __grid
             prefetch_l2(a.seg_last + seg);
             prefetch_l2(a.seg_x + seg);
             prefetch_l2(a.src_recent + j);
-            const float* snap = a.pre_snap + static_cast<long long>(j) * a.pre_depth;
-            for (int o = 0; o < a.pre_depth; o += 32) prefetch_l2(snap + o);
         }
     }
     __syncthreads();
