@@ -1,6 +1,7 @@
-"""The network partitioned over 2 GPUs (one process per GPU, spike ids
-exchanged by NCCL all-gather once per window) gives the same spikes and
-plastic weights as the same network on one GPU.  Needs 2 GPUs."""
+"""The network partitioned over 2, 4 or 8 GPUs (one process per GPU, spike
+ids exchanged by NCCL all-gather once per window) gives the same spikes and
+plastic weights as the same network on one GPU.  Each case needs as many
+GPUs as ranks."""
 import os
 import socket
 
@@ -11,7 +12,11 @@ import torch.multiprocessing as mp
 
 pytestmark = pytest.mark.gpu
 
-needs2 = pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def needs(n):
+    return pytest.mark.skipif(torch.cuda.device_count() < n, reason=f"needs {n} GPUs")
+
+
+needs2 = needs(2)
 
 
 def spec_of(name, steps):
@@ -82,13 +87,14 @@ def merged_raster(parts):
     return st[o], gid[o]
 
 
-@needs2
+@pytest.mark.parametrize("world", [pytest.param(2, marks=needs(2)), pytest.param(4, marks=needs(4)),
+                                   pytest.param(8, marks=needs(8))])
 @pytest.mark.parametrize("name", ["brunel", "brunel_stdp"])
-def test_two_gpus_equal_one(name):
+def test_partitioned_equals_one_gpu(name, world):
     steps = 600   # a whole number of 15-step windows
     ref = run_one(spec_of(name, steps))
     assert ref["err"] is None, ref["err"]
-    parts = run_partitioned(name, steps)
+    parts = run_partitioned(name, steps, world)
     for p in parts:
         assert p["err"] is None, p["err"]
     st, gid = merged_raster(parts)
