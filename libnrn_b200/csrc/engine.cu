@@ -493,10 +493,15 @@ struct nrn_engine {
         // different history slots and only add into the accumulators).
         NRN_CUDA_TRY(cudaEventRecord(fork_ev, stream));
         NRN_CUDA_TRY(cudaStreamWaitEvent(side, fork_ev, 0));
-        for (size_t i = 0; i < pops.size(); ++i) {
-            if (!pops[i].drive_buf) continue;
-            nrn_pop_step_t pa = pop_args(static_cast<int>(i), dt, off, true);
-            NRN_TRY(nrn_cuda_drive_fill(&pa, pops[i].drive_buf, reinterpret_cast<nrn_stream_t>(side)));
+        {
+            std::vector<nrn_pop_step_t> da;
+            std::vector<float*> dout;
+            for (size_t i = 0; i < pops.size(); ++i) {
+                if (!pops[i].drive_buf) continue;
+                da.push_back(pop_args(static_cast<int>(i), dt, off, true));
+                dout.push_back(pops[i].drive_buf);
+            }
+            if (!da.empty()) NRN_TRY(drive_fill_group(da.data(), dout.data(), static_cast<int>(da.size()), side));
         }
         cudaStream_t ds = any_walk ? side : stream;
         NRN_TRY(nrn_cuda_deliver_counted(dp.data(), static_cast<int32_t>(dp.size()), hs.data(),

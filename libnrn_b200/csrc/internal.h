@@ -59,6 +59,10 @@ int sm_count_current();
 // kind share one launch (neuron.cu).
 nrn_status_t pop_step_group(const nrn_pop_step_t* list, int n, cudaStream_t s);
 
+// This step's drive of several populations drawn ahead into out[q] (one
+// launch for up to four populations; neuron.cu).
+nrn_status_t drive_fill_group(const nrn_pop_step_t* list, float* const* out, int n, cudaStream_t s);
+
 // Pair STDP applied by segment walks (plastic.cu).  Steps are int32.
 enum { WALK_STEP = 0, WALK_FLUSH = 1 };
 struct WalkArgs {

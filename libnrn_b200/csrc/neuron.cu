@@ -486,6 +486,32 @@ __global__ void __launch_bounds__(256) drive_fill_kernel(const __grid_constant__
     }
 }
 
+// The drive of several populations in one launch: block ranges per
+// population as in PopGroup, one thread per Philox block (four neurons).
+struct DriveGroup {
+    PopArgs p[kMaxGroup];
+    float* out[kMaxGroup];
+    int start[kMaxGroup + 1];
+    int n;
+};
+
+__global__ void __launch_bounds__(256) drive_fill_group_kernel(const __grid_constant__ DriveGroup g) {
+    int q = 0;
+    while (q + 1 < g.n && static_cast<int>(blockIdx.x) >= g.start[q + 1]) ++q;
+    const PopArgs& a = g.p[q];
+    long long step = a.step;
+    if (a.step_base) step += *a.step_base;
+    const long long m0 = a.gid_offset >> 2, m1 = (static_cast<long long>(a.gid_offset) + a.n + 3) >> 2;
+    const long long m = m0 + static_cast<long long>(blockIdx.x - g.start[q]) * blockDim.x + threadIdx.x;
+    if (m >= m1) return;
+    const float4 x = drive_value4(a, static_cast<uint32_t>(4 * m), static_cast<uint32_t>(step));
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const long long i = 4 * m + k - a.gid_offset;
+        if (i >= 0 && i < a.n) g.out[q][i] = k == 0 ? x.x : k == 1 ? x.y : k == 2 ? x.z : x.w;
+    }
+}
+
 template <int MODEL, bool HET, bool COND>
 void launch_kind(const PopGroup& g, cudaStream_t s) {
     if (g.n == 1) pop_step_kernel<MODEL, HET, COND><<<g.start[1], kPopThreads, 0, s>>>(g.p[0]);
@@ -675,6 +701,30 @@ nrn_status_t pop_step_group(const nrn_pop_step_t* list, int n, cudaStream_t s) {
         } else {
             launch_group(g, list[q].model, het, cond, s);
         }
+        NRN_CUDA_TRY(cudaGetLastError());
+    }
+    return NRN_OK;
+}
+
+nrn_status_t drive_fill_group(const nrn_pop_step_t* list, float* const* out, int n, cudaStream_t s) {
+    for (int q0 = 0; q0 < n; q0 += kMaxGroup) {
+        DriveGroup g{};
+        int b = 0;
+        for (int q = q0; q < n && g.n < kMaxGroup; ++q) {
+            bool het = false, cond = false;
+            NRN_TRY(make_args(list[q], g.p[g.n], het, cond));
+            NRN_CHECK_ARG(out[q] != nullptr || list[q].n == 0, "drive fill: null output");
+            if (list[q].n == 0 || g.p[g.n].drive_kind == NRN_DRIVE_NONE) continue;
+            g.out[g.n] = out[q];
+            g.start[g.n] = b;
+            const long long groups = ((static_cast<long long>(list[q].gid_offset) + list[q].n + 3) >> 2) -
+                                     (list[q].gid_offset >> 2);
+            b += static_cast<int>((groups + 255) / 256);
+            ++g.n;
+        }
+        g.start[g.n] = b;
+        if (g.n == 0) continue;
+        drive_fill_group_kernel<<<b, 256, 0, s>>>(g);
         NRN_CUDA_TRY(cudaGetLastError());
     }
     return NRN_OK;
