@@ -35,7 +35,9 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kMaxPairs = 1024;   // (projection, delay) pairs per launch
-constexpr int kChunk = 128;       // synapses per warp work unit (4 per lane)
+constexpr int kChunk = 128;       // synapses per warp work unit of the STDP kernels (4 per lane)
+constexpr int kDeliverVec = 4;    // synapses per lane of one delivery unit
+constexpr int kDeliverChunk = 32 * kDeliverVec;
 
 struct DeliverParams {
     nrn_proj_t proj[NRN_MAX_PROJ];
@@ -53,7 +55,7 @@ struct DeliverParams {
 struct PairView {
     long long* start;   // [npairs + 1] exclusive prefix of work units
     int* slot;          // [npairs]
-    int* chunks;        // [npairs] units per spike (ceil(max segment / kChunk))
+    int* chunks;        // [npairs] units per spike (ceil(max segment / kDeliverChunk))
     short* proj;        // [npairs]
     short* k;           // [npairs]
 };
@@ -72,9 +74,9 @@ size_t pair_smem(int npairs) {
     return static_cast<size_t>(npairs + 1) * sizeof(long long) + static_cast<size_t>(npairs) * (4 + 4 + 2 + 2) + 16;
 }
 
-// Work unit = (spike, delay segment, chunk of kChunk synapses), one warp
+// Work unit = (spike, delay segment, chunk of kDeliverChunk synapses), one warp
 // each.  Every segment of a projection is given ceil(max segment length /
-// kChunk) units (units past the segment's end are empty), so the units of
+// kDeliverChunk) units (units past the segment's end are empty), so the units of
 // one step are numbered without a prefix over segment lengths and spread
 // evenly over a full-occupancy grid.
 __global__ void __launch_bounds__(kThreads) deliver_kernel(const __grid_constant__ DeliverParams P) {
@@ -101,7 +103,7 @@ __global__ void __launch_bounds__(kThreads) deliver_kernel(const __grid_constant
             const int k = pi - acc;
             const nrn_proj_t& pr = P.proj[q];
             const long long src_step = step - (pr.dmin + k);
-            const int chunks = (pr.max_seg + kChunk - 1) / kChunk;
+            const int chunks = (pr.max_seg + kDeliverChunk - 1) / kDeliverChunk;
             tab.proj[pi] = static_cast<short>(q);
             tab.k[pi] = static_cast<short>(k);
             tab.chunks[pi] = chunks > 0 ? chunks : 1;
@@ -143,14 +145,14 @@ __global__ void __launch_bounds__(kThreads) deliver_kernel(const __grid_constant
         const int j = h.ids[static_cast<long long>(tab.slot[lo]) * h.cap + spike];
         const long long seg = static_cast<long long>(j) * pr.nd + tab.k[lo];
         const long long e0 = pr.seg_ptr[seg + 1];
-        const long long s0 = pr.seg_ptr[seg] + static_cast<long long>(chunk) * kChunk;
-        const long long s1 = s0 + kChunk < e0 ? s0 + kChunk : e0;
+        const long long s0 = pr.seg_ptr[seg] + static_cast<long long>(chunk) * kDeliverChunk;
+        const long long s1 = s0 + kDeliverChunk < e0 ? s0 + kDeliverChunk : e0;
         if (s0 >= s1) continue;
         if (lane == 0) my_events += static_cast<unsigned long long>(s1 - s0);
-        uint32_t t[4];
-        float w[4];
+        uint32_t t[kDeliverVec];
+        float w[kDeliverVec];
 #pragma unroll
-        for (int v = 0; v < 4; ++v) {
+        for (int v = 0; v < kDeliverVec; ++v) {
             const long long syn = s0 + lane + 32 * v;
             if (syn < s1) {
                 t[v] = __ldg(pr.tgt + syn);
@@ -159,7 +161,7 @@ __global__ void __launch_bounds__(kThreads) deliver_kernel(const __grid_constant
             }
         }
 #pragma unroll
-        for (int v = 0; v < 4; ++v)
+        for (int v = 0; v < kDeliverVec; ++v)
             if (s0 + lane + 32 * v < s1) atomicAdd(pr.acc + t[v], w[v]);
     }
     if (P.events && lane == 0 && my_events) atomicAdd(P.events, my_events);
