@@ -483,6 +483,22 @@ NRN_API nrn_status_t nrn_engine_profile(nrn_engine* e, int64_t steps, double* ms
 /* Counters: total spikes and delivered synaptic events since creation. */
 NRN_API nrn_status_t nrn_engine_counters(nrn_engine* e, int64_t* spikes, int64_t* events);
 
+/* Checkpoint of the engine's device state: neuron state and synaptic input,
+ * spike histories, weights, plasticity state (traces, walk state, trace
+ * snapshots and rings), step counter, event counter and the raster not yet
+ * read.  Fills the reference's I/O stub (src/simulation/runner.cpp:222,
+ * "save() -- stub, not yet implemented").  A checkpoint restores into an
+ * engine built from the same network (same populations, projections and
+ * partition), finalized; the run then continues as the saved one would.
+ * A partitioned engine is checkpointed at window boundaries only (the
+ * spike exchange holds nothing then); NRN_ERR_STATE otherwise.
+ * nrn_engine_checkpoint_size gives the bytes of a checkpoint now; save
+ * writes exactly that many into host memory; load reads them back and
+ * returns NRN_ERR_INVALID for a checkpoint of another network. */
+NRN_API nrn_status_t nrn_engine_checkpoint_size(nrn_engine* e, int64_t* bytes);
+NRN_API nrn_status_t nrn_engine_checkpoint_save(nrn_engine* e, void* buf, int64_t bytes);
+NRN_API nrn_status_t nrn_engine_checkpoint_load(nrn_engine* e, const void* buf, int64_t bytes);
+
 #ifdef __cplusplus
 }
 #endif

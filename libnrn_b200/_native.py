@@ -34,7 +34,8 @@ EXPORTS = [
     "nrn_cuda_block_deliver", "nrn_cuda_block_stdp", "nrn_cuda_compact", "nrn_cuda_gather_ring",
     "nrn_cuda_scatter", "nrn_engine_raster_noalloc", "nrn_comm_unique_id", "nrn_engine_set_partition",
     "nrn_cuda_bsr_propagate", "nrn_cuda_bsr_pack", "nrn_cuda_bsr_pack_spikes", "nrn_cuda_bsr_unpack_spikes",
-    "nrn_cuda_bsr_spikes", "nrn_cuda_drive_fill",
+    "nrn_cuda_bsr_spikes", "nrn_cuda_drive_fill", "nrn_engine_checkpoint_size", "nrn_engine_checkpoint_save",
+    "nrn_engine_checkpoint_load",
 ]
 
 
@@ -165,6 +166,9 @@ def lib() -> C.CDLL:
             "nrn_engine_nnz": [vp, i32, C.POINTER(i64)],
             "nrn_engine_counters": [vp, C.POINTER(i64), C.POINTER(i64)],
             "nrn_engine_profile": [vp, i64, C.POINTER(C.c_double)],
+            "nrn_engine_checkpoint_size": [vp, C.POINTER(i64)],
+            "nrn_engine_checkpoint_save": [vp, vp, i64],
+            "nrn_engine_checkpoint_load": [vp, vp, i64],
         }
         for name, args in sig.items():
             f = getattr(L, name)

@@ -591,7 +591,66 @@ struct nrn_engine {
         for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
         graphs.clear();
     }
+
+    // Every device buffer a checkpoint holds, in a fixed order (buffers an
+    // engine does not have are left out; an engine built from the same
+    // network has the same list).
+    struct StateBuf {
+        void* p;
+        size_t bytes;
+    };
+    std::vector<StateBuf> state_buffers() {
+        std::vector<StateBuf> b;
+        auto add = [&](void* p, size_t bytes) {
+            if (p != nullptr && bytes > 0) b.push_back({p, bytes});
+        };
+        for (auto& p : pops) {
+            const size_t n = static_cast<size_t>(p.d.n);
+            add(p.d.v, n * 4);
+            add(p.d.aux, n * 4);
+            add(p.d.refractory, n * 4);
+            add(p.d.spike, n * 4);
+            add(p.d.i_syn, n * 4);
+            add(p.g_exc, n * 4);
+            add(p.g_inh, n * 4);
+            add(p.gin_exc, n * 4);
+            add(p.gin_inh, n * 4);
+            add(p.hist_ids, static_cast<size_t>(depth) * p.hist_cap * 4);
+            add(p.hist_count, static_cast<size_t>(depth) * 4);
+            add(p.mask, static_cast<size_t>(p.n_global) * 4);
+            add(p.recent, static_cast<size_t>(p.n_global) * 16);
+            add(p.ring, n * kRing * 4);
+            add(p.cnt, n * 4);
+        }
+        for (auto& q : projs) {
+            add(q.csr.w, static_cast<size_t>(q.csr.nnz) * 4);
+            add(q.x_pre, static_cast<size_t>(pops[q.src_pop].d.n) * 4);
+            add(q.x_post, static_cast<size_t>(pops[q.tgt_pop].d.n) * 4);
+            if (q.walk) {
+                const size_t nseg = static_cast<size_t>(q.csr.n_src) * q.csr.nd;
+                add(q.seg_last, nseg * 4);
+                add(q.seg_x, nseg * 4);
+                add(q.pre_snap, static_cast<size_t>(q.pre_depth) * q.csr.n_src * 4);
+                add(q.post_ring, static_cast<size_t>(ring_depth) * q.csr.n_tgt * 4);
+            }
+        }
+        add(d_events, sizeof(unsigned long long));
+        return b;
+    }
 };
+
+// Checkpoint layout: header, the byte count of every state buffer, one
+// flag byte per projection (weights already clamped), padded to 8 bytes,
+// the buffers, then the raster not yet read (steps, then ids).
+struct CkptHeader {
+    char magic[8];
+    int64_t step;
+    int64_t spikes_flushed;
+    int64_t raster_n;
+    int32_t world, rank;
+    int32_t n_buf, n_proj;
+};
+constexpr char kCkptMagic[8] = {'N', 'R', 'N', 'C', 'K', 'P', 'T', '1'};
 
 #define ENGINE_GUARD(e)                                                          \
     do {                                                                         \
@@ -1196,6 +1255,131 @@ nrn_status_t nrn_engine_counters(nrn_engine* e, int64_t* spikes, int64_t* events
     NRN_CUDA_TRY(cudaStreamSynchronize(e->stream));
     if (events) *events = static_cast<int64_t>(ev);
     if (spikes) *spikes = e->spikes_flushed + static_cast<int64_t>(rc);
+    return NRN_OK;
+}
+
+namespace {
+
+size_t ckpt_bytes(const std::vector<nrn_engine::StateBuf>& b, size_t n_proj, int64_t raster_n) {
+    size_t s = sizeof(CkptHeader) + 8 * b.size() + (n_proj + 7) / 8 * 8;
+    for (const auto& x : b) s += x.bytes;
+    return s + 8 * static_cast<size_t>(raster_n);
+}
+
+// The engine can be checkpointed now: finalized, no error pending, and for
+// a partitioned engine at a window boundary.  *raster_n: spikes recorded
+// and not yet read.
+nrn_status_t ckpt_ready(nrn_engine* e, int64_t* raster_n) {
+    NRN_CHECK_ARG(e->finalized, "checkpoint: finalize the engine first");
+    if (e->world > 1 && e->step % e->win != 0)
+        return fail(NRN_ERR_STATE, "checkpoint: a partitioned engine is checkpointed at window boundaries (step " +
+                                       std::to_string(e->step) + ", window " + std::to_string(e->win) + ")");
+    NRN_TRY(e->check_err());
+    unsigned long long rc = 0;
+    NRN_CUDA_TRY(cudaMemcpyAsync(&rc, e->d_raster_count, sizeof(rc), cudaMemcpyDeviceToHost, e->stream));
+    NRN_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    if (static_cast<int64_t>(rc) > e->raster_cap)
+        return fail(NRN_ERR_CAPACITY, "checkpoint: the spike raster overflowed; read it first");
+    *raster_n = static_cast<int64_t>(rc);
+    return NRN_OK;
+}
+
+}  // namespace
+
+nrn_status_t nrn_engine_checkpoint_size(nrn_engine* e, int64_t* bytes) {
+    ENGINE_GUARD(e);
+    NRN_CHECK_ARG(bytes != nullptr, "checkpoint_size: null output");
+    int64_t rn = 0;
+    NRN_TRY(ckpt_ready(e, &rn));
+    *bytes = static_cast<int64_t>(ckpt_bytes(e->state_buffers(), e->projs.size(), rn));
+    return NRN_OK;
+}
+
+nrn_status_t nrn_engine_checkpoint_save(nrn_engine* e, void* buf, int64_t bytes) {
+    ENGINE_GUARD(e);
+    NRN_CHECK_ARG(buf != nullptr, "checkpoint_save: null buffer");
+    int64_t rn = 0;
+    NRN_TRY(ckpt_ready(e, &rn));
+    const auto b = e->state_buffers();
+    const size_t n_proj = e->projs.size();
+    NRN_CHECK_ARG(bytes == static_cast<int64_t>(ckpt_bytes(b, n_proj, rn)),
+                  "checkpoint_save: buffer size differs from nrn_engine_checkpoint_size");
+    char* out = static_cast<char*>(buf);
+    CkptHeader h{};
+    std::memcpy(h.magic, kCkptMagic, sizeof(h.magic));
+    h.step = e->step;
+    h.spikes_flushed = e->spikes_flushed;
+    h.raster_n = rn;
+    h.world = e->world;
+    h.rank = e->rank;
+    h.n_buf = static_cast<int32_t>(b.size());
+    h.n_proj = static_cast<int32_t>(n_proj);
+    std::memcpy(out, &h, sizeof(h));
+    out += sizeof(h);
+    for (const auto& x : b) {
+        const uint64_t sz = x.bytes;
+        std::memcpy(out, &sz, 8);
+        out += 8;
+    }
+    std::memset(out, 0, (n_proj + 7) / 8 * 8);
+    for (size_t q = 0; q < n_proj; ++q) out[q] = e->projs[q].clamped ? 1 : 0;
+    out += (n_proj + 7) / 8 * 8;
+    for (const auto& x : b) {
+        NRN_CUDA_TRY(cudaMemcpyAsync(out, x.p, x.bytes, cudaMemcpyDeviceToHost, e->stream));
+        out += x.bytes;
+    }
+    if (rn > 0) {
+        NRN_CUDA_TRY(cudaMemcpyAsync(out, e->raster_step, rn * 4, cudaMemcpyDeviceToHost, e->stream));
+        NRN_CUDA_TRY(cudaMemcpyAsync(out + rn * 4, e->raster_gid, rn * 4, cudaMemcpyDeviceToHost, e->stream));
+    }
+    NRN_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    return NRN_OK;
+}
+
+nrn_status_t nrn_engine_checkpoint_load(nrn_engine* e, const void* buf, int64_t bytes) {
+    ENGINE_GUARD(e);
+    NRN_CHECK_ARG(e->finalized, "checkpoint_load: finalize the engine first");
+    NRN_CHECK_ARG(buf != nullptr && bytes >= static_cast<int64_t>(sizeof(CkptHeader)), "checkpoint_load: not a checkpoint");
+    const char* in = static_cast<const char*>(buf);
+    CkptHeader h;
+    std::memcpy(&h, in, sizeof(h));
+    NRN_CHECK_ARG(std::memcmp(h.magic, kCkptMagic, sizeof(h.magic)) == 0, "checkpoint_load: not a checkpoint");
+    NRN_CHECK_ARG(h.world == e->world && h.rank == e->rank,
+                  "checkpoint_load: taken by another rank or with another number of GPUs");
+    const auto b = e->state_buffers();
+    const size_t n_proj = e->projs.size();
+    NRN_CHECK_ARG(h.n_buf == static_cast<int32_t>(b.size()) && h.n_proj == static_cast<int32_t>(n_proj) &&
+                      h.raster_n >= 0 && h.raster_n <= e->raster_cap && h.step >= 0,
+                  "checkpoint_load: the checkpoint is of another network");
+    NRN_CHECK_ARG(bytes == static_cast<int64_t>(ckpt_bytes(b, n_proj, h.raster_n)),
+                  "checkpoint_load: the checkpoint is of another network (size)");
+    in += sizeof(h);
+    for (const auto& x : b) {
+        uint64_t sz = 0;
+        std::memcpy(&sz, in, 8);
+        in += 8;
+        NRN_CHECK_ARG(sz == x.bytes, "checkpoint_load: the checkpoint is of another network (buffer sizes)");
+    }
+    NRN_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    for (size_t q = 0; q < n_proj; ++q) e->projs[q].clamped = in[q] != 0;
+    in += (n_proj + 7) / 8 * 8;
+    for (const auto& x : b) {
+        NRN_CUDA_TRY(cudaMemcpyAsync(x.p, in, x.bytes, cudaMemcpyHostToDevice, e->stream));
+        in += x.bytes;
+    }
+    const unsigned long long rc = static_cast<unsigned long long>(h.raster_n);
+    NRN_CUDA_TRY(cudaMemcpyAsync(e->d_raster_count, &rc, sizeof(rc), cudaMemcpyHostToDevice, e->stream));
+    if (h.raster_n > 0) {
+        NRN_CUDA_TRY(cudaMemcpyAsync(e->raster_step, in, h.raster_n * 4, cudaMemcpyHostToDevice, e->stream));
+        NRN_CUDA_TRY(cudaMemcpyAsync(e->raster_gid, in + h.raster_n * 4, h.raster_n * 4, cudaMemcpyHostToDevice,
+                                     e->stream));
+    }
+    const long long st = h.step;
+    NRN_CUDA_TRY(cudaMemcpyAsync(e->d_step, &st, sizeof(st), cudaMemcpyHostToDevice, e->stream));
+    NRN_CUDA_TRY(cudaMemsetAsync(e->d_err, 0, sizeof(int), e->stream));
+    NRN_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    e->step = h.step;
+    e->spikes_flushed = h.spikes_flushed;
     return NRN_OK;
 }
 

@@ -187,6 +187,21 @@ class Network:
         N.check(self.L.nrn_engine_counters(self.h, C.byref(s), C.byref(e)), "counters")
         return s.value, e.value
 
+    def checkpoint(self) -> bytes:
+        """The engine's device state (neurons, spike histories, weights,
+        plasticity state, step, counters, unread raster) as bytes; see
+        nrn_engine_checkpoint_save."""
+        n = C.c_int64()
+        N.check(self.L.nrn_engine_checkpoint_size(self.h, C.byref(n)), "checkpoint_size")
+        buf = np.empty(n.value, np.uint8)
+        N.check(self.L.nrn_engine_checkpoint_save(self.h, buf.ctypes.data, n.value), "checkpoint_save")
+        return buf.tobytes()
+
+    def restore(self, ckpt: bytes) -> None:
+        """Loads a checkpoint taken from an engine built from the same network."""
+        buf = np.frombuffer(ckpt, np.uint8)
+        N.check(self.L.nrn_engine_checkpoint_load(self.h, buf.ctypes.data, buf.size), "checkpoint_load")
+
     def state(self, name: str) -> np.ndarray:
         """Concatenated state variable over all populations (host copy)."""
         self.sync()
