@@ -185,6 +185,8 @@ typedef struct {
      * same arguments): if non-NULL, drive_values[i] replaces drawing the
      * drive of neuron i here -- the same numbers. */
     const float* drive_values;
+    /* Per-neuron spike statistics updated at each spike, or NULL. */
+    struct nrn_spike_stat* spike_stats;
 } nrn_pop_step_t;
 
 #define NRN_MAX_TRACES 4
@@ -198,6 +200,19 @@ NRN_API nrn_status_t nrn_cuda_drive_fill(const nrn_pop_step_t* a, float* out, nr
 /* ------------------------------------------------------------------------ */
 /* Spike delivery                                                           */
 /* ------------------------------------------------------------------------ */
+
+/* Spike statistics of one neuron, accumulated on the device at each of its
+ * spikes (population statistics without reading the raster: rate = count /
+ * time, CV of the inter-spike interval = sqrt(isi_sum2/m - (isi_sum/m)^2)
+ * / (isi_sum/m) with m = count - 1 intervals).  No counterpart in the
+ * reference, whose design notes list mean rate and CV_ISI as population
+ * statistics to record. */
+typedef struct nrn_spike_stat {
+    int32_t last;              /* step of the last spike + 1 (0: none yet)  */
+    int32_t count;             /* spikes                                    */
+    int64_t isi_sum;           /* sum of the inter-spike intervals, steps   */
+    int64_t isi_sum2;          /* sum of their squares                      */
+} nrn_spike_stat_t;
 
 /* Compacted spike history of one population: ring of depth `depth` steps,
  * slot s % depth holding the local ids of the neurons that spiked at s. */
@@ -495,6 +510,13 @@ NRN_API nrn_status_t nrn_engine_counters(nrn_engine* e, int64_t* spikes, int64_t
  * nrn_engine_checkpoint_size gives the bytes of a checkpoint now; save
  * writes exactly that many into host memory; load reads them back and
  * returns NRN_ERR_INVALID for a checkpoint of another network. */
+/* Spike statistics: enabled before nrn_engine_finalize (one
+ * nrn_spike_stat_t per neuron of every population, zeroed), copied out for
+ * this rank's neurons of a population (n = its local size), zeroed again by
+ * reset.  They are part of a checkpoint. */
+NRN_API nrn_status_t nrn_engine_enable_spike_stats(nrn_engine* e);
+NRN_API nrn_status_t nrn_engine_spike_stats(nrn_engine* e, int32_t pop, nrn_spike_stat_t* out, int64_t n);
+NRN_API nrn_status_t nrn_engine_spike_stats_reset(nrn_engine* e);
 NRN_API nrn_status_t nrn_engine_checkpoint_size(nrn_engine* e, int64_t* bytes);
 NRN_API nrn_status_t nrn_engine_checkpoint_save(nrn_engine* e, void* buf, int64_t bytes);
 NRN_API nrn_status_t nrn_engine_checkpoint_load(nrn_engine* e, const void* buf, int64_t bytes);

@@ -35,7 +35,8 @@ EXPORTS = [
     "nrn_cuda_scatter", "nrn_engine_raster_noalloc", "nrn_comm_unique_id", "nrn_engine_set_partition",
     "nrn_cuda_bsr_propagate", "nrn_cuda_bsr_pack", "nrn_cuda_bsr_pack_spikes", "nrn_cuda_bsr_unpack_spikes",
     "nrn_cuda_bsr_spikes", "nrn_cuda_drive_fill", "nrn_engine_checkpoint_size", "nrn_engine_checkpoint_save",
-    "nrn_engine_checkpoint_load",
+    "nrn_engine_checkpoint_load", "nrn_engine_enable_spike_stats", "nrn_engine_spike_stats",
+    "nrn_engine_spike_stats_reset",
 ]
 
 
@@ -69,6 +70,7 @@ class PopStep(C.Structure):
         ("post_ring_k", C.c_int32), ("id_offset", C.c_int32), ("win", C.c_int32),
         ("win_mask", C.c_void_p), ("send_hdr", C.c_void_p), ("send_ids", C.c_void_p),
         ("send_cap", C.c_int32), ("pad2", C.c_int32), ("err", C.c_void_p), ("drive_values", C.c_void_p),
+        ("spike_stats", C.c_void_p),
     ]
 
 
@@ -169,6 +171,9 @@ def lib() -> C.CDLL:
             "nrn_engine_checkpoint_size": [vp, C.POINTER(i64)],
             "nrn_engine_checkpoint_save": [vp, vp, i64],
             "nrn_engine_checkpoint_load": [vp, vp, i64],
+            "nrn_engine_enable_spike_stats": [vp],
+            "nrn_engine_spike_stats": [vp, i32, vp, i64],
+            "nrn_engine_spike_stats_reset": [vp],
         }
         for name, args in sig.items():
             f = getattr(L, name)

@@ -91,6 +91,7 @@ struct EnginePop {
     int32_t* ring = nullptr;         // [n][kRing] spike steps of this rank's neurons
     int32_t* cnt = nullptr;          // [n]
     float* drive_buf = nullptr;      // [n] this step's drive, drawn ahead on the side stream
+    nrn_spike_stat_t* stats = nullptr;   // [n] spike statistics (when enabled)
 };
 
 struct EngineProj {
@@ -136,6 +137,7 @@ struct nrn_engine {
     std::map<int, cudaGraphExec_t> graphs;
     int* d_err = nullptr;                 // device error flag (plasticity, exchange)
     bool use_graphs = true;
+    bool spike_stats = false;             // per-neuron spike statistics kept
     // partition over GPUs
     int32_t rank = 0, world = 1;
     ncclComm_t comm = nullptr;
@@ -155,7 +157,7 @@ struct nrn_engine {
             if (p.owns_isyn) cudaFree(p.d.i_syn);
             cudaFree(p.g_exc); cudaFree(p.g_inh); cudaFree(p.gin_exc); cudaFree(p.gin_inh);
             cudaFree(p.hist_ids); cudaFree(p.hist_count);
-            cudaFree(p.mask); cudaFree(p.recent); cudaFree(p.ring); cudaFree(p.cnt); cudaFree(p.drive_buf);
+            cudaFree(p.mask); cudaFree(p.recent); cudaFree(p.ring); cudaFree(p.cnt); cudaFree(p.drive_buf); cudaFree(p.stats);
         }
         for (auto& q : projs) {
             free_csr(q.csr);
@@ -234,6 +236,7 @@ struct nrn_engine {
             a.id_offset = p.lo;
             a.err = d_err;
             a.drive_values = p.drive_buf;
+            a.spike_stats = p.stats;
             if (world > 1) {
                 // ids go to the window send buffer; the ring is filled by the exchange
                 a.win = win;
@@ -621,6 +624,7 @@ struct nrn_engine {
             add(p.recent, static_cast<size_t>(p.n_global) * 16);
             add(p.ring, n * kRing * 4);
             add(p.cnt, n * 4);
+            add(p.stats, n * sizeof(nrn_spike_stat_t));
         }
         for (auto& q : projs) {
             add(q.csr.w, static_cast<size_t>(q.csr.nnz) * 4);
@@ -1072,6 +1076,8 @@ nrn_status_t nrn_engine_finalize(nrn_engine* e, int32_t init_update) {
     }
     for (auto& p : e->pops)
         if (p.d.drive.kind != NRN_DRIVE_NONE) NRN_TRY(dalloc0(&p.drive_buf, static_cast<size_t>(p.d.n), e->stream));
+    if (e->spike_stats)
+        for (auto& p : e->pops) NRN_TRY(dalloc0(&p.stats, static_cast<size_t>(p.d.n), e->stream));
     if (init_update) {
         for (size_t i = 0; i < e->pops.size(); ++i) {
             nrn_pop_step_t a = e->pop_args(static_cast<int>(i), 0.0, 0, false);
@@ -1285,6 +1291,34 @@ nrn_status_t ckpt_ready(nrn_engine* e, int64_t* raster_n) {
 }
 
 }  // namespace
+
+nrn_status_t nrn_engine_enable_spike_stats(nrn_engine* e) {
+    ENGINE_GUARD(e);
+    NRN_CHECK_ARG(!e->finalized, "enable_spike_stats: call before nrn_engine_finalize");
+    e->spike_stats = true;
+    return NRN_OK;
+}
+
+nrn_status_t nrn_engine_spike_stats(nrn_engine* e, int32_t pop, nrn_spike_stat_t* out, int64_t n) {
+    ENGINE_GUARD(e);
+    NRN_CHECK_ARG(pop >= 0 && pop < static_cast<int32_t>(e->pops.size()), "bad population index");
+    const auto& p = e->pops[pop];
+    if (p.stats == nullptr) return fail(NRN_ERR_STATE, "spike statistics were not enabled before finalize");
+    NRN_CHECK_ARG(n == p.d.n && out != nullptr, "spike_stats: output size must equal the population's local size");
+    NRN_CUDA_TRY(cudaMemcpyAsync(out, p.stats, static_cast<size_t>(n) * sizeof(nrn_spike_stat_t),
+                                 cudaMemcpyDeviceToHost, e->stream));
+    NRN_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    return NRN_OK;
+}
+
+nrn_status_t nrn_engine_spike_stats_reset(nrn_engine* e) {
+    ENGINE_GUARD(e);
+    if (!e->spike_stats || !e->finalized) return fail(NRN_ERR_STATE, "spike statistics are not enabled");
+    for (const auto& p : e->pops)
+        NRN_CUDA_TRY(cudaMemsetAsync(p.stats, 0, static_cast<size_t>(p.d.n) * sizeof(nrn_spike_stat_t), e->stream));
+    NRN_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    return NRN_OK;
+}
 
 nrn_status_t nrn_engine_checkpoint_size(nrn_engine* e, int64_t* bytes) {
     ENGINE_GUARD(e);

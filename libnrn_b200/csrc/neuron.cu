@@ -51,6 +51,7 @@ struct PopArgs {
     float cdf[32];
     int n_cdf;
     const float* drive_values;   // this step's drive drawn ahead, or null
+    nrn_spike_stat_t* spike_stats;   // per-neuron spike statistics, or null
     uint64_t seed;
     int64_t step;
     const int64_t* step_base;
@@ -127,6 +128,20 @@ __device__ __forceinline__ float4 drive_value4(const PopArgs& a, uint32_t gid0, 
     }
     return make_float4(drive_value(a, gid0, step), drive_value(a, gid0 + 1, step), drive_value(a, gid0 + 2, step),
                        drive_value(a, gid0 + 3, step));
+}
+
+// A spike of neuron i at step t into its statistics: count, and the
+// interval since its previous spike (exact integer sums).
+__device__ __forceinline__ void record_spike_stat(nrn_spike_stat_t* s, int i, int t) {
+    nrn_spike_stat_t r = s[i];
+    if (r.last > 0) {
+        const long long isi = static_cast<long long>(t) + 1 - r.last;
+        r.isi_sum += isi;
+        r.isi_sum2 += isi * isi;
+    }
+    r.last = t + 1;
+    r.count += 1;
+    s[i] = r;
 }
 
 // The LIF update of one neuron (src/neuron/lif.cpp:80-97), each operation
@@ -254,6 +269,7 @@ __device__ __forceinline__ void pop_body(const PopArgs& a, const int i) {
             a.post_cnt[i] = c + 1;
         }
         if (spiked && a.win_mask != nullptr) a.win_mask[i] |= 1u << static_cast<int>(step % a.win);
+        if (spiked && a.spike_stats != nullptr) record_spike_stat(a.spike_stats, i, static_cast<int>(step));
         if (a.i_syn) a.i_syn[i] = 0.0f;
         if (COND) {
             a.gin_exc[i] = 0.0f;
@@ -445,6 +461,7 @@ __global__ void __launch_bounds__(256) lif4_group_kernel(const __grid_constant__
                 a.post_cnt[i] = c + 1;
             }
             if (a.win_mask != nullptr) a.win_mask[i] |= 1u << static_cast<int>(step % a.win);
+            if (a.spike_stats != nullptr) record_spike_stat(a.spike_stats, i, static_cast<int>(step));
         }
     }
     base = __shfl_sync(0xffffffffu, base, 31);
@@ -657,6 +674,7 @@ nrn_status_t make_args(const nrn_pop_step_t& d, PopArgs& a, bool& het, bool& con
     a.send_cap = d.send_cap;
     a.err = d.err;
     a.drive_values = d.drive_values;
+    a.spike_stats = d.spike_stats;
     NRN_CHECK_ARG(a.send_hdr == nullptr || (d.send_ids != nullptr && d.send_cap >= 0),
                   "nrn_cuda_pop_step: send buffer without ids");
     if (d.model != NRN_MODEL_ADEX) cond = false;

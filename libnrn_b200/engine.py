@@ -187,6 +187,30 @@ class Network:
         N.check(self.L.nrn_engine_counters(self.h, C.byref(s), C.byref(e)), "counters")
         return s.value, e.value
 
+    def enable_spike_stats(self) -> None:
+        """Keep per-neuron spike statistics (before finalize)."""
+        N.check(self.L.nrn_engine_enable_spike_stats(self.h), "enable_spike_stats")
+        self._stats_from = None
+
+    def spike_stats(self, pop: int) -> np.ndarray:
+        """This rank's neurons' spike records of a population
+        (libnrn_b200.stats.SPIKE_STAT)."""
+        from .stats import SPIKE_STAT
+        out = np.zeros(self.pops[pop]["n"], SPIKE_STAT)
+        N.check(self.L.nrn_engine_spike_stats(self.h, pop, out.ctypes.data, out.size), "spike_stats")
+        return out
+
+    def reset_spike_stats(self) -> None:
+        N.check(self.L.nrn_engine_spike_stats_reset(self.h), "spike_stats_reset")
+        self._stats_from = self.step
+
+    def population_stats(self, pop: int) -> dict:
+        """Rate and CV of the inter-spike interval of a population's neurons on
+        this rank since the statistics were enabled or reset."""
+        from .stats import summarize
+        start = getattr(self, "_stats_from", None) or 0
+        return summarize(self.spike_stats(pop), self.step - start, self.dt)
+
     def checkpoint(self) -> bytes:
         """The engine's device state (neurons, spike histories, weights,
         plasticity state, step, counters, unread raster) as bytes; see
@@ -224,7 +248,7 @@ class Network:
 
     # -- builders ----------------------------------------------------------
     @classmethod
-    def from_net(cls, net: dict, device: int = 0, record: bool = True) -> "Network":
+    def from_net(cls, net: dict, device: int = 0, record: bool = True, spike_stats: bool = False) -> "Network":
         """From a network description with explicit synapse lists (the
         oracle's form)."""
         nw = cls(net["dt"], net.get("slow_ratio", 1), device)
@@ -237,11 +261,14 @@ class Network:
                                     receptor=q.get("receptor", "current"), mod=q.get("mod"))
             if q.get("plastic"):
                 nw.set_stdp(qid, q["stdp"])
+        if spike_stats:
+            nw.enable_spike_stats()
         nw.finalize(True)
         return nw
 
     @classmethod
-    def from_spec(cls, spec: dict, device: int = 0, record: bool = True, partition=None) -> "Network":
+    def from_spec(cls, spec: dict, device: int = 0, record: bool = True, partition=None,
+                  spike_stats: bool = False) -> "Network":
         """From a workload spec (libnrn_b200.workloads), connectivity
         generated on the device; with ``partition``, this rank's slice."""
         from . import workloads as W
@@ -270,5 +297,7 @@ class Network:
                                          receptor=q["receptor"])
             if q.get("plastic"):
                 nw.set_stdp(qid, q["stdp"])
+        if spike_stats:
+            nw.enable_spike_stats()
         nw.finalize(True)
         return nw
