@@ -118,18 +118,20 @@ __global__ void gather_u32(const uint32_t* perm, int64_t n, const uint32_t* in, 
         out[k] = in[perm[k]];
 }
 
-__global__ void raster_pack(const int32_t* step, const int32_t* gid, int64_t n, unsigned long long* key) {
+// Raster entries as sort keys: the step above `shift` bits of neuron id.
+__global__ void raster_pack(const int32_t* step, const int32_t* gid, int64_t n, int shift, unsigned long long* key) {
     for (int64_t k = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; k < n;
          k += static_cast<int64_t>(gridDim.x) * blockDim.x)
-        key[k] = (static_cast<unsigned long long>(static_cast<uint32_t>(step[k])) << 32) |
+        key[k] = (static_cast<unsigned long long>(static_cast<uint32_t>(step[k])) << shift) |
                  static_cast<uint32_t>(gid[k]);
 }
 
-__global__ void raster_unpack(const unsigned long long* key, int64_t n, int32_t* step, int32_t* gid) {
+__global__ void raster_unpack(const unsigned long long* key, int64_t n, int shift, int32_t* step, int32_t* gid) {
+    const unsigned long long mask = (1ull << shift) - 1;
     for (int64_t k = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; k < n;
          k += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        step[k] = static_cast<int32_t>(key[k] >> 32);
-        gid[k] = static_cast<int32_t>(key[k] & 0xFFFFFFFFull);
+        step[k] = static_cast<int32_t>(key[k] >> shift);
+        gid[k] = static_cast<int32_t>(key[k] & mask);
     }
 }
 
@@ -369,31 +371,45 @@ nrn_status_t build_transpose(DevCsr& c, cudaStream_t s) {
 #undef STEP
 }
 
-nrn_status_t sort_raster(int32_t* step, int32_t* gid, int64_t n, cudaStream_t s) {
+nrn_status_t sort_raster(int32_t* step, int32_t* gid, int64_t n, int gid_bits, int step_bits, RasterSortScratch& sc,
+                         cudaStream_t s) {
     if (n <= 1) return NRN_OK;
     NRN_CHECK_ARG(n < (int64_t(1) << 31), "raster too large to sort at once");
-    unsigned long long *a = nullptr, *b = nullptr;
-    void* tmp = nullptr;
-    size_t tmp_bytes = 0;
-    nrn_status_t st = dalloc(&a, n);
-    if (st == NRN_OK) st = dalloc(&b, n);
-    if (st == NRN_OK) {
-        raster_pack<<<grid_for(n), 256, 0, s>>>(step, gid, n, a);
-        cub::DoubleBuffer<unsigned long long> db(a, b);
-        cudaError_t e = cub::DeviceRadixSort::SortKeys(nullptr, tmp_bytes, db, static_cast<int>(n), 0, 64, s);
-        if (e == cudaSuccess) e = cudaMalloc(&tmp, tmp_bytes);
-        if (e == cudaSuccess) e = cub::DeviceRadixSort::SortKeys(tmp, tmp_bytes, db, static_cast<int>(n), 0, 64, s);
-        if (e == cudaSuccess) {
-            raster_unpack<<<grid_for(n), 256, 0, s>>>(db.Current(), n, step, gid);
-            e = cudaGetLastError();
+    NRN_CHECK_ARG(gid_bits >= 1 && gid_bits <= 32 && step_bits >= 1 && gid_bits + step_bits <= 64,
+                  "raster sort: key does not fit 64 bits");
+    const int end_bit = gid_bits + step_bits;
+    // buffers kept from earlier reads, grown when a read is larger
+    if (n > sc.cap) {
+        sc.release();
+        nrn_status_t st = dalloc(&sc.a, n);
+        if (st == NRN_OK) st = dalloc(&sc.b, n);
+        if (st != NRN_OK) {
+            sc.release();
+            return st;
         }
-        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
-        if (e != cudaSuccess) st = cuda_fail(e, "raster sort");
+        sc.cap = n;
     }
-    if (tmp) cudaFree(tmp);
-    dfree(a);
-    dfree(b);
-    return st;
+    cub::DoubleBuffer<unsigned long long> db(sc.a, sc.b);
+    size_t need = 0;
+    cudaError_t e = cub::DeviceRadixSort::SortKeys(nullptr, need, db, static_cast<int>(n), 0, end_bit, s);
+    if (e != cudaSuccess) return cuda_fail(e, "raster sort size");
+    if (need > sc.tmp_bytes) {
+        if (sc.tmp) cudaFree(sc.tmp);
+        sc.tmp = nullptr;
+        sc.tmp_bytes = 0;
+        e = cudaMalloc(&sc.tmp, need);
+        if (e != cudaSuccess) return cuda_fail(e, "raster sort scratch");
+        sc.tmp_bytes = need;
+    }
+    raster_pack<<<grid_for(n), 256, 0, s>>>(step, gid, n, gid_bits, sc.a);
+    size_t bytes = sc.tmp_bytes;
+    e = cub::DeviceRadixSort::SortKeys(sc.tmp, bytes, db, static_cast<int>(n), 0, end_bit, s);
+    if (e == cudaSuccess) {
+        raster_unpack<<<grid_for(n), 256, 0, s>>>(db.Current(), n, gid_bits, step, gid);
+        e = cudaGetLastError();
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "raster sort");
+    return NRN_OK;
 }
 
 nrn_status_t generate(const GenArgs& g, int32_t* src, int32_t* tgt, float* w, uint8_t* delay, cudaStream_t s) {

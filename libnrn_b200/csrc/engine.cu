@@ -127,6 +127,8 @@ struct nrn_engine {
     bool finalized = false;
     int32_t depth = 2;
     int64_t step = 0;                     // host mirror of the device step
+    int64_t step_high = 0;                // largest step number reached (bounds the raster's steps)
+    RasterSortScratch sort_scratch;       // raster sort buffers, kept between reads
     long long* d_step = nullptr;          // device step base
     unsigned long long* d_events = nullptr;
     unsigned long long* d_raster_count = nullptr;
@@ -168,6 +170,7 @@ struct nrn_engine {
         }
         cudaFree(d_step); cudaFree(d_events); cudaFree(d_raster_count); cudaFree(d_err);
         cudaFree(raster_step); cudaFree(raster_gid);
+        sort_scratch.release();
         cudaFree(send); cudaFree(recv);
         if (comm) ncclCommDestroy(comm);
         if (fork_ev) cudaEventDestroy(fork_ev);
@@ -1116,6 +1119,7 @@ nrn_status_t nrn_engine_run(nrn_engine* e, int64_t steps, int32_t chunk) {
     }
     for (; left > 0; ++s, --left) NRN_TRY(e->eager_step(s));
     e->step += steps;
+    e->step_high = std::max(e->step_high, e->step);
     return NRN_OK;
 }
 
@@ -1145,6 +1149,7 @@ nrn_status_t nrn_engine_profile(nrn_engine* e, int64_t steps, double* ms) {
     if (st == NRN_OK) {
         NRN_CUDA_TRY(cudaStreamSynchronize(e->stream));
         e->step += steps;
+        e->step_high = std::max(e->step_high, e->step);
     }
     return st;
 }
@@ -1156,6 +1161,7 @@ nrn_status_t nrn_engine_set_step(nrn_engine* e, int64_t step) {
     NRN_CUDA_TRY(cudaMemcpyAsync(e->d_step, &s, sizeof(s), cudaMemcpyHostToDevice, e->stream));
     NRN_CUDA_TRY(cudaStreamSynchronize(e->stream));
     e->step = step;
+    e->step_high = std::max(e->step_high, e->step);
     return NRN_OK;
 }
 
@@ -1178,7 +1184,15 @@ nrn_status_t nrn_engine_raster(nrn_engine* e, int32_t* step, int32_t* gid, int64
                                           " spikes, capacity " + std::to_string(e->raster_cap) + ")");
     if (static_cast<int64_t>(cnt) > cap) return fail(NRN_ERR_CAPACITY, "output buffer too small for the raster");
     // order of the reference's recorder: by step, ascending ids within a step
-    NRN_TRY(sort_raster(e->raster_step, e->raster_gid, static_cast<int64_t>(cnt), e->stream));
+    int64_t total = 0;
+    for (const auto& p : e->pops) total += p.n_global;
+    auto bits_for = [](int64_t max_value) {   // bits that hold 0 .. max_value
+        int b = 1;
+        while (b < 62 && (int64_t(1) << b) <= max_value) ++b;
+        return b;
+    };
+    NRN_TRY(sort_raster(e->raster_step, e->raster_gid, static_cast<int64_t>(cnt), bits_for(total - 1),
+                        bits_for(std::max<int64_t>(e->step_high, 1)), e->sort_scratch, e->stream));
     NRN_CUDA_TRY(cudaMemcpyAsync(step, e->raster_step, cnt * 4, cudaMemcpyDeviceToHost, e->stream));
     NRN_CUDA_TRY(cudaMemcpyAsync(gid, e->raster_gid, cnt * 4, cudaMemcpyDeviceToHost, e->stream));
     NRN_CUDA_TRY(cudaMemsetAsync(e->d_raster_count, 0, sizeof(unsigned long long), e->stream));
@@ -1413,6 +1427,7 @@ nrn_status_t nrn_engine_checkpoint_load(nrn_engine* e, const void* buf, int64_t 
     NRN_CUDA_TRY(cudaMemsetAsync(e->d_err, 0, sizeof(int), e->stream));
     NRN_CUDA_TRY(cudaStreamSynchronize(e->stream));
     e->step = h.step;
+    e->step_high = std::max(e->step_high, e->step);
     e->spikes_flushed = h.spikes_flushed;
     return NRN_OK;
 }

@@ -158,6 +158,26 @@ struct EngineRasterView {
 nrn_status_t engine_raster_view(nrn_engine* e, EngineRasterView* v);
 
 // Sorts n raster entries in place by (step, global id).
-nrn_status_t sort_raster(int32_t* step, int32_t* gid, int64_t n, cudaStream_t s);
+// Device buffers of the raster sort, kept between reads (grown on demand).
+struct RasterSortScratch {
+    unsigned long long* a = nullptr;
+    unsigned long long* b = nullptr;
+    void* tmp = nullptr;
+    size_t tmp_bytes = 0;
+    int64_t cap = 0;
+    void release() {
+        if (a) cudaFree(a);
+        if (b) cudaFree(b);
+        if (tmp) cudaFree(tmp);
+        a = b = nullptr;
+        tmp = nullptr;
+        tmp_bytes = 0;
+        cap = 0;
+    }
+};
+// Sorts n raster entries by (step, gid) in place on stream s; gid < 2^gid_bits,
+// step < 2^step_bits (the sort reads only those key bits).
+nrn_status_t sort_raster(int32_t* step, int32_t* gid, int64_t n, int gid_bits, int step_bits, RasterSortScratch& sc,
+                         cudaStream_t s);
 
 }  // namespace nrn

@@ -165,13 +165,20 @@ class Network:
     def step(self) -> int:
         return int(self.L.nrn_engine_step(self.h))
 
-    def raster(self, cap: int | None = None):
+    def raster(self, cap: int | None = None, out=None):
         """Spikes recorded since the last call: (step, gid), sorted by step then
-        id (the engine sorts on the device before the copy)."""
+        id (the engine sorts on the device before the copy).  ``out``: two
+        int32 arrays to copy into (for instance page-locked ones, which copy
+        fastest); the result is then a prefix view of them."""
         n = C.c_int64()
-        cap = cap if cap is not None else 1 << 26
-        st = np.empty(cap, np.int32)
-        gd = np.empty(cap, np.int32)
+        if out is not None:
+            st, gd = out
+            assert st.dtype == np.int32 and gd.dtype == np.int32 and st.flags.c_contiguous and gd.flags.c_contiguous
+            cap = min(st.size, gd.size)
+        else:
+            cap = cap if cap is not None else 1 << 26
+            st = np.empty(cap, np.int32)
+            gd = np.empty(cap, np.int32)
         N.check(self.L.nrn_engine_raster(self.h, st.ctypes.data, gd.ctypes.data, cap, C.byref(n)), "raster")
         return st[:n.value], gd[:n.value]   # sorted on the device
 
