@@ -510,7 +510,8 @@ def main():
     exch_ms = None
     if dist is not None:
         win = min(15, 32)
-        block = sum(win + 1 + max(4096, int(p["n"] * win * args.max_rate * spec["dt"] + 0.999999))
+        # the same size on every rank (largest slice), as the engine's blocks
+        block = sum(win + 1 + max(4096, int(-(-p["n_global"] // world) * win * args.max_rate * spec["dt"] + 0.999999))
                     for p in nw.pops)
         sb = torch.zeros(block, dtype=torch.int32, device="cuda")
         rb = torch.zeros(block * world, dtype=torch.int32, device="cuda")

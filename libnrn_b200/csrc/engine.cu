@@ -1010,9 +1010,13 @@ nrn_status_t nrn_engine_finalize(nrn_engine* e, int32_t init_update) {
     for (auto& p : e->pops) {
         // ring capacity per step: every neuron (one rank), or what all ranks can send
         if (e->world > 1) {
-            const double per_window = std::ceil(static_cast<double>(p.d.n) * e->win * e->max_rate_hz * e->dt);
-            p.send_cap = static_cast<int32_t>(std::min<double>(static_cast<double>(p.d.n) * e->win,
-                                                               std::max(4096.0, per_window)));
+            // Every rank's send block has the same layout (the all-gather moves
+            // equal blocks and the unpack reads the other ranks' blocks with
+            // this rank's offsets), so it is sized from the largest slice of
+            // the population, not from this rank's own slice.
+            const double n_max = static_cast<double>((static_cast<int64_t>(p.n_global) + e->world - 1) / e->world);
+            const double per_window = std::ceil(n_max * e->win * e->max_rate_hz * e->dt);
+            p.send_cap = static_cast<int32_t>(std::min<double>(n_max * e->win, std::max(4096.0, per_window)));
             p.hist_cap = static_cast<int32_t>(std::min<int64_t>(p.n_global,
                                                                 static_cast<int64_t>(p.send_cap) * e->world));
         } else {

@@ -37,8 +37,9 @@ def spec_of(name, steps):
 
 def run_one(spec, device=0, partition=None):
     from libnrn_b200.engine import Network
-    nw = Network.from_spec(spec, device=device, partition=partition)
+    nw = None
     try:
+        nw = Network.from_spec(spec, device=device, partition=partition)
         nw.run(spec["steps"])
         nw.sync()
         st, gid = nw.raster()
@@ -47,7 +48,8 @@ def run_one(spec, device=0, partition=None):
     except Exception as ex:   # reported to the parent
         return {"err": f"{type(ex).__name__}: {ex}"}
     finally:
-        nw.close()
+        if nw is not None:
+            nw.close()
 
 
 def _worker(rank, world, port, name, steps, q):
@@ -74,9 +76,13 @@ def run_partitioned(name, steps, world=2):
     procs = [ctx.Process(target=_worker, args=(r, world, port, name, steps, q)) for r in range(world)]
     for p in procs:
         p.start()
-    out = dict(q.get(timeout=600) for _ in procs)
-    for p in procs:
-        p.join(timeout=120)
+    try:
+        out = dict(q.get(timeout=300) for _ in procs)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():   # a rank that did not finish: end it, report below
+                p.kill()
     return [out[r] for r in range(world)]
 
 

@@ -80,8 +80,11 @@ def _worker(rank, world, port, q):
         uid = share_unique_id(comm_unique_id)
         ids = [None] * world
         dist.all_gather_object(ids, uid)
-        # a population of 1000 neurons, spikes drawn from one seed for all
-        n, win, steps, cap = 1000, 15, 90, 400
+        # a population of 1000 neurons, spikes drawn from one seed for all;
+        # every rank's block has the same size, from the largest slice
+        # (uneven splits give ranks different slice sizes)
+        n, win, steps = 1000, 15, 90
+        cap = min(-(-n // world) * win, 400)
         rng = np.random.default_rng(5)
         spikes = [np.flatnonzero(rng.random(n) < 0.02) for _ in range(steps)]
         lo, k = partition_range(n, rank, world)
@@ -102,11 +105,12 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_window_exchange_two_ranks():
+@pytest.mark.parametrize("world", [2, 3])
+def test_window_exchange(world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=120) for _ in procs]
