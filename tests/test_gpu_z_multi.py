@@ -1,7 +1,8 @@
 """The network partitioned over 2, 4 or 8 GPUs (one process per GPU, spike
 ids exchanged by NCCL all-gather once per window) gives the same spikes and
 plastic weights as the same network on one GPU.  Each case needs as many
-GPUs as ranks."""
+GPUs as ranks.  The file is collected after the single-GPU tests, so that
+a run stopping at its first failure has run those."""
 import os
 import socket
 
