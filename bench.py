@@ -94,6 +94,12 @@ class ClockSampler:
         for line in self.proc.stdout:
             self.rows.append([x.strip() for x in line.split(",")])
 
+    def wait_first(self, limit_s: float) -> None:
+        """Waits (at most limit_s) until nvidia-smi has printed a sample."""
+        t0 = time.perf_counter()
+        while self.proc and not self.rows and time.perf_counter() - t0 < limit_s:
+            time.sleep(0.02)
+
     def __exit__(self, *a):
         if self.proc:
             self.proc.terminate()
@@ -119,8 +125,14 @@ class ClockSampler:
 
 
 def cpu_reference(args, world_steps_hint=None):
-    """The reference implementation (compiled from its sources into
-    oracle/_ref) on a bounded sample of the workload, all host threads."""
+    """The reference's own CPU implementation (compiled from its unmodified
+    sources into oracle/_ref) on a bounded sample of the workload, with all
+    host threads.  The reference stores every projection as dense B x B
+    blocks (memory grows as N_src * N_tgt: about 4 TB at the bench's 1M
+    neurons), so the sample is the 12,500-neuron Brunel network of the
+    reference's own example configuration.  Without oracle/_ref (a snapshot
+    built without the reference sources) the C restatement runs instead, on
+    one thread, and the line says why."""
     sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
     import numpy as np
     from libnrn_b200 import workloads as W
@@ -144,12 +156,16 @@ def cpu_reference(args, world_steps_hint=None):
         sample = f"Izhikevich 16,000 neurons, out-degree 1,000, {steps} steps, block 256"
     net = S.realize(spec)
     net["threads"] = threads
-    kind = "reference" if O.reference_available() else "port"
-    t0 = time.perf_counter()
-    if kind == "reference":
+    reason = None
+    if O.reference_available():
+        kind, cores = "reference", threads
         res = O.run_reference(net, block=256)
         elapsed = res["elapsed_s"]
     else:
+        kind, cores = "port", 1
+        reason = ("oracle/_ref was not built (the reference sources were absent when build() ran); "
+                  "the single-threaded C restatement oracle/nrn_oracle.c ran instead")
+        t0 = time.perf_counter()
         res = O.run_oracle(net)
         elapsed = time.perf_counter() - t0
     # delivered events: spikes whose delay has elapsed within the sample
@@ -169,11 +185,15 @@ def cpu_reference(args, world_steps_hint=None):
     # that deliver, time per step over all steps.
     per_step_s = elapsed / steps
     ev_per_step = ev / max(1, steps - dmin)
-    return {
+    out = {
         "events_per_s": ev_per_step / per_step_s, "neuron_updates_per_s": n_total * steps / elapsed,
-        "rtf": elapsed / (steps * spec["dt"]), "elapsed_s": elapsed, "cores": threads, "kind": kind,
-        "sample": sample,
+        "rtf": elapsed / (steps * spec["dt"]), "elapsed_s": elapsed, "cores": cores, "kind": kind,
+        "sample": sample, "same_config": False,
+        "same_config_note": "the reference's dense-block storage cannot hold the bench network",
     }
+    if reason:
+        out["reason"] = reason
+    return out
 
 
 # dram__bytes_read.sum + dram__bytes_write.sum of walk_kernel (8.349 MB) and
@@ -344,41 +364,17 @@ def run_reference_arm(args, rank: int):
         "higher_is_better": True, "dtype": "f32", "data": "synthetic",
         "config": {"workload": args.workload + " (bounded CPU sample)"},
         "neuron_updates_per_s": r["neuron_updates_per_s"], "rtf": r["rtf"],
-        "cpu_baseline": {"value": r["events_per_s"], "unit": "events/s", "cores": r["cores"],
-                         "kind": r["kind"], "sample": r["sample"]},
+        "cpu_baseline": {k: r[k] for k in ("cores", "kind", "sample", "same_config", "same_config_note", "reason")
+                         if k in r} | {"value": r["events_per_s"], "unit": "events/s"},
         "e2e": {"value": r["events_per_s"], "unit": "events/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10_000)
-    ap.add_argument("--warmup", type=int, default=200)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="brunel_stdp", choices=["brunel_stdp", "brunel_1m", "brunel", "adex", "izh", "bsr"])
-    ap.add_argument("--chunk", type=int, default=0)
-    ap.add_argument("--profile-steps", type=int, default=300)
-    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
-    ap.add_argument("--max-rate", type=float, default=200.0,
-                    help="mean firing rate bound (Hz) that sizes the multi-GPU spike exchange buffers")
-    ap.add_argument("--scale", type=float, default=1.0,
-                    help="network size factor (profiling of small cases only; the bench line uses 1)")
-    args = ap.parse_args()
-    args.warmup = max(3, args.warmup)
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-
-    if args.impl == "reference":
-        run_reference_arm(args, rank)
-        return
-    if args.workload == "bsr":
-        run_bsr(args, rank, world, local)
-        return
-
+def run_network(args, rank: int, world: int, local: int) -> None:
+    """The spiking-network workloads (default: Brunel + STDP, 1,048,576
+    neurons per GPU)."""
     import numpy as np
     import torch
 
@@ -419,85 +415,85 @@ def main():
     n_total = spec["n_total"]
     stream = torch.cuda.ExternalStream(nw.stream())
 
+    # burn-in (untimed): the network leaves its start-up transient
+    burn = max(0, args.burn_in)
+    while burn > 0:
+        k = min(burn, 2000)
+        nw.run(k, args.chunk)
+        nw.sync()
+        nw.raster()
+        burn -= k
+    # Priming (untimed): the engine runs every step inside CUDA graphs keyed
+    # by the window phase and length of each piece of a run; one untimed run
+    # of the timed length from the same window phase captures the graphs the
+    # timed run replays, so no graph is captured inside the timed region.
+    win = 15
+    phase0 = (nw.step + args.warmup) % win
     nw.run(args.warmup, args.chunk)
+    nw.run(args.steps, args.chunk)
+    pad = (phase0 - nw.step) % win
+    if pad:
+        nw.run(pad, args.chunk)
     nw.sync()
     nw.raster()
-    s0, e0 = nw.counters()
-    barrier()
+    # Clocks are sampled from the warm-up through the end-to-end run: a
+    # short timed region (tens of steps) holds no sample of its own.
     with ClockSampler(local) as clk:
+        clk.wait_first(2.0)
+        nw.run(args.warmup, args.chunk)     # the same phase and lengths as in the priming
+        nw.sync()
+        nw.raster()
+        s0, e0 = nw.counters()
+        barrier()
         ev_a = torch.cuda.Event(enable_timing=True)
         ev_b = torch.cuda.Event(enable_timing=True)
         ev_a.record(stream)
         nw.run(args.steps, args.chunk)
         ev_b.record(stream)
         torch.cuda.synchronize()
-    ms = all_reduce(ev_a.elapsed_time(ev_b), "max")
-    barrier()
-    nw.sync()
-    s1, e1 = nw.counters()
-    nw.raster()
-    events = all_reduce(float(e1 - e0), "sum")
-    spikes = all_reduce(float(s1 - s0), "sum")
-    sec = ms / 1e3
-    value = events / sec
+        ms = all_reduce(ev_a.elapsed_time(ev_b), "max")
+        barrier()
+        nw.sync()
+        s1, e1 = nw.counters()
+        nw.raster()
+        events = all_reduce(float(e1 - e0), "sum")
+        spikes = all_reduce(float(s1 - s0), "sum")
+        sec = ms / 1e3
+        value = events / sec
 
-    # Per-phase device times (eager launches, events around each phase).
-    ps0, pe0 = nw.counters()
-    prof = nw.profile(args.profile_steps)
-    ps1, pe1 = nw.counters()
-    _, gid_p = nw.raster()
-    ev_p, sp_p = pe1 - pe0, ps1 - ps0
-    phases = {"deliver": prof[0], "neuron": prof[1], "stdp": prof[2]}
-    # Algorithmic bytes of the delivery phase (static delivery and the STDP
-    # walks): 8 B per static event (target + weight), 12 B per event through
-    # a plastic segment (target, weight read and write), 16 B per synapse of
-    # a spiking target's plastic in-list (potentiation: synapse, weight r/w),
-    # and 16 B of segment offsets per spike.  The plastic events and
-    # potentiations follow from the spikes of the plastic projections'
-    # source and target populations in the profiled steps (the raster).
-    plastic_ev = ltp = 0.0
-    for q in spec["projs"]:
-        if not q.get("plastic"):
-            continue
-        ps_, pt_ = spec["pops"][q["src"]], spec["pops"][q["tgt"]]
-        deg = q["gen"]["degree"]   # in-degree of each target
-        s_src = np.count_nonzero((gid_p >= ps_["offset"]) & (gid_p < ps_["offset"] + ps_["n"]))
-        s_tgt = np.count_nonzero((gid_p >= pt_["offset"]) & (gid_p < pt_["offset"] + pt_["n"]))
-        plastic_ev += s_src * deg * pt_["n"] / ps_["n"]   # mean out-degree onto this rank's targets
-        ltp += s_tgt * deg
-    static_ev = max(0.0, ev_p - plastic_ev)
-    deliver_bytes = 8.0 * static_ev + 12.0 * plastic_ev + 16.0 * ltp + 16.0 * sp_p
-    dom = max(phases, key=phases.get)
-    achieved = deliver_bytes / (phases["deliver"] / 1e3) / 1e9 if phases["deliver"] > 0 else 0.0
-
-    # e2e: this rank's initial state from pinned host, run, raster to host,
-    # all timed (wall clock, max over ranks).  The copies run on torch's
-    # stream; the engine stream starts after them.
-    host_state = []
-    for p in nw.pops:
-        for k in ("v", "ref"):
-            t = p[k]
-            if t is not None:
-                host_state.append((t, t.cpu().pin_memory()))
-    h2d = sum(h.numel() * 4 for _, h in host_state)
-    # the raster is read into page-locked host arrays allocated up front
-    rcap = sum(p["n"] for p in nw.pops) * 64
-    rcap = min(max(rcap, 1 << 20), 1 << 26)
-    r_st = torch.empty(rcap, dtype=torch.int32).pin_memory().numpy()
-    r_gid = torch.empty(rcap, dtype=torch.int32).pin_memory().numpy()
-    barrier()
-    t0 = time.perf_counter()
-    for dev_t, h in host_state:
-        dev_t.copy_(h, non_blocking=True)
-    torch.cuda.current_stream().synchronize()
-    t_up = time.perf_counter()
-    e_s0, e_e0 = nw.counters()
-    nw.run(args.steps, args.chunk)
-    nw.sync()
-    t_run = time.perf_counter()
-    st2, gid2 = nw.raster(out=(r_st, r_gid))
-    e_s1, e_e1 = nw.counters()
-    t1 = time.perf_counter()
+        # e2e: this rank's initial state from pinned host, run, raster to
+        # host, all timed (wall clock, max over ranks).  The copies run on
+        # torch's stream; the engine stream starts after them.
+        host_state = []
+        for p in nw.pops:
+            for k in ("v", "ref"):
+                t = p[k]
+                if t is not None:
+                    host_state.append((t, t.cpu().pin_memory()))
+        h2d = sum(h.numel() * 4 for _, h in host_state)
+        # the raster is read into page-locked host arrays allocated up front
+        rcap = sum(p["n"] for p in nw.pops) * 64
+        rcap = min(max(rcap, 1 << 20), 1 << 26)
+        r_st = torch.empty(rcap, dtype=torch.int32).pin_memory().numpy()
+        r_gid = torch.empty(rcap, dtype=torch.int32).pin_memory().numpy()
+        pad = (phase0 + args.warmup - nw.step) % win   # the timed run's phase: its graphs again
+        if pad:
+            nw.run(pad, args.chunk)
+        nw.sync()
+        nw.raster()
+        barrier()
+        t0 = time.perf_counter()
+        for dev_t, h in host_state:
+            dev_t.copy_(h, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        t_up = time.perf_counter()
+        e_s0, e_e0 = nw.counters()
+        nw.run(args.steps, args.chunk)
+        nw.sync()
+        t_run = time.perf_counter()
+        st2, gid2 = nw.raster(out=(r_st, r_gid))
+        e_s1, e_e1 = nw.counters()
+        t1 = time.perf_counter()
     e2e_s = all_reduce(t1 - t0, "max")
     e2e = all_reduce(float(e_e1 - e_e0), "sum") / e2e_s
     d2h = all_reduce(float(len(gid2) * 8), "sum")
@@ -505,14 +501,66 @@ def main():
     del host_state, r_st, r_gid, st2, gid2
     torch.cuda.synchronize()
 
-    # Partitioned runs: one all-gather of the engine's per-window exchange
-    # block size alone (same sizes, torch's communicator), for the line.
+    # Per-kernel device times: the same steps with the kernels serialised
+    # on the engine stream, CUDA events between them (the timed run above
+    # overlaps static delivery and the drive with the STDP walks).
+    prof, cnt = nw.profile_kernels(args.profile_steps)
+    finish_network_line(args, spec, nw, world, rank, dist, all_reduce, peaks, peaks_kind, clk, ms, value, events,
+                        spikes, nnz, setup_s, prof, cnt, e2e, e2e_s, h2d, d2h, (t0, t_up, t_run, t1))
+
+
+def finish_network_line(args, spec, nw, world, rank, dist, all_reduce, peaks, peaks_kind, clk, ms, value, events,
+                        spikes, nnz, setup_s, prof, cnt, e2e, e2e_s, h2d, d2h, tmarks):
+    import numpy as np
+    import torch
+
+    P = max(1, cnt["steps"])
+    _, gid_p = nw.raster()            # the profiled steps' spikes
+    n_total = spec["n_total"]
+    sec = ms / 1e3
+    # Algorithmic HBM bytes per launch (one launch per step):
+    #  walk_kernel: 12 B per event through a plastic segment (target index,
+    #    weight read and write) + 32 B per arriving spike (segment bounds 16 B,
+    #    segment state read and write 16 B);
+    #  deliver_kernel: 8 B per static event (target, weight) + 16 B per
+    #    (spike, delay segment) for its bounds;
+    #  neuron update: 40 B per neuron (v, refractory, input read and zeroed,
+    #    drive, spike flag, target trace ring read and write).
+    pop_spikes = []
+    for p_ in spec["pops"]:
+        pop_spikes.append(int(np.count_nonzero((gid_p >= p_["offset"]) & (gid_p < p_["offset"] + p_["n"]))))
+    arrivals, segs = 0.0, 0.0
+    for q in spec["projs"]:
+        g = q["gen"]
+        nd = g["dmax"] - g["dmin"] + 1
+        if q.get("plastic"):
+            ps_, pt_ = spec["pops"][q["src"]], spec["pops"][q["tgt"]]
+            mean_out = g["degree"] * (pt_["n"] / world) / ps_["n"] if g["mode"] == "in" else g["degree"] / world
+            arrivals += cnt["walk_events"] / max(mean_out, 1e-9)
+        else:
+            segs += pop_spikes[q["src"]] * nd
+    walk_bytes = 12.0 * cnt["walk_events"] + 32.0 * arrivals
+    deliver_bytes = 8.0 * cnt["static_events"] + 16.0 * segs
+    neuron_bytes = 40.0 * sum(p_["n"] for p_ in nw.pops) * P
+    kern = {"walk_kernel": ("stdp_walks", walk_bytes), "deliver_kernel": ("static_delivery", deliver_bytes),
+            "lif4_group_kernel": ("neuron_update", neuron_bytes)}
+    dom = max(kern, key=lambda k: prof[kern[k][0]])
+    dom_ms = prof[kern[dom][0]]
+    dom_bytes = kern[dom][1]
+    achieved = dom_bytes / (dom_ms / 1e3) / 1e9 if dom_ms > 0 else 0.0
+    # Random L2 operations of the delivery (the measured limit of this
+    # path): one reduction per event, plus per plastic event one target
+    # record load (two loads without the walk record: spike steps and trace).
+    walk_rec = os.environ.get("NRN_WALK_REC") is not None
+    l2_ops = cnt["static_events"] + cnt["walk_events"] * (2 if walk_rec else 3)
+    deliv_ms = prof["static_delivery"] + prof["stdp_walks"]
+    traffic = DELIVERY_TRAFFIC_PER_STEP if args.workload == "brunel_stdp" and args.scale == 1.0 else None
+
     exch_ms = None
     if dist is not None:
         win = min(15, 32)
-        # the same size on every rank (largest slice), as the engine's blocks
-        block = sum(win + 1 + max(4096, int(-(-p["n_global"] // world) * win * args.max_rate * spec["dt"] + 0.999999))
-                    for p in nw.pops)
+        block = sum(win + 1 + max(4096, int(-(-p_["n_global"] // world) * win * args.max_rate * spec["dt"] + 0.999999))
+                    for p_ in nw.pops)
         sb = torch.zeros(block, dtype=torch.int32, device="cuda")
         rb = torch.zeros(block * world, dtype=torch.int32, device="cuda")
         for _ in range(3):
@@ -534,19 +582,19 @@ def main():
         except Exception as ex:  # report, do not fail the GPU line
             cpu = {"error": str(ex)[:200]}
 
-    clocks = clk.summary()
     n_walk = sum(1 for q in spec["projs"] if q.get("plastic"))
     windows = args.steps // 15 if (world > 1 or n_walk) else 0
-    kernels_per_step = 1 + n_walk + len(nw.pops)
+    kernels_per_step = 3 + n_walk     # drive, static delivery, walks, one neuron launch (one model)
     chunk = args.chunk if args.chunk > 0 else 45
+    t0, t_up, t_run, t1 = tmarks
     line = {
         "metric": "synaptic_events_per_s", "value": value, "unit": "events/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (Philox-generated connectivity and drive)",
         "config": {"workload": args.workload, "neurons": n_total, "synapses": int(nnz),
-                   "dt_ms": spec["dt"] * 1e3, "l2": "inputs larger than L2 (synapse store "
-                   f"{nnz * 8 / 1e9:.1f} GB)",
+                   "dt_ms": spec["dt"] * 1e3, "burn_in_steps": max(0, args.burn_in),
+                   "l2": f"inputs larger than L2 (synapse store {nnz * 8 / 1e9:.1f} GB)",
                    "parallelism": "single GPU" if world == 1 else
                    f"partitioned by neuron over {world} GPUs, NCCL all-gather of spike ids per 15-step window"},
         "neuron_updates_per_s": n_total * args.steps / sec,
@@ -555,28 +603,39 @@ def main():
         "setup_s": setup_s,
         "gpu_launches": kernels_per_step * args.steps + windows * (1 + len(nw.pops) * (2 if world > 1 else 0))
         + (args.steps + chunk - 1) // chunk,
-        "phase_ms_per_step": {k: v / args.profile_steps for k, v in phases.items()},
+        "kernel_ms_per_step": {k: v / P for k, v in prof.items()},
+        "kernel_ms_note": "the kernels run one after the other with CUDA events between them over "
+                          f"{P} further steps; the timed run overlaps static delivery and the drive with the walks",
         "exchange_ms_per_window": exch_ms,
-        "roofline": {"kernel": "walk_kernel + deliver_kernel (delivery phase)", "dominant_phase": dom,
-                     "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+        "roofline": {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / peaks["hbm_gbs"], "peak_kind": peaks_kind,
-                     "traffic": DELIVERY_TRAFFIC_PER_STEP if args.workload == "brunel_stdp" and args.scale == 1.0
-                     else None,
-                     "traffic_note": "DRAM bytes per step of walk_kernel + deliver_kernel from the ncu captures "
-                                     "at 262,144 neurons, x4 to the bench size (the units scale with the network)"},
+                     "bytes_per_launch": dom_bytes / P, "ms_per_launch": dom_ms / P,
+                     "counts_per_step": {"walk_events": cnt["walk_events"] / P,
+                                         "static_events": cnt["static_events"] / P,
+                                         "arriving_plastic_spikes": arrivals / P,
+                                         "static_segments": segs / P, "profiled_steps": P},
+                     "step_frac": (walk_bytes + deliver_bytes + neuron_bytes) / P / (ms / args.steps / 1e3) / 1e9
+                     / peaks["hbm_gbs"],
+                     "traffic": traffic,
+                     "traffic_note": "DRAM bytes per step of walk_kernel + deliver_kernel from ncu captures at "
+                                     "262,144 neurons, x4 to the bench size" if traffic else None,
+                     "l2_random_ops_per_s": l2_ops / (deliv_ms / 1e3) if deliv_ms > 0 else None,
+                     "l2_note": "random L2 reductions and loads of static delivery + walks per second of their "
+                                "serialised time; measured ceilings of one kind alone: 186 G/s reductions, 222 G/s "
+                                "16-byte loads, 285 G/s 4-byte loads"},
         "e2e": {"value": e2e, "unit": "events/s", "h2d_bytes_per_step": h2d / args.steps,
                 "d2h_bytes_per_step": d2h / args.steps,
                 "seconds": {"upload": t_up - t0, "run": t_run - t_up, "raster": t1 - t_run}},
-        "clocks": clocks,
+        "clocks": clk.summary() | {"window": "sampled through the warm-up, timed and end-to-end runs"},
     }
     if cpu is not None:
         if "error" in cpu:
             line["cpu_baseline"] = cpu
         else:
-            line["cpu_baseline"] = {"value": cpu["events_per_s"], "unit": "events/s", "cores": cpu["cores"],
-                                    "kind": cpu["kind"], "sample": cpu["sample"],
-                                    "neuron_updates_per_s": cpu["neuron_updates_per_s"], "rtf": cpu["rtf"]}
-    del stream
+            line["cpu_baseline"] = {k: cpu[k] for k in ("same_config", "same_config_note", "reason") if k in cpu}
+            line["cpu_baseline"] |= {"value": cpu["events_per_s"], "unit": "events/s", "cores": cpu["cores"],
+                                     "kind": cpu["kind"], "sample": cpu["sample"],
+                                     "neuron_updates_per_s": cpu["neuron_updates_per_s"], "rtf": cpu["rtf"]}
     torch.cuda.synchronize()
     nw.close()
     if dist is not None:
@@ -584,6 +643,38 @@ def main():
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10_000)
+    ap.add_argument("--warmup", type=int, default=200)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="brunel_stdp", choices=["brunel_stdp", "brunel_1m", "brunel", "adex", "izh", "bsr"])
+    ap.add_argument("--chunk", type=int, default=0)
+    ap.add_argument("--burn-in", type=int, default=1000,
+                    help="untimed steps after set-up and before the warm-up, so that the timed steps see the "
+                         "network's steady activity rather than its start-up transient")
+    ap.add_argument("--profile-steps", type=int, default=300)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--max-rate", type=float, default=200.0,
+                    help="mean firing rate bound (Hz) that sizes the multi-GPU spike exchange buffers")
+    ap.add_argument("--scale", type=float, default=1.0,
+                    help="network size factor (profiling of small cases only; the bench line uses 1)")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        run_reference_arm(args, rank)
+        return
+    if args.workload == "bsr":
+        run_bsr(args, rank, world, local)
+        return
+    run_network(args, rank, world, local)
 
 
 if __name__ == "__main__":

@@ -23,7 +23,7 @@
  *                             launch_synaptic_current_block_dense,
  *                             src/synapse/kernels/synapse_kernels.cu:56-79)
  *       nrn_cuda_stdp_*       pair STDP (src/plasticity/stdp.cpp:43-141)
- *       nrn_cuda_bsr_spmm     batched-trial block-sparse product on the
+ *       nrn_cuda_bsr_propagate batched-trial block-sparse product on the
  *                             tensor cores (the stub's intended block-dense
  *                             matmul, synapse_kernels.cu:30-51, for many trials)
  *
@@ -187,6 +187,27 @@ typedef struct {
     const float* drive_values;
     /* Per-neuron spike statistics updated at each spike, or NULL. */
     struct nrn_spike_stat* spike_stats;
+    /* Walk record of each neuron as the target of a plastic projection
+     * whose synapses all have delay rec_lag + 1 (int4 per neuron, 16-byte
+     * aligned), or NULL: x, y, z = its newest three spike steps (newest
+     * first, -1 = none) and w = the bits of trace slot rec_trace's value
+     * rec_lag steps before this one, written at every step.  The STDP walk
+     * of the next step then reads one record per synapse instead of the
+     * spike steps and the trace ring separately. */
+    int32_t* walk_rec;
+    int32_t rec_trace;
+    int32_t rec_lag;
+    /* Synapse channels (nrn_syn_desc_t kinds), applied before the model
+     * update: chan_in[c] is the input delivered this step (read, then
+     * zeroed), chan_s[c] the decay state, chan_r[c] the rise state (DEXP,
+     * AMPA).  n_chan = 0: none. */
+    int32_t n_chan;
+    int32_t chan_kind[4];
+    float chan_e_rev[4];
+    double chan_tau_rise[4], chan_tau_decay[4];
+    float* chan_in[4];
+    float* chan_s[4];
+    float* chan_r[4];
 } nrn_pop_step_t;
 
 #define NRN_MAX_TRACES 4
@@ -398,7 +419,32 @@ typedef struct {
     nrn_drive_t drive;
 } nrn_pop_desc_t;
 
-enum { NRN_RECV_CURRENT = 0, NRN_RECV_GEXC = 1, NRN_RECV_GINH = 2 };
+/* Receptor of a projection: the target's input current, its AdEx
+ * conductance inputs, or NRN_RECV_CHANNEL + c for synapse channel c of the
+ * target population (nrn_engine_add_synapse_channel). */
+enum { NRN_RECV_CURRENT = 0, NRN_RECV_GEXC = 1, NRN_RECV_GINH = 2, NRN_RECV_CHANNEL = 16 };
+
+/* A synapse channel: per-neuron synapse state of a population, fused into
+ * its neuron update.  These are the reference's synapse models, declared in
+ * include/nrn/synapse/exponential.h:16-21, double_exponential.h:17-25 and
+ * ampa.h:17-29 (their forward is a stub there,
+ * src/synapse/exponential.cpp:37-42).  Each step, before the neuron
+ * integrates, with `in` the weights delivered into the channel this step and
+ * dec = (float)exp(-dt/tau):
+ *   NRN_SYN_EXP : s = s*dec_decay + in;  I += s
+ *   NRN_SYN_DEXP: s = s*dec_decay + in;  r = r*dec_rise + in;  I += s - r
+ *   NRN_SYN_AMPA: s, r as DEXP; g = s - r;  I += g*(e_rev - v)
+ * (AMPA's declared I_syn = g*(V - E_rev) is the outward membrane current;
+ * the neuron models add inward current, hence e_rev - v). */
+enum { NRN_SYN_EXP = 1, NRN_SYN_DEXP = 2, NRN_SYN_AMPA = 3 };
+#define NRN_MAX_CHANNELS 4
+typedef struct {
+    int32_t kind;
+    int32_t pad;
+    double tau_rise;           /* s (DEXP, AMPA)                             */
+    double tau_decay;          /* s                                          */
+    double e_rev;              /* reversal potential (AMPA), the population's units */
+} nrn_syn_desc_t;
 
 /* Synapse list of a projection (host or device memory, see `on_device`),
  * any order; delays in steps.  The engine keeps its own copy. */
@@ -444,13 +490,37 @@ NRN_API nrn_status_t nrn_engine_destroy(nrn_engine* e);
  * Every rank must run the same step counts.  No counterpart in the
  * reference (its runner is single-device, src/simulation/runner.cpp). */
 NRN_API nrn_status_t nrn_comm_unique_id(uint8_t id[128]);
+/* The communicator is non-blocking and every host wait on it is bounded
+ * (nrn_engine_set_comm_timeout, default 120 s): its set-up here, the layout
+ * check in nrn_engine_finalize (every rank must build the same network:
+ * otherwise NRN_ERR_COMM), and every wait on the engine stream of a
+ * partitioned run (nrn_engine_sync, raster and weight reads, checkpoints).
+ * A rank that stopped, ran other step counts or failed makes the others'
+ * waits end with NRN_ERR_COMM: the communicator is aborted (its waiting
+ * NCCL kernels end) and later runs return NRN_ERR_STATE. */
 NRN_API nrn_status_t nrn_engine_set_partition(nrn_engine* e, int32_t rank, int32_t world, const uint8_t id[128],
                                               double max_rate_hz);
+/* Time limit of the host waits on a partitioned engine (set before
+ * nrn_engine_set_partition to bound its set-up too). */
+NRN_API nrn_status_t nrn_engine_set_comm_timeout(nrn_engine* e, double seconds);
+/* The bounded wait the engine uses: calls poll(ctx) until it returns > 0
+ * (NRN_OK) or < 0 (NRN_ERR_COMM), spinning at first and then sleeping
+ * between calls; NRN_ERR_TIMEOUT after timeout_s seconds.  Host only. */
+NRN_API nrn_status_t nrn_comm_bounded_wait(int (*poll)(void*), void* ctx, double timeout_s);
+/* Test hook: the next query of a communicator's asynchronous state reports
+ * nccl_result (an ncclResult_t) instead of NCCL's own; 0 clears it.  Lets a
+ * test drive the abort path with an error code, without a failing GPU. */
+NRN_API nrn_status_t nrn_comm_fake_async_error(int32_t nccl_result);
 NRN_API nrn_status_t nrn_engine_add_population(nrn_engine* e, const nrn_pop_desc_t* d, int32_t* id);
 /* Update the uniform/per-neuron parameters of a population (between runs). */
 NRN_API nrn_status_t nrn_engine_set_params(nrn_engine* e, int32_t pop, const float* const* param,
                                    const float* uniform);
 NRN_API nrn_status_t nrn_engine_add_projection(nrn_engine* e, const nrn_proj_desc_t* d, int32_t* id);
+/* Adds synapse channel *channel (0..NRN_MAX_CHANNELS-1) to population pop;
+ * projections deliver into it with receptor NRN_RECV_CHANNEL + channel.
+ * Before nrn_engine_finalize. */
+NRN_API nrn_status_t nrn_engine_add_synapse_channel(nrn_engine* e, int32_t pop, const nrn_syn_desc_t* d,
+                                                    int32_t* channel);
 NRN_API nrn_status_t nrn_engine_generate_projection(nrn_engine* e, const nrn_gen_desc_t* g, int32_t* id,
                                             int64_t* nnz);
 /* stdp = {tau_plus, tau_minus, a_plus, a_minus, w_min, w_max, learning_rate} */
@@ -495,6 +565,14 @@ NRN_API nrn_status_t nrn_engine_nnz(nrn_engine* e, int32_t proj, int64_t* nnz);
  * the engine stream: ms[0] delivery, ms[1] neuron updates, ms[2] plasticity
  * (summed over the steps).  For profiling; results equal nrn_engine_run. */
 NRN_API nrn_status_t nrn_engine_profile(nrn_engine* e, int64_t steps, double* ms);
+/* Runs `steps` steps with every kernel on the engine stream one after the
+ * other (no overlap), timing each with CUDA events: ms[0] external drive,
+ * ms[1] static delivery, ms[2] STDP walks (plastic delivery), ms[3] neuron
+ * updates, ms[4] per-step STDP kernels, ms[5] window ends (spike exchange,
+ * trace snapshots), summed over the steps.  counts[0] events delivered by
+ * the static delivery, counts[1] by the walks, counts[2] window ends,
+ * counts[3] steps.  Results equal nrn_engine_run's. */
+NRN_API nrn_status_t nrn_engine_profile_kernels(nrn_engine* e, int64_t steps, double* ms, int64_t* counts);
 /* Counters: total spikes and delivered synaptic events since creation. */
 NRN_API nrn_status_t nrn_engine_counters(nrn_engine* e, int64_t* spikes, int64_t* events);
 

@@ -19,7 +19,8 @@ NRN_MAX_POPS = 32
 
 MODEL = {"lif": 0, "adex": 1, "izh": 2}
 DRIVE = {None: 0, "poisson": 1, "gauss": 2, "poisson_gexc": 3}
-RECEPTOR = {"current": 0, "gexc": 1, "ginh": 2}
+RECEPTOR = {"current": 0, "gexc": 1, "ginh": 2, "chan0": 16, "chan1": 17, "chan2": 18, "chan3": 19}
+SYN_KIND = {"exp": 1, "dexp": 2, "ampa": 3}
 
 # Public entry points of include/nrn_cuda.h (checked by the test suite).
 EXPORTS = [
@@ -36,7 +37,8 @@ EXPORTS = [
     "nrn_cuda_bsr_propagate", "nrn_cuda_bsr_pack", "nrn_cuda_bsr_pack_spikes", "nrn_cuda_bsr_unpack_spikes",
     "nrn_cuda_bsr_spikes", "nrn_cuda_drive_fill", "nrn_engine_checkpoint_size", "nrn_engine_checkpoint_save",
     "nrn_engine_checkpoint_load", "nrn_engine_enable_spike_stats", "nrn_engine_spike_stats",
-    "nrn_engine_spike_stats_reset",
+    "nrn_engine_spike_stats_reset", "nrn_engine_set_comm_timeout", "nrn_comm_bounded_wait",
+    "nrn_comm_fake_async_error", "nrn_engine_profile_kernels", "nrn_engine_add_synapse_channel",
 ]
 
 
@@ -70,8 +72,16 @@ class PopStep(C.Structure):
         ("post_ring_k", C.c_int32), ("id_offset", C.c_int32), ("win", C.c_int32),
         ("win_mask", C.c_void_p), ("send_hdr", C.c_void_p), ("send_ids", C.c_void_p),
         ("send_cap", C.c_int32), ("pad2", C.c_int32), ("err", C.c_void_p), ("drive_values", C.c_void_p),
-        ("spike_stats", C.c_void_p),
+        ("spike_stats", C.c_void_p), ("walk_rec", C.c_void_p), ("rec_trace", C.c_int32),
+        ("rec_lag", C.c_int32), ("n_chan", C.c_int32), ("chan_kind", C.c_int32 * 4),
+        ("chan_e_rev", C.c_float * 4), ("chan_tau_rise", C.c_double * 4), ("chan_tau_decay", C.c_double * 4),
+        ("chan_in", C.c_void_p * 4), ("chan_s", C.c_void_p * 4), ("chan_r", C.c_void_p * 4),
     ]
+
+
+class SynDesc(C.Structure):
+    _fields_ = [("kind", C.c_int32), ("pad", C.c_int32), ("tau_rise", C.c_double), ("tau_decay", C.c_double),
+                ("e_rev", C.c_double)]
 
 
 class SpikeHist(C.Structure):
@@ -121,6 +131,10 @@ class GenDesc(C.Structure):
 
 
 _lib = None
+
+
+# int (*poll)(void* ctx) of nrn_comm_bounded_wait
+POLL_FN = C.CFUNCTYPE(C.c_int, C.c_void_p)
 
 
 def lib() -> C.CDLL:
@@ -174,6 +188,11 @@ def lib() -> C.CDLL:
             "nrn_engine_enable_spike_stats": [vp],
             "nrn_engine_spike_stats": [vp, i32, vp, i64],
             "nrn_engine_spike_stats_reset": [vp],
+            "nrn_engine_set_comm_timeout": [vp, C.c_double],
+            "nrn_comm_bounded_wait": [POLL_FN, vp, C.c_double],
+            "nrn_comm_fake_async_error": [i32],
+            "nrn_engine_add_synapse_channel": [vp, i32, C.POINTER(SynDesc), C.POINTER(i32)],
+            "nrn_engine_profile_kernels": [vp, i64, C.POINTER(C.c_double), C.POINTER(i64)],
         }
         for name, args in sig.items():
             f = getattr(L, name)

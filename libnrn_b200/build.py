@@ -25,7 +25,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-std=c++17", "-O3", "-lineinfo", "-fmad=false", "-cudart=shared", "-Xcompiler", "-fPIC", "-Xcompiler",
          "-fvisibility=hidden", f"-I{os.path.join(ROOT, 'include')}", f"-I{CSRC}"]
-SOURCES = ["neuron.cu", "deliver.cu", "connect.cu", "engine.cu", "blockdense.cu", "raster_noalloc.cu", "plastic.cu",
+SOURCES = ["neuron.cu", "deliver.cu", "connect.cu", "engine.cu", "comm.cu", "blockdense.cu", "raster_noalloc.cu", "plastic.cu",
            "exchange.cu", "bsr.cu"]
 
 

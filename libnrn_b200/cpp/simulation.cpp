@@ -25,6 +25,7 @@
 #include <nrn/plasticity/plasticity_rule.h>
 #include <nrn/plasticity/stdp.h>
 #include <nrn/simulation/runner.h>
+#include <nrn/synapse/synapse.h>
 
 #include <algorithm>
 #include <cmath>
@@ -261,6 +262,42 @@ void build_engine(Simulation* sim) {
         return -1;
     };
     const torch::Device dev(torch::kCUDA, static_cast<c10::DeviceIndex>(eng->device));
+    // Synapse modules of the connections (Connection::synapse) become synapse
+    // channels of their target population: one channel per distinct
+    // (model, time constants, reversal) on a population; static synapses
+    // (or none) deliver into I_syn directly.
+    std::vector<std::vector<nrn_syn_desc_t>> chans(eng->pops.size());
+    auto receptor_of = [&](const NrnModule& m, int32_t tgt) -> int32_t {
+        nrn_syn_desc_t d{};
+        if (m.ops == &synapse::exp_synapse_ops && m.impl) {
+            const auto& o = static_cast<synapse::ExponentialSynapse*>(m.impl)->options;
+            d.kind = NRN_SYN_EXP;
+            d.tau_decay = o.tau_decay();
+        } else if (m.ops == &synapse::dexp_synapse_ops && m.impl) {
+            const auto& o = static_cast<synapse::DoubleExponentialSynapse*>(m.impl)->options;
+            d.kind = NRN_SYN_DEXP;
+            d.tau_rise = o.tau_rise();
+            d.tau_decay = o.tau_decay();
+        } else if (m.ops == &synapse::ampa_ops && m.impl) {
+            const auto& o = static_cast<synapse::AMPASynapse*>(m.impl)->options;
+            d.kind = NRN_SYN_AMPA;
+            d.tau_rise = o.tau_rise();
+            d.tau_decay = o.tau_decay();
+            d.e_rev = o.e_rev();
+        } else {
+            return NRN_RECV_CURRENT;
+        }
+        auto& list = chans[static_cast<size_t>(tgt)];
+        for (size_t k = 0; k < list.size(); ++k)
+            if (list[k].kind == d.kind && list[k].tau_rise == d.tau_rise && list[k].tau_decay == d.tau_decay &&
+                list[k].e_rev == d.e_rev)
+                return NRN_RECV_CHANNEL + static_cast<int32_t>(k);
+        int32_t ch = 0;
+        detail::check(nrn_engine_add_synapse_channel(eng->e, eng->pops[static_cast<size_t>(tgt)].id, &d, &ch),
+                      "sim: synapse channel");
+        list.push_back(d);
+        return NRN_RECV_CHANNEL + ch;
+    };
     for (auto& cp : region->connections) {
         Connection* c = cp.get();
         auto& ct = c->connectivity;
@@ -311,7 +348,7 @@ void build_engine(Simulation* sim) {
         nrn_proj_desc_t pd{};
         pd.src_pop = pop_index(c->source);
         pd.tgt_pop = pop_index(c->target);
-        pd.receptor = NRN_RECV_CURRENT;
+        pd.receptor = receptor_of(c->synapse, pd.tgt_pop);
         pd.on_device = 1;
         pd.nnz = cc.nnz;
         pd.src = src.data_ptr<int32_t>();

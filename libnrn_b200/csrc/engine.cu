@@ -92,6 +92,12 @@ struct EnginePop {
     int32_t* cnt = nullptr;          // [n]
     float* drive_buf = nullptr;      // [n] this step's drive, drawn ahead on the side stream
     nrn_spike_stat_t* stats = nullptr;   // [n] spike statistics (when enabled)
+    // synapse channels (per-neuron synapse state, nrn_syn_desc_t)
+    int32_t n_chan = 0;
+    nrn_syn_desc_t chan[NRN_MAX_CHANNELS]{};
+    float* chan_in[NRN_MAX_CHANNELS] = {};
+    float* chan_s[NRN_MAX_CHANNELS] = {};
+    float* chan_r[NRN_MAX_CHANNELS] = {};
 };
 
 struct EngineProj {
@@ -108,6 +114,8 @@ struct EngineProj {
     float* seg_x = nullptr;
     float* pre_snap = nullptr;   // [pre_depth][n_src] source trace at window ends
     float* post_ring = nullptr;  // [ring_depth][n_tgt] target trace at every step
+    int32_t* walk_rec = nullptr; // [n_tgt][4] walk record (single-delay walk projections)
+    unsigned int* work_ctr = nullptr;   // [3] unit counters of the walk launches
     int32_t pre_depth = 1;
 };
 
@@ -130,19 +138,22 @@ struct nrn_engine {
     int64_t step_high = 0;                // largest step number reached (bounds the raster's steps)
     RasterSortScratch sort_scratch;       // raster sort buffers, kept between reads
     long long* d_step = nullptr;          // device step base
-    unsigned long long* d_events = nullptr;
+    unsigned long long* d_events = nullptr;   // [2]: static delivery, walks
     unsigned long long* d_raster_count = nullptr;
     int32_t* raster_step = nullptr;
     int32_t* raster_gid = nullptr;
     int64_t raster_cap = 0;
     int64_t spikes_flushed = 0;
-    std::map<int, cudaGraphExec_t> graphs;
+    std::map<std::pair<int, int>, cudaGraphExec_t> graphs;   // (window phase of the first step, steps)
     int* d_err = nullptr;                 // device error flag (plasticity, exchange)
     bool use_graphs = true;
     bool spike_stats = false;             // per-neuron spike statistics kept
     // partition over GPUs
     int32_t rank = 0, world = 1;
     ncclComm_t comm = nullptr;
+    double comm_timeout_s = 120.0;        // bound of every host wait on the communicator
+    bool comm_failed = false;             // the communicator was aborted: no further runs
+    bool stuck = false;                   // the stream did not drain after an abort
     double max_rate_hz = 200.0;           // sizes the exchange buffers
     // windows (exchange of spikes, STDP trace snapshots)
     bool windows = false;
@@ -154,25 +165,32 @@ struct nrn_engine {
 
     ~nrn_engine() {
         if (device >= 0) cudaSetDevice(device);
+        if (stuck) {
+            // work still queued on the stream after a communicator abort:
+            // freeing would wait for it, so the buffers are left to the process
+            comm = nullptr;
+            return;
+        }
         for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
         for (auto& p : pops) {
             if (p.owns_isyn) cudaFree(p.d.i_syn);
             cudaFree(p.g_exc); cudaFree(p.g_inh); cudaFree(p.gin_exc); cudaFree(p.gin_inh);
             cudaFree(p.hist_ids); cudaFree(p.hist_count);
             cudaFree(p.mask); cudaFree(p.recent); cudaFree(p.ring); cudaFree(p.cnt); cudaFree(p.drive_buf); cudaFree(p.stats);
+            for (int c = 0; c < p.n_chan; ++c) { cudaFree(p.chan_in[c]); cudaFree(p.chan_s[c]); cudaFree(p.chan_r[c]); }
         }
         for (auto& q : projs) {
             free_csr(q.csr);
             cudaFree(q.x_pre);
             cudaFree(q.x_post);
             cudaFree(q.seg_last); cudaFree(q.seg_x);
-            cudaFree(q.pre_snap); cudaFree(q.post_ring);
+            cudaFree(q.pre_snap); cudaFree(q.post_ring); cudaFree(q.walk_rec); cudaFree(q.work_ctr);
         }
         cudaFree(d_step); cudaFree(d_events); cudaFree(d_raster_count); cudaFree(d_err);
         cudaFree(raster_step); cudaFree(raster_gid);
         sort_scratch.release();
         cudaFree(send); cudaFree(recv);
-        if (comm) ncclCommDestroy(comm);
+        if (comm) comm_destroy(&comm, comm_timeout_s);
         if (fork_ev) cudaEventDestroy(fork_ev);
         if (join_ev) cudaEventDestroy(join_ev);
         if (side) cudaStreamDestroy(side);
@@ -181,6 +199,7 @@ struct nrn_engine {
 
     float* acc_of(const EngineProj& q) const {
         const EnginePop& t = pops[q.tgt_pop];
+        if (q.receptor >= NRN_RECV_CHANNEL) return t.chan_in[q.receptor - NRN_RECV_CHANNEL];
         return q.receptor == NRN_RECV_CURRENT ? t.d.i_syn : q.receptor == NRN_RECV_GEXC ? t.gin_exc : t.gin_inh;
     }
 
@@ -233,6 +252,16 @@ struct nrn_engine {
             a.uniform[k] = p.d.uniform[k];
         }
         if (in_run) {
+            a.n_chan = p.n_chan;
+            for (int c = 0; c < p.n_chan; ++c) {
+                a.chan_kind[c] = p.chan[c].kind;
+                a.chan_tau_rise[c] = p.chan[c].tau_rise;
+                a.chan_tau_decay[c] = p.chan[c].tau_decay;
+                a.chan_e_rev[c] = static_cast<float>(p.chan[c].e_rev);
+                a.chan_in[c] = p.chan_in[c];
+                a.chan_s[c] = p.chan_s[c];
+                a.chan_r[c] = p.chan_r[c];
+            }
             a.drive = p.d.drive;
             a.step = step_off;
             a.step_base = reinterpret_cast<const int64_t*>(d_step);
@@ -266,6 +295,11 @@ struct nrn_engine {
             a.trace_slow_ratio = slow_ratio;
             for (const auto& q : projs) {
                 if (q.walk && q.tgt_pop == i) {
+                    if (q.walk_rec) {
+                        a.walk_rec = q.walk_rec;
+                        a.rec_trace = a.n_traces;
+                        a.rec_lag = q.csr.dmin - 1;
+                    }
                     a.trace_ring[a.n_traces] = q.post_ring;
                     a.trace_ring_depth = ring_depth;
                     a.trace_decay[a.n_traces++] = static_cast<float>(std::exp(-dt / q.stdp[1]));
@@ -339,6 +373,7 @@ struct nrn_engine {
         a.src_lo = ps.lo;
         a.src_hi = ps.lo + ps.d.n;
         a.tgt_recent = reinterpret_cast<const int4*>(pt.recent + static_cast<int64_t>(pt.lo) * 4);
+        a.tgt_rec = reinterpret_cast<const int4*>(q.walk_rec);
         a.tgt_ring = pt.ring;
         a.tgt_cnt = pt.cnt;
         a.ring_k = kRing;
@@ -359,7 +394,8 @@ struct nrn_engine {
         a.sweep_rows = (q.csr.n_src + kSweepPeriod - 1) / kSweepPeriod;
         a.stale = kStale;
         a.err = d_err;
-        a.events = d_events;
+        a.events = d_events + 1;   // [1]: events delivered by the walks
+        a.work_ctr = q.work_ctr;
         return a;
     }
 
@@ -403,10 +439,24 @@ struct nrn_engine {
         return NRN_OK;
     }
 
+    // Waits for the engine stream.  A partitioned engine polls it with the
+    // communicator's time limit: a peer that stopped turns into NRN_ERR_COMM
+    // (communicator aborted) instead of a hang.
+    nrn_status_t wait_stream() {
+        if (stuck) return fail(NRN_ERR_COMM, "the engine stream did not drain after the communicator was aborted");
+        if (world > 1 && comm != nullptr) {
+            const nrn_status_t st = comm_wait_stream(&comm, stream, comm_timeout_s, &stuck);
+            if (st != NRN_OK) comm_failed = true;
+            return st;
+        }
+        NRN_CUDA_TRY(cudaStreamSynchronize(stream));
+        return NRN_OK;
+    }
+
     nrn_status_t check_err() {
         int h = 0;
         NRN_CUDA_TRY(cudaMemcpyAsync(&h, d_err, sizeof(int), cudaMemcpyDeviceToHost, stream));
-        NRN_CUDA_TRY(cudaStreamSynchronize(stream));
+        NRN_TRY(wait_stream());
         if (h == 1) return fail(NRN_ERR_CAPACITY, "STDP: a neuron spiked more often than its spike history holds");
         if (h == 2) return fail(NRN_ERR_STATE, "STDP: a segment was not walked within the trace snapshot window");
         if (h == 3)
@@ -456,8 +506,13 @@ struct nrn_engine {
     // snapshots.
     nrn_status_t enqueue_window_end(int64_t off) {
         if (world > 1) {
-            ncclResult_t r = ncclAllGather(send, recv, static_cast<size_t>(rank_block), ncclInt32, comm, stream);
-            if (r != ncclSuccess) return fail(NRN_ERR_COMM, std::string("ncclAllGather: ") + ncclGetErrorString(r));
+            if (comm == nullptr) return fail(NRN_ERR_STATE, "partitioned engine: the communicator was aborted");
+            const ncclResult_t r =
+                ncclAllGather(send, recv, static_cast<size_t>(rank_block), ncclInt32, comm, stream);
+            if (r != ncclSuccess) {
+                comm_failed = true;
+                return comm_settle(&comm, r, comm_timeout_s, "ncclAllGather (window spike exchange)");
+            }
             for (size_t i = 0; i < pops.size(); ++i) {
                 const EnginePop& p = pops[i];
                 UnpackArgs u;
@@ -482,14 +537,19 @@ struct nrn_engine {
     }
 
     // Enqueues one step at offset `off` from *d_step; with `ev` non-null,
-    // records events around the three phases (ev[0..3]).
-    nrn_status_t enqueue_step(int64_t off, bool win_end, cudaEvent_t* ev = nullptr) {
+    // records events around the three phases (ev[0..3]).  With `kev`
+    // non-null every kernel runs on the main stream, one after the other,
+    // with events between them (kev[0..6]: start, drive, static delivery,
+    // STDP walks, neuron updates, per-step STDP, window end), for per-kernel
+    // timing.
+    nrn_status_t enqueue_step(int64_t off, bool win_end, cudaEvent_t* ev = nullptr, cudaEvent_t* kev = nullptr) {
         std::vector<nrn_proj_t> dp;
         for (auto& q : projs)
             if (!q.walk) dp.push_back(dev_proj(q));
         std::vector<nrn_spike_hist_t> hs;
         for (size_t i = 0; i < pops.size(); ++i) hs.push_back(hist(static_cast<int>(i)));
         if (ev) NRN_CUDA_TRY(cudaEventRecord(ev[0], stream));
+        if (kev) NRN_CUDA_TRY(cudaEventRecord(kev[0], stream));
         bool any_walk = false;
         for (auto& q : projs) any_walk = any_walk || q.walk;
         // Side stream, concurrent with the main stream's delivery work: this
@@ -497,8 +557,11 @@ struct nrn_engine {
         // neuron updates) and, with STDP walks on the main stream, the static
         // delivery (it also clears this step's history slots; the two touch
         // different history slots and only add into the accumulators).
-        NRN_CUDA_TRY(cudaEventRecord(fork_ev, stream));
-        NRN_CUDA_TRY(cudaStreamWaitEvent(side, fork_ev, 0));
+        cudaStream_t sd = kev ? stream : side;
+        if (!kev) {
+            NRN_CUDA_TRY(cudaEventRecord(fork_ev, stream));
+            NRN_CUDA_TRY(cudaStreamWaitEvent(side, fork_ev, 0));
+        }
         {
             std::vector<nrn_pop_step_t> da;
             std::vector<float*> dout;
@@ -507,36 +570,45 @@ struct nrn_engine {
                 da.push_back(pop_args(static_cast<int>(i), dt, off, true));
                 dout.push_back(pops[i].drive_buf);
             }
-            if (!da.empty()) NRN_TRY(drive_fill_group(da.data(), dout.data(), static_cast<int>(da.size()), side));
+            if (!da.empty()) NRN_TRY(drive_fill_group(da.data(), dout.data(), static_cast<int>(da.size()), sd));
         }
-        cudaStream_t ds = any_walk ? side : stream;
+        if (kev) NRN_CUDA_TRY(cudaEventRecord(kev[1], stream));
+        cudaStream_t ds = any_walk ? sd : stream;
         NRN_TRY(nrn_cuda_deliver_counted(dp.data(), static_cast<int32_t>(dp.size()), hs.data(),
                                          static_cast<int32_t>(hs.size()), off,
                                          reinterpret_cast<const int64_t*>(d_step), d_events,
                                          reinterpret_cast<nrn_stream_t>(ds)));
+        if (kev) NRN_CUDA_TRY(cudaEventRecord(kev[2], stream));
         for (auto& q : projs)
             if (q.walk) NRN_TRY(walk_launch(walk_args(q), WALK_STEP, off, d_step, stream));
-        NRN_CUDA_TRY(cudaEventRecord(join_ev, side));
-        NRN_CUDA_TRY(cudaStreamWaitEvent(stream, join_ev, 0));
+        if (kev) NRN_CUDA_TRY(cudaEventRecord(kev[3], stream));
+        if (!kev) {
+            NRN_CUDA_TRY(cudaEventRecord(join_ev, side));
+            NRN_CUDA_TRY(cudaStreamWaitEvent(stream, join_ev, 0));
+        }
         if (ev) NRN_CUDA_TRY(cudaEventRecord(ev[1], stream));
         std::vector<nrn_pop_step_t> pa;
         for (size_t i = 0; i < pops.size(); ++i) pa.push_back(pop_args(static_cast<int>(i), dt, off, true));
         NRN_TRY(pop_step_group(pa.data(), static_cast<int>(pa.size()), stream));
         if (ev) NRN_CUDA_TRY(cudaEventRecord(ev[2], stream));
+        if (kev) NRN_CUDA_TRY(cudaEventRecord(kev[4], stream));
         for (auto& q : projs) {
             if (!q.plastic || q.walk) continue;
             nrn_stdp_t s = stdp_args(q);
             NRN_TRY(nrn_cuda_stdp_step(&s, off, reinterpret_cast<const int64_t*>(d_step),
                                         reinterpret_cast<nrn_stream_t>(stream)));
         }
+        if (kev) NRN_CUDA_TRY(cudaEventRecord(kev[5], stream));
         if (win_end) NRN_TRY(enqueue_window_end(off));
         if (ev) NRN_CUDA_TRY(cudaEventRecord(ev[3], stream));
+        if (kev) NRN_CUDA_TRY(cudaEventRecord(kev[6], stream));
         return NRN_OK;
     }
 
     // A graph of `chunk` steps starting at a window start (when windows are on).
-    nrn_status_t graph_for(int chunk, cudaGraphExec_t* out) {
-        auto it = graphs.find(chunk);
+    nrn_status_t graph_for(int chunk, cudaGraphExec_t* out, int phase = 0) {
+        const auto key = std::make_pair(phase, chunk);
+        auto it = graphs.find(key);
         if (it != graphs.end()) {
             *out = it->second;
             return NRN_OK;
@@ -544,7 +616,7 @@ struct nrn_engine {
         cudaGraph_t g = nullptr;
         NRN_CUDA_TRY(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
         nrn_status_t st = NRN_OK;
-        for (int k = 0; k < chunk && st == NRN_OK; ++k) st = enqueue_step(k, window_end(k));
+        for (int k = 0; k < chunk && st == NRN_OK; ++k) st = enqueue_step(k, window_end(phase + k));
         if (st == NRN_OK) {
             advance_kernel<<<1, 1, 0, stream>>>(d_step, chunk);
             if (cudaGetLastError() != cudaSuccess) st = fail(NRN_ERR_CUDA, "advance_kernel launch failed");
@@ -559,7 +631,7 @@ struct nrn_engine {
         e = cudaGraphInstantiate(&ex, g, 0);
         cudaGraphDestroy(g);
         if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
-        graphs[chunk] = ex;
+        graphs[key] = ex;
         *out = ex;
         return NRN_OK;
     }
@@ -572,8 +644,18 @@ struct nrn_engine {
         return NRN_OK;
     }
 
+    // The walk launches' unit counters start at zero (the launch of step s
+    // uses counter s % 2 and clears the other for step s + 1; a run may start
+    // at any step).
+    nrn_status_t reset_walk_ctr() {
+        for (auto& q : projs)
+            if (q.work_ctr) NRN_CUDA_TRY(cudaMemsetAsync(q.work_ctr, 0, 3 * sizeof(unsigned int), stream));
+        return NRN_OK;
+    }
+
     // First run: weights clamped, walk state starting at the current step.
     nrn_status_t prepare_plastic() {
+        NRN_TRY(reset_walk_ctr());
         for (auto& q : projs) {
             if (!q.plastic || q.clamped) continue;
             // The reference clamps every weight of a plastic connection on
@@ -586,7 +668,7 @@ struct nrn_engine {
                                                 static_cast<int32_t>(step - 1));
                 NRN_CUDA_TRY(cudaMemcpyAsync(q.seg_last, last.data(), last.size() * sizeof(int32_t),
                                              cudaMemcpyHostToDevice, stream));
-                NRN_CUDA_TRY(cudaStreamSynchronize(stream));
+                NRN_TRY(wait_stream());
             }
             q.clamped = true;
         }
@@ -628,6 +710,11 @@ struct nrn_engine {
             add(p.ring, n * kRing * 4);
             add(p.cnt, n * 4);
             add(p.stats, n * sizeof(nrn_spike_stat_t));
+            for (int c = 0; c < p.n_chan; ++c) {
+                add(p.chan_in[c], n * 4);
+                add(p.chan_s[c], n * 4);
+                add(p.chan_r[c], n * 4);
+            }
         }
         for (auto& q : projs) {
             add(q.csr.w, static_cast<size_t>(q.csr.nnz) * 4);
@@ -639,9 +726,10 @@ struct nrn_engine {
                 add(q.seg_x, nseg * 4);
                 add(q.pre_snap, static_cast<size_t>(q.pre_depth) * q.csr.n_src * 4);
                 add(q.post_ring, static_cast<size_t>(ring_depth) * q.csr.n_tgt * 4);
+                add(q.walk_rec, static_cast<size_t>(q.csr.n_tgt) * 16);
             }
         }
-        add(d_events, sizeof(unsigned long long));
+        add(d_events, 2 * sizeof(unsigned long long));
         return b;
     }
 };
@@ -670,6 +758,7 @@ namespace nrn {
 
 nrn_status_t engine_raster_view(nrn_engine* e, EngineRasterView* v) {
     NRN_CHECK_ARG(e != nullptr && v != nullptr, "null engine");
+    if (!e->finalized) return fail(NRN_ERR_STATE, "raster read before nrn_engine_finalize");
     v->device = e->device;
     v->stream = e->stream;
     v->step = e->raster_step;
@@ -729,7 +818,7 @@ nrn_status_t nrn_engine_create(nrn_engine** out, int device, double dt, int32_t 
     NRN_CUDA_TRY(cudaEventCreateWithFlags(&e->fork_ev, cudaEventDisableTiming));
     NRN_CUDA_TRY(cudaEventCreateWithFlags(&e->join_ev, cudaEventDisableTiming));
     NRN_TRY(dalloc0(&e->d_step, 1, e->stream));
-    NRN_TRY(dalloc0(&e->d_events, 1, e->stream));
+    NRN_TRY(dalloc0(&e->d_events, 2, e->stream));   // [0] static delivery, [1] walks
     NRN_TRY(dalloc0(&e->d_raster_count, 1, e->stream));
     NRN_TRY(dalloc0(&e->d_err, 1, e->stream));
     *out = e.release();
@@ -739,7 +828,7 @@ nrn_status_t nrn_engine_create(nrn_engine** out, int device, double dt, int32_t 
 nrn_status_t nrn_engine_destroy(nrn_engine* e) {
     if (e == nullptr) return NRN_OK;
     cudaSetDevice(e->device);
-    cudaStreamSynchronize(e->stream);
+    e->wait_stream();
     delete e;
     return NRN_OK;
 }
@@ -766,14 +855,12 @@ nrn_status_t nrn_engine_set_partition(nrn_engine* e, int32_t rank, int32_t world
     e->world = world;
     if (world == 1) return NRN_OK;
     NRN_CHECK_ARG(id != nullptr, "nrn_engine_set_partition: null NCCL id");
-    ncclUniqueId u;
-    std::memcpy(&u, id, sizeof(u));
-    ncclResult_t r = ncclCommInitRank(&e->comm, world, u, rank);
-    if (r != ncclSuccess) {
+    const nrn_status_t st = comm_init(&e->comm, world, id, rank, e->comm_timeout_s);
+    if (st != NRN_OK) {
         e->comm = nullptr;
         e->world = 1;
         e->rank = 0;
-        return fail(NRN_ERR_COMM, std::string("ncclCommInitRank: ") + ncclGetErrorString(r));
+        return st;
     }
     return NRN_OK;
 }
@@ -838,6 +925,40 @@ nrn_status_t nrn_engine_set_params(nrn_engine* e, int32_t pop, const float* cons
     return NRN_OK;
 }
 
+static nrn_status_t check_receptor(nrn_engine* e, int32_t tgt, int32_t receptor) {
+    const EnginePop& t = e->pops[tgt];
+    if (receptor >= NRN_RECV_CHANNEL) {
+        NRN_CHECK_ARG(receptor - NRN_RECV_CHANNEL < t.n_chan, "receptor names a synapse channel the target lacks");
+        return NRN_OK;
+    }
+    NRN_CHECK_ARG(receptor >= NRN_RECV_CURRENT && receptor <= NRN_RECV_GINH, "bad receptor");
+    NRN_CHECK_ARG(receptor == NRN_RECV_CURRENT || t.cond,
+                  "conductance receptor on a population without conductance input");
+    return NRN_OK;
+}
+
+nrn_status_t nrn_engine_add_synapse_channel(nrn_engine* e, int32_t pop, const nrn_syn_desc_t* d, int32_t* channel) {
+    ENGINE_GUARD(e);
+    NRN_CHECK_ARG(d != nullptr, "null synapse channel");
+    NRN_CHECK_ARG(!e->finalized, "nrn_engine_add_synapse_channel: engine already finalized");
+    NRN_CHECK_ARG(pop >= 0 && pop < static_cast<int32_t>(e->pops.size()), "bad population index");
+    EnginePop& p = e->pops[pop];
+    NRN_CHECK_ARG(p.n_chan < NRN_MAX_CHANNELS, "at most 4 synapse channels per population");
+    NRN_CHECK_ARG(d->kind >= NRN_SYN_EXP && d->kind <= NRN_SYN_AMPA, "unknown synapse channel kind");
+    NRN_CHECK_ARG(d->tau_decay > 0.0 && (d->kind == NRN_SYN_EXP || d->tau_rise > 0.0) && std::isfinite(d->e_rev),
+                  "synapse time constants must be positive");
+    const int c = p.n_chan;
+    const size_t n = static_cast<size_t>(p.d.n);
+    NRN_TRY(dalloc0(&p.chan_in[c], n, e->stream));
+    NRN_TRY(dalloc0(&p.chan_s[c], n, e->stream));
+    if (d->kind != NRN_SYN_EXP) NRN_TRY(dalloc0(&p.chan_r[c], n, e->stream));
+    p.chan[c] = *d;
+    p.n_chan = c + 1;
+    e->drop_graphs();
+    if (channel) *channel = c;
+    return NRN_OK;
+}
+
 static nrn_status_t add_projection_dev(nrn_engine* e, int32_t src_pop, int32_t tgt_pop, int32_t receptor,
                                        const int32_t* src, const int32_t* tgt, const float* w, const uint8_t* delay,
                                        const float* mod, int64_t n, bool keep_orig, int32_t dmin, int32_t dmax,
@@ -863,9 +984,7 @@ nrn_status_t nrn_engine_add_projection(nrn_engine* e, const nrn_proj_desc_t* d, 
     NRN_CHECK_ARG(e->projs.size() < NRN_MAX_PROJ, "too many projections");
     const int np = static_cast<int>(e->pops.size());
     NRN_CHECK_ARG(d->src_pop >= 0 && d->src_pop < np && d->tgt_pop >= 0 && d->tgt_pop < np, "bad population index");
-    NRN_CHECK_ARG(d->receptor >= NRN_RECV_CURRENT && d->receptor <= NRN_RECV_GINH, "bad receptor");
-    NRN_CHECK_ARG(d->receptor == NRN_RECV_CURRENT || e->pops[d->tgt_pop].cond,
-                  "conductance receptor on a population without conductance input");
+    NRN_TRY(check_receptor(e, d->tgt_pop, d->receptor));
     NRN_CHECK_ARG(d->nnz >= 0, "negative synapse count");
     NRN_CHECK_ARG(d->nnz == 0 || (d->src && d->tgt && d->w && d->delay), "null synapse arrays");
     const int64_t n = d->nnz;
@@ -909,7 +1028,7 @@ nrn_status_t nrn_engine_add_projection(nrn_engine* e, const nrn_proj_desc_t* d, 
         return cuda_fail(ce, "projection upload");
     }
     st = add_projection_dev(e, d->src_pop, d->tgt_pop, d->receptor, s, t, w, dl, m, n, true, dmin, dmax, id);
-    cudaStreamSynchronize(e->stream);
+    e->wait_stream();
     cleanup();
     return st;
 }
@@ -922,8 +1041,7 @@ nrn_status_t nrn_engine_generate_projection(nrn_engine* e, const nrn_gen_desc_t*
     const int np = static_cast<int>(e->pops.size());
     NRN_CHECK_ARG(g->src_pop >= 0 && g->src_pop < np && g->tgt_pop >= 0 && g->tgt_pop < np, "bad population index");
     NRN_CHECK_ARG(g->degree >= 0 && g->dmin >= 1 && g->dmax >= g->dmin && g->dmax <= 255, "bad generator range");
-    NRN_CHECK_ARG(g->receptor == NRN_RECV_CURRENT || e->pops[g->tgt_pop].cond,
-                  "conductance receptor on a population without conductance input");
+    NRN_TRY(check_receptor(e, g->tgt_pop, g->receptor));
     const EnginePop& ps = e->pops[g->src_pop];
     const EnginePop& pt = e->pops[g->tgt_pop];
     // sources over the whole population, targets on this rank
@@ -960,7 +1078,7 @@ nrn_status_t nrn_engine_generate_projection(nrn_engine* e, const nrn_gen_desc_t*
     if (st == NRN_OK)
         st = add_projection_dev(e, g->src_pop, g->tgt_pop, g->receptor, s, t, w, dl, nullptr, total, false, g->dmin,
                                 g->dmax, id);
-    cudaStreamSynchronize(e->stream);
+    e->wait_stream();
     cleanup();
     if (st == NRN_OK && nnz) *nnz = e->projs.back().csr.nnz;
     return st;
@@ -978,6 +1096,74 @@ nrn_status_t nrn_engine_set_stdp(nrn_engine* e, int32_t proj, const double* p) {
     std::memcpy(q.stdp, p, sizeof(q.stdp));
     q.plastic = true;
     e->drop_graphs();
+    return NRN_OK;
+}
+
+// Every rank of a partitioned network must agree on the exchange layout:
+// the all-gather moves rank_block ids from each rank, and a rank whose count
+// differs leaves the others waiting.  At finalize the ranks exchange a
+// fixed-size record of what sets the layout (one all-gather of a fixed
+// count, which cannot disagree) and compare it.
+static nrn_status_t check_layout(nrn_engine* e) {
+    constexpr int kRec = 128;
+    std::vector<long long> rec(kRec, 0);
+    auto bits = [](double x) {
+        long long b = 0;
+        std::memcpy(&b, &x, sizeof(b));
+        return b;
+    };
+    rec[0] = 0x4E524E4C41594F55LL;   // record tag
+    rec[1] = e->world;
+    rec[2] = e->win;
+    rec[3] = e->depth;
+    rec[4] = e->rank_block;
+    rec[5] = static_cast<long long>(e->pops.size());
+    rec[6] = static_cast<long long>(e->projs.size());
+    rec[7] = bits(e->dt);
+    rec[8] = e->slow_ratio;
+    rec[9] = bits(e->max_rate_hz);
+    for (size_t i = 0; i < e->pops.size(); ++i) {
+        rec[16 + i] = e->pops[i].send_cap;
+        rec[16 + NRN_MAX_POPS + i] = e->pops[i].n_global;
+        rec[16 + 2 * NRN_MAX_POPS + i] = e->pops[i].send_off;
+    }
+    long long* d = nullptr;
+    NRN_TRY(dalloc0(&d, static_cast<size_t>(kRec) * (1 + e->world), e->stream));
+    std::vector<long long> all(static_cast<size_t>(kRec) * e->world);
+    nrn_status_t st = NRN_OK;
+    cudaError_t ce = cudaMemcpyAsync(d, rec.data(), kRec * sizeof(long long), cudaMemcpyHostToDevice, e->stream);
+    if (ce != cudaSuccess) st = cuda_fail(ce, "layout record upload");
+    if (st == NRN_OK) {
+        const ncclResult_t r = ncclAllGather(d, d + kRec, kRec, ncclInt64, e->comm, e->stream);
+        st = comm_settle(&e->comm, r, e->comm_timeout_s, "ncclAllGather (exchange layout check)");
+        if (st != NRN_OK) e->comm_failed = true;
+    }
+    if (st == NRN_OK) {
+        ce = cudaMemcpyAsync(all.data(), d + kRec, all.size() * sizeof(long long), cudaMemcpyDeviceToHost, e->stream);
+        st = ce != cudaSuccess ? cuda_fail(ce, "layout record download") : e->wait_stream();
+    }
+    if (!e->stuck) cudaFree(d);
+    NRN_TRY(st);
+    for (int r = 0; r < e->world; ++r) {
+        const long long* o = all.data() + static_cast<size_t>(r) * kRec;
+        for (int k = 0; k < kRec; ++k) {
+            if (o[k] == rec[k]) continue;
+            comm_destroy(&e->comm, e->comm_timeout_s);
+            e->comm_failed = true;
+            return fail(NRN_ERR_COMM, "partitioned network: rank " + std::to_string(r) + " and rank " +
+                                          std::to_string(e->rank) + " disagree on the spike exchange (layout field " +
+                                          std::to_string(k) +
+                                          "); every rank must build the same populations, projections, dt, "
+                                          "slow ratio and max_rate_hz");
+        }
+    }
+    return NRN_OK;
+}
+
+nrn_status_t nrn_engine_set_comm_timeout(nrn_engine* e, double seconds) {
+    ENGINE_GUARD(e);
+    NRN_CHECK_ARG(seconds > 0.0 && std::isfinite(seconds), "nrn_engine_set_comm_timeout: seconds must be positive");
+    e->comm_timeout_s = seconds;
     return NRN_OK;
 }
 
@@ -1034,6 +1220,7 @@ nrn_status_t nrn_engine_finalize(nrn_engine* e, int32_t init_update) {
         }
         NRN_TRY(dalloc0(&e->send, static_cast<size_t>(e->rank_block), e->stream));
         NRN_TRY(dalloc0(&e->recv, static_cast<size_t>(e->rank_block) * e->world, e->stream));
+        NRN_TRY(check_layout(e));
     }
     int64_t rec_n = 0;
     for (auto& p : e->pops)
@@ -1072,6 +1259,7 @@ nrn_status_t nrn_engine_finalize(nrn_engine* e, int32_t init_update) {
     for (auto& q : e->projs) {
         if (!q.walk) continue;
         const size_t nseg = static_cast<size_t>(q.csr.n_src) * q.csr.nd;
+        NRN_TRY(dalloc0(&q.work_ctr, 3, e->stream));
         NRN_TRY(dalloc0(&q.seg_last, nseg, e->stream));
         NRN_TRY(dalloc0(&q.seg_x, nseg, e->stream));
         const int dmax = q.csr.dmin + q.csr.nd - 1;
@@ -1080,6 +1268,21 @@ nrn_status_t nrn_engine_finalize(nrn_engine* e, int32_t init_update) {
         NRN_TRY(dalloc0(&q.post_ring, static_cast<size_t>(e->ring_depth) * q.csr.n_tgt, e->stream));
         NRN_TRY(need_history(e->pops[q.src_pop]));
         NRN_TRY(need_history(e->pops[q.tgt_pop]));
+    }
+    // Walk records for single-delay walk projections that are the only walk
+    // projection onto their target population (the neuron update keeps one
+    // record per neuron).
+    for (auto& q : e->projs) {
+        if (!q.walk || q.csr.nd != 1 || q.csr.dmin > e->ring_depth - 1) continue;
+        int onto = 0;
+        for (const auto& o : e->projs) onto += o.walk && o.tgt_pop == q.tgt_pop;
+        if (onto != 1 || !std::getenv("NRN_WALK_REC")) continue;   // opt-in: see the walk kernel notes
+        const size_t n = static_cast<size_t>(q.csr.n_tgt);
+        NRN_TRY(dalloc0(&q.walk_rec, n * 4, e->stream));
+        std::vector<int32_t> init(n * 4, -1);
+        for (size_t i = 0; i < n; ++i) init[4 * i + 3] = 0;   // trace 0.0f
+        NRN_CUDA_TRY(cudaMemcpyAsync(q.walk_rec, init.data(), n * 16, cudaMemcpyHostToDevice, e->stream));
+        NRN_TRY(e->wait_stream());
     }
     for (auto& p : e->pops)
         if (p.d.drive.kind != NRN_DRIVE_NONE) NRN_TRY(dalloc0(&p.drive_buf, static_cast<size_t>(p.d.n), e->stream));
@@ -1091,7 +1294,7 @@ nrn_status_t nrn_engine_finalize(nrn_engine* e, int32_t init_update) {
             NRN_TRY(nrn_cuda_pop_step(&a, reinterpret_cast<nrn_stream_t>(e->stream)));
         }
     }
-    NRN_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    NRN_TRY(e->wait_stream());
     e->finalized = true;
     return NRN_OK;
 }
@@ -1100,28 +1303,34 @@ nrn_status_t nrn_engine_run(nrn_engine* e, int64_t steps, int32_t chunk) {
     ENGINE_GUARD(e);
     NRN_CHECK_ARG(e->finalized, "nrn_engine_run: finalize first");
     NRN_CHECK_ARG(steps >= 0, "negative step count");
+    if (e->comm_failed) return fail(NRN_ERR_STATE, "nrn_engine_run: the communicator was aborted after an error");
     if (steps == 0) return NRN_OK;
     NRN_TRY(e->prepare_plastic());
     if (chunk <= 0) chunk = 50;
     int64_t s = e->step, left = steps;
-    auto graph_run = [&](int c) -> nrn_status_t {
-        cudaGraphExec_t g = nullptr;
-        NRN_TRY(e->graph_for(c, &g));
-        NRN_CUDA_TRY(cudaGraphLaunch(g, e->stream));
-        s += c;
-        left -= c;
-        return NRN_OK;
-    };
-    if (e->use_graphs && e->windows) {
-        // graphs hold whole windows and start at a window start
-        chunk = std::max(e->win, chunk / e->win * e->win);
-        for (; left > 0 && s % e->win != 0; ++s, --left) NRN_TRY(e->eager_step(s));
-        while (left >= e->win)
-            NRN_TRY(graph_run(static_cast<int>(std::min<int64_t>(chunk, left / e->win * e->win))));
-    } else if (e->use_graphs) {
-        while (left > 0) NRN_TRY(graph_run(static_cast<int>(std::min<int64_t>(chunk, left))));
+    if (!e->use_graphs) {
+        for (; left > 0; ++s, --left) NRN_TRY(e->eager_step(s));
+    } else {
+        // Every step runs inside a graph.  With windows, graphs are keyed by
+        // the window phase of their first step: a run that starts inside a
+        // window first completes it, then runs whole windows (chunks a
+        // multiple of the window), then the rest; the graphs of each shape
+        // are captured once and replayed.
+        const int w = e->windows ? e->win : 1;
+        if (e->windows) chunk = std::max(w, chunk / w * w);
+        while (left > 0) {
+            const int phase = static_cast<int>(s % w);
+            int c;
+            if (phase != 0) c = static_cast<int>(std::min<int64_t>(left, w - phase));
+            else if (left >= w) c = static_cast<int>(std::min<int64_t>(chunk, left / w * w));
+            else c = static_cast<int>(left);
+            cudaGraphExec_t g = nullptr;
+            NRN_TRY(e->graph_for(c, &g, phase));
+            NRN_CUDA_TRY(cudaGraphLaunch(g, e->stream));
+            s += c;
+            left -= c;
+        }
     }
-    for (; left > 0; ++s, --left) NRN_TRY(e->eager_step(s));
     e->step += steps;
     e->step_high = std::max(e->step_high, e->step);
     return NRN_OK;
@@ -1130,6 +1339,7 @@ nrn_status_t nrn_engine_run(nrn_engine* e, int64_t steps, int32_t chunk) {
 nrn_status_t nrn_engine_profile(nrn_engine* e, int64_t steps, double* ms) {
     ENGINE_GUARD(e);
     NRN_CHECK_ARG(e->finalized, "nrn_engine_profile: finalize first");
+    if (e->comm_failed) return fail(NRN_ERR_STATE, "nrn_engine_profile: the communicator was aborted after an error");
     NRN_CHECK_ARG(steps >= 0 && ms != nullptr, "bad arguments");
     ms[0] = ms[1] = ms[2] = 0.0;
     if (steps == 0) return NRN_OK;
@@ -1151,9 +1361,53 @@ nrn_status_t nrn_engine_profile(nrn_engine* e, int64_t steps, double* ms) {
     }
     for (auto& x : ev) cudaEventDestroy(x);
     if (st == NRN_OK) {
-        NRN_CUDA_TRY(cudaStreamSynchronize(e->stream));
+        NRN_TRY(e->wait_stream());
         e->step += steps;
         e->step_high = std::max(e->step_high, e->step);
+    }
+    return st;
+}
+
+nrn_status_t nrn_engine_profile_kernels(nrn_engine* e, int64_t steps, double* ms, int64_t* counts) {
+    ENGINE_GUARD(e);
+    NRN_CHECK_ARG(e->finalized, "nrn_engine_profile_kernels: finalize first");
+    NRN_CHECK_ARG(steps >= 0 && ms != nullptr && counts != nullptr, "bad arguments");
+    if (e->comm_failed) return fail(NRN_ERR_STATE, "nrn_engine_profile_kernels: the communicator was aborted");
+    for (int k = 0; k < 6; ++k) ms[k] = 0.0;
+    for (int k = 0; k < 4; ++k) counts[k] = 0;
+    if (steps == 0) return NRN_OK;
+    NRN_TRY(e->prepare_plastic());
+    unsigned long long c0[2] = {0, 0}, c1[2] = {0, 0};
+    NRN_CUDA_TRY(cudaMemcpyAsync(c0, e->d_events, sizeof(c0), cudaMemcpyDeviceToHost, e->stream));
+    NRN_TRY(e->wait_stream());
+    cudaEvent_t ev[7];
+    for (auto& x : ev) NRN_CUDA_TRY(cudaEventCreate(&x));
+    nrn_status_t st = NRN_OK;
+    int64_t wins = 0;
+    for (int64_t k = 0; k < steps && st == NRN_OK; ++k) {
+        const bool we = e->window_end(e->step + k);
+        wins += we ? 1 : 0;
+        st = e->enqueue_step(0, we, nullptr, ev);
+        if (st != NRN_OK) break;
+        advance_kernel<<<1, 1, 0, e->stream>>>(e->d_step, 1);
+        cudaError_t ce = cudaEventSynchronize(ev[6]);
+        if (ce != cudaSuccess) { st = cuda_fail(ce, "cudaEventSynchronize"); break; }
+        for (int p = 0; p < 6; ++p) {
+            float t = 0.0f;
+            cudaEventElapsedTime(&t, ev[p], ev[p + 1]);
+            ms[p] += t;
+        }
+    }
+    for (auto& x : ev) cudaEventDestroy(x);
+    if (st == NRN_OK) {
+        NRN_CUDA_TRY(cudaMemcpyAsync(c1, e->d_events, sizeof(c1), cudaMemcpyDeviceToHost, e->stream));
+        NRN_TRY(e->wait_stream());
+        e->step += steps;
+        e->step_high = std::max(e->step_high, e->step);
+        counts[0] = static_cast<int64_t>(c1[0] - c0[0]);
+        counts[1] = static_cast<int64_t>(c1[1] - c0[1]);
+        counts[2] = wins;
+        counts[3] = steps;
     }
     return st;
 }
@@ -1163,7 +1417,7 @@ nrn_status_t nrn_engine_set_step(nrn_engine* e, int64_t step) {
     NRN_CHECK_ARG(step >= 0, "step must be >= 0");
     const long long s = step;
     NRN_CUDA_TRY(cudaMemcpyAsync(e->d_step, &s, sizeof(s), cudaMemcpyHostToDevice, e->stream));
-    NRN_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    NRN_TRY(e->wait_stream());
     e->step = step;
     e->step_high = std::max(e->step_high, e->step);
     return NRN_OK;
@@ -1171,7 +1425,7 @@ nrn_status_t nrn_engine_set_step(nrn_engine* e, int64_t step) {
 
 nrn_status_t nrn_engine_sync(nrn_engine* e) {
     ENGINE_GUARD(e);
-    NRN_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    NRN_TRY(e->wait_stream());
     return e->check_err();
 }
 
@@ -1180,7 +1434,7 @@ nrn_status_t nrn_engine_raster(nrn_engine* e, int32_t* step, int32_t* gid, int64
     NRN_CHECK_ARG(n != nullptr, "null count");
     unsigned long long cnt = 0;
     NRN_CUDA_TRY(cudaMemcpyAsync(&cnt, e->d_raster_count, sizeof(cnt), cudaMemcpyDeviceToHost, e->stream));
-    NRN_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    NRN_TRY(e->wait_stream());
     *n = static_cast<int64_t>(cnt);
     if (cnt == 0) return NRN_OK;
     if (static_cast<int64_t>(cnt) > e->raster_cap)
@@ -1200,7 +1454,7 @@ nrn_status_t nrn_engine_raster(nrn_engine* e, int32_t* step, int32_t* gid, int64
     NRN_CUDA_TRY(cudaMemcpyAsync(step, e->raster_step, cnt * 4, cudaMemcpyDeviceToHost, e->stream));
     NRN_CUDA_TRY(cudaMemcpyAsync(gid, e->raster_gid, cnt * 4, cudaMemcpyDeviceToHost, e->stream));
     NRN_CUDA_TRY(cudaMemsetAsync(e->d_raster_count, 0, sizeof(unsigned long long), e->stream));
-    NRN_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    NRN_TRY(e->wait_stream());
     e->spikes_flushed += static_cast<int64_t>(cnt);
     return NRN_OK;
 }
@@ -1220,7 +1474,7 @@ nrn_status_t nrn_engine_weights(nrn_engine* e, int32_t proj, float* out, int64_t
     NRN_TRY(e->flush_walks());
     NRN_TRY(e->check_err());
     std::vector<float> w(static_cast<size_t>(c.nnz));
-    NRN_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    NRN_TRY(e->wait_stream());
     if (c.nnz) NRN_CUDA_TRY(cudaMemcpy(w.data(), c.w, c.nnz * 4, cudaMemcpyDeviceToHost));
     if (c.orig) {
         std::vector<int64_t> o(static_cast<size_t>(c.nnz));
@@ -1273,11 +1527,11 @@ nrn_status_t nrn_engine_set_state(nrn_engine* e, int32_t pop, float* v, float* a
 
 nrn_status_t nrn_engine_counters(nrn_engine* e, int64_t* spikes, int64_t* events) {
     ENGINE_GUARD(e);
-    unsigned long long ev = 0, rc = 0;
-    NRN_CUDA_TRY(cudaMemcpyAsync(&ev, e->d_events, sizeof(ev), cudaMemcpyDeviceToHost, e->stream));
+    unsigned long long ev2[2] = {0, 0}, rc = 0;
+    NRN_CUDA_TRY(cudaMemcpyAsync(ev2, e->d_events, sizeof(ev2), cudaMemcpyDeviceToHost, e->stream));
     NRN_CUDA_TRY(cudaMemcpyAsync(&rc, e->d_raster_count, sizeof(rc), cudaMemcpyDeviceToHost, e->stream));
-    NRN_CUDA_TRY(cudaStreamSynchronize(e->stream));
-    if (events) *events = static_cast<int64_t>(ev);
+    NRN_TRY(e->wait_stream());
+    if (events) *events = static_cast<int64_t>(ev2[0] + ev2[1]);
     if (spikes) *spikes = e->spikes_flushed + static_cast<int64_t>(rc);
     return NRN_OK;
 }
@@ -1301,7 +1555,7 @@ nrn_status_t ckpt_ready(nrn_engine* e, int64_t* raster_n) {
     NRN_TRY(e->check_err());
     unsigned long long rc = 0;
     NRN_CUDA_TRY(cudaMemcpyAsync(&rc, e->d_raster_count, sizeof(rc), cudaMemcpyDeviceToHost, e->stream));
-    NRN_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    NRN_TRY(e->wait_stream());
     if (static_cast<int64_t>(rc) > e->raster_cap)
         return fail(NRN_ERR_CAPACITY, "checkpoint: the spike raster overflowed; read it first");
     *raster_n = static_cast<int64_t>(rc);
@@ -1325,7 +1579,7 @@ nrn_status_t nrn_engine_spike_stats(nrn_engine* e, int32_t pop, nrn_spike_stat_t
     NRN_CHECK_ARG(n == p.d.n && out != nullptr, "spike_stats: output size must equal the population's local size");
     NRN_CUDA_TRY(cudaMemcpyAsync(out, p.stats, static_cast<size_t>(n) * sizeof(nrn_spike_stat_t),
                                  cudaMemcpyDeviceToHost, e->stream));
-    NRN_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    NRN_TRY(e->wait_stream());
     return NRN_OK;
 }
 
@@ -1334,7 +1588,7 @@ nrn_status_t nrn_engine_spike_stats_reset(nrn_engine* e) {
     if (!e->spike_stats || !e->finalized) return fail(NRN_ERR_STATE, "spike statistics are not enabled");
     for (const auto& p : e->pops)
         NRN_CUDA_TRY(cudaMemsetAsync(p.stats, 0, static_cast<size_t>(p.d.n) * sizeof(nrn_spike_stat_t), e->stream));
-    NRN_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    NRN_TRY(e->wait_stream());
     return NRN_OK;
 }
 
@@ -1384,7 +1638,7 @@ nrn_status_t nrn_engine_checkpoint_save(nrn_engine* e, void* buf, int64_t bytes)
         NRN_CUDA_TRY(cudaMemcpyAsync(out, e->raster_step, rn * 4, cudaMemcpyDeviceToHost, e->stream));
         NRN_CUDA_TRY(cudaMemcpyAsync(out + rn * 4, e->raster_gid, rn * 4, cudaMemcpyDeviceToHost, e->stream));
     }
-    NRN_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    NRN_TRY(e->wait_stream());
     return NRN_OK;
 }
 
@@ -1412,7 +1666,7 @@ nrn_status_t nrn_engine_checkpoint_load(nrn_engine* e, const void* buf, int64_t 
         in += 8;
         NRN_CHECK_ARG(sz == x.bytes, "checkpoint_load: the checkpoint is of another network (buffer sizes)");
     }
-    NRN_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    NRN_TRY(e->wait_stream());
     for (size_t q = 0; q < n_proj; ++q) e->projs[q].clamped = in[q] != 0;
     in += (n_proj + 7) / 8 * 8;
     for (const auto& x : b) {
@@ -1429,7 +1683,7 @@ nrn_status_t nrn_engine_checkpoint_load(nrn_engine* e, const void* buf, int64_t 
     const long long st = h.step;
     NRN_CUDA_TRY(cudaMemcpyAsync(e->d_step, &st, sizeof(st), cudaMemcpyHostToDevice, e->stream));
     NRN_CUDA_TRY(cudaMemsetAsync(e->d_err, 0, sizeof(int), e->stream));
-    NRN_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    NRN_TRY(e->wait_stream());
     e->step = h.step;
     e->step_high = std::max(e->step_high, e->step);
     e->spikes_flushed = h.spikes_flushed;

@@ -1,6 +1,7 @@
 // internal.h -- device-side building blocks shared by the engine.
 #pragma once
 #include <cuda_runtime.h>
+#include <nccl.h>
 
 #include <cstdint>
 
@@ -83,6 +84,9 @@ struct WalkArgs {
     int32_t src_lo = 0, src_hi = 0;
     // spike steps of the targets (local index)
     const int4* tgt_recent = nullptr;
+    // per-target walk record (newest three spike steps and the target trace
+    // at the arriving spikes' step, written by the neuron update), or null
+    const int4* tgt_rec = nullptr;
     const int32_t* tgt_ring = nullptr;
     const int32_t* tgt_cnt = nullptr;
     int32_t ring_k = 64;
@@ -102,6 +106,8 @@ struct WalkArgs {
     int32_t stale = 1;                // the sweep walks a segment not walked for this many steps
     int* err = nullptr;
     unsigned long long* events = nullptr;
+    // [3] unit counters of the launches (zero before a run's first launch)
+    unsigned int* work_ctr = nullptr;
 };
 nrn_status_t walk_launch(const WalkArgs& a, int mode, long long step_off, const long long* step_base,
                          cudaStream_t s);
@@ -144,6 +150,18 @@ struct UnpackArgs {
     int* err = nullptr;
 };
 nrn_status_t unpack_launch(const UnpackArgs& a, long long step_off, const long long* step_base, cudaStream_t s);
+
+// The engine's NCCL communicator (comm.cu): non-blocking, every host wait
+// bounded by timeout_s; on an error or a timeout the communicator is
+// aborted (*c becomes null) and NRN_ERR_COMM returned.
+nrn_status_t comm_init(ncclComm_t* out, int world, const uint8_t id[128], int rank, double timeout_s);
+// After an NCCL call that returned r.
+nrn_status_t comm_settle(ncclComm_t* c, ncclResult_t r, double timeout_s, const char* what);
+// Waits for stream s of a partitioned engine; *stuck is set when the stream
+// did not drain even after the abort.
+nrn_status_t comm_wait_stream(ncclComm_t* c, cudaStream_t s, double timeout_s, bool* stuck);
+nrn_status_t comm_abort(ncclComm_t* c);
+nrn_status_t comm_destroy(ncclComm_t* c, double timeout_s);
 
 // The engine's spike raster buffers (for entry points outside engine.cu).
 struct EngineRasterView {

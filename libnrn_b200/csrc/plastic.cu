@@ -292,7 +292,7 @@ __device__ __forceinline__ void build_table(const WalkArgs& a, const Seg& g, flo
 }
 
 constexpr int kConsumers = kThreads - 32;   // threads that walk synapses (warps 1..)
-constexpr int kGroup = 8;                    // segments a sweep or flush unit looks at
+constexpr int kGroup = 4;                    // segments a sweep or flush unit looks at
 
 __device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
 
@@ -305,6 +305,12 @@ __device__ __forceinline__ unsigned walk_block(const WalkArgs& a, const Seg& g, 
     const bool has_pre = g.P.n > 0;
     const int t0 = has_pre ? g.P[0] : 0;
     const float* ring0 = a.post_ring + static_cast<long long>(t0 & (a.post_depth - 1)) * a.n_tgt;
+    // With the walk record, one 16-byte load per synapse gives the target's
+    // newest three spike steps and its trace at step now - dmin (the step of
+    // every spike arriving now through a single-delay projection); the full
+    // spike-step record is read only when the third newest spike is after T.
+    const bool rec = a.tgt_rec != nullptr;
+    const bool rec_x = rec && (!has_pre || t0 == now - a.dmin);
     // the next round's target and weight (the HBM stream) are loaded a round
     // ahead; the target's spike steps and trace (L2) within the round
     unsigned n = 0;
@@ -320,8 +326,16 @@ __device__ __forceinline__ unsigned walk_block(const WalkArgs& a, const Seg& g, 
         const uint32_t syn = g.s0 + o;
         const uint32_t t = t_next;
         const float w = w_next;
-        const int4 r = a.tgt_recent[t];
-        const float xp0 = has_pre ? ring0[t] : 0.0f;
+        int4 r;
+        float xp0;
+        if (rec) {
+            const int4 rc = a.tgt_rec[t];
+            xp0 = rec_x ? __int_as_float(rc.w) : (has_pre ? ring0[t] : 0.0f);
+            r = rc.z <= g.T ? make_int4(rc.x, rc.y, rc.z, rc.z) : a.tgt_recent[t];
+        } else {
+            r = a.tgt_recent[t];
+            xp0 = has_pre ? ring0[t] : 0.0f;
+        }
         const float md = MOD ? __ldcs(a.mod + syn) : 1.0f;
         if (o + kConsumers < len) {
             t_next = __ldcs(a.tgt + syn + kConsumers);
@@ -368,7 +382,8 @@ struct Item {
 
 // What the producer warp needs to step through the block's units.
 struct Producer {
-    long long u;          // next unit of this block
+    unsigned int* ctr;    // the launch's unit counter (units are taken dynamically)
+    long long u;          // unused (kept for the layout of the shared state)
     long long n_units, n_arr;
     long long base, g_end;   // group units cover segments [base, g_end), kGroup each
     unsigned pending;     // segments g0 + bit of the current group still to look at
@@ -466,12 +481,19 @@ __device__ void produce(const WalkArgs& a, Producer& shared_pr, Item& it, int* s
                           now, m_new, lane);
         }
         if (got) break;
-        if (pr.u >= pr.n_units) {
+        // The next unit of the launch, taken from its counter: blocks that
+        // finish early take more, so uneven units (sweep groups walk 0 to
+        // kGroup segments) do not leave a tail.  Sweep and flush groups come
+        // first, arrivals (all about the same size) after them.
+        unsigned int k = 0;
+        if (lane == 0) k = atomicAdd(pr.ctr, 1u);
+        k = __shfl_sync(0xffffffffu, k, 0);
+        if (static_cast<long long>(k) >= pr.n_units) {
             if (lane == 0) it.kind = ITEM_DONE;
             break;
         }
-        const long long u = pr.u;
-        pr.u += gridDim.x;
+        const long long n_grp = pr.n_units - pr.n_arr;
+        const long long u = static_cast<long long>(k) < n_grp ? pr.n_arr + k : static_cast<long long>(k) - n_grp;
         if (u < pr.n_arr) {
             int lo = 0, hi = a.nd - 1;
             while (lo < hi) {
@@ -562,7 +584,12 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) walk_kernel(const __grid
         sweep = true;
     }
     if (tid == 0) {
-        pr.u = blockIdx.x;
+        // unit counters: [0], [1] by step parity (each step's launch clears
+        // the other's for the next step), [2] for flushes (cleared by the host)
+        const int slot = mode == WALK_FLUSH ? 2 : static_cast<int>(step & 1);
+        pr.ctr = a.work_ctr + slot;
+        if (blockIdx.x == 0 && mode != WALK_FLUSH) a.work_ctr[(step + 1) & 1] = 0u;
+        pr.u = 0;
         pr.pending = 0;
         pr.g0 = 0;
     }
@@ -625,6 +652,8 @@ nrn_status_t walk_launch(const WalkArgs& a, int mode, long long step_off, const 
                          cudaStream_t s) {
     NRN_CHECK_ARG(a.nd >= 1 && a.nd <= 256, "plastic projection: at most 256 delay values");
     NRN_CHECK_ARG(a.win >= 1 && a.sweep_period >= 1, "plastic projection: bad window or sweep period");
+    NRN_CHECK_ARG(a.work_ctr != nullptr, "plastic projection: no unit counters");
+    if (mode == WALK_FLUSH) NRN_CUDA_TRY(cudaMemsetAsync(a.work_ctr + 2, 0, sizeof(unsigned int), s));
     NRN_CHECK_ARG(a.pre_depth > 0 && (a.pre_depth & (a.pre_depth - 1)) == 0 && a.post_depth > 0 &&
                       (a.post_depth & (a.post_depth - 1)) == 0,
                   "plastic projection: trace ring depths must be powers of two");

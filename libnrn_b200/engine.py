@@ -29,7 +29,8 @@ class Network:
     (libnrn_b200.partition); populations are then added with their whole
     size ``n_global`` and this rank's slice."""
 
-    def __init__(self, dt: float, slow_ratio: int = 1, device: int = 0, partition=None):
+    def __init__(self, dt: float, slow_ratio: int = 1, device: int = 0, partition=None,
+                 comm_timeout: float | None = None):
         self.L = N.lib()
         self.device = device
         self.dt = float(dt)
@@ -38,6 +39,8 @@ class Network:
         N.check(self.L.nrn_engine_create(C.byref(h), device, self.dt, int(slow_ratio)), "nrn_engine_create")
         self.h = h
         self.rank, self.world = 0, 1
+        if comm_timeout is not None:
+            N.check(self.L.nrn_engine_set_comm_timeout(self.h, float(comm_timeout)), "nrn_engine_set_comm_timeout")
         if partition is not None:
             rank, world, uid, max_rate = partition
             buf = (C.c_uint8 * 128)(*bytes(uid))
@@ -104,6 +107,17 @@ class Network:
                           "spike": spike, "i_syn": i_syn, "hp": hpt, "record": record})
         return pid.value
 
+    def add_synapse_channel(self, pop: int, kind: str, tau_rise: float, tau_decay: float, e_rev: float = 0.0) -> int:
+        """Synapse channel of population pop ("exp", "dexp" or "ampa",
+        nrn_syn_desc_t); projections deliver into it with receptor
+        "chan<k>"."""
+        d = N.SynDesc()
+        d.kind = N.SYN_KIND[kind]
+        d.tau_rise, d.tau_decay, d.e_rev = float(tau_rise), float(tau_decay), float(e_rev)
+        c = C.c_int32()
+        N.check(self.L.nrn_engine_add_synapse_channel(self.h, int(pop), C.byref(d), C.byref(c)), "add_synapse_channel")
+        return c.value
+
     def add_projection(self, src: int, tgt: int, src_idx, tgt_idx, w, delay, *, receptor="current",
                        mod=None) -> int:
         arrs = [np.ascontiguousarray(src_idx, np.int32), np.ascontiguousarray(tgt_idx, np.int32),
@@ -152,6 +166,18 @@ class Network:
         ms = (C.c_double * 3)()
         N.check(self.L.nrn_engine_profile(self.h, int(steps), ms), "profile")
         return tuple(ms)
+
+    KERNEL_PHASES = ("drive", "static_delivery", "stdp_walks", "neuron_update", "stdp_step", "window_end")
+
+    def profile_kernels(self, steps: int):
+        """Runs steps with the kernels serialised on the engine stream; returns
+        ({phase: summed device ms}, {"static_events", "walk_events",
+        "windows", "steps"}) (nrn_engine_profile_kernels)."""
+        ms = (C.c_double * 6)()
+        cnt = (C.c_int64 * 4)()
+        N.check(self.L.nrn_engine_profile_kernels(self.h, int(steps), ms, cnt), "profile_kernels")
+        return (dict(zip(self.KERNEL_PHASES, list(ms))),
+                dict(zip(("static_events", "walk_events", "windows", "steps"), list(cnt))))
 
     def sync(self) -> None:
         N.check(self.L.nrn_engine_sync(self.h), "sync")
@@ -260,9 +286,11 @@ class Network:
         oracle's form)."""
         nw = cls(net["dt"], net.get("slow_ratio", 1), device)
         for p in net["pops"]:
-            nw.add_population(p["model"], p["n"], p["params"], hp=p.get("hp"), drive=p.get("drive"),
-                              cond=p.get("cond"), init_v=p.get("init_v"), init_aux=p.get("init_aux"),
-                              record=record, seed=net.get("seed", 0))
+            pid = nw.add_population(p["model"], p["n"], p["params"], hp=p.get("hp"), drive=p.get("drive"),
+                                    cond=p.get("cond"), init_v=p.get("init_v"), init_aux=p.get("init_aux"),
+                                    record=record, seed=net.get("seed", 0))
+            for ch in p.get("syn") or []:
+                nw.add_synapse_channel(pid, ch[0], ch[1], ch[2], ch[3])
         for q in net.get("projs", []):
             qid = nw.add_projection(q["src"], q["tgt"], q["src_idx"], q["tgt_idx"], q["w"], q["delay"],
                                     receptor=q.get("receptor", "current"), mod=q.get("mod"))
@@ -275,13 +303,13 @@ class Network:
 
     @classmethod
     def from_spec(cls, spec: dict, device: int = 0, record: bool = True, partition=None,
-                  spike_stats: bool = False) -> "Network":
+                  spike_stats: bool = False, comm_timeout: float | None = None) -> "Network":
         """From a workload spec (libnrn_b200.workloads), connectivity
         generated on the device; with ``partition``, this rank's slice."""
         from . import workloads as W
         from .partition import partition_range
 
-        nw = cls(spec["dt"], spec.get("slow_ratio", 1), device, partition=partition)
+        nw = cls(spec["dt"], spec.get("slow_ratio", 1), device, partition=partition, comm_timeout=comm_timeout)
         for p in spec["pops"]:
             arr = W.population_arrays(spec, p)
             lo, n = partition_range(p["n"], nw.rank, nw.world)

@@ -52,3 +52,38 @@ def share_unique_id(make=comm_unique_id) -> bytes:
     if not isinstance(uid, (bytes, bytearray)) or len(uid) != 128:
         raise RuntimeError("NCCL unique id: expected 128 bytes")
     return bytes(uid)
+
+
+class StepAgreement:
+    """Host-side check, before each run of a partitioned network, that every
+    rank is still there and runs the same steps: each rank posts (run index,
+    first step, step count) to the torch.distributed store and waits, with a
+    time limit, for the others' posts.  A rank that stopped between runs is
+    then found on the host before any GPU work of the next run is launched
+    (the engine's own bounded waits cover a rank that stops inside a run).
+    Raises RuntimeError naming the missing or disagreeing rank."""
+
+    def __init__(self, store, rank: int, world: int, timeout_s: float = 60.0, prefix: str = "nrn/run"):
+        self.store, self.rank, self.world = store, int(rank), int(world)
+        self.timeout_s = float(timeout_s)
+        self.prefix = prefix
+        self.k = 0
+
+    def check(self, first_step: int, steps: int) -> None:
+        import datetime
+
+        key = f"{self.prefix}/{self.k}"
+        mine = f"{int(first_step)}:{int(steps)}"
+        self.store.set(f"{key}/{self.rank}", mine)
+        others = [f"{key}/{r}" for r in range(self.world) if r != self.rank]
+        try:
+            self.store.wait(others, datetime.timedelta(seconds=self.timeout_s))
+        except Exception as ex:
+            missing = [r for r in range(self.world) if r != self.rank and not self.store.check([f"{key}/{r}"])]
+            raise RuntimeError(f"partitioned run {self.k}: rank(s) {missing} did not reach it within "
+                               f"{self.timeout_s:g} s") from ex
+        for r in range(self.world):
+            got = self.store.get(f"{key}/{r}").decode()
+            if got != mine:
+                raise RuntimeError(f"partitioned run {self.k}: rank {r} runs steps {got}, rank {self.rank} {mine}")
+        self.k += 1

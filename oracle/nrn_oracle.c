@@ -54,6 +54,8 @@ typedef struct {
     float* ge;      /* conductances (AdEx with conductance input) */
     float* gi;
     int cond;       /* population receives conductance input */
+    float* cs[ORC_MAX_CHAN];   /* synapse channel decay state */
+    float* cr[ORC_MAX_CHAN];   /* synapse channel rise state  */
 } pop_state;
 
 static void init_pop(const orc_pop* P, pop_state* S) {
@@ -63,6 +65,10 @@ static void init_pop(const orc_pop* P, pop_state* S) {
     S->ref = (float*)calloc((size_t)n, sizeof(float));
     S->ge = (float*)calloc((size_t)n, sizeof(float));
     S->gi = (float*)calloc((size_t)n, sizeof(float));
+    for (int c = 0; c < ORC_MAX_CHAN; ++c) {
+        S->cs[c] = (float*)calloc((size_t)n, sizeof(float));
+        S->cr[c] = (float*)calloc((size_t)n, sizeof(float));
+    }
     for (int i = 0; i < n; ++i) {
         float v0, a0 = 0.0f;
         if (P->model == ORC_IZH) {
@@ -80,6 +86,20 @@ static void init_pop(const orc_pop* P, pop_state* S) {
 
 static void free_pop(pop_state* S) {
     free(S->v); free(S->aux); free(S->ref); free(S->ge); free(S->gi);
+    for (int c = 0; c < ORC_MAX_CHAN; ++c) { free(S->cs[c]); free(S->cr[c]); }
+}
+
+/* This step's synapse channel currents added to the input of every neuron
+ * (before the model update); cin[c] is channel c's input, or NULL. */
+static void apply_channels(const orc_pop* P, pop_state* S, float* I, float* const* cin, double dt) {
+    for (int c = 0; c < P->n_chan && c < ORC_MAX_CHAN; ++c) {
+        float dr = (float)exp(-dt / P->chan_tau[c][0]);
+        float dd = (float)exp(-dt / P->chan_tau[c][1]);
+        float e = (float)P->chan_e[c];
+        for (int i = 0; i < P->n; ++i)
+            I[i] = orc_chan_current(P->chan_kind[c], I[i], &S->cs[c][i], &S->cr[c][i],
+                                    cin && cin[c] ? cin[c][i] : 0.0f, dr, dd, e, S->v[i]);
+    }
 }
 
 /* One update of population P with per-neuron inputs I[], conductance
@@ -173,7 +193,7 @@ ORC_EXPORT int orc_net_run(const orc_net* net) {
     pop_state* S = (pop_state*)calloc((size_t)np, sizeof(pop_state));
     for (int p = 0; p < np; ++p) init_pop(&net->pops[p], &S[p]);
     for (int q = 0; q < nq; ++q) {
-        if (net->projs[q].receptor != ORC_RECV_CURRENT)
+        if (net->projs[q].receptor == ORC_RECV_GEXC || net->projs[q].receptor == ORC_RECV_GINH)
             S[net->projs[q].tgt_pop].cond = 1;
     }
     for (int p = 0; p < np; ++p)
@@ -182,6 +202,9 @@ ORC_EXPORT int orc_net_run(const orc_net* net) {
     float* I = (float*)calloc((size_t)N, sizeof(float));
     float* ie = (float*)calloc((size_t)N, sizeof(float));
     float* ii = (float*)calloc((size_t)N, sizeof(float));
+    /* synapse channel inputs, global-id indexed per channel slot */
+    float* cin_all[ORC_MAX_CHAN];
+    for (int c = 0; c < ORC_MAX_CHAN; ++c) cin_all[c] = (float*)calloc((size_t)N, sizeof(float));
     uint8_t* hist = (uint8_t*)calloc((size_t)H * N, 1);
 
     /* Working copies of the weights and STDP traces. */
@@ -213,11 +236,13 @@ ORC_EXPORT int orc_net_run(const orc_net* net) {
         memset(I, 0, (size_t)N * sizeof(float));
         memset(ie, 0, (size_t)N * sizeof(float));
         memset(ii, 0, (size_t)N * sizeof(float));
+        for (int c = 0; c < ORC_MAX_CHAN; ++c) memset(cin_all[c], 0, (size_t)N * sizeof(float));
         /* P2: arrival-time delivery with the weights as they are now. */
         for (int q = 0; q < nq; ++q) {
             const orc_proj* Q = &net->projs[q];
             int so = net->pops[Q->src_pop].offset, to = net->pops[Q->tgt_pop].offset;
-            float* acc = Q->receptor == ORC_RECV_CURRENT ? I
+            float* acc = Q->receptor >= ORC_RECV_CHANNEL ? cin_all[(Q->receptor - ORC_RECV_CHANNEL) % ORC_MAX_CHAN]
+                       : Q->receptor == ORC_RECV_CURRENT ? I
                        : Q->receptor == ORC_RECV_GEXC ? ie : ii;
             for (int64_t k = 0; k < Q->nnz; ++k) {
                 int d = Q->delay[k];
@@ -243,6 +268,9 @@ ORC_EXPORT int orc_net_run(const orc_net* net) {
         uint8_t* h = hist + (size_t)(t % H) * N;
         for (int p = 0; p < np; ++p) {
             const orc_pop* P = &net->pops[p];
+            float* cin[ORC_MAX_CHAN];
+            for (int c = 0; c < ORC_MAX_CHAN; ++c) cin[c] = cin_all[c] + P->offset;
+            apply_channels(P, &S[p], I + P->offset, cin, net->dt);
             update_pop(P, &S[p], I + P->offset, ie + P->offset, ii + P->offset,
                        net->dt, h + P->offset);
         }
@@ -310,6 +338,7 @@ ORC_EXPORT int orc_net_run(const orc_net* net) {
     free(W); free(xpre); free(xpost);
     for (int p = 0; p < np; ++p) free_pop(&S[p]);
     free(S); free(I); free(ie); free(ii); free(hist);
+    for (int c = 0; c < ORC_MAX_CHAN; ++c) free(cin_all[c]);
     return nspk > net->spike_cap ? 1 : 0;
 }
 

@@ -17,6 +17,8 @@ A network is a dict::
     {"pops":  [pop, ...], "projs": [proj, ...], "steps": T, "dt": 1e-4,
      "slow_ratio": 1, "seed": 7, "trace_ids": [...]}
     pop  = {"model": "lif"|"adex"|"izh", "n": n, "params": [...],
+            "syn": None | [(kind "exp"|"dexp"|"ampa", tau_rise, tau_decay, e_rev), ...]
+                   (synapse channels; receptor "chanK" delivers into channel K),
             "drive": None | ("poisson", lam, amp) | ("gauss", mean, std)
                         | ("poisson_gexc", lam, amp),
             "cond": None | [tau_e, tau_i, e_exc, e_inh],
@@ -44,7 +46,8 @@ HARNESS_SO = os.path.join(REF_DIR, "libnrn_ref_harness.so")
 MODELS = {"lif": 0, "adex": 1, "izh": 2}
 NPARAM = {"lif": 7, "adex": 13, "izh": 5}
 DRIVES = {None: 0, "poisson": 1, "gauss": 2, "poisson_gexc": 3}
-RECEPTORS = {"current": 0, "gexc": 1, "ginh": 2}
+RECEPTORS = {"current": 0, "gexc": 1, "ginh": 2, "chan0": 16, "chan1": 17, "chan2": 18, "chan3": 19}
+SYN_KINDS = {"exp": 1, "dexp": 2, "ampa": 3}
 
 # Default parameters of the reference's option structs
 # (include/nrn/neuron/options.h:23-92).
@@ -58,7 +61,8 @@ class OrcPop(C.Structure):
     _fields_ = [("model", C.c_int32), ("n", C.c_int32), ("offset", C.c_int32),
                 ("drive_kind", C.c_int32), ("p", C.c_double * 16), ("cond", C.c_double * 4),
                 ("drive", C.c_double * 4), ("init_v", C.c_void_p), ("init_aux", C.c_void_p),
-                ("hp", C.c_void_p)]
+                ("hp", C.c_void_p), ("n_chan", C.c_int32), ("chan_kind", C.c_int32 * 4),
+                ("chan_tau", (C.c_double * 2) * 4), ("chan_e", C.c_double * 4)]
 
 
 class OrcProj(C.Structure):
@@ -82,10 +86,34 @@ def _ptr(a):
     return None if a is None else a.ctypes.data
 
 
-def build(reference: bool = False) -> None:
-    """Builds the C restatement (and, with reference=True, the reference)."""
-    targets = ["cport"] + (["ref"] if reference else [])
-    subprocess.run(["make", "-s", "-C", HERE, f"PY={sys.executable}"] + targets,
+# Where the reference's sources are read from when the reference is built:
+# $NRN_REFERENCE_DIR, else the build container's copy.  The GPU box has no
+# reference tree; it uses the libraries built here (oracle/_ref).
+DEFAULT_REFERENCE_DIR = "/root/reference"
+
+
+def reference_dir() -> str | None:
+    """The reference source tree, or None (reported) when it is absent."""
+    d = os.environ.get("NRN_REFERENCE_DIR", DEFAULT_REFERENCE_DIR)
+    if os.path.isdir(os.path.join(d, "src")) and os.path.isdir(os.path.join(d, "include")):
+        return d
+    print(f"oracle: no reference sources at {d} (set NRN_REFERENCE_DIR); "
+          "building the C restatement only", file=sys.stderr)
+    return None
+
+
+def build(reference: bool | None = None) -> None:
+    """Builds the C restatement and, when the reference sources are present
+    (reference=None: look for them; True: required), the reference itself
+    from its unmodified sources into oracle/_ref (a parallel make: its CUDA
+    files take minutes each through the LibTorch headers)."""
+    ref = reference_dir() if reference is not False else None
+    if reference is True and ref is None:
+        raise FileNotFoundError("reference sources not found (NRN_REFERENCE_DIR)")
+    targets = ["cport"] + (["ref"] if ref else [])
+    jobs = str(max(2, min(16, os.cpu_count() or 2)))
+    extra = [f"REF={ref}"] if ref else []
+    subprocess.run(["make", "-s", "-j", jobs, "-C", HERE, f"PY={sys.executable}"] + extra + targets,
                    check=True, stdout=subprocess.DEVNULL)
 
 
@@ -145,6 +173,12 @@ def _fill_pop(pop: dict, offset: int, keep: list) -> OrcPop:
     if drive:
         for i, x in enumerate(drive[1:]):
             P.drive[i] = float(x)
+    # synapse channels: [(kind, tau_rise, tau_decay, e_rev), ...]
+    for c, ch in enumerate(pop.get("syn") or []):
+        P.chan_kind[c] = SYN_KINDS[ch[0]]
+        P.chan_tau[c][0], P.chan_tau[c][1] = float(ch[1]), float(ch[2])
+        P.chan_e[c] = float(ch[3])
+        P.n_chan = c + 1
     for name in ("init_v", "init_aux", "hp"):
         a = pop.get(name)
         if a is not None:

@@ -50,8 +50,23 @@ enum {
     ORC_DRIVE_POISSON_GEXC = 3       /* g_exc input += amp * Poisson(lambda)  */
 };
 
-/* Receptor a projection delivers into. */
-enum { ORC_RECV_CURRENT = 0, ORC_RECV_GEXC = 1, ORC_RECV_GINH = 2 };
+/* Receptor a projection delivers into; ORC_RECV_CHANNEL + c: synapse
+ * channel c of the target population (below). */
+enum { ORC_RECV_CURRENT = 0, ORC_RECV_GEXC = 1, ORC_RECV_GINH = 2, ORC_RECV_CHANNEL = 16 };
+
+/* Synapse channels: per-target synapse state of the reference's declared
+ * synapse models (include/nrn/synapse/exponential.h:16-21,
+ * double_exponential.h:17-25, ampa.h:17-29; their forward is a stub in the
+ * reference, so these equations are restated from the declarations alone:
+ * parity unpinned).  Each step, before the neuron integrates, with `in` the
+ * weights delivered into the channel this step:
+ *   EXP : s = s*dec_decay + in;               I += s
+ *   DEXP: s = s*dec_decay + in; r = r*dec_rise + in;  I += s - r
+ *   AMPA: the same s, r; g = s - r;           I += g*(e_rev - v)
+ * (dec = (float)exp(-dt/tau)); AMPA's inward current g*(e_rev - v) is the
+ * declared I_syn = g*(V - E_rev) with the sign of current into the cell. */
+enum { ORC_SYN_EXP = 1, ORC_SYN_DEXP = 2, ORC_SYN_AMPA = 3 };
+#define ORC_MAX_CHAN 4
 
 /* Number of model parameters, in this order:
  *  LIF : v_rest v_thresh v_reset tau_m tau_ref c_m i_bg                    (7)
@@ -75,6 +90,10 @@ typedef struct {
     const float* init_v;       /* [n] or NULL (model default)                */
     const float* init_aux;     /* [n] w (AdEx) / u (Izh) or NULL             */
     const float* hp;           /* [np][n] per-neuron parameters or NULL      */
+    int32_t n_chan;            /* synapse channels (0..ORC_MAX_CHAN)         */
+    int32_t chan_kind[ORC_MAX_CHAN];
+    double chan_tau[ORC_MAX_CHAN][2];   /* tau_rise, tau_decay (s)           */
+    double chan_e[ORC_MAX_CHAN];        /* AMPA reversal potential            */
 } orc_pop;
 
 typedef struct {
@@ -324,6 +343,20 @@ static inline float orc_cond_current(float I, float* ge, float* gi, float in_e,
     float r = I + g_e * (e_exc - v);
     r = r + g_i * (e_inh - v);
     return r;
+}
+
+/* One synapse channel of one neuron (see ORC_SYN_*): returns I plus the
+ * channel's current; s (decay state) and r (rise state) updated. */
+static inline float orc_chan_current(int kind, float I, float* s, float* r, float in, float dec_rise,
+                                     float dec_decay, float e_rev, float v) {
+    float sd = (*s * dec_decay) + in;
+    *s = sd;
+    if (kind == ORC_SYN_EXP) return I + sd;
+    float sr = (*r * dec_rise) + in;
+    *r = sr;
+    float g = sd - sr;
+    if (kind == ORC_SYN_DEXP) return I + g;
+    return I + g * (e_rev - v);
 }
 
 #ifdef __cplusplus

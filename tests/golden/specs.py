@@ -69,3 +69,30 @@ def small_adex(steps=300, seed=12):
 
 def small_izh(steps=300, seed=13):
     return W.izhikevich(500, 50, steps=steps, seed=seed, w_scale=20.0)
+
+
+def synapse_channel_net(steps=600, seed=21, scale=(0.1, 0.2, 0.3)):
+    """The small Brunel network with the reference's declared synapse models
+    as synapse channels (parity unpinned: the reference's forwards are
+    stubs): E->E through an exponential current channel (tau 5 ms), E->I
+    through a double-exponential channel (0.5 / 5 ms), I->E through an
+    AMPA-form conductance channel (0.5 / 5 ms) with reversal -10 mV, I->I
+    static.  Weights are dyadic, so the channel inputs sum exactly in any
+    order."""
+    spec = small_brunel(stdp=False, steps=steps, seed=seed)
+    net = realize(spec, dyadic_bits=44)
+    net["pops"][0]["syn"] = [("exp", 0.5e-3, 5e-3, 0.0), ("ampa", 0.5e-3, 5e-3, -0.010)]
+    net["pops"][1]["syn"] = [("dexp", 0.5e-3, 5e-3, 0.0)]
+    q = net["projs"]
+    q[0]["receptor"] = "chan0"     # E -> E, exponential
+    q[1]["receptor"] = "chan0"     # E -> I, double exponential
+    q[2]["receptor"] = "chan1"     # I -> E, AMPA form
+    q[0]["w"] = _dyadic(q[0]["w"] * np.float32(scale[0]), 44)
+    q[1]["w"] = _dyadic(q[1]["w"] * np.float32(scale[1]), 44)
+    # conductance weights: |w| / 25 mV
+    q[2]["w"] = _dyadic(np.abs(q[2]["w"]) / np.float32(0.025) * np.float32(scale[2]), 44)
+    return net
+
+
+def _dyadic(w, bits):
+    return (np.round(np.asarray(w, np.float64) * 2.0 ** bits) / 2.0 ** bits).astype(np.float32)

@@ -93,3 +93,24 @@ def test_poisson_drive_statistics():
     assert abs(x.mean() - 2.0) < 0.02 and abs(x.var() - 2.0) < 0.05
     g = O.drive_values("gauss", 0.0, 1.0, 9, 0, 200_000, 3)
     assert abs(g.mean()) < 0.01 and abs(g.std() - 1.0) < 0.01
+
+
+def test_oracle_synapse_channel_equations():
+    """The oracle's channel recurrences against a direct numpy restatement
+    for one neuron with a known input train (float32, one rounding per
+    operation)."""
+    import specs as S
+    f = np.float32
+    dt, tr, td = 1e-4, 0.5e-3, 5e-3
+    dr, dd = f(np.exp(-dt / tr)), f(np.exp(-dt / td))
+    s = r = f(0.0)
+    ins = [f(1.0), f(0.0), f(0.5), f(0.0), f(0.0)]
+    out = []
+    for x in ins:
+        s = f(f(s * dd) + x)
+        r = f(f(r * dr) + x)
+        out.append(f(s - r))
+    assert out[0] == 0.0 and out[1] > 0.0 and out[4] > 0.0
+    net = S.synapse_channel_net(steps=50)
+    a = O.run_oracle(net)
+    assert len(a["spike_id"]) > 0
