@@ -548,11 +548,9 @@ def finish_network_line(args, spec, nw, world, rank, dist, all_reduce, peaks, pe
     dom_ms = prof[kern[dom][0]]
     dom_bytes = kern[dom][1]
     achieved = dom_bytes / (dom_ms / 1e3) / 1e9 if dom_ms > 0 else 0.0
-    # Random L2 operations of the delivery (the measured limit of this
-    # path): one reduction per event, plus per plastic event one target
-    # record load (two loads without the walk record: spike steps and trace).
-    walk_rec = os.environ.get("NRN_WALK_REC") is not None
-    l2_ops = cnt["static_events"] + cnt["walk_events"] * (2 if walk_rec else 3)
+    # Random L2 operations of the delivery: one reduction per event, plus per
+    # plastic event two loads (the target's spike steps and its trace).
+    l2_ops = cnt["static_events"] + cnt["walk_events"] * 3
     deliv_ms = prof["static_delivery"] + prof["stdp_walks"]
     traffic = DELIVERY_TRAFFIC_PER_STEP if args.workload == "brunel_stdp" and args.scale == 1.0 else None
 

@@ -187,16 +187,6 @@ typedef struct {
     const float* drive_values;
     /* Per-neuron spike statistics updated at each spike, or NULL. */
     struct nrn_spike_stat* spike_stats;
-    /* Walk record of each neuron as the target of a plastic projection
-     * whose synapses all have delay rec_lag + 1 (int4 per neuron, 16-byte
-     * aligned), or NULL: x, y, z = its newest three spike steps (newest
-     * first, -1 = none) and w = the bits of trace slot rec_trace's value
-     * rec_lag steps before this one, written at every step.  The STDP walk
-     * of the next step then reads one record per synapse instead of the
-     * spike steps and the trace ring separately. */
-    int32_t* walk_rec;
-    int32_t rec_trace;
-    int32_t rec_lag;
     /* Synapse channels (nrn_syn_desc_t kinds), applied before the model
      * update: chan_in[c] is the input delivered this step (read, then
      * zeroed), chan_s[c] the decay state, chan_r[c] the rise state (DEXP,
@@ -525,6 +515,15 @@ NRN_API nrn_status_t nrn_engine_generate_projection(nrn_engine* e, const nrn_gen
                                             int64_t* nnz);
 /* stdp = {tau_plus, tau_minus, a_plus, a_minus, w_min, w_max, learning_rate} */
 NRN_API nrn_status_t nrn_engine_set_stdp(nrn_engine* e, int32_t proj, const double* stdp);
+/* Deterministic delivery (before nrn_engine_finalize; one GPU): each
+ * neuron input is the sum, in a fixed order -- projection by projection in
+ * index order, each by source, then delay, then the order its synapses were
+ * given -- of the weights
+ * of the synapses whose source spiked `delay` steps ago: the order of a
+ * sequential CPU loop, so results do not depend on thread timing and a
+ * checkpointed run resumes bit for bit.  It visits every in-synapse of every
+ * neuron each step (a test and reproducibility mode, not the fast path). */
+NRN_API nrn_status_t nrn_engine_set_deterministic(nrn_engine* e, int32_t on);
 /* Allocates the history and traces and runs the initialising update
  * (dt = 0, as sim_create does, src/simulation/runner.cpp:36-38). */
 NRN_API nrn_status_t nrn_engine_finalize(nrn_engine* e, int32_t init_update);

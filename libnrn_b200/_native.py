@@ -39,6 +39,7 @@ EXPORTS = [
     "nrn_engine_checkpoint_load", "nrn_engine_enable_spike_stats", "nrn_engine_spike_stats",
     "nrn_engine_spike_stats_reset", "nrn_engine_set_comm_timeout", "nrn_comm_bounded_wait",
     "nrn_comm_fake_async_error", "nrn_engine_profile_kernels", "nrn_engine_add_synapse_channel",
+    "nrn_engine_set_deterministic",
 ]
 
 
@@ -72,8 +73,7 @@ class PopStep(C.Structure):
         ("post_ring_k", C.c_int32), ("id_offset", C.c_int32), ("win", C.c_int32),
         ("win_mask", C.c_void_p), ("send_hdr", C.c_void_p), ("send_ids", C.c_void_p),
         ("send_cap", C.c_int32), ("pad2", C.c_int32), ("err", C.c_void_p), ("drive_values", C.c_void_p),
-        ("spike_stats", C.c_void_p), ("walk_rec", C.c_void_p), ("rec_trace", C.c_int32),
-        ("rec_lag", C.c_int32), ("n_chan", C.c_int32), ("chan_kind", C.c_int32 * 4),
+        ("spike_stats", C.c_void_p), ("n_chan", C.c_int32), ("chan_kind", C.c_int32 * 4),
         ("chan_e_rev", C.c_float * 4), ("chan_tau_rise", C.c_double * 4), ("chan_tau_decay", C.c_double * 4),
         ("chan_in", C.c_void_p * 4), ("chan_s", C.c_void_p * 4), ("chan_r", C.c_void_p * 4),
     ]
@@ -192,6 +192,7 @@ def lib() -> C.CDLL:
             "nrn_comm_bounded_wait": [POLL_FN, vp, C.c_double],
             "nrn_comm_fake_async_error": [i32],
             "nrn_engine_add_synapse_channel": [vp, i32, C.POINTER(SynDesc), C.POINTER(i32)],
+            "nrn_engine_set_deterministic": [vp, i32],
             "nrn_engine_profile_kernels": [vp, i64, C.POINTER(C.c_double), C.POINTER(i64)],
         }
         for name, args in sig.items():

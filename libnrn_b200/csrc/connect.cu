@@ -118,6 +118,38 @@ __global__ void gather_u32(const uint32_t* perm, int64_t n, const uint32_t* in, 
         out[k] = in[perm[k]];
 }
 
+// Delay (steps) of every CSR position: one thread per (source, delay) segment.
+__global__ void seg_delays(const int64_t* seg_ptr, int32_t n_src, int32_t nd, int32_t dmin, uint8_t* delay_of) {
+    const int64_t nseg = static_cast<int64_t>(n_src) * nd;
+    for (int64_t g = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; g < nseg;
+         g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const uint8_t d = static_cast<uint8_t>(dmin + static_cast<int32_t>(g % nd));
+        for (int64_t p = seg_ptr[g]; p < seg_ptr[g + 1]; ++p) delay_of[p] = d;
+    }
+}
+
+// Sort keys of the deterministic index: target above the CSR position (the
+// CSR is ordered by source, then delay, then the caller's list order).
+__global__ void det_keys(const uint32_t* tgt, int64_t n, unsigned long long* key, uint32_t* pos) {
+    for (int64_t k = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; k < n;
+         k += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        key[k] = (static_cast<unsigned long long>(tgt[k]) << 32) | static_cast<unsigned long long>(k);
+        pos[k] = static_cast<uint32_t>(k);
+    }
+}
+
+__global__ void det_targets(const unsigned long long* key, int64_t n, uint32_t* tgt_of) {
+    for (int64_t k = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; k < n;
+         k += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        tgt_of[k] = static_cast<uint32_t>(key[k] >> 32);
+}
+
+__global__ void gather_u8(const uint32_t* perm, int64_t n, const uint8_t* in, uint8_t* out) {
+    for (int64_t k = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; k < n;
+         k += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        out[k] = in[perm[k]];
+}
+
 // Raster entries as sort keys: the step above `shift` bits of neuron id.
 __global__ void raster_pack(const int32_t* step, const int32_t* gid, int64_t n, int shift, unsigned long long* key) {
     for (int64_t k = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; k < n;
@@ -177,6 +209,90 @@ void free_csr(DevCsr& c) {
     dfree(c.in_ptr);
     dfree(c.in_syn);
     dfree(c.in_src);
+    dfree(c.det_ptr);
+    dfree(c.det_syn);
+    dfree(c.det_src);
+    dfree(c.det_delay);
+}
+
+nrn_status_t build_det_index(DevCsr& c, cudaStream_t s) {
+    const int64_t n = c.nnz;
+    unsigned long long *k1 = nullptr, *k2 = nullptr;
+    uint32_t *p1 = nullptr, *p2 = nullptr, *src_of = nullptr, *tgt_of = nullptr;
+    uint8_t* d_of = nullptr;
+    int64_t* counts = nullptr;
+    void* tmp = nullptr;
+    size_t tmp_bytes = 0;
+    nrn_status_t st = NRN_OK;
+    auto cleanup = [&]() {
+        dfree(k1); dfree(k2); dfree(p1); dfree(p2); dfree(src_of); dfree(tgt_of); dfree(d_of); dfree(counts);
+        if (tmp) cudaFree(tmp);
+        tmp = nullptr;
+    };
+#define STEP(x)                       \
+    do {                              \
+        st = (x);                     \
+        if (st != NRN_OK) {           \
+            cleanup();                \
+            return st;                \
+        }                             \
+    } while (0)
+#define CSTEP(x) STEP(((x) == cudaSuccess) ? NRN_OK : cuda_fail(cudaGetLastError(), #x))
+    STEP(dalloc(&k1, n));
+    STEP(dalloc(&k2, n));
+    STEP(dalloc(&p1, n));
+    STEP(dalloc(&p2, n));
+    STEP(dalloc(&src_of, n));
+    STEP(dalloc(&tgt_of, n));
+    STEP(dalloc(&d_of, n));
+    STEP(dalloc(&counts, static_cast<size_t>(c.n_tgt) + 1));
+    if (n > 0) {
+        det_keys<<<grid_for(n), 256, 0, s>>>(c.tgt, n, k1, p1);
+        CSTEP(cudaGetLastError());
+        seg_sources<<<grid_for(static_cast<int64_t>(c.n_src) * c.nd), 256, 0, s>>>(c.seg_ptr, c.n_src, c.nd, src_of);
+        CSTEP(cudaGetLastError());
+        seg_delays<<<grid_for(static_cast<int64_t>(c.n_src) * c.nd), 256, 0, s>>>(c.seg_ptr, c.n_src, c.nd, c.dmin,
+                                                                                   d_of);
+        CSTEP(cudaGetLastError());
+    }
+    {
+        cub::DoubleBuffer<unsigned long long> dk(k1, k2);
+        cub::DoubleBuffer<uint32_t> dv(p1, p2);
+        CSTEP(cub::DeviceRadixSort::SortPairs(nullptr, tmp_bytes, dk, dv, static_cast<int>(n), 0, 64, s));
+        CSTEP(cudaMalloc(&tmp, tmp_bytes));
+        CSTEP(cub::DeviceRadixSort::SortPairs(tmp, tmp_bytes, dk, dv, static_cast<int>(n), 0, 64, s));
+        if (dk.Current() != k1) std::swap(k1, k2);
+        if (dv.Current() != p1) std::swap(p1, p2);
+        cudaFree(tmp);
+        tmp = nullptr;
+    }
+    CSTEP(cudaMemsetAsync(counts, 0, (static_cast<size_t>(c.n_tgt) + 1) * sizeof(int64_t), s));
+    if (n > 0) {
+        det_targets<<<grid_for(n), 256, 0, s>>>(k1, n, tgt_of);
+        CSTEP(cudaGetLastError());
+        count_keys<<<grid_for(n), 256, 0, s>>>(tgt_of, n, static_cast<uint32_t>(c.n_tgt), counts);
+        CSTEP(cudaGetLastError());
+    }
+    STEP(dalloc(&c.det_ptr, static_cast<size_t>(c.n_tgt) + 1));
+    tmp_bytes = 0;
+    CSTEP(cub::DeviceScan::ExclusiveSum(nullptr, tmp_bytes, counts, c.det_ptr, static_cast<int64_t>(c.n_tgt) + 1, s));
+    CSTEP(cudaMalloc(&tmp, tmp_bytes));
+    CSTEP(cub::DeviceScan::ExclusiveSum(tmp, tmp_bytes, counts, c.det_ptr, static_cast<int64_t>(c.n_tgt) + 1, s));
+    STEP(dalloc(&c.det_syn, n));
+    STEP(dalloc(&c.det_src, n));
+    STEP(dalloc(&c.det_delay, n));
+    CSTEP(cudaMemcpyAsync(c.det_syn, p1, n * sizeof(uint32_t), cudaMemcpyDeviceToDevice, s));
+    if (n > 0) {
+        gather_u32<<<grid_for(n), 256, 0, s>>>(p1, n, src_of, c.det_src);
+        CSTEP(cudaGetLastError());
+        gather_u8<<<grid_for(n), 256, 0, s>>>(p1, n, d_of, c.det_delay);
+        CSTEP(cudaGetLastError());
+    }
+    CSTEP(cudaStreamSynchronize(s));
+    cleanup();
+    return NRN_OK;
+#undef CSTEP
+#undef STEP
 }
 
 nrn_status_t build_csr(DevCsr& c, int32_t n_src, int32_t n_tgt, const int32_t* src, const int32_t* tgt,

@@ -29,6 +29,7 @@
 #include <cub/block/block_scan.cuh>
 
 #include "common.cuh"
+#include "internal.h"
 
 namespace nrn {
 namespace {
@@ -304,7 +305,85 @@ int sm_count() {
     return n;
 }
 
+// Deterministic delivery: one warp per target; the lanes look at 32
+// in-synapses at a time (in order), and the weights of those whose source
+// spiked are added one by one in that order (a ballot of the hits, then the
+// warp walks its set bits), so the sum is the sequential one.
+__global__ void __launch_bounds__(256) det_deliver_kernel(const __grid_constant__ DetAcc A, int ring,
+                                                         long long step_off, const long long* step_base,
+                                                         unsigned long long* events) {
+    const long long step = step_off + (step_base ? *step_base : 0);
+    const int lane = threadIdx.x & 31;
+    const long long warp = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const long long n_warps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
+    unsigned long long hits = 0;
+    for (long long t = warp; t < A.n; t += n_warps) {
+        float sum = 0.0f;
+        for (int q = 0; q < A.nproj; ++q) {
+            const DetProj& P = A.proj[q];
+            const long long b = P.ptr[t], e = P.ptr[t + 1];
+            for (long long base = b; base < e; base += 32) {
+                const long long k = base + lane;
+                float v = 0.0f;
+                bool hit = false;
+                if (k < e) {
+                    const int d = P.delay[k];
+                    const long long s_src = step - d;
+                    if (s_src >= 0) {
+                        const uint32_t j = P.src[k];
+                        hit = P.flags[static_cast<long long>(s_src % ring) * P.flag_n + j] != 0;
+                    }
+                    if (hit) {
+                        const uint32_t syn = P.syn[k];
+                        v = P.w[syn];
+                        if (P.mod) v = v * P.mod[syn];
+                    }
+                }
+                unsigned m = __ballot_sync(0xffffffffu, hit);
+                hits += __popc(m);
+                while (m) {
+                    const int l = __ffs(m) - 1;
+                    sum = sum + __shfl_sync(0xffffffffu, v, l);
+                    m &= m - 1;
+                }
+            }
+        }
+        if (lane == 0) A.acc[t] = sum;
+    }
+    if (events && lane == 0 && hits) atomicAdd(events, hits);
+}
+
+__global__ void det_flags_kernel(const float* spike, int n, uint8_t* flags, int ring, long long step_off,
+                                 const long long* step_base) {
+    const long long step = step_off + (step_base ? *step_base : 0);
+    uint8_t* row = flags + static_cast<long long>(step % ring) * n;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+        row[i] = spike[i] != 0.0f ? 1 : 0;
+}
+
 }  // namespace
+
+nrn_status_t det_deliver(const DetAcc& a, int32_t ring, long long step_off, const long long* step_base,
+                         unsigned long long* events, cudaStream_t s) {
+    NRN_CHECK_ARG(a.nproj >= 0 && a.nproj <= 8, "deterministic delivery: at most 8 projections per input");
+    NRN_CHECK_ARG(ring >= 1, "deterministic delivery: bad flag ring");
+    if (a.n == 0) return NRN_OK;
+    const int blocks = static_cast<int>(std::min<long long>((static_cast<long long>(a.n) * 32 + 255) / 256,
+                                                            32LL * sm_count()));
+    det_deliver_kernel<<<blocks, 256, 0, s>>>(a, ring, step_off, step_base, events);
+    NRN_CUDA_TRY(cudaGetLastError());
+    return NRN_OK;
+}
+
+nrn_status_t det_flags(const float* spike, int32_t n, uint8_t* flags, int32_t ring, long long step_off,
+                       const long long* step_base, cudaStream_t s) {
+    if (n == 0) return NRN_OK;
+    const int blocks = std::min((n + 255) / 256, 8 * sm_count());
+    det_flags_kernel<<<blocks, 256, 0, s>>>(spike, n, flags, ring, step_off, step_base);
+    NRN_CUDA_TRY(cudaGetLastError());
+    return NRN_OK;
+}
+
 }  // namespace nrn
 
 extern "C" nrn_status_t nrn_cuda_deliver(const nrn_proj_t* projs, int32_t nproj, const nrn_spike_hist_t* hists,

@@ -98,6 +98,7 @@ struct EnginePop {
     float* chan_in[NRN_MAX_CHANNELS] = {};
     float* chan_s[NRN_MAX_CHANNELS] = {};
     float* chan_r[NRN_MAX_CHANNELS] = {};
+    uint8_t* flags = nullptr;        // deterministic delivery: [det_ring][n] spiked at step s
 };
 
 struct EngineProj {
@@ -114,7 +115,6 @@ struct EngineProj {
     float* seg_x = nullptr;
     float* pre_snap = nullptr;   // [pre_depth][n_src] source trace at window ends
     float* post_ring = nullptr;  // [ring_depth][n_tgt] target trace at every step
-    int32_t* walk_rec = nullptr; // [n_tgt][4] walk record (single-delay walk projections)
     unsigned int* work_ctr = nullptr;   // [3] unit counters of the walk launches
     int32_t pre_depth = 1;
 };
@@ -147,6 +147,8 @@ struct nrn_engine {
     std::map<std::pair<int, int>, cudaGraphExec_t> graphs;   // (window phase of the first step, steps)
     int* d_err = nullptr;                 // device error flag (plasticity, exchange)
     bool use_graphs = true;
+    bool det = false;                     // deterministic delivery (nrn_engine_set_deterministic)
+    int32_t det_ring = 1;
     bool spike_stats = false;             // per-neuron spike statistics kept
     // partition over GPUs
     int32_t rank = 0, world = 1;
@@ -178,13 +180,14 @@ struct nrn_engine {
             cudaFree(p.hist_ids); cudaFree(p.hist_count);
             cudaFree(p.mask); cudaFree(p.recent); cudaFree(p.ring); cudaFree(p.cnt); cudaFree(p.drive_buf); cudaFree(p.stats);
             for (int c = 0; c < p.n_chan; ++c) { cudaFree(p.chan_in[c]); cudaFree(p.chan_s[c]); cudaFree(p.chan_r[c]); }
+            cudaFree(p.flags);
         }
         for (auto& q : projs) {
             free_csr(q.csr);
             cudaFree(q.x_pre);
             cudaFree(q.x_post);
             cudaFree(q.seg_last); cudaFree(q.seg_x);
-            cudaFree(q.pre_snap); cudaFree(q.post_ring); cudaFree(q.walk_rec); cudaFree(q.work_ctr);
+            cudaFree(q.pre_snap); cudaFree(q.post_ring); cudaFree(q.work_ctr);
         }
         cudaFree(d_step); cudaFree(d_events); cudaFree(d_raster_count); cudaFree(d_err);
         cudaFree(raster_step); cudaFree(raster_gid);
@@ -295,11 +298,6 @@ struct nrn_engine {
             a.trace_slow_ratio = slow_ratio;
             for (const auto& q : projs) {
                 if (q.walk && q.tgt_pop == i) {
-                    if (q.walk_rec) {
-                        a.walk_rec = q.walk_rec;
-                        a.rec_trace = a.n_traces;
-                        a.rec_lag = q.csr.dmin - 1;
-                    }
                     a.trace_ring[a.n_traces] = q.post_ring;
                     a.trace_ring_depth = ring_depth;
                     a.trace_decay[a.n_traces++] = static_cast<float>(std::exp(-dt / q.stdp[1]));
@@ -373,7 +371,6 @@ struct nrn_engine {
         a.src_lo = ps.lo;
         a.src_hi = ps.lo + ps.d.n;
         a.tgt_recent = reinterpret_cast<const int4*>(pt.recent + static_cast<int64_t>(pt.lo) * 4);
-        a.tgt_rec = reinterpret_cast<const int4*>(q.walk_rec);
         a.tgt_ring = pt.ring;
         a.tgt_cnt = pt.cnt;
         a.ring_k = kRing;
@@ -396,6 +393,7 @@ struct nrn_engine {
         a.err = d_err;
         a.events = d_events + 1;   // [1]: events delivered by the walks
         a.work_ctr = q.work_ctr;
+        a.no_deliver = det ? 1 : 0;
         return a;
     }
 
@@ -545,7 +543,7 @@ struct nrn_engine {
     nrn_status_t enqueue_step(int64_t off, bool win_end, cudaEvent_t* ev = nullptr, cudaEvent_t* kev = nullptr) {
         std::vector<nrn_proj_t> dp;
         for (auto& q : projs)
-            if (!q.walk) dp.push_back(dev_proj(q));
+            if (!q.walk && !det) dp.push_back(dev_proj(q));
         std::vector<nrn_spike_hist_t> hs;
         for (size_t i = 0; i < pops.size(); ++i) hs.push_back(hist(static_cast<int>(i)));
         if (ev) NRN_CUDA_TRY(cudaEventRecord(ev[0], stream));
@@ -586,10 +584,14 @@ struct nrn_engine {
             NRN_CUDA_TRY(cudaEventRecord(join_ev, side));
             NRN_CUDA_TRY(cudaStreamWaitEvent(stream, join_ev, 0));
         }
+        if (det) NRN_TRY(enqueue_det_delivery(off));
         if (ev) NRN_CUDA_TRY(cudaEventRecord(ev[1], stream));
         std::vector<nrn_pop_step_t> pa;
         for (size_t i = 0; i < pops.size(); ++i) pa.push_back(pop_args(static_cast<int>(i), dt, off, true));
         NRN_TRY(pop_step_group(pa.data(), static_cast<int>(pa.size()), stream));
+        if (det)
+            for (auto& p : pops)
+                NRN_TRY(det_flags(p.d.spike, p.d.n, p.flags, det_ring, off, d_step, stream));
         if (ev) NRN_CUDA_TRY(cudaEventRecord(ev[2], stream));
         if (kev) NRN_CUDA_TRY(cudaEventRecord(kev[4], stream));
         for (auto& q : projs) {
@@ -602,6 +604,39 @@ struct nrn_engine {
         if (win_end) NRN_TRY(enqueue_window_end(off));
         if (ev) NRN_CUDA_TRY(cudaEventRecord(ev[3], stream));
         if (kev) NRN_CUDA_TRY(cudaEventRecord(kev[6], stream));
+        return NRN_OK;
+    }
+
+    // Deterministic delivery of this step into every input of every
+    // population (projections in index order), after the walks updated the
+    // weights of the arriving spikes' segments.
+    nrn_status_t enqueue_det_delivery(int64_t off) {
+        for (size_t i = 0; i < pops.size(); ++i) {
+            const EnginePop& t = pops[i];
+            const int n_acc = 3 + t.n_chan;
+            for (int r = 0; r < n_acc; ++r) {
+                const int receptor = r < 3 ? r : NRN_RECV_CHANNEL + (r - 3);
+                DetAcc A;
+                A.n = t.d.n;
+                for (const auto& q : projs) {
+                    if (q.tgt_pop != static_cast<int>(i) || q.receptor != receptor) continue;
+                    if (A.nproj == 8) return fail(NRN_ERR_UNSUPPORTED, "deterministic delivery: more than 8 "
+                                                                      "projections into one input");
+                    DetProj& P = A.proj[A.nproj++];
+                    P.ptr = q.csr.det_ptr;
+                    P.syn = q.csr.det_syn;
+                    P.src = q.csr.det_src;
+                    P.delay = q.csr.det_delay;
+                    P.w = q.csr.w;
+                    P.mod = q.csr.mod;
+                    P.flags = pops[q.src_pop].flags;
+                    P.flag_n = pops[q.src_pop].n_global;
+                    A.acc = acc_of(q);
+                }
+                if (A.nproj == 0) continue;
+                NRN_TRY(det_deliver(A, det_ring, off, d_step, d_events, stream));
+            }
+        }
         return NRN_OK;
     }
 
@@ -710,6 +745,7 @@ struct nrn_engine {
             add(p.ring, n * kRing * 4);
             add(p.cnt, n * 4);
             add(p.stats, n * sizeof(nrn_spike_stat_t));
+            add(p.flags, static_cast<size_t>(det_ring) * p.n_global);
             for (int c = 0; c < p.n_chan; ++c) {
                 add(p.chan_in[c], n * 4);
                 add(p.chan_s[c], n * 4);
@@ -726,7 +762,6 @@ struct nrn_engine {
                 add(q.seg_x, nseg * 4);
                 add(q.pre_snap, static_cast<size_t>(q.pre_depth) * q.csr.n_src * 4);
                 add(q.post_ring, static_cast<size_t>(ring_depth) * q.csr.n_tgt * 4);
-                add(q.walk_rec, static_cast<size_t>(q.csr.n_tgt) * 16);
             }
         }
         add(d_events, 2 * sizeof(unsigned long long));
@@ -1160,6 +1195,15 @@ static nrn_status_t check_layout(nrn_engine* e) {
     return NRN_OK;
 }
 
+nrn_status_t nrn_engine_set_deterministic(nrn_engine* e, int32_t on) {
+    ENGINE_GUARD(e);
+    NRN_CHECK_ARG(!e->finalized, "nrn_engine_set_deterministic: call before nrn_engine_finalize");
+    NRN_CHECK_ARG(e->world == 1 || !on, "nrn_engine_set_deterministic: deterministic delivery runs on one GPU");
+    e->det = on != 0;
+    e->drop_graphs();
+    return NRN_OK;
+}
+
 nrn_status_t nrn_engine_set_comm_timeout(nrn_engine* e, double seconds) {
     ENGINE_GUARD(e);
     NRN_CHECK_ARG(seconds > 0.0 && std::isfinite(seconds), "nrn_engine_set_comm_timeout: seconds must be positive");
@@ -1178,6 +1222,14 @@ nrn_status_t nrn_engine_finalize(nrn_engine* e, int32_t init_update) {
     if (e->projs.empty()) mind = 1;
     for (auto& q : e->projs)
         if (q.plastic) NRN_TRY(build_transpose(q.csr, e->stream));
+    if (e->det) {
+        NRN_CHECK_ARG(e->world == 1, "deterministic delivery runs on one GPU");
+        for (auto& q : e->projs) NRN_TRY(build_det_index(q.csr, e->stream));
+        int r = 1;
+        while (r < maxd + 1) r <<= 1;
+        e->det_ring = r;
+        for (auto& p : e->pops) NRN_TRY(dalloc0(&p.flags, static_cast<size_t>(r) * p.n_global, e->stream));
+    }
     e->assign_plasticity();
     bool any_walk = false;
     for (auto& q : e->projs) {
@@ -1268,21 +1320,6 @@ nrn_status_t nrn_engine_finalize(nrn_engine* e, int32_t init_update) {
         NRN_TRY(dalloc0(&q.post_ring, static_cast<size_t>(e->ring_depth) * q.csr.n_tgt, e->stream));
         NRN_TRY(need_history(e->pops[q.src_pop]));
         NRN_TRY(need_history(e->pops[q.tgt_pop]));
-    }
-    // Walk records for single-delay walk projections that are the only walk
-    // projection onto their target population (the neuron update keeps one
-    // record per neuron).
-    for (auto& q : e->projs) {
-        if (!q.walk || q.csr.nd != 1 || q.csr.dmin > e->ring_depth - 1) continue;
-        int onto = 0;
-        for (const auto& o : e->projs) onto += o.walk && o.tgt_pop == q.tgt_pop;
-        if (onto != 1 || !std::getenv("NRN_WALK_REC")) continue;   // opt-in: see the walk kernel notes
-        const size_t n = static_cast<size_t>(q.csr.n_tgt);
-        NRN_TRY(dalloc0(&q.walk_rec, n * 4, e->stream));
-        std::vector<int32_t> init(n * 4, -1);
-        for (size_t i = 0; i < n; ++i) init[4 * i + 3] = 0;   // trace 0.0f
-        NRN_CUDA_TRY(cudaMemcpyAsync(q.walk_rec, init.data(), n * 16, cudaMemcpyHostToDevice, e->stream));
-        NRN_TRY(e->wait_stream());
     }
     for (auto& p : e->pops)
         if (p.d.drive.kind != NRN_DRIVE_NONE) NRN_TRY(dalloc0(&p.drive_buf, static_cast<size_t>(p.d.n), e->stream));

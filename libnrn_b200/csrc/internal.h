@@ -26,6 +26,12 @@ struct DevCsr {
     int64_t* in_ptr = nullptr;    // [n_tgt+1]
     uint32_t* in_syn = nullptr;   // [nnz]
     uint32_t* in_src = nullptr;   // [nnz]
+    // deterministic delivery: target-major index in CSR order (source, delay,
+    // the caller's list order), with each synapse's source and delay
+    int64_t* det_ptr = nullptr;   // [n_tgt+1]
+    uint32_t* det_syn = nullptr;  // [nnz] CSR position
+    uint32_t* det_src = nullptr;  // [nnz]
+    uint8_t* det_delay = nullptr; // [nnz]
 };
 
 void free_csr(DevCsr& c);
@@ -37,6 +43,36 @@ nrn_status_t build_csr(DevCsr& c, int32_t n_src, int32_t n_tgt, const int32_t* s
                        cudaStream_t s);
 // Adds the target-major index (in_ptr/in_syn/in_src).
 nrn_status_t build_transpose(DevCsr& c, cudaStream_t s);
+// Adds the deterministic delivery index (det_*).
+nrn_status_t build_det_index(DevCsr& c, cudaStream_t s);
+
+// Deterministic delivery (deliver.cu): each target's input is the sum, in
+// a fixed order (projection; source; delay; the caller's list order), of the
+// weights of its synapses whose source spiked `delay` steps ago -- the
+// order of a sequential CPU loop, so the result does not depend on thread
+// timing.  Spikes are read from per-population flag rings
+// ([ring][n_global] bytes, row s % ring = spiked at step s).
+struct DetProj {
+    const int64_t* ptr = nullptr;
+    const uint32_t* syn = nullptr;
+    const uint32_t* src = nullptr;
+    const uint8_t* delay = nullptr;
+    const float* w = nullptr;
+    const float* mod = nullptr;
+    const uint8_t* flags = nullptr;   // the source population's flag ring
+    int64_t flag_n = 0;               // its row length (the population's size)
+};
+struct DetAcc {
+    float* acc = nullptr;             // [n] written (not added)
+    int32_t n = 0;
+    int32_t nproj = 0;
+    DetProj proj[8];
+};
+nrn_status_t det_deliver(const DetAcc& a, int32_t ring, long long step_off, const long long* step_base,
+                         unsigned long long* events, cudaStream_t s);
+// Row (step % ring) of a flag ring from a population's 0/1 spike vector.
+nrn_status_t det_flags(const float* spike, int32_t n, uint8_t* flags, int32_t ring, long long step_off,
+                       const long long* step_base, cudaStream_t s);
 
 // Fixed in/out-degree generation into device arrays of length rows*degree;
 // entries whose target falls outside [keep_lo, keep_hi) get src = -1.
@@ -84,9 +120,6 @@ struct WalkArgs {
     int32_t src_lo = 0, src_hi = 0;
     // spike steps of the targets (local index)
     const int4* tgt_recent = nullptr;
-    // per-target walk record (newest three spike steps and the target trace
-    // at the arriving spikes' step, written by the neuron update), or null
-    const int4* tgt_rec = nullptr;
     const int32_t* tgt_ring = nullptr;
     const int32_t* tgt_cnt = nullptr;
     int32_t ring_k = 64;
@@ -108,6 +141,7 @@ struct WalkArgs {
     unsigned long long* events = nullptr;
     // [3] unit counters of the launches (zero before a run's first launch)
     unsigned int* work_ctr = nullptr;
+    int32_t no_deliver = 0;           // 1: update weights only (deterministic delivery)
 };
 nrn_status_t walk_launch(const WalkArgs& a, int mode, long long step_off, const long long* step_base,
                          cudaStream_t s);

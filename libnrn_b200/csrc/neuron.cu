@@ -80,9 +80,6 @@ struct PopArgs {
     int* send_ids;
     int send_cap;
     int* err;
-    int4* walk_rec;            // STDP walk record (newest 3 spike steps, lagged trace), or null
-    int rec_trace;
-    int rec_lag;
     int n_chan;                // synapse channels
     int chan_kind[4];
     float chan_dec_rise[4], chan_dec_decay[4], chan_e_rev[4];
@@ -109,18 +106,6 @@ __device__ __forceinline__ float apply_channels(const PopArgs& a, int i, float I
         I = a.chan_kind[c] == NRN_SYN_DEXP ? I + g : I + g * (a.chan_e_rev[c] - v);
     }
     return I;
-}
-
-// The walk record of neuron i after this step's update (x_new: the value of
-// trace slot rec_trace just written): .w every step, the spike steps when it
-// spiked at t.
-__device__ __forceinline__ void write_walk_rec(const PopArgs& a, int i, bool spiked, int t, float xw) {
-    if (spiked) {
-        const int4 r = a.walk_rec[i];
-        a.walk_rec[i] = make_int4(t, r.x, r.y, __float_as_int(xw));
-    } else {
-        reinterpret_cast<float*>(a.walk_rec + i)[3] = xw;
-    }
 }
 
 template <bool HET>
@@ -302,11 +287,6 @@ __device__ __forceinline__ void pop_body(const PopArgs& a, const int i) {
                 }
             }
         }
-        if (a.walk_rec != nullptr) {
-            const long long mask = a.trace_ring_depth - 1;
-            const float xw = a.trace_ring[a.rec_trace][((step - a.rec_lag) & mask) * a.n + i];
-            write_walk_rec(a, i, spiked, static_cast<int>(step), xw);
-        }
         if (spiked && a.post_recent != nullptr) {
             const int t = static_cast<int>(step);
             int4 r = a.post_recent[i];
@@ -440,7 +420,6 @@ __global__ void __launch_bounds__(256) lif4_group_kernel(const __grid_constant__
         st4(a.ref, i0, ref);
         const float4 s4 = make_float4(sp[0] ? 1.f : 0.f, sp[1] ? 1.f : 0.f, sp[2] ? 1.f : 0.f, sp[3] ? 1.f : 0.f);
         if (a.spike) st4(a.spike, i0, s4);
-        float4 xr = make_float4(0.f, 0.f, 0.f, 0.f);
         if (traces_now) {
             for (int k = 0; k < a.n_traces; ++k) {
                 const float d = a.trace_decay[k];
@@ -455,13 +434,7 @@ __global__ void __launch_bounds__(256) lif4_group_kernel(const __grid_constant__
                 }
                 x.x = x.x * d + s4.x; x.y = x.y * d + s4.y; x.z = x.z * d + s4.z; x.w = x.w * d + s4.w;
                 st4(dst, i0, x);
-                if (a.walk_rec != nullptr && k == a.rec_trace) xr = x;
             }
-        }
-        if (a.walk_rec != nullptr) {
-            if (a.rec_lag > 0) xr = ld4(a.trace_ring[a.rec_trace] + ((step - a.rec_lag) & ring_mask) * a.n, i0);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) write_walk_rec(a, i0 + k, sp[k] != 0, static_cast<int>(step), at(xr, k));
         }
         if (a.i_syn) st4(a.i_syn, i0, make_float4(0.f, 0.f, 0.f, 0.f));
     }
@@ -747,15 +720,6 @@ nrn_status_t make_args(const nrn_pop_step_t& d, PopArgs& a, bool& het, bool& con
         a.chan_s[c] = d.chan_s[c];
         a.chan_r[c] = d.chan_r[c];
     }
-    a.walk_rec = reinterpret_cast<int4*>(d.walk_rec);
-    a.rec_trace = d.rec_trace;
-    a.rec_lag = d.rec_lag;
-    NRN_CHECK_ARG(d.walk_rec == nullptr ||
-                      ((reinterpret_cast<uintptr_t>(d.walk_rec) % 16) == 0 && d.rec_trace >= 0 &&
-                       d.rec_trace < d.n_traces && d.trace_ring[d.rec_trace] != nullptr && d.rec_lag >= 0 &&
-                       d.rec_lag < d.trace_ring_depth && (d.trace_slow_ratio <= 1)),
-                  "nrn_cuda_pop_step: walk record needs a 16-byte aligned array, a per-step trace ring slot "
-                  "and a lag inside the ring");
     NRN_CHECK_ARG(a.send_hdr == nullptr || (d.send_ids != nullptr && d.send_cap >= 0),
                   "nrn_cuda_pop_step: send buffer without ids");
     if (d.model != NRN_MODEL_ADEX) cond = false;

@@ -305,12 +305,6 @@ __device__ __forceinline__ unsigned walk_block(const WalkArgs& a, const Seg& g, 
     const bool has_pre = g.P.n > 0;
     const int t0 = has_pre ? g.P[0] : 0;
     const float* ring0 = a.post_ring + static_cast<long long>(t0 & (a.post_depth - 1)) * a.n_tgt;
-    // With the walk record, one 16-byte load per synapse gives the target's
-    // newest three spike steps and its trace at step now - dmin (the step of
-    // every spike arriving now through a single-delay projection); the full
-    // spike-step record is read only when the third newest spike is after T.
-    const bool rec = a.tgt_rec != nullptr;
-    const bool rec_x = rec && (!has_pre || t0 == now - a.dmin);
     // the next round's target and weight (the HBM stream) are loaded a round
     // ahead; the target's spike steps and trace (L2) within the round
     unsigned n = 0;
@@ -326,16 +320,8 @@ __device__ __forceinline__ unsigned walk_block(const WalkArgs& a, const Seg& g, 
         const uint32_t syn = g.s0 + o;
         const uint32_t t = t_next;
         const float w = w_next;
-        int4 r;
-        float xp0;
-        if (rec) {
-            const int4 rc = a.tgt_rec[t];
-            xp0 = rec_x ? __int_as_float(rc.w) : (has_pre ? ring0[t] : 0.0f);
-            r = rc.z <= g.T ? make_int4(rc.x, rc.y, rc.z, rc.z) : a.tgt_recent[t];
-        } else {
-            r = a.tgt_recent[t];
-            xp0 = has_pre ? ring0[t] : 0.0f;
-        }
+        const int4 r = a.tgt_recent[t];
+        const float xp0 = has_pre ? ring0[t] : 0.0f;
         const float md = MOD ? __ldcs(a.mod + syn) : 1.0f;
         if (o + kConsumers < len) {
             t_next = __ldcs(a.tgt + syn + kConsumers);
@@ -502,8 +488,10 @@ __device__ void produce(const WalkArgs& a, Producer& shared_pr, Item& it, int* s
             }
             const int spike = static_cast<int>(u - start[lo]);
             const int j = a.hist_src.ids[static_cast<long long>(slot[lo]) * a.hist_src.cap + spike];
-            prepare(a, it, sP, sX, j, lo, now - 1, true, now, m_new, lane);   // always an item
-            break;
+            // an item, except for an up-to-date segment when delivery is left
+            // to the deterministic delivery
+            if (prepare(a, it, sP, sX, j, lo, now - 1, a.no_deliver == 0, now, m_new, lane)) break;
+            continue;
         }
         // a group of segments: each lane looks at one
         pr.g0 = pr.base + (u - pr.n_arr) * kGroup;
@@ -657,16 +645,14 @@ nrn_status_t walk_launch(const WalkArgs& a, int mode, long long step_off, const 
     NRN_CHECK_ARG(a.pre_depth > 0 && (a.pre_depth & (a.pre_depth - 1)) == 0 && a.post_depth > 0 &&
                       (a.post_depth & (a.post_depth - 1)) == 0,
                   "plastic projection: trace ring depths must be powers of two");
-    int per_sm = 0;
-    if (a.mod) {
-        NRN_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, walk_kernel<true>, kThreads, 0));
-        walk_kernel<true><<<std::max(1, per_sm) * sm_count_current(), kThreads, 0, s>>>(a, mode, step_off, step_base);
-    } else {
-        NRN_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, walk_kernel<false>, kThreads, 0));
-        walk_kernel<false><<<std::max(1, per_sm) * sm_count_current(), kThreads, 0, s>>>(a, mode, step_off, step_base);
-    }
-    NRN_CUDA_TRY(cudaGetLastError());
-    return NRN_OK;
+    auto launch = [&](auto kern) -> nrn_status_t {
+        int per_sm = 0;
+        NRN_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, 0));
+        kern<<<std::max(1, per_sm) * sm_count_current(), kThreads, 0, s>>>(a, mode, step_off, step_base);
+        NRN_CUDA_TRY(cudaGetLastError());
+        return NRN_OK;
+    };
+    return a.mod ? launch(walk_kernel<true>) : launch(walk_kernel<false>);
 }
 
 }  // namespace nrn

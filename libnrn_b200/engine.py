@@ -152,6 +152,11 @@ class Network:
         arr = (C.c_double * 7)(*[float(x) for x in params])
         N.check(self.L.nrn_engine_set_stdp(self.h, proj, arr), "set_stdp")
 
+    def set_deterministic(self, on: bool = True) -> None:
+        """Deterministic delivery (nrn_engine_set_deterministic): inputs summed
+        in the synapse-list order, before finalize."""
+        N.check(self.L.nrn_engine_set_deterministic(self.h, int(on)), "set_deterministic")
+
     def finalize(self, init_update: bool = True) -> None:
         N.check(self.L.nrn_engine_finalize(self.h, int(init_update)), "finalize")
         self.finalized = True
@@ -281,7 +286,8 @@ class Network:
 
     # -- builders ----------------------------------------------------------
     @classmethod
-    def from_net(cls, net: dict, device: int = 0, record: bool = True, spike_stats: bool = False) -> "Network":
+    def from_net(cls, net: dict, device: int = 0, record: bool = True, spike_stats: bool = False,
+                 deterministic: bool = False) -> "Network":
         """From a network description with explicit synapse lists (the
         oracle's form)."""
         nw = cls(net["dt"], net.get("slow_ratio", 1), device)
@@ -298,6 +304,8 @@ class Network:
                 nw.set_stdp(qid, q["stdp"])
         if spike_stats:
             nw.enable_spike_stats()
+        if deterministic:
+            nw.set_deterministic(True)
         nw.finalize(True)
         return nw
 

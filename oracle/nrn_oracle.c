@@ -207,6 +207,41 @@ ORC_EXPORT int orc_net_run(const orc_net* net) {
     for (int c = 0; c < ORC_MAX_CHAN; ++c) cin_all[c] = (float*)calloc((size_t)N, sizeof(float));
     uint8_t* hist = (uint8_t*)calloc((size_t)H * N, 1);
 
+    /* Event-driven indices: per projection, synapse positions ordered by
+     * (source, delay, list position) with row offsets per source, and for
+     * plastic projections the synapses of every target. */
+    int64_t** row = (int64_t**)calloc((size_t)(nq > 0 ? nq : 1), sizeof(int64_t*));
+    int64_t** perm = (int64_t**)calloc((size_t)(nq > 0 ? nq : 1), sizeof(int64_t*));
+    int64_t** inrow = (int64_t**)calloc((size_t)(nq > 0 ? nq : 1), sizeof(int64_t*));
+    int64_t** inlist = (int64_t**)calloc((size_t)(nq > 0 ? nq : 1), sizeof(int64_t*));
+    int* first_stdp = (int*)calloc((size_t)(nq > 0 ? nq : 1), sizeof(int));
+    for (int q = 0; q < nq; ++q) {
+        const orc_proj* Q = &net->projs[q];
+        int ns = net->pops[Q->src_pop].n, nt = net->pops[Q->tgt_pop].n;
+        int64_t* cnt = (int64_t*)calloc((size_t)ns * 256 + 1, sizeof(int64_t));
+        for (int64_t k = 0; k < Q->nnz; ++k) cnt[(size_t)Q->src[k] * 256 + Q->delay[k] + 1]++;
+        for (size_t b = 0; b < (size_t)ns * 256; ++b) cnt[b + 1] += cnt[b];
+        perm[q] = (int64_t*)malloc((size_t)(Q->nnz > 0 ? Q->nnz : 1) * sizeof(int64_t));
+        row[q] = (int64_t*)malloc(((size_t)ns + 1) * sizeof(int64_t));
+        for (int j = 0; j <= ns; ++j) row[q][j] = cnt[(size_t)j * 256];
+        for (int64_t k = 0; k < Q->nnz; ++k) perm[q][cnt[(size_t)Q->src[k] * 256 + Q->delay[k]]++] = k;
+        free(cnt);
+        first_stdp[q] = 1;
+        if (Q->plastic) {
+            int64_t* c2 = (int64_t*)calloc((size_t)nt + 1, sizeof(int64_t));
+            for (int64_t k = 0; k < Q->nnz; ++k) c2[Q->tgt[k] + 1]++;
+            for (int i = 0; i < nt; ++i) c2[i + 1] += c2[i];
+            inrow[q] = (int64_t*)malloc(((size_t)nt + 1) * sizeof(int64_t));
+            memcpy(inrow[q], c2, ((size_t)nt + 1) * sizeof(int64_t));
+            inlist[q] = (int64_t*)malloc((size_t)(Q->nnz > 0 ? Q->nnz : 1) * sizeof(int64_t));
+            for (int64_t k = 0; k < Q->nnz; ++k) inlist[q][c2[Q->tgt[k]]++] = k;
+            free(c2);
+        }
+    }
+    /* newest spike step of every neuron (delivery skips silent sources) */
+    int32_t* last = (int32_t*)malloc((size_t)N * sizeof(int32_t));
+    for (int64_t g = 0; g < N; ++g) last[g] = -1000000;
+
     /* Working copies of the weights and STDP traces. */
     float** W = (float**)calloc((size_t)(nq > 0 ? nq : 1), sizeof(float*));
     float** xpre = (float**)calloc((size_t)(nq > 0 ? nq : 1), sizeof(float*));
@@ -244,11 +279,17 @@ ORC_EXPORT int orc_net_run(const orc_net* net) {
             float* acc = Q->receptor >= ORC_RECV_CHANNEL ? cin_all[(Q->receptor - ORC_RECV_CHANNEL) % ORC_MAX_CHAN]
                        : Q->receptor == ORC_RECV_CURRENT ? I
                        : Q->receptor == ORC_RECV_GEXC ? ie : ii;
-            for (int64_t k = 0; k < Q->nnz; ++k) {
-                int d = Q->delay[k];
-                if (t - d < 0) continue;
-                if (hist[(size_t)((t - d) % H) * N + so + Q->src[k]])
-                    acc[to + Q->tgt[k]] += W[q][k];
+            /* per target: sources ascending, then delay, then list position */
+            int ns = net->pops[Q->src_pop].n;
+            for (int j = 0; j < ns; ++j) {
+                if (last[so + j] < t - maxd) continue;
+                for (int64_t r = row[q][j]; r < row[q][j + 1]; ++r) {
+                    int64_t k = perm[q][r];
+                    int d = Q->delay[k];
+                    if (t - d < 0) continue;
+                    if (hist[(size_t)((t - d) % H) * N + so + j])
+                        acc[to + Q->tgt[k]] += W[q][k];
+                }
             }
         }
         /* external drive */
@@ -293,20 +334,44 @@ ORC_EXPORT int orc_net_run(const orc_net* net) {
                     xpre[q][j] = xpre[q][j] * dpre + (float)pre[j];
                 for (int i = 0; i < Pt->n; ++i)
                     xpost[q][i] = xpost[q][i] * dpost + (float)post[i];
-                for (int64_t k = 0; k < Q->nnz; ++k) {
-                    int j = Q->src[k], i = Q->tgt[k];
-                    float dw = (ap * xpre[q][j]) * (float)post[i]
-                             - (am * xpost[q][i]) * (float)pre[j];
-                    float wn = W[q][k] + ((dw * lr) * 1.0f) * 1.0f;
-                    if (wn < wmin) wn = wmin;
-                    if (wn > wmax) wn = wmax;
-                    W[q][k] = wn;
+                /* Every synapse is updated (and clamped) at the first update;
+                 * afterwards only synapses whose source or target spiked can
+                 * change (dw = 0 otherwise, the weight already in range), so
+                 * only those are visited: the out-rows of spiking sources,
+                 * then the in-lists of spiking targets whose source did not. */
+#define ORC_STDP_SYN(k)                                                          \
+    do {                                                                         \
+        int j_ = Q->src[k], i_ = Q->tgt[k];                                      \
+        float dw = (ap * xpre[q][j_]) * (float)post[i_]                          \
+                 - (am * xpost[q][i_]) * (float)pre[j_];                         \
+        float wn = W[q][k] + ((dw * lr) * 1.0f) * 1.0f;                          \
+        if (wn < wmin) wn = wmin;                                                \
+        if (wn > wmax) wn = wmax;                                                \
+        W[q][k] = wn;                                                            \
+    } while (0)
+                if (first_stdp[q]) {
+                    for (int64_t k = 0; k < Q->nnz; ++k) ORC_STDP_SYN(k);
+                    first_stdp[q] = 0;
+                } else {
+                    for (int j = 0; j < Ps->n; ++j) {
+                        if (!pre[j]) continue;
+                        for (int64_t r = row[q][j]; r < row[q][j + 1]; ++r) ORC_STDP_SYN(perm[q][r]);
+                    }
+                    for (int i = 0; i < Pt->n; ++i) {
+                        if (!post[i]) continue;
+                        for (int64_t r = inrow[q][i]; r < inrow[q][i + 1]; ++r) {
+                            int64_t k = inlist[q][r];
+                            if (!pre[Q->src[k]]) ORC_STDP_SYN(k);
+                        }
+                    }
                 }
+#undef ORC_STDP_SYN
             }
         }
         /* P6 */
         for (int64_t g = 0; g < N; ++g) {
             if (!h[g]) continue;
+            last[g] = t;
             if (nspk < net->spike_cap) {
                 net->spike_step[nspk] = t;
                 net->spike_id[nspk] = (int32_t)g;
@@ -337,6 +402,8 @@ ORC_EXPORT int orc_net_run(const orc_net* net) {
     }
     free(W); free(xpre); free(xpost);
     for (int p = 0; p < np; ++p) free_pop(&S[p]);
+    for (int q = 0; q < nq; ++q) { free(row[q]); free(perm[q]); free(inrow[q]); free(inlist[q]); }
+    free(row); free(perm); free(inrow); free(inlist); free(first_stdp); free(last);
     free(S); free(I); free(ie); free(ii); free(hist);
     for (int c = 0; c < ORC_MAX_CHAN; ++c) free(cin_all[c]);
     return nspk > net->spike_cap ? 1 : 0;

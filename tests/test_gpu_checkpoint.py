@@ -1,7 +1,9 @@
 """Checkpoint and restore of the engine's device state: a run continued
 from a checkpoint -- in the same engine, or in a new engine built from the
-same network -- gives the spikes and weights of the uninterrupted run, bit
-for bit (membrane potentials to float rounding); checkpoints of another
+same network -- gives the uninterrupted run bit for bit (spikes, weights and
+membrane potentials, with deterministic delivery, whose input sums do not
+depend on thread timing); a restored engine's own checkpoint equals the one
+it was restored from, with the fast delivery too; checkpoints of another
 network are refused."""
 import numpy as np
 import pytest
@@ -21,7 +23,7 @@ def net_stdp(steps):
 
 def test_continue_from_checkpoint_equals_uninterrupted_run():
     net = net_stdp(900)
-    a = Network.from_net(net)
+    a = Network.from_net(net, deterministic=True)
     a.run(300)
     ckpt = a.checkpoint()
     a.run(600)
@@ -36,7 +38,7 @@ def test_continue_from_checkpoint_equals_uninterrupted_run():
     w_b = [a.weights(q) for q in range(len(net["projs"]))]
     a.close()
     # a new engine from the same network
-    c = Network.from_net(net)
+    c = Network.from_net(net, deterministic=True)
     c.restore(ckpt)
     c.run(600)
     st_c, gid_c = c.raster()
@@ -49,9 +51,21 @@ def test_continue_from_checkpoint_equals_uninterrupted_run():
         assert np.array_equal(st, st_a) and np.array_equal(gid, gid_a)
         for x, y in zip(w, w_a):
             assert np.array_equal(x, y)
-    # float reductions sum a step's inputs in an order that varies from run
-    # to run: potentials agree to rounding, spikes and weights exactly
-    assert float(np.abs(v_c - v_a).max()) <= 1e-5 * float(np.abs(v_a).max())
+    assert np.array_equal(v_c, v_a)
+
+
+def test_restore_round_trip_fast_delivery():
+    net = net_stdp(300)
+    a = Network.from_net(net)
+    a.run(300)
+    ckpt = a.checkpoint()
+    a.close()
+    c = Network.from_net(net)
+    c.restore(ckpt)
+    assert c.step == 300
+    assert c.checkpoint() == ckpt
+    c.run(30)
+    c.close()
 
 
 def test_checkpoint_of_another_network_is_refused():
