@@ -3,6 +3,11 @@
 // tests/simulation/test_clock.cpp, tests/simulation/test_spike_buffer.cpp).
 // Host-only: runs without a GPU.
 #include <nrn/nrn.h>
+#include <nrn/config/config.h>
+
+#include <unistd.h>
+
+#include <cstdio>
 
 #include "nrn_test.h"
 
@@ -197,9 +202,111 @@ TEST(Topology, RandomCsrInvariants) {
     random_topology_destroy(topo);
 }
 
-TEST(Config, NotImplementedThrows) {
-    EXPECT_THROW(config::load("x.yaml"), std::runtime_error);
-    EXPECT_THROW(config::load_region("x.yaml"), std::runtime_error);
+// YAML configuration (nrn::config; a stub that throws in the reference,
+// src/config/config.cpp:8-18): a Region from a file, and the errors.
+static std::string write_tmp(const char* name, const char* text) {
+    std::string path = std::string("/tmp/nrn_cfg_") + std::to_string(::getpid()) + "_" + name;
+    FILE* f = std::fopen(path.c_str(), "w");
+    std::fputs(text, f);
+    std::fclose(f);
+    return path;
+}
+
+TEST(Config, MissingFileThrows) {
+    EXPECT_THROW(config::load("/nonexistent/x.yaml"), std::runtime_error);
+    EXPECT_THROW(config::load_region("/nonexistent/x.yaml"), std::runtime_error);
+}
+
+TEST(Config, LoadRegion) {
+    const std::string path = write_tmp("region.yaml", R"(# a small balanced network
+name: cortex
+seed: 7
+simulation:
+  dt_fast: 0.1ms
+  device: cpu
+populations:
+- name: exc
+  model: LIF
+  count: 80
+  params: {v_rest: 0mV, v_thresh: 20mV, v_reset: 10mV, tau_m: 20ms, i_bg: 300pA}
+- name: inh
+  model: Izhikevich
+  count: 20
+  params:
+    a: 0.1
+    d: 2
+connections:
+  - source: exc
+    target: inh
+    topology: random
+    probability: 0.2
+    weight: 250pA
+    block_size: 16
+    synapse: exponential
+    synapse_params: {tau_decay: 5ms}
+  - source: exc
+    target: exc
+    probability: 0.1
+    block_size: 16
+    plasticity: stdp
+    plasticity_params: {a_plus: 0.01, w_max: 500pA}
+)");
+    Region* r = config::load_region(path);
+    ASSERT_TRUE(r != nullptr);
+    EXPECT_EQ(r->name, std::string("cortex"));
+    EXPECT_EQ(r->populations.size(), 2u);
+    EXPECT_EQ(r->connections.size(), 2u);
+    EXPECT_EQ(region_total_size(r), 100);
+    auto exc = region_find_population(r, "exc");
+    ASSERT_TRUE(exc != nullptr);
+    EXPECT_EQ(exc->module.ops, &neuron::lif_ops);
+    auto* lif = static_cast<neuron::LIFNeuron*>(exc->module.impl);
+    EXPECT_NEAR(lif->options.v_thresh(), 0.020, 1e-12);
+    EXPECT_NEAR(lif->options.i_bg(), 300e-12, 1e-20);
+    auto inh = region_find_population(r, "inh");
+    EXPECT_EQ(inh->module.ops, &neuron::izh_ops);
+    EXPECT_NEAR(static_cast<neuron::IzhikevichNeuron*>(inh->module.impl)->options.a(), 0.1, 1e-12);
+    auto& c0 = r->connections[0];
+    EXPECT_EQ(c0->synapse.ops, &synapse::exp_synapse_ops);
+    EXPECT_EQ(c0->connectivity.block_size, 16);
+    EXPECT_EQ(c0->plasticity_rules.size(), 0u);
+    EXPECT_EQ(r->connections[1]->plasticity_rules.size(), 1u);
+    EXPECT_EQ(r->connections[1]->synapse.ops, &synapse::static_synapse_ops);
+    // seeded: the same file gives the same connectivity
+    Region* r2 = config::load_region(path);
+    EXPECT_TRUE(torch::equal(r->connections[0]->connectivity.structural_mask,
+                             r2->connections[0]->connectivity.structural_mask));
+    region_destroy(r2);
+    region_destroy(r);
+    std::remove(path.c_str());
+}
+
+TEST(Config, ErrorsNameTheLine) {
+    auto expect_error = [](const char* body, const char* needle) {
+        // populations on the host (no GPU needed); the line numbers below
+        // count this first line
+        const std::string text = std::string("simulation: {device: cpu}\n") + body;
+        const std::string path = write_tmp("bad.yaml", text.c_str());
+        bool ok = false;
+        try {
+            Region* r = config::load_region(path);
+            region_destroy(r);
+        } catch (const std::runtime_error& e) {
+            ok = std::string(e.what()).find(needle) != std::string::npos;
+            if (!ok) std::printf("    message: %s\n", e.what());
+        }
+        std::remove(path.c_str());
+        EXPECT_TRUE(ok);
+    };
+    expect_error("populations:\n  - name: a\n    model: HH\n    count: 3\n", ":4: unknown neuron model 'HH'");
+    expect_error("populations:\n  - name: a\n    model: LIF\n    count: 3\n    params: {tau_q: 1ms}\n",
+                 "unknown field 'tau_q'");
+    expect_error("populations:\n  - name: a\n    model: LIF\n    count: 3\nconnections:\n  - source: a\n"
+                 "    target: b\n",
+                 "no population 'b'");
+    expect_error("populations:\n  - name: a\n    model: LIF\n    count: 3 apples\n", "unknown unit");
+    expect_error("populations: [1, 2\n", "expected ','");
+    expect_error("a: 1\na: 2\n", "duplicate key 'a'");
 }
 
 NRN_TEST_MAIN()

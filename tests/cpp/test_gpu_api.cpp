@@ -3,6 +3,11 @@
 // test_adex.cpp, test_izhikevich.cpp, tests/plasticity/test_stdp.cpp,
 // tests/integration/test_brunel_network.cpp).  Needs a CUDA GPU.
 #include <nrn/nrn.h>
+#include <nrn/config/config.h>
+
+#include <unistd.h>
+
+#include <cstdio>
 
 #include "nrn_test.h"
 
@@ -309,6 +314,60 @@ TEST(Simulation, RecordersCallbacksAndNoNaN) {
     sim_destroy(sim);
     region_destroy(region);
     neuron::lif_destroy(lif);
+}
+
+// A Simulation from a YAML file (nrn::config::load): populations with
+// synapse channels and STDP, run on the GPU, spikes recorded.
+TEST(Config, LoadAndRunSimulation) {
+    const std::string path = std::string("/tmp/nrn_cfg_sim_") + std::to_string(::getpid()) + ".yaml";
+    FILE* f = std::fopen(path.c_str(), "w");
+    std::fputs(R"(name: yaml_net
+seed: 3
+simulation:
+  dt_fast: 0.1ms
+  dt_slow: 0.1ms
+  duration: 20ms
+populations:
+  - name: exc
+    model: LIF
+    count: 400
+    params: {v_rest: -65mV, v_thresh: -50mV, v_reset: -65mV, tau_m: 20ms, i_bg: 400pA}
+  - name: inh
+    model: LIF
+    count: 100
+    params: {v_rest: -65mV, v_thresh: -50mV, v_reset: -65mV, tau_m: 10ms, i_bg: 400pA}
+connections:
+  - source: exc
+    target: exc
+    probability: 0.1
+    weight: 200pA
+    block_size: 64
+    synapse: exponential
+    synapse_params: {tau_decay: 2ms}
+    plasticity: stdp
+    plasticity_params: {learning_rate: 1e-9, w_max: 400pA}
+  - source: exc
+    target: inh
+    probability: 0.1
+    weight: 200pA
+    block_size: 64
+    synapse: AMPA
+    synapse_params: {tau_rise: 0.5ms, tau_decay: 3ms, e_rev: 0mV}
+  - {source: inh, target: exc, probability: 0.1, weight: -800pA, block_size: 64}
+record:
+  - population: exc
+    variables: [spike]
+)",
+               f);
+    std::fclose(f);
+    Simulation* sim = config::load(path);
+    ASSERT_TRUE(sim != nullptr);
+    sim_run(sim);
+    auto exc = region_find_population(sim->region, "exc");
+    auto sp = sim_get_spikes(sim, exc);
+    EXPECT_GT(sp.size(0), 10);
+    sim_destroy(sim);
+    std::remove(path.c_str());
 }
 
 NRN_TEST_MAIN()

@@ -119,3 +119,110 @@ def test_two_gpus_report_sources_faster_than_their_delay():
     parts = run_partitioned("burst", 240)
     errs = [p["err"] for p in parts]
     assert any(e is not None and "spiked twice within one synaptic delay" in e for e in errs)
+
+
+# --- failure handling (no GPU is faulted: errors are made on the host) ------
+
+def _fail_worker(rank, world, port, scenario, q):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from libnrn_b200 import _native as N
+    from libnrn_b200.engine import Network
+    from libnrn_b200.partition import StepAgreement, share_unique_id
+    nw = None
+    out = {"rank": rank}
+    try:
+        uid = share_unique_id()
+        spec = spec_of("brunel", 60)
+        max_rate = 2000.0 if not (scenario == "layout" and rank == 1) else 1000.0
+        try:
+            nw = Network.from_spec(spec, device=rank, partition=(rank, world, uid, max_rate), comm_timeout=20.0)
+        except N.NrnError as ex:
+            out["build"] = str(ex)
+            q.put(out)
+            return
+        ag = StepAgreement(dist.distributed_c10d._get_default_store(), rank, world, timeout_s=5.0,
+                           prefix=f"nrn/{scenario}")
+        ag.check(0, 30)
+        nw.run(30)
+        nw.sync()
+        if scenario == "fake_error":
+            if rank == 0:
+                N.lib().nrn_comm_fake_async_error(6)   # ncclRemoteError, reported by the next wait
+            try:
+                nw.sync()
+                out["sync"] = "ok"
+            except N.NrnError as ex:
+                out["sync"] = str(ex)
+                try:
+                    nw.run(15)
+                    out["run_after"] = "ok"
+                except N.NrnError as ex2:
+                    out["run_after"] = str(ex2)
+        elif scenario == "leave":
+            if rank == 1:
+                out["left"] = True       # between runs: nothing in flight
+            else:
+                try:
+                    ag.check(30, 30)
+                    out["check"] = "ok"
+                except RuntimeError as ex:
+                    out["check"] = str(ex)
+        q.put(out)
+    except Exception as ex:
+        out["err"] = f"{type(ex).__name__}: {ex}"
+        q.put(out)
+    finally:
+        if nw is not None:
+            nw.close()
+        if scenario == "leave" and rank == 0:
+            import time
+            time.sleep(1.0)
+        dist.destroy_process_group()
+
+
+def run_failure(scenario, world=2):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    procs = [ctx.Process(target=_fail_worker, args=(r, world, port, scenario, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        out = {}
+        for _ in procs:
+            r = q.get(timeout=180)
+            out[r["rank"]] = r
+    finally:
+        for p in procs:
+            p.join(timeout=90)
+            if p.is_alive():
+                p.kill()
+    return out
+
+
+@needs2
+def test_nccl_error_aborts_communicator():
+    out = run_failure("fake_error")
+    assert "communicator aborted" in out[0]["sync"] or "NCCL reported" in out[0]["sync"]
+    assert "aborted" in out[0]["run_after"]
+    assert out[1]["sync"] == "ok"
+
+
+@needs2
+def test_ranks_disagreeing_on_layout_are_refused():
+    out = run_failure("layout")
+    for r in (0, 1):
+        assert "disagree on the spike exchange" in out[r].get("build", ""), out[r]
+
+
+@needs2
+def test_rank_leaving_between_runs_is_found_on_the_host():
+    out = run_failure("leave")
+    assert out[1].get("left")
+    assert "did not reach" in out[0]["check"]
