@@ -451,8 +451,21 @@ typedef struct {
     const float* mod;          /* [nnz] modulatory gain, or NULL            */
 } nrn_proj_desc_t;
 
-/* Fixed in/out-degree connectivity generated on the device; the same draws
- * as the oracle's generator (Philox keyed by (seed; row gid, slot, id)). */
+/* Connectivity generated on the device from Philox counters, so every GPU
+ * of a partition and the host oracle draw the same synapses:
+ *   NRN_GEN_FIXED    fixed in-degree (out_degree 0) or out-degree (1);
+ *   NRN_GEN_ER       every (source, target) pair with probability p, the
+ *                    rule of the reference's random topology
+ *                    (src/connectivity/topology/random.cpp:25-95);
+ *   NRN_GEN_DISTANCE pairs with probability max(exp(-d^2/(2 sigma^2)),
+ *                    min_probability), d the distance of 1D positions
+ *                    i * max_distance / n, the rule of the reference's
+ *                    distance-dependent topology
+ *                    (src/connectivity/topology/distance_dependent.cpp:28-144).
+ * The reference draws these with the torch generator into block-dense
+ * tensors (the nrn:: connect() path keeps that sequence); these draw per
+ * synapse on the device, without the N_src x N_tgt storage. */
+enum { NRN_GEN_FIXED = 0, NRN_GEN_ER = 1, NRN_GEN_DISTANCE = 2 };
 typedef struct {
     int32_t src_pop;
     int32_t tgt_pop;
@@ -465,6 +478,10 @@ typedef struct {
     int32_t dmin, dmax;
     float w_lo, w_span;
     uint64_t seed;
+    int32_t rule;              /* NRN_GEN_*                                  */
+    int32_t pad;
+    double p;                  /* ER probability                             */
+    double sigma, max_distance, min_probability;   /* distance rule          */
 } nrn_gen_desc_t;
 
 NRN_API nrn_status_t nrn_engine_create(nrn_engine** out, int device, double dt, int32_t slow_ratio);

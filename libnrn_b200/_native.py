@@ -126,7 +126,8 @@ class GenDesc(C.Structure):
         ("src_pop", C.c_int32), ("tgt_pop", C.c_int32), ("receptor", C.c_int32), ("out_degree", C.c_int32),
         ("degree", C.c_int32), ("gen_id", C.c_int32), ("col_offset", C.c_int32), ("col_n", C.c_int32),
         ("dmin", C.c_int32), ("dmax", C.c_int32), ("w_lo", C.c_float), ("w_span", C.c_float),
-        ("seed", C.c_uint64),
+        ("seed", C.c_uint64), ("rule", C.c_int32), ("pad", C.c_int32), ("p", C.c_double),
+        ("sigma", C.c_double), ("max_distance", C.c_double), ("min_probability", C.c_double),
     ]
 
 

@@ -17,6 +17,7 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "detmath.cuh"
 #include "rng.cuh"
 
 namespace nrn {
@@ -191,7 +192,150 @@ __global__ void gen_kernel(const GenArgs g, int32_t* src, int32_t* tgt, float* w
     }
 }
 
+// ---------------------------------------------------------------------------
+// Random (Erdos-Renyi) and distance-dependent connectivity, one thread per
+// target row.  Rows are this GPU's targets (population indices lo .. lo +
+// n_rows); sources are the whole source population.
+//   ER: each (source, target) pair with probability p, drawn by geometric
+//       skips over the sources: gap = floor(ln u / ln(1 - p)), u from
+//       Philox(seed; row gid, draw k, gen, ER stream) word 0;
+//   distance-dependent: 1D positions x_s = s L / n_src, x_t = t L / n_tgt
+//       (L = max_distance), p = max(exp(-d^2 / 2 sigma^2), p_min); pair
+//       (t, s) connected iff word (s % 4) of Philox(seed; row gid, s / 4, gen,
+//       distance stream) < floor(p 2^32), sources outside the window where
+//       p < 2^-40 skipped.
+// Delay and weight of a synapse from Philox(seed; row gid, k, gen, delay
+// stream): delay dmin + floor(w0 span / 2^32), weight w_lo + w_span u01(w1),
+// k the synapse's rank in its row.  Autapses are skipped when the source and
+// target populations are the same.  exp and log are detmath's, so the host
+// oracle draws the same synapses.
+constexpr uint32_t kStreamEr = 0x45524E44u;
+constexpr uint32_t kStreamDist = 0x44495354u;
+constexpr uint32_t kStreamSyn = 0x53594E31u;
+
+__device__ __forceinline__ uint32_t prob_threshold(double p) {
+    if (!(p > 0.0)) return 0u;
+    const double t = floor(p * 4294967296.0);
+    return t >= 4294967295.0 ? 0xFFFFFFFFu : static_cast<uint32_t>(t);
+}
+
+// Calls emit(source index, rank in row) for the row's synapses in source order.
+template <class F>
+__device__ void random_row(const RandArgs& a, int32_t r, F&& emit) {
+    const int32_t t = a.tgt_lo + r;                                   // target population index
+    const uint32_t gid = static_cast<uint32_t>(a.tgt_gid_offset + t);
+    const int32_t self = a.same_pop ? t : -1;
+    uint32_t k = 0;
+    if (a.rule == NRN_GEN_ER) {
+        if (a.p <= 0.0) return;
+        int64_t pos = -1;
+        for (uint32_t draw = 0;; ++draw) {
+            int64_t step = 1;
+            if (a.p < 1.0) {
+                const U4 x = philox4x32_10(U4{gid, draw, a.gen_id, kStreamEr}, a.seed);
+                const double u = (static_cast<double>(x.x) + 0.5) * (1.0 / 4294967296.0);
+                double l = det_log(u);
+                if (l > 0.0) l = 0.0;
+                const double gap = floor(l / a.log1mp);
+                if (gap >= static_cast<double>(a.n_src)) break;
+                step = 1 + static_cast<int64_t>(gap);
+            }
+            pos += step;
+            if (pos >= a.n_src) break;
+            if (pos != self) emit(static_cast<int32_t>(pos), k++);
+        }
+        return;
+    }
+    // distance-dependent
+    const double xt = static_cast<double>(t) * a.spacing_tgt;
+    int64_t s0 = 0, s1 = a.n_src;
+    if (a.half_window >= 0.0 && a.spacing_src > 0.0) {
+        const double lo = floor((xt - a.half_window) / a.spacing_src);
+        const double hi = ceil((xt + a.half_window) / a.spacing_src) + 1.0;
+        s0 = lo < 0.0 ? 0 : static_cast<int64_t>(lo);
+        s1 = hi > static_cast<double>(a.n_src) ? a.n_src : static_cast<int64_t>(hi);
+    }
+    U4 x{0u, 0u, 0u, 0u};
+    for (int64_t s = s0; s < s1; ++s) {
+        if ((s & 3) == 0 || s == s0)
+            x = philox4x32_10(U4{gid, static_cast<uint32_t>(s >> 2), a.gen_id, kStreamDist}, a.seed);
+        if (s == self) continue;
+        const double d = xt - static_cast<double>(s) * a.spacing_src;
+        double p = det_exp_neg((d * d) * a.inv_two_sigma_sq);
+        if (p < a.p_min) p = a.p_min;
+        const uint32_t w = (s & 3) == 0 ? x.x : (s & 3) == 1 ? x.y : (s & 3) == 2 ? x.z : x.w;
+        if (w < prob_threshold(p)) emit(static_cast<int32_t>(s), k++);
+    }
+}
+
+__global__ void random_count(const RandArgs a, int64_t* counts) {
+    for (int32_t r = blockIdx.x * blockDim.x + threadIdx.x; r < a.n_rows; r += gridDim.x * blockDim.x) {
+        int64_t c = 0;
+        random_row(a, r, [&](int32_t, uint32_t) { ++c; });
+        counts[r] = c;
+    }
+}
+
+__global__ void random_fill(const RandArgs a, const int64_t* offsets, int32_t* src, int32_t* tgt, float* w,
+                            uint8_t* delay) {
+    const uint32_t span = static_cast<uint32_t>(a.dmax - a.dmin + 1);
+    for (int32_t r = blockIdx.x * blockDim.x + threadIdx.x; r < a.n_rows; r += gridDim.x * blockDim.x) {
+        int64_t o = offsets[r];
+        const uint32_t gid = static_cast<uint32_t>(a.tgt_gid_offset + a.tgt_lo + r);
+        random_row(a, r, [&](int32_t sidx, uint32_t k) {
+            const U4 y = philox4x32_10(U4{gid, k, a.gen_id, kStreamSyn}, a.seed);
+            src[o] = sidx;
+            tgt[o] = r;
+            delay[o] = static_cast<uint8_t>(static_cast<uint32_t>(a.dmin) + __umulhi(y.x, span));
+            w[o] = a.w_lo + a.w_span * u01(y.y);
+            ++o;
+        });
+    }
+}
+
 }  // namespace
+
+nrn_status_t generate_random(const RandArgs& a, DevSynList* out, cudaStream_t s) {
+    int64_t* counts = nullptr;
+    void* tmp = nullptr;
+    size_t tmp_bytes = 0;
+    nrn_status_t st = NRN_OK;
+    *out = DevSynList{};
+    NRN_TRY(dalloc(&counts, static_cast<size_t>(a.n_rows) + 1));
+    auto fin = [&](nrn_status_t r) {
+        dfree(counts);
+        if (tmp) cudaFree(tmp);
+        if (r != NRN_OK) out->release();
+        return r;
+    };
+    if (cudaMemsetAsync(counts, 0, (static_cast<size_t>(a.n_rows) + 1) * sizeof(int64_t), s) != cudaSuccess)
+        return fin(cuda_fail(cudaGetLastError(), "generator counts"));
+    if (a.n_rows > 0) {
+        random_count<<<grid_for(a.n_rows, 128), 128, 0, s>>>(a, counts);
+        if (cudaGetLastError() != cudaSuccess) return fin(cuda_fail(cudaGetLastError(), "random_count"));
+    }
+    // exclusive scan in place: counts -> row offsets, counts[n_rows] = total
+    if (cub::DeviceScan::ExclusiveSum(nullptr, tmp_bytes, counts, counts, static_cast<int64_t>(a.n_rows) + 1, s) !=
+            cudaSuccess ||
+        cudaMalloc(&tmp, tmp_bytes) != cudaSuccess ||
+        cub::DeviceScan::ExclusiveSum(tmp, tmp_bytes, counts, counts, static_cast<int64_t>(a.n_rows) + 1, s) !=
+            cudaSuccess)
+        return fin(cuda_fail(cudaGetLastError(), "generator scan"));
+    int64_t total = 0;
+    if (cudaMemcpyAsync(&total, counts + a.n_rows, sizeof(int64_t), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess)
+        return fin(cuda_fail(cudaGetLastError(), "generator total"));
+    out->n = total;
+    if ((st = dalloc(&out->src, total)) != NRN_OK || (st = dalloc(&out->tgt, total)) != NRN_OK ||
+        (st = dalloc(&out->w, total)) != NRN_OK || (st = dalloc(&out->delay, total)) != NRN_OK)
+        return fin(st);
+    if (total > 0 && a.n_rows > 0) {
+        random_fill<<<grid_for(a.n_rows, 128), 128, 0, s>>>(a, counts, out->src, out->tgt, out->w, out->delay);
+        if (cudaGetLastError() != cudaSuccess) return fin(cuda_fail(cudaGetLastError(), "random_fill"));
+    }
+    if (cudaStreamSynchronize(s) != cudaSuccess) return fin(cuda_fail(cudaGetLastError(), "generator"));
+    return fin(NRN_OK);
+}
 
 int sm_count_current() {
     int dev = 0, n = 0;

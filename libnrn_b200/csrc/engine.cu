@@ -29,6 +29,7 @@
 #include <nccl.h>
 
 #include "common.cuh"
+#include "detmath.cuh"
 #include "internal.h"
 
 namespace nrn {
@@ -1079,6 +1080,45 @@ nrn_status_t nrn_engine_generate_projection(nrn_engine* e, const nrn_gen_desc_t*
     NRN_TRY(check_receptor(e, g->tgt_pop, g->receptor));
     const EnginePop& ps = e->pops[g->src_pop];
     const EnginePop& pt = e->pops[g->tgt_pop];
+    if (g->rule == NRN_GEN_ER || g->rule == NRN_GEN_DISTANCE) {
+        NRN_CHECK_ARG(g->rule != NRN_GEN_ER || (g->p >= 0.0 && g->p <= 1.0), "ER probability outside [0, 1]");
+        NRN_CHECK_ARG(g->rule != NRN_GEN_DISTANCE ||
+                          (g->sigma > 0.0 && g->max_distance > 0.0 && g->min_probability >= 0.0 &&
+                           g->min_probability <= 1.0),
+                      "distance rule: sigma and max_distance must be positive, min_probability in [0, 1]");
+        RandArgs a;
+        a.rule = g->rule;
+        a.seed = g->seed;
+        a.gen_id = static_cast<uint32_t>(g->gen_id);
+        a.n_src = ps.n_global;
+        a.n_tgt = pt.n_global;
+        a.tgt_lo = pt.lo;
+        a.n_rows = pt.d.n;
+        a.tgt_gid_offset = pt.d.gid_offset;
+        a.same_pop = g->src_pop == g->tgt_pop;
+        a.p = g->p;
+        a.log1mp = g->p < 1.0 ? det_log(1.0 - g->p) : 0.0;
+        a.spacing_src = ps.n_global > 1 ? g->max_distance / ps.n_global : 0.0;
+        a.spacing_tgt = pt.n_global > 1 ? g->max_distance / pt.n_global : 0.0;
+        a.inv_two_sigma_sq = g->rule == NRN_GEN_DISTANCE ? 1.0 / (2.0 * g->sigma * g->sigma) : 0.0;
+        a.p_min = g->min_probability;
+        // beyond sigma * sqrt(2 ln 2^40) the Gaussian is below 2^-40: no pair
+        // there can pass the 32-bit threshold
+        a.half_window = g->min_probability > 0.0 ? -1.0 : g->sigma * std::sqrt(2.0 * 40.0 * kLn2);
+        a.dmin = g->dmin;
+        a.dmax = g->dmax;
+        a.w_lo = g->w_lo;
+        a.w_span = g->w_span;
+        DevSynList list;
+        NRN_TRY(generate_random(a, &list, e->stream));
+        nrn_status_t st = add_projection_dev(e, g->src_pop, g->tgt_pop, g->receptor, list.src, list.tgt, list.w,
+                                             list.delay, nullptr, list.n, false, g->dmin, g->dmax, id);
+        e->wait_stream();
+        list.release();
+        if (st == NRN_OK && nnz) *nnz = e->projs.back().csr.nnz;
+        return st;
+    }
+    NRN_CHECK_ARG(g->rule == NRN_GEN_FIXED, "unknown connectivity rule");
     // sources over the whole population, targets on this rank
     const int32_t src_gid = ps.d.gid_offset, tgt_gid = pt.d.gid_offset;
     GenArgs a{};

@@ -90,6 +90,43 @@ struct GenArgs {
 };
 nrn_status_t generate(const GenArgs& g, int32_t* src, int32_t* tgt, float* w, uint8_t* delay, cudaStream_t s);
 
+// Random (Erdos-Renyi) and distance-dependent connectivity (connect.cu).
+struct RandArgs {
+    int32_t rule = 0;                 // NRN_GEN_ER or NRN_GEN_DISTANCE
+    uint64_t seed = 0;
+    uint32_t gen_id = 0;
+    int32_t n_src = 0;                // source population size
+    int32_t n_tgt = 0;                // target population size
+    int32_t tgt_lo = 0, n_rows = 0;   // this GPU's targets (population indices)
+    int32_t tgt_gid_offset = 0;       // global id of target 0
+    int32_t same_pop = 0;             // skip autapses
+    double p = 0.0, log1mp = 0.0;     // ER: p and det_log(1 - p)
+    double spacing_src = 0.0, spacing_tgt = 0.0, inv_two_sigma_sq = 0.0, p_min = 0.0;
+    double half_window = -1.0;        // distance rule: window half width (< 0: all sources)
+    int32_t dmin = 1, dmax = 1;
+    float w_lo = 0.0f, w_span = 0.0f;
+};
+// A synapse list in device memory (source and target population indices,
+// target relative to this GPU's first).
+struct DevSynList {
+    int64_t n = 0;
+    int32_t* src = nullptr;
+    int32_t* tgt = nullptr;
+    float* w = nullptr;
+    uint8_t* delay = nullptr;
+    void release() {
+        if (src) cudaFree(src);
+        if (tgt) cudaFree(tgt);
+        if (w) cudaFree(w);
+        if (delay) cudaFree(delay);
+        src = tgt = nullptr;
+        w = nullptr;
+        delay = nullptr;
+        n = 0;
+    }
+};
+nrn_status_t generate_random(const RandArgs& a, DevSynList* out, cudaStream_t s);
+
 int sm_count_current();
 
 // Neuron updates of several populations; populations of the same model and

@@ -133,11 +133,17 @@ class Network:
         self.projs.append({"src": src, "tgt": tgt, "nnz": d.nnz})
         return qid.value
 
-    def generate_projection(self, src: int, tgt: int, *, out_degree: bool, degree: int, gen_id: int,
+    def generate_projection(self, src: int, tgt: int, *, out_degree: bool = False, degree: int = 0, gen_id: int,
                             dmin: int, dmax: int, w_lo: float, w_span: float, seed: int,
-                            cols=None, receptor="current") -> int:
+                            cols=None, receptor="current", rule: str = "fixed", p: float = 0.0,
+                            sigma: float = 0.0, max_distance: float = 0.0, min_probability: float = 0.0) -> int:
+        """Connectivity generated on the device (nrn_gen_desc_t): rule
+        "fixed" (in/out-degree), "er" (probability p) or "distance"."""
         g = N.GenDesc()
         g.src_pop, g.tgt_pop, g.receptor = src, tgt, N.RECEPTOR[receptor]
+        g.rule = {"fixed": 0, "er": 1, "distance": 2}[rule]
+        g.p, g.sigma, g.max_distance, g.min_probability = float(p), float(sigma), float(max_distance), \
+            float(min_probability)
         g.out_degree, g.degree, g.gen_id = int(out_degree), degree, gen_id
         g.col_offset, g.col_n = cols if cols is not None else (0, 0)
         g.dmin, g.dmax, g.w_lo, g.w_span, g.seed = dmin, dmax, w_lo, w_span, seed
@@ -334,10 +340,13 @@ class Network:
         for q in spec["projs"]:
             g = q["gen"]
             cols = (0, spec["n_total"]) if g.get("cols") == "all" else None
+            rule = g["mode"] if g["mode"] in ("er", "distance") else "fixed"
             qid = nw.generate_projection(q["src"], q["tgt"], out_degree=g["mode"] == "out",
-                                         degree=g["degree"], gen_id=g["id"], dmin=g["dmin"], dmax=g["dmax"],
-                                         w_lo=g["w_lo"], w_span=g["w_span"], seed=spec["seed"], cols=cols,
-                                         receptor=q["receptor"])
+                                         degree=g.get("degree", 0), gen_id=g["id"], dmin=g["dmin"],
+                                         dmax=g["dmax"], w_lo=g["w_lo"], w_span=g["w_span"], seed=spec["seed"],
+                                         cols=cols, receptor=q["receptor"], rule=rule, p=g.get("p", 0.0),
+                                         sigma=g.get("sigma", 0.0), max_distance=g.get("max_distance", 0.0),
+                                         min_probability=g.get("min_probability", 0.0))
             if q.get("plastic"):
                 nw.set_stdp(qid, q["stdp"])
         if spike_stats:

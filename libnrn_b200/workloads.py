@@ -13,6 +13,10 @@ Izhikevich, as in the reference's option structs (include/nrn/neuron/options.h).
 Generator rule ``gen`` of a projection:
   mode    "in"  : every target draws ``degree`` sources (fixed in-degree)
           "out" : every source draws ``degree`` targets (fixed out-degree)
+          "er"  : every pair with probability ``p``
+          "distance": every pair with probability max(exp(-d^2/(2 sigma^2)),
+                  min_probability), d the distance of 1D positions
+                  i * max_distance / n
   cols    global id range (offset, n) the draws pick from; defaults to the
           source population ("in") or the target population ("out").
           Draws outside the target population are discarded ("out" mode over
@@ -163,6 +167,28 @@ def izhikevich(n: int = 1_000_000, k_out: int = 1_000, *, dt: float = 1e-3, step
             })
             gid += 1
     return _offsets(spec)
+
+
+def random_network(n_exc: int = 4_000, n_inh: int = 1_000, *, rule: str = "er", p: float = 0.02,
+                   sigma: float = 50e-6, max_distance: float = 1e-3, min_probability: float = 0.0,
+                   delay: int = 15, dt: float = 1e-4, steps: int = 1_000, g: float = 5.0,
+                   j_psp: float = 0.1e-3, seed: int = 5) -> dict:
+    """The Brunel LIF populations connected by the reference's other
+    topologies, generated on the device: Erdos-Renyi with probability p
+    (rule "er", src/connectivity/topology/random.cpp) or the 1D Gaussian
+    distance rule (rule "distance", positions i * max_distance / n,
+    src/connectivity/topology/distance_dependent.cpp).  Weights and drive
+    as in brunel()."""
+    spec = brunel(n_exc, n_inh, 1, 1, delay=delay, dt=dt, steps=steps, g=g, j_psp=j_psp, seed=seed)
+    for q in spec["projs"]:
+        gen = q["gen"]
+        gen["mode"] = rule
+        gen.pop("degree", None)
+        if rule == "er":
+            gen["p"] = p
+        else:
+            gen.update(sigma=sigma, max_distance=max_distance, min_probability=min_probability)
+    return spec
 
 
 def scaled(spec: dict, **over) -> dict:

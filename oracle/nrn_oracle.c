@@ -517,3 +517,107 @@ ORC_EXPORT void orc_philox(uint64_t seed, uint32_t c0, uint32_t c1, uint32_t c2,
 ORC_EXPORT float orc_normal_from_words(uint32_t a, uint32_t b) {
     return orc_normal(orc_u01(a), orc_u01(b));
 }
+
+/* ------------------------------------------------------------------------ */
+/* Random and distance-dependent connectivity, restating the rules of the   */
+/* reference's random (src/connectivity/topology/random.cpp:25-95: each     */
+/* pair with probability p, autapses removed) and distance-dependent        */
+/* (src/connectivity/topology/distance_dependent.cpp:28-144: 1D positions   */
+/* i * L / n, p = max(exp(-d^2 / 2 sigma^2), p_min)) topologies with the    */
+/* Philox draws of the device generators: per target row g (global id),     */
+/*   ER: geometric skips, gap = floor(ln u / ln(1 - p)),                    */
+/*       u = (Philox(seed; g, draw, gen, ER)[0] + 0.5) / 2^32;              */
+/*   distance: pair (t, s) iff Philox(seed; g, s/4, gen, DIST)[s%4]         */
+/*       < floor(p 2^32);                                                    */
+/*   delay and weight of the k-th synapse of the row from                   */
+/*       Philox(seed; g, k, gen, SYN): dmin + (w0 * span >> 32),            */
+/*       w_lo + w_span * u01(w1).                                            */
+/* Rows are target population indices [tgt_lo, tgt_lo + n_rows); synapses   */
+/* are emitted row by row, sources ascending.  Returns the count (outputs   */
+/* may be NULL to count).                                                    */
+/* ------------------------------------------------------------------------ */
+#define ORC_STREAM_ER 0x45524E44u
+#define ORC_STREAM_DIST 0x44495354u
+#define ORC_STREAM_SYN 0x53594E31u
+
+static inline uint32_t orc_prob_threshold(double p) {
+    if (!(p > 0.0)) return 0u;
+    double t = floor(p * 4294967296.0);
+    return t >= 4294967295.0 ? 0xFFFFFFFFu : (uint32_t)t;
+}
+
+ORC_EXPORT int64_t orc_gen_random(int rule, uint64_t seed, uint32_t gen, int32_t n_src, int32_t n_tgt,
+                                  int32_t tgt_lo, int32_t n_rows, int32_t tgt_gid_offset, int same_pop,
+                                  double p, double sigma, double max_distance, double p_min,
+                                  int32_t dmin, int32_t dmax, float w_lo, float w_span,
+                                  int32_t* out_src, int32_t* out_tgt, float* out_w, uint8_t* out_delay) {
+    int64_t e = 0;
+    uint32_t span = (uint32_t)(dmax - dmin + 1);
+    double log1mp = p < 1.0 ? orc_log(1.0 - p) : 0.0;
+    double sp_s = n_src > 1 ? max_distance / n_src : 0.0, sp_t = n_tgt > 1 ? max_distance / n_tgt : 0.0;
+    double inv2s2 = rule == 2 ? 1.0 / (2.0 * sigma * sigma) : 0.0;
+    for (int32_t r = 0; r < n_rows; ++r) {
+        int32_t t = tgt_lo + r;
+        uint32_t g = (uint32_t)(tgt_gid_offset + t);
+        int32_t self = same_pop ? t : -1;
+        uint32_t k = 0;
+        /* emits source s as the row's k-th synapse */
+#define ORC_EMIT(s)                                                              \
+    do {                                                                         \
+        if (out_src) {                                                           \
+            uint32_t y[4];                                                       \
+            y[0] = g; y[1] = k; y[2] = gen; y[3] = ORC_STREAM_SYN;               \
+            orc_philox4x32_10(y, (uint32_t)seed, (uint32_t)(seed >> 32));        \
+            out_src[e] = (s);                                                    \
+            out_tgt[e] = r;                                                      \
+            out_delay[e] = (uint8_t)((uint32_t)dmin + (uint32_t)(((uint64_t)y[0] * span) >> 32)); \
+            out_w[e] = w_lo + w_span * orc_u01(y[1]);                            \
+        }                                                                        \
+        ++e;                                                                     \
+        ++k;                                                                     \
+    } while (0)
+        if (rule == 1) {
+            if (!(p > 0.0)) continue;
+            int64_t pos = -1;
+            for (uint32_t draw = 0;; ++draw) {
+                int64_t step = 1;
+                if (p < 1.0) {
+                    uint32_t x[4] = {g, draw, gen, ORC_STREAM_ER};
+                    orc_philox4x32_10(x, (uint32_t)seed, (uint32_t)(seed >> 32));
+                    double u = ((double)x[0] + 0.5) * (1.0 / 4294967296.0);
+                    double l = orc_log(u);
+                    if (l > 0.0) l = 0.0;
+                    double gap = floor(l / log1mp);
+                    if (gap >= (double)n_src) break;
+                    step = 1 + (int64_t)gap;
+                }
+                pos += step;
+                if (pos >= n_src) break;
+                if (pos != self) ORC_EMIT((int32_t)pos);
+            }
+        } else {
+            double xt = (double)t * sp_t;
+            int64_t s0 = 0, s1 = n_src;
+            if (!(p_min > 0.0) && sp_s > 0.0) {
+                double hw = sigma * sqrt(2.0 * 40.0 * 6.93147180559945309417e-01);
+                double lo = floor((xt - hw) / sp_s), hi = ceil((xt + hw) / sp_s) + 1.0;
+                s0 = lo < 0.0 ? 0 : (int64_t)lo;
+                s1 = hi > (double)n_src ? n_src : (int64_t)hi;
+            }
+            uint32_t x[4] = {0, 0, 0, 0};
+            for (int64_t s = s0; s < s1; ++s) {
+                if ((s & 3) == 0 || s == s0) {
+                    x[0] = g; x[1] = (uint32_t)(s >> 2); x[2] = gen; x[3] = ORC_STREAM_DIST;
+                    orc_philox4x32_10(x, (uint32_t)seed, (uint32_t)(seed >> 32));
+                }
+                if (s == self) continue;
+                double d = xt - (double)s * sp_s;
+                double pp = orc_exp_neg((d * d) * inv2s2);
+                if (pp < p_min) pp = p_min;
+                if (x[s & 3] < orc_prob_threshold(pp)) ORC_EMIT((int32_t)s);
+            }
+        }
+#undef ORC_EMIT
+    }
+    return e;
+}

@@ -141,6 +141,9 @@ def _lib(which: str):
             lib.orc_drive_values.argtypes = [C.c_int, C.c_double, C.c_double, C.c_uint64,
                                              C.c_int32, C.c_int32, C.c_int32, C.c_void_p]
             lib.orc_philox.argtypes = [C.c_uint64] + [C.c_uint32] * 4 + [C.c_void_p]
+            lib.orc_gen_random.restype = C.c_int64
+            lib.orc_gen_random.argtypes = [C.c_int, C.c_uint64, C.c_uint32] + [C.c_int32] * 5 + [C.c_int] + \
+                [C.c_double] * 4 + [C.c_int32, C.c_int32, C.c_float, C.c_float] + [C.c_void_p] * 4
             lib.orc_normal_from_words.restype = C.c_float
             lib.orc_normal_from_words.argtypes = [C.c_uint32, C.c_uint32]
         else:
@@ -305,6 +308,27 @@ def gen_fixed_degree(seed: int, gen: int, n_src: int, src_offset: int, n_tgt: in
     w = np.zeros(total, np.float32)
     d = np.zeros(total, np.uint8)
     lib.orc_gen_fixed_degree(*args, s.ctypes.data, t.ctypes.data, w.ctypes.data, d.ctypes.data)
+    return s, t, w, d
+
+
+def gen_random(rule: str, seed: int, gen: int, n_src: int, n_tgt: int, tgt_gid_offset: int, *,
+               same_pop: bool, p: float = 0.0, sigma: float = 0.0, max_distance: float = 0.0,
+               min_probability: float = 0.0, dmin: int = 1, dmax: int = 1, w_lo: float = 1.0,
+               w_span: float = 0.0, keep=None):
+    """Random ("er") or distance-dependent ("distance") synapse list, rows =
+    target population indices keep = (lo, n) (default all), in row order;
+    targets relative to lo."""
+    lo, nr = keep if keep is not None else (0, n_tgt)
+    lib = _lib("oracle")
+    args = ({"er": 1, "distance": 2}[rule], seed, gen, n_src, n_tgt, lo, nr, tgt_gid_offset, int(same_pop),
+            float(p), float(sigma), float(max_distance), float(min_probability), dmin, dmax, float(w_lo),
+            float(w_span))
+    total = lib.orc_gen_random(*args, None, None, None, None)
+    s = np.zeros(total, np.int32)
+    t = np.zeros(total, np.int32)
+    w = np.zeros(total, np.float32)
+    d = np.zeros(total, np.uint8)
+    lib.orc_gen_random(*args, s.ctypes.data, t.ctypes.data, w.ctypes.data, d.ctypes.data)
     return s, t, w, d
 
 

@@ -345,6 +345,33 @@ static inline float orc_cond_current(float I, float* ge, float* gi, float in_e,
     return r;
 }
 
+/* exp(-x) and log(u) that give the same bits on every platform (the
+ * device generators use the same method): only IEEE double +, -, *, / and
+ * exact scaling by powers of two.  exp(-x): Cody and Waite's reduction
+ * x = k ln2 + r (ln2 split into an exact high part and a low part), then
+ * 22 Taylor terms of exp(-r); log(u): u = m 2^e, ln m = 2 atanh((m-1)/(m+1))
+ * by its series to the 45th power, plus e ln2. */
+static inline double orc_exp_neg(double x) {
+    if (!(x > 0.0)) return 1.0;
+    if (x > 745.0) return 0.0;
+    const double lh = 6.93147180369123816490e-01, ll = 1.90821492927058770002e-10;
+    const double k = floor(x / 6.93147180559945309417e-01);
+    const double r = (x - k * lh) - k * ll;
+    double s = 1.0;
+    for (int i = 22; i >= 1; --i) s = 1.0 - (r / (double)i) * s;
+    return ldexp(s, -(int)k);
+}
+
+static inline double orc_log(double u) {
+    int e = 0;
+    const double m = frexp(u, &e);
+    const double z = (m - 1.0) / (m + 1.0);
+    const double z2 = z * z;
+    double s = 0.0;
+    for (int i = 45; i >= 3; i -= 2) s = (s + 1.0 / (double)i) * z2;
+    return 2.0 * z * (1.0 + s) + (double)e * 6.93147180559945309417e-01;
+}
+
 /* One synapse channel of one neuron (see ORC_SYN_*): returns I plus the
  * channel's current; s (decay state) and r (rise state) updated. */
 static inline float orc_chan_current(int kind, float I, float* s, float* r, float in, float dec_rise,

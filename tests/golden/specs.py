@@ -20,6 +20,7 @@ def gen_args(spec: dict, q: dict):
     """Arguments of the fixed-degree generator for projection q."""
     ps, pt = spec["pops"][q["src"]], spec["pops"][q["tgt"]]
     g = q["gen"]
+    assert g["mode"] in ("in", "out"), "random rules: gen_lists"
     out = g["mode"] == "out"
     if out:
         if g.get("cols") == "all":
@@ -34,6 +35,20 @@ def gen_args(spec: dict, q: dict):
     return args, kw
 
 
+def gen_lists(spec: dict, q: dict):
+    """The synapse list of projection q drawn by the oracle's generator of
+    its rule (fixed degree, Erdos-Renyi or distance-dependent)."""
+    g = q["gen"]
+    if g["mode"] in ("er", "distance"):
+        ps, pt = spec["pops"][q["src"]], spec["pops"][q["tgt"]]
+        return O.gen_random(g["mode"], spec["seed"], g["id"], ps["n"], pt["n"], pt["offset"],
+                            same_pop=q["src"] == q["tgt"], p=g.get("p", 0.0), sigma=g.get("sigma", 0.0),
+                            max_distance=g.get("max_distance", 0.0), min_probability=g.get("min_probability", 0.0),
+                            dmin=g["dmin"], dmax=g["dmax"], w_lo=g["w_lo"], w_span=g["w_span"])
+    args, kw = gen_args(spec, q)
+    return O.gen_fixed_degree(*args, **kw)
+
+
 def realize(spec: dict, *, steps=None, trace_ids=None, dyadic_bits=None) -> dict:
     """dyadic_bits=k rounds every weight to a multiple of 2^-k, so that sums
     of a few weights are exact in fp32 and independent of summation order."""
@@ -45,8 +60,7 @@ def realize(spec: dict, *, steps=None, trace_ids=None, dyadic_bits=None) -> dict
                             "drive": p.get("drive"), "cond": p.get("cond"),
                             "init_v": arr["init_v"], "init_aux": arr["init_aux"], "hp": arr["hp"]})
     for q in spec["projs"]:
-        args, kw = gen_args(spec, q)
-        s, t, w, d = O.gen_fixed_degree(*args, **kw)
+        s, t, w, d = gen_lists(spec, q)
         if dyadic_bits is not None:
             w = (np.round(w.astype(np.float64) * 2.0 ** dyadic_bits) / 2.0 ** dyadic_bits).astype(np.float32)
         net["projs"].append({"src": q["src"], "tgt": q["tgt"], "receptor": q["receptor"],

@@ -154,3 +154,41 @@ def test_long_run_statistics_match_oracle():
     rb, cb = stats(b["spike_step"], b["spike_id"], spec["n_total"], 3000, spec["dt"])
     assert abs(rb - ra) <= 0.02 * ra
     assert abs(cb - ca) <= 0.02 * ca
+
+
+@pytest.mark.parametrize("rule", ["er", "distance"])
+def test_random_connectivity_matches_oracle_generator(rule):
+    """Erdos-Renyi and distance-dependent connectivity drawn on the device
+    equals the oracle generator's synapse for synapse (engine order: by
+    source and delay, ties in generation order)."""
+    import specs as S
+    from libnrn_b200 import workloads as W
+    spec = W.random_network(3_000, 750, rule=rule, p=0.02, sigma=20e-6, max_distance=1e-3, steps=1)
+    for q in spec["projs"]:
+        q["gen"]["dmin"], q["gen"]["dmax"], q["gen"]["w_span"] = 10, 20, abs(q["gen"]["w_lo"])
+    nw = Network.from_spec(spec, record=False)
+    for qi, q in enumerate(spec["projs"]):
+        s, t, w, d = S.gen_lists(spec, q)
+        order = np.lexsort((d, s))
+        got = nw.weights(qi)
+        assert len(got) == len(w) > 1000
+        assert np.array_equal(got, w[order])
+    nw.close()
+
+
+def test_random_network_runs_like_oracle():
+    """A network on device-drawn ER connectivity: the engine's spike trains
+    equal the oracle's on the same lists (deterministic delivery)."""
+    import specs as S
+    from libnrn_b200 import workloads as W
+    spec = W.random_network(2_000, 500, rule="er", p=0.04, steps=300)
+    net = S.realize(spec)
+    want = O.run_oracle(net)
+    nw = Network.from_spec(spec, record=True)
+    nw.close()
+    nw = Network.from_net(net, deterministic=True)
+    nw.run(300)
+    st, gid = nw.raster()
+    nw.close()
+    assert len(gid) > 500
+    assert np.array_equal(st, want["spike_step"]) and np.array_equal(gid, want["spike_id"])

@@ -114,3 +114,22 @@ def test_oracle_synapse_channel_equations():
     net = S.synapse_channel_net(steps=50)
     a = O.run_oracle(net)
     assert len(a["spike_id"]) > 0
+
+
+def test_oracle_random_generators_follow_their_rules():
+    """ER: the connection count is binomial(n_src n_tgt, p) within 5 sigma,
+    no autapses; distance rule: the fraction connected at distance d follows
+    exp(-d^2 / 2 sigma^2)."""
+    n = 2000
+    s, t, w, d = O.gen_random("er", 9, 0, n, n, 0, same_pop=True, p=0.01, dmin=2, dmax=4)
+    m = n * (n - 1)
+    assert abs(len(s) - 0.01 * m) <= 5 * np.sqrt(m * 0.01 * 0.99)
+    assert not np.any(s == t) and d.min() == 2 and d.max() == 4
+    sig, L = 10e-6, 1e-3
+    s, t, w, d = O.gen_random("distance", 9, 1, n, n, 0, same_pop=False, sigma=sig, max_distance=L)
+    sp = L / n
+    dist = np.abs(s - t) * sp
+    for k in (0, 10, 20, 30):
+        frac = np.count_nonzero(np.abs(s - t) == k) / (2 * n if k else n)
+        assert abs(frac - np.exp(-(k * sp) ** 2 / (2 * sig ** 2))) < 0.06
+    assert dist.max() < 10 * sig
