@@ -568,6 +568,17 @@ NRN_API nrn_status_t nrn_engine_raster(nrn_engine* e, int32_t* step, int32_t* gi
  * address (cudaGetSymbolAddress) and should come before any stream capture. */
 NRN_API nrn_status_t nrn_engine_raster_noalloc(nrn_engine* e, int32_t* step, int32_t* gid, int64_t cap,
                                                int64_t* n);
+/* State probes (the reference's state recorder, src/monitor/state_recorder.cpp:41-58,
+ * which clones the state to the host at every recorded step): after every
+ * step's neuron update, variable `var` (NRN_VAR_*) of this GPU's neurons of
+ * population `pop` is copied into row (step % depth) of `ring`, a caller's
+ * device array [depth][n], inside the engine's step graphs.  The caller
+ * reads the rows at most depth steps later.  Adding or clearing probes
+ * recaptures the graphs. */
+enum { NRN_VAR_V = 0, NRN_VAR_AUX = 1, NRN_VAR_REFRACTORY = 2, NRN_VAR_SPIKE = 3, NRN_VAR_ISYN = 4 };
+NRN_API nrn_status_t nrn_engine_add_probe(nrn_engine* e, int32_t pop, int32_t var, float* ring, int32_t depth,
+                                          int32_t* id);
+NRN_API nrn_status_t nrn_engine_clear_probes(nrn_engine* e);
 /* Weights of a projection in the order the synapses were given, into a
  * device array of nnz floats (enqueued on the engine stream). */
 NRN_API nrn_status_t nrn_engine_weights_device(nrn_engine* e, int32_t proj, float* out, int64_t n);

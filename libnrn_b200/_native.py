@@ -39,7 +39,7 @@ EXPORTS = [
     "nrn_engine_checkpoint_load", "nrn_engine_enable_spike_stats", "nrn_engine_spike_stats",
     "nrn_engine_spike_stats_reset", "nrn_engine_set_comm_timeout", "nrn_comm_bounded_wait",
     "nrn_comm_fake_async_error", "nrn_engine_profile_kernels", "nrn_engine_add_synapse_channel",
-    "nrn_engine_set_deterministic",
+    "nrn_engine_set_deterministic", "nrn_engine_add_probe", "nrn_engine_clear_probes",
 ]
 
 
@@ -194,6 +194,8 @@ def lib() -> C.CDLL:
             "nrn_comm_fake_async_error": [i32],
             "nrn_engine_add_synapse_channel": [vp, i32, C.POINTER(SynDesc), C.POINTER(i32)],
             "nrn_engine_set_deterministic": [vp, i32],
+            "nrn_engine_add_probe": [vp, i32, i32, vp, i32, C.POINTER(i32)],
+            "nrn_engine_clear_probes": [vp],
             "nrn_engine_profile_kernels": [vp, i64, C.POINTER(C.c_double), C.POINTER(i64)],
         }
         for name, args in sig.items():

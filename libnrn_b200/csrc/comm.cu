@@ -16,6 +16,7 @@
 #include <atomic>
 #include <chrono>
 #include <cstring>
+#include <memory>
 #include <string>
 #include <thread>
 
@@ -81,27 +82,41 @@ nrn_status_t comm_abort(ncclComm_t* c) {
 }
 
 nrn_status_t comm_init(ncclComm_t* out, int world, const uint8_t id[128], int rank, double timeout_s) {
+    // The communicator is blocking (its collectives are captured in CUDA
+    // graphs like any kernel launch); its set-up, which waits for every
+    // rank, runs on a helper thread so that the wait is bounded.  A set-up
+    // that times out is left to finish or fail on its own: its thread and
+    // communicator are abandoned.
+    struct Job {
+        ncclComm_t comm = nullptr;
+        ncclResult_t r = ncclSuccess;
+        std::atomic<bool> done{false};
+    };
+    auto job = std::make_shared<Job>();
     ncclUniqueId u;
     static_assert(sizeof(u) == 128, "NCCL unique id size");
     std::memcpy(&u, id, sizeof(u));
-    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
-    cfg.blocking = 0;
-    ncclComm_t c = nullptr;
-    const ncclResult_t r = ncclCommInitRankConfig(&c, world, u, rank, &cfg);
-    if (r != ncclSuccess && r != ncclInProgress) {
-        if (c) ncclCommAbort(c);
-        return fail(NRN_ERR_COMM, std::string("ncclCommInitRankConfig: ") + ncclGetErrorString(r));
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::thread([job, u, world, rank, dev] {
+        cudaSetDevice(dev);
+        ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+        cfg.blocking = 1;
+        ncclComm_t c = nullptr;
+        job->r = ncclCommInitRankConfig(&c, world, u, rank, &cfg);
+        job->comm = c;
+        job->done.store(true);
+    }).detach();
+    const nrn_status_t st = nrn_comm_bounded_wait(
+        [](void* ctx) -> int { return static_cast<Job*>(ctx)->done.load() ? 1 : 0; }, job.get(), timeout_s);
+    if (st != NRN_OK)
+        return fail(NRN_ERR_COMM, "NCCL communicator set-up timed out after " + std::to_string(timeout_s) +
+                                      " s: every rank must call nrn_engine_set_partition with the same id");
+    if (job->r != ncclSuccess) {
+        if (job->comm) ncclCommAbort(job->comm);
+        return fail(NRN_ERR_COMM, std::string("NCCL communicator set-up: ") + ncclGetErrorString(job->r));
     }
-    AsyncPoll p{c};
-    const nrn_status_t st = nrn_comm_bounded_wait(poll_async, &p, timeout_s);
-    if (st != NRN_OK) {
-        ncclCommAbort(c);
-        return fail(NRN_ERR_COMM, st == NRN_ERR_TIMEOUT
-                                      ? "NCCL communicator set-up timed out after " + std::to_string(timeout_s) +
-                                            " s: every rank must call nrn_engine_set_partition with the same id"
-                                      : std::string("NCCL communicator set-up: ") + ncclGetErrorString(p.last));
-    }
-    *out = c;
+    *out = job->comm;
     return NRN_OK;
 }
 
@@ -150,18 +165,27 @@ nrn_status_t comm_wait_stream(ncclComm_t* c, cudaStream_t s, double timeout_s, b
 }
 
 nrn_status_t comm_destroy(ncclComm_t* c, double timeout_s) {
+    // Called with nothing of this communicator in flight (the engine stream
+    // was drained, within the time limit, before).  Its teardown may wait
+    // for peers that already left: it runs on a helper thread, and one that
+    // does not end in time is abandoned.
     if (*c == nullptr) return NRN_OK;
-    const ncclResult_t r = ncclCommFinalize(*c);
-    nrn_status_t st = NRN_OK;
-    if (r == ncclSuccess || r == ncclInProgress) {
-        AsyncPoll p{*c};
-        st = r == ncclSuccess ? NRN_OK : nrn_comm_bounded_wait(poll_async, &p, timeout_s);
-    } else {
-        st = NRN_ERR_COMM;
-    }
-    if (st == NRN_OK) ncclCommDestroy(*c);
-    else ncclCommAbort(*c);
+    struct Job {
+        ncclComm_t comm;
+        std::atomic<bool> done{false};
+    };
+    auto job = std::make_shared<Job>();
+    job->comm = *c;
     *c = nullptr;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::thread([job, dev] {
+        cudaSetDevice(dev);
+        if (ncclCommDestroy(job->comm) != ncclSuccess) ncclCommAbort(job->comm);
+        job->done.store(true);
+    }).detach();
+    nrn_comm_bounded_wait([](void* ctx) -> int { return static_cast<Job*>(ctx)->done.load() ? 1 : 0; }, job.get(),
+                          timeout_s);
     return NRN_OK;
 }
 

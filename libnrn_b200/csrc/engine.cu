@@ -120,6 +120,19 @@ struct EngineProj {
     int32_t pre_depth = 1;
 };
 
+struct EngineProbe {
+    int32_t pop = 0, var = 0, depth = 1;
+    float* ring = nullptr;
+};
+
+// Row (step % depth) of a probe ring from a population's state variable.
+__global__ void probe_kernel(const float* src, int n, float* ring, int depth, long long step_off,
+                             const long long* step_base) {
+    const long long step = step_off + *step_base;
+    float* row = ring + (step % depth) * static_cast<long long>(n);
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) row[i] = src[i];
+}
+
 constexpr int kRing = 64;           // spike steps kept per neuron
 constexpr int kSweepPeriod = 640;   // the sweep looks at every row this often
 constexpr int kStale = 480;         // and walks segments not walked for this many steps
@@ -133,6 +146,7 @@ struct nrn_engine {
     cudaEvent_t fork_ev = nullptr, join_ev = nullptr;
     std::vector<EnginePop> pops;
     std::vector<EngineProj> projs;
+    std::vector<EngineProbe> probes;
     bool finalized = false;
     int32_t depth = 2;
     int64_t step = 0;                     // host mirror of the device step
@@ -593,6 +607,15 @@ struct nrn_engine {
         if (det)
             for (auto& p : pops)
                 NRN_TRY(det_flags(p.d.spike, p.d.n, p.flags, det_ring, off, d_step, stream));
+        for (const auto& pr : probes) {
+            const EnginePop& p = pops[pr.pop];
+            const float* src = pr.var == NRN_VAR_V ? p.d.v : pr.var == NRN_VAR_AUX ? p.d.aux
+                             : pr.var == NRN_VAR_REFRACTORY ? p.d.refractory : pr.var == NRN_VAR_SPIKE ? p.d.spike
+                             : p.d.i_syn;
+            const int blocks = std::max(1, std::min((p.d.n + 255) / 256, 4 * sm_count_current()));
+            probe_kernel<<<blocks, 256, 0, stream>>>(src, p.d.n, pr.ring, pr.depth, off, d_step);
+            NRN_CUDA_TRY(cudaGetLastError());
+        }
         if (ev) NRN_CUDA_TRY(cudaEventRecord(ev[2], stream));
         if (kev) NRN_CUDA_TRY(cudaEventRecord(kev[4], stream));
         for (auto& q : projs) {
@@ -1231,6 +1254,36 @@ static nrn_status_t check_layout(nrn_engine* e) {
                                           "); every rank must build the same populations, projections, dt, "
                                           "slow ratio and max_rate_hz");
         }
+    }
+    return NRN_OK;
+}
+
+nrn_status_t nrn_engine_add_probe(nrn_engine* e, int32_t pop, int32_t var, float* ring, int32_t depth,
+                                  int32_t* id) {
+    ENGINE_GUARD(e);
+    NRN_CHECK_ARG(pop >= 0 && pop < static_cast<int32_t>(e->pops.size()), "bad population index");
+    NRN_CHECK_ARG(var >= NRN_VAR_V && var <= NRN_VAR_ISYN, "unknown probe variable");
+    NRN_CHECK_ARG(ring != nullptr && depth >= 1, "probe: null ring or depth < 1");
+    const EnginePop& p = e->pops[pop];
+    NRN_CHECK_ARG((var != NRN_VAR_AUX || p.d.aux) && (var != NRN_VAR_REFRACTORY || p.d.refractory),
+                  "probe: the population's model has no such variable");
+    EngineProbe pr;
+    pr.pop = pop;
+    pr.var = var;
+    pr.ring = ring;
+    pr.depth = depth;
+    e->probes.push_back(pr);
+    e->drop_graphs();
+    if (id) *id = static_cast<int32_t>(e->probes.size() - 1);
+    return NRN_OK;
+}
+
+nrn_status_t nrn_engine_clear_probes(nrn_engine* e) {
+    ENGINE_GUARD(e);
+    if (!e->probes.empty()) {
+        NRN_TRY(e->wait_stream());
+        e->probes.clear();
+        e->drop_graphs();
     }
     return NRN_OK;
 }
