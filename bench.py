@@ -649,7 +649,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10_000)
     ap.add_argument("--warmup", type=int, default=200)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="brunel_stdp", choices=["brunel_stdp", "brunel_1m", "brunel", "adex", "izh", "bsr"])
+    ap.add_argument("--workload", default="brunel_stdp", choices=["brunel_stdp", "brunel_1m", "brunel", "adex", "izh", "bsr", "api_c1"])
     ap.add_argument("--chunk", type=int, default=0)
     ap.add_argument("--burn-in", type=int, default=1000,
                     help="untimed steps after set-up and before the warm-up, so that the timed steps see the "
@@ -672,7 +672,25 @@ def main():
     if args.workload == "bsr":
         run_bsr(args, rank, world, local)
         return
+    if args.workload == "api_c1":
+        run_api(args, rank)
+        return
     run_network(args, rank, world, local)
+
+
+def run_api(args, rank: int) -> None:
+    """The reference's Brunel example configuration (10,000 E + 2,500 I,
+    p = 0.1, STDP on E->E) through the nrn:: C++ API (libnrn.so): one
+    sim_run_steps(K) call against K sim_step calls (tests/cpp/api_bench.cpp)."""
+    if rank != 0:
+        return
+    exe = os.path.join(ROOT, "tests", "cpp", "_bin", "api_bench")
+    if not os.path.exists(exe):
+        raise SystemExit(f"{exe} not built (python -c 'import __graft_entry__ as g; g.build()')")
+    out = subprocess.run([exe, str(args.steps)], capture_output=True, text=True, check=True).stdout
+    line = json.loads([x for x in out.splitlines() if x.startswith("{")][-1])
+    line["n_gpus"] = 1
+    print(json.dumps(line), flush=True)
 
 
 if __name__ == "__main__":

@@ -50,6 +50,12 @@ void sim_record(Simulation* sim, std::shared_ptr<Population> population, std::ve
 void sim_run(Simulation* sim);
 void sim_run_steps(Simulation* sim, int64_t n);
 void sim_step(Simulation* sim);
+// Not in the reference: reads back the recorders' pending data and writes
+// the plastic weights into the connections' ConnectivityTensors now.
+// sim_run / sim_run_steps / sim_destroy do this at their end; a loop of
+// sim_step calls leaves both on the device until one of those (or a
+// recorder query) runs.
+void sim_sync(Simulation* sim);
 // [K, 2] float: (neuron id, time)
 torch::Tensor sim_get_spikes(const Simulation* sim, const std::shared_ptr<Population>& population);
 // [T, N]

@@ -121,7 +121,7 @@ def build_cpp(verbose: bool = False) -> str:
     return CPP_LIB
 
 
-CPP_TESTS = ["test_core", "test_gpu_api", "dropin_brunel", "er_dump"]
+CPP_TESTS = ["test_core", "test_gpu_api", "dropin_brunel", "er_dump", "api_bench"]
 TEST_DIR = os.path.join(ROOT, "tests", "cpp")
 TEST_BIN = os.path.join(TEST_DIR, "_bin")
 
@@ -139,8 +139,9 @@ def build_cpp_tests(verbose: bool = False) -> dict:
         if _stale(exe, [src, os.path.join(TEST_DIR, "nrn_test.h"), lib] + _cpp_headers()):
             cmd = [os.environ.get("CXX", "g++"), "-std=c++20", "-O1", "-D_GLIBCXX_USE_CXX11_ABI=1",
                    f"-I{os.path.join(ROOT, 'include')}", f"-I{inc}", f"-I{os.path.join(inc, 'torch/csrc/api/include')}",
-                   src, "-o", exe, f"-L{OUT}", "-lnrn", "-lnrn_cuda", f"-L{tlib}", "-ltorch", "-ltorch_cpu",
-                   "-ltorch_cuda", "-lc10", "-lc10_cuda", f"-Wl,-rpath,{OUT}", f"-Wl,-rpath,{tlib}"]
+                   "-I/usr/local/cuda/include", src, "-o", exe, f"-L{OUT}", "-lnrn", "-lnrn_cuda", f"-L{tlib}",
+                   "-ltorch", "-ltorch_cpu", "-ltorch_cuda", "-lc10", "-lc10_cuda", "-L/usr/local/cuda/lib64",
+                   "-lcudart", f"-Wl,-rpath,{OUT}", f"-Wl,-rpath,{tlib}", "-Wl,-rpath,/usr/local/cuda/lib64"]
             r = subprocess.run(cmd, capture_output=True, text=True)
             if r.returncode != 0:
                 raise RuntimeError(f"build of {name} failed:\n{r.stderr[-6000:]}")

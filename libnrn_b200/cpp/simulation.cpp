@@ -28,6 +28,7 @@
 #include <nrn/synapse/synapse.h>
 
 #include <algorithm>
+#include <map>
 #include <cmath>
 #include <stdexcept>
 #include <vector>
@@ -135,11 +136,28 @@ struct SimEngine {
         float w_min = 0.0f, w_max = 0.0f;
         torch::Tensor coo_pos;   // flat index into [n_blocks, B, B] of each synapse
         torch::Tensor valid;     // in-range entries (the reference clamps these)
+        torch::Tensor w_dev;     // plastic: [n_blocks, B, B] float32 on the engine's device
+        torch::Tensor w_buf;     // plastic: [nnz] the engine's weights in synapse order
+        bool aliased = false;    // ConnectivityTensor::weights is w_dev itself
+    };
+    // A state recorder's variable, copied on the device at every step into
+    // a ring of probe_depth rows (nrn_engine_add_probe).
+    struct Probe {
+        StateRecorderState* rec = nullptr;
+        std::string var;
+        int32_t pop = 0;
+        torch::Tensor ring;      // [probe_depth, n]
     };
     std::vector<Pop> pops;
     std::vector<Conn> conns;
+    std::vector<Probe> probes;
+    int32_t probe_depth = 0;
     size_t n_pops = 0, n_conns = 0;
     std::vector<int32_t> raster_step, raster_gid;
+    // steps run and not yet read back (spike raster, probes), and whether
+    // the plastic weights changed since the last write-back
+    int64_t pending_first = 0, pending_steps = 0;
+    bool weights_dirty = false;
 
     ~SimEngine() {
         if (e) nrn_engine_destroy(e);
@@ -201,12 +219,6 @@ void param_slots(SimEngine::Pop& p, const std::vector<torch::Tensor*>& par, cons
 bool wants_spikes(const Simulation* sim, const std::string& name) {
     for (const auto& r : sim->recorders)
         if (r.ops == &spike_recorder_ops && name == r.ops->population_name(r.impl)) return true;
-    return false;
-}
-
-bool has_state_recorders(const Simulation* sim) {
-    for (const auto& r : sim->recorders)
-        if (r.ops == &state_recorder_ops) return true;
     return false;
 }
 
@@ -371,6 +383,52 @@ void build_engine(Simulation* sim) {
         }
         eng->conns.push_back(std::move(cc));
     }
+    // Plastic weights stay on the device between steps: w_dev is the block
+    // tensor the engine's weights are written back into (clamped once now,
+    // as the reference clamps every in-range entry at each update); it
+    // becomes ConnectivityTensor::weights when that already lives on this
+    // device as float32.
+    for (auto& cc : eng->conns) {
+        if (!cc.plastic) continue;
+        auto& ct = cc.conn->connectivity;
+        auto W = ct.weights.to(dev).to(torch::kFloat32).contiguous().clone();
+        cc.w_dev = torch::where(cc.valid, W.clamp(cc.w_min, cc.w_max), W).contiguous();
+        cc.w_buf = torch::empty({std::max<int64_t>(cc.nnz, 1)}, torch::TensorOptions().dtype(torch::kFloat32).device(dev));
+        cc.aliased = ct.weights.is_cuda() && ct.weights.device() == dev && ct.weights.scalar_type() == torch::kFloat32;
+        if (cc.aliased) ct.weights = cc.w_dev.view(ct.weights.sizes());
+    }
+    // state recorders: device probes, read back every probe_depth steps
+    for (auto& r : sim->recorders) {
+        if (r.ops != &state_recorder_ops) continue;
+        auto* sr = static_cast<StateRecorderState*>(r.impl);
+        for (size_t i = 0; i < eng->pops.size(); ++i) {
+            auto& p = eng->pops[i];
+            if (p.pop->name != sr->pop_name) continue;
+            for (const auto& var : sr->variables) {
+                int slot = -1;
+                if (var == "v") slot = NRN_VAR_V;
+                else if ((var == "w" && p.model == NRN_MODEL_ADEX) || (var == "u" && p.model == NRN_MODEL_IZH))
+                    slot = NRN_VAR_AUX;
+                else if (var == "refractory" && p.model != NRN_MODEL_IZH) slot = NRN_VAR_REFRACTORY;
+                else if (var == "spike") slot = NRN_VAR_SPIKE;
+                else if (var == "I_syn") slot = NRN_VAR_ISYN;
+                if (slot < 0) continue;   // not in the model's state: not recorded (state_contains)
+                if (eng->probe_depth == 0) {
+                    int64_t tot = 0;
+                    for (auto& q : eng->pops) tot += q.pop->n;
+                    eng->probe_depth = static_cast<int32_t>(std::max<int64_t>(8, std::min<int64_t>(256, (int64_t(1) << 26) / std::max<int64_t>(tot, 1))));
+                }
+                SimEngine::Probe pr;
+                pr.rec = sr;
+                pr.var = var;
+                pr.pop = static_cast<int32_t>(i);
+                pr.ring = torch::empty({eng->probe_depth, p.pop->n}, torch::TensorOptions().dtype(torch::kFloat32).device(dev));
+                detail::check(nrn_engine_add_probe(eng->e, p.id, slot, pr.ring.data_ptr<float>(), eng->probe_depth, nullptr),
+                              "sim: state probe");
+                eng->probes.push_back(std::move(pr));
+            }
+        }
+    }
     // sim_create already ran the initialising update (forward with dt = 0)
     detail::check(nrn_engine_finalize(eng->e, 0), "sim: finalize");
     // continue the clock's step numbering (slow-clock boundaries, raster)
@@ -457,33 +515,82 @@ void drain_raster(Simulation* sim, int64_t first_step, int64_t n_steps) {
     }
 }
 
-void write_back(Simulation* sim) {
+// The plastic weights into the ConnectivityTensors: the engine's weights in
+// synapse order (its own kernels, on the engine stream) scattered into w_dev
+// -- no allocation, no host wait.  Only a connectivity kept off this device
+// (or in another dtype) is then copied, which waits.
+void sync_weights(Simulation* sim) {
     SimEngine& g = *sim->engine;
-    const torch::Device dev(torch::kCUDA, static_cast<c10::DeviceIndex>(g.device));
+    if (!g.weights_dirty) return;
+    nrn_stream_t es = nullptr;
+    detail::check(nrn_engine_stream(g.e, &es), "sim");
+    bool host_copy = false;
     for (auto& c : g.conns) {
-        if (!c.plastic) continue;
-        auto& ct = c.conn->connectivity;
-        auto w = torch::empty({c.nnz}, torch::TensorOptions().dtype(torch::kFloat32).device(dev));
-        detail::check(nrn_engine_weights_device(g.e, c.proj, w.data_ptr<float>(), c.nnz), "sim: weights");
-        detail::check(nrn_engine_sync(g.e), "sim");
-        auto W = ct.weights.to(dev).to(torch::kFloat32).contiguous();
-        // the reference clamps every in-range entry on each update
-        W = torch::where(c.valid, W.clamp(c.w_min, c.w_max), W).contiguous();
-        detail::check(nrn_cuda_scatter(w.data_ptr<float>(), c.coo_pos.data_ptr<int64_t>(), c.nnz,
-                                       W.data_ptr<float>(), detail::stream_of(W)),
+        if (!c.plastic || c.nnz == 0) continue;
+        detail::check(nrn_engine_weights_device(g.e, c.proj, c.w_buf.data_ptr<float>(), c.nnz), "sim: weights");
+        detail::check(nrn_cuda_scatter(c.w_buf.data_ptr<float>(), c.coo_pos.data_ptr<int64_t>(), c.nnz,
+                                       c.w_dev.data_ptr<float>(), es),
                       "sim: weight write-back");
-        ct.weights = W.to(ct.weights.device());
+        host_copy = host_copy || !c.aliased;
     }
+    if (host_copy) {
+        detail::check(nrn_engine_sync(g.e), "sim");
+        for (auto& c : g.conns) {
+            if (!c.plastic || c.aliased) continue;
+            auto& ct = c.conn->connectivity;
+            ct.weights.copy_(c.w_dev.view(ct.weights.sizes()));
+        }
+    }
+    g.weights_dirty = false;
 }
 
-void run_steps(Simulation* sim, int64_t n) {
+// Reads back what the steps run since the last call recorded: the spike
+// raster into the spike recorders, the probe rows into the state recorders
+// (one host wait).
+void drain(Simulation* sim) {
+    SimEngine& g = *sim->engine;
+    if (g.pending_steps == 0) return;
+    detail::check(nrn_engine_sync(g.e), "sim");
+    drain_raster(sim, g.pending_first, g.pending_steps);
+    if (!g.probes.empty()) {
+        const double dt = sim->options.dt_fast();
+        std::map<StateRecorderState*, std::vector<SimEngine::Probe*>> by_rec;
+        for (auto& pr : g.probes) by_rec[pr.rec].push_back(&pr);
+        for (auto& kv : by_rec) {
+            StateRecorderState* sr = kv.first;
+            std::vector<torch::Tensor> host;
+            for (auto* pr : kv.second) host.push_back(pr->ring.cpu());
+            for (int64_t s = g.pending_first; s < g.pending_first + g.pending_steps; ++s) {
+                ++sr->call_count;
+                if (sr->call_count % sr->subsample != 0) continue;
+                const int64_t row = s % g.probe_depth;
+                for (size_t k = 0; k < kv.second.size(); ++k)
+                    sr->history[kv.second[k]->var].push_back(host[k][row].clone());
+                sr->times.push_back(static_cast<float>(static_cast<double>(s) * dt));
+            }
+        }
+    }
+    g.pending_first += g.pending_steps;
+    g.pending_steps = 0;
+}
+
+// Runs n steps.  No host wait per step: the spike raster and the state
+// probes are read back when a callback or a query needs them, when the
+// probe rings are full, and at the end of a multi-step call, which also
+// writes the plastic weights back (bulk=true); sim_step leaves both on the
+// device until then.
+void run_steps(Simulation* sim, int64_t n, bool bulk) {
     if (n <= 0) return;
     Region* region = sim->region;
     if (!sim->engine || sim->engine->n_pops != region->populations.size() ||
         sim->engine->n_conns != region->connections.size()) {
-        if (sim->engine) write_back(sim);
+        if (sim->engine) {
+            drain(sim);
+            sync_weights(sim);
+        }
         sim->engine.reset();
         build_engine(sim);
+        sim->engine->pending_first = static_cast<int64_t>(sim->clock.step());
     }
     SimEngine& g = *sim->engine;
     refresh(sim);
@@ -494,44 +601,49 @@ void run_steps(Simulation* sim, int64_t n) {
     cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
     cudaEventRecord(ev, c10::cuda::getCurrentCUDAStream(g.device).stream());
     cudaStreamWaitEvent(reinterpret_cast<cudaStream_t>(es), ev, 0);
-    const bool per_step = has_state_recorders(sim);
     const int64_t chunk = sim->options.use_cuda_graphs() ? 50 : 1;
+    bool any_spike_rec = false;
+    for (auto& r : sim->recorders) any_spike_rec = any_spike_rec || r.ops == &spike_recorder_ops;
+    bool plastic = false;
+    for (auto& c : g.conns) plastic = plastic || c.plastic;
     int64_t done = 0;
     while (done < n) {
         const int64_t step = static_cast<int64_t>(sim->clock.step());
         // a callback fires after step k (k > 0, k % every == 0): the segment
         // ends there so the callback sees that step's state
-        int64_t seg = std::min<int64_t>(n - done, per_step ? 1 : 1000);
+        int64_t seg = n - done;
         for (auto& cb : sim->callbacks) {
             const int64_t every = cb.first;
             const int64_t first = std::max<int64_t>(step, 1);
             const int64_t k = ((first + every - 1) / every) * every;
             seg = std::min(seg, k - step + 1);
         }
+        if (!g.probes.empty()) seg = std::min<int64_t>(seg, g.probe_depth - g.pending_steps);
+        if (any_spike_rec) seg = std::min<int64_t>(seg, std::max<int64_t>(1, 64 - g.pending_steps));
         seg = std::max<int64_t>(seg, 1);
         detail::check(nrn_engine_run(g.e, seg, static_cast<int32_t>(std::min(seg, chunk))), "sim: run");
-        detail::check(nrn_engine_sync(g.e), "sim");
-        drain_raster(sim, step, seg);
+        g.pending_steps += seg;
+        g.weights_dirty = g.weights_dirty || plastic;
         for (int64_t k = 0; k < seg; ++k) {
             const int64_t s_k = step + k;
             const double t = sim->clock.time();
-            if (per_step) {
-                for (auto& rec : sim->recorders) {
-                    if (rec.ops != &state_recorder_ops) continue;
-                    for (auto& p : region->populations)
-                        if (p->name == rec.ops->population_name(rec.impl)) {
-                            rec.ops->record(rec.impl, p->state, t);
-                            break;
-                        }
-                }
-            }
+            bool first_cb = true;
             for (auto& cb : sim->callbacks)
-                if (s_k > 0 && s_k % cb.first == 0) cb.second(*sim, t);
+                if (s_k > 0 && s_k % cb.first == 0) {
+                    if (first_cb) drain(sim);   // the callback sees the recorders up to this step
+                    first_cb = false;
+                    cb.second(*sim, t);
+                }
             sim->clock.advance_fast();
         }
+        if ((!g.probes.empty() && g.pending_steps >= g.probe_depth) || (any_spike_rec && g.pending_steps >= 64))
+            drain(sim);
         done += seg;
     }
-    write_back(sim);
+    if (bulk) {
+        drain(sim);
+        sync_weights(sim);
+    }
     // the caller's stream continues after the engine's work
     cudaEventRecord(ev, reinterpret_cast<cudaStream_t>(es));
     cudaStreamWaitEvent(c10::cuda::getCurrentCUDAStream(g.device).stream(), ev, 0);
@@ -554,7 +666,21 @@ Simulation* sim_create(Region* region, SimulationOptions options) {
     return sim;
 }
 
-void sim_destroy(Simulation* sim) { delete sim; }
+void sim_destroy(Simulation* sim) {
+    if (sim && sim->engine) {
+        drain(sim);
+        sync_weights(sim);
+    }
+    delete sim;
+}
+
+void sim_sync(Simulation* sim) {
+    TORCH_CHECK(sim != nullptr, "sim_sync: null simulation");
+    if (!sim->engine) return;
+    drain(sim);
+    sync_weights(sim);
+    detail::check(nrn_engine_sync(sim->engine->e), "sim_sync");
+}
 
 void sim_record(Simulation* sim, std::shared_ptr<Population> population, std::vector<std::string> variables,
                 int64_t subsample) {
@@ -569,9 +695,11 @@ void sim_record(Simulation* sim, std::shared_ptr<Population> population, std::ve
     if (!vars.empty())
         sim->recorders.push_back(
             state_recorder_as_recorder(state_recorder_create(population->name, std::move(vars), subsample)));
-    if (sim->engine && spikes) {
-        // the raster flag is fixed at engine build; rebuild to record this population
-        write_back(sim);
+    if (sim->engine) {
+        // the raster flags and state probes are fixed at engine build:
+        // rebuild to record this population
+        drain(sim);
+        sync_weights(sim);
         sim->engine.reset();
     }
 }
@@ -581,12 +709,13 @@ void sim_run(Simulation* sim) {
     sim_run_steps(sim, n);
 }
 
-void sim_run_steps(Simulation* sim, int64_t n) { run_steps(sim, n); }
+void sim_run_steps(Simulation* sim, int64_t n) { run_steps(sim, n, true); }
 
-void sim_step(Simulation* sim) { run_steps(sim, 1); }
+void sim_step(Simulation* sim) { run_steps(sim, 1, false); }
 
 torch::Tensor sim_get_spikes(const Simulation* sim, const std::shared_ptr<Population>& population) {
     TORCH_CHECK(population != nullptr, "Cannot query spikes for null population");
+    if (sim->engine) drain(const_cast<Simulation*>(sim));
     for (const auto& r : sim->recorders)
         if (r.ops == &spike_recorder_ops && population->name == r.ops->population_name(r.impl))
             return spike_recorder_get_spikes(static_cast<SpikeRecorderState*>(r.impl));
@@ -597,6 +726,7 @@ torch::Tensor sim_get_spikes(const Simulation* sim, const std::shared_ptr<Popula
 torch::Tensor sim_get_recorded(const Simulation* sim, const std::shared_ptr<Population>& population,
                                const std::string& variable) {
     TORCH_CHECK(population != nullptr, "Cannot query recorded data for null population");
+    if (sim->engine) drain(const_cast<Simulation*>(sim));
     for (const auto& r : sim->recorders)
         if (r.ops == &state_recorder_ops && population->name == r.ops->population_name(r.impl))
             return state_recorder_get(static_cast<StateRecorderState*>(r.impl), variable);

@@ -316,6 +316,51 @@ TEST(Simulation, RecordersCallbacksAndNoNaN) {
     neuron::lif_destroy(lif);
 }
 
+// State recorders read through device probes: the rows equal the state
+// after each step, read directly, with sim_step calls and no host wait in
+// between; spikes recorded by a sim_step loop equal those of sim_run_steps.
+TEST(Simulation, ProbesEqualDirectReadsAndStepLoopEqualsRun) {
+    auto make = [](neuron::LIFNeuron** out) {
+        auto* lif = neuron::lif_create(64, neuron::LIFOptions().i_bg(500e-12));
+        neuron::lif_to_device(lif, torch::kCUDA);
+        lif->v.copy_(-0.065 + 0.01 * torch::arange(64, torch::TensorOptions().device(torch::kCUDA)) / 64.0);
+        *out = lif;
+        return std::shared_ptr<Population>(population_create("p", neuron::lif_as_module(lif), 64, torch::kCUDA),
+                                           population_destroy);
+    };
+    neuron::LIFNeuron* l1 = nullptr;
+    auto pop = make(&l1);
+    auto* region = region_create("r");
+    region_add_population(region, pop);
+    auto* sim = sim_create(region, SimulationOptions().dt_fast(1e-4));
+    sim_record(sim, pop, {"v", "spike"});
+    std::vector<torch::Tensor> direct;
+    for (int k = 0; k < 40; ++k) {
+        sim_step(sim);
+        direct.push_back(state_get(pop->state, "v").cpu().clone());
+    }
+    auto rec = sim_get_recorded(sim, pop, "v");
+    ASSERT_TRUE(rec.size(0) == 40);
+    for (int k = 0; k < 40; ++k) EXPECT_TRUE(torch::equal(rec[k], direct[k]));
+    auto sp_steps = sim_get_spikes(sim, pop).clone();
+    neuron::LIFNeuron* l2 = nullptr;
+    auto pop2 = make(&l2);
+    auto* region2 = region_create("r2");
+    region_add_population(region2, pop2);
+    auto* sim2 = sim_create(region2, SimulationOptions().dt_fast(1e-4));
+    sim_record(sim2, pop2, {"spike"});
+    sim_run_steps(sim2, 40);
+    auto sp_run = sim_get_spikes(sim2, pop2);
+    EXPECT_GT(sp_run.size(0), 0);
+    EXPECT_TRUE(torch::equal(sp_steps, sp_run));
+    sim_destroy(sim2);
+    region_destroy(region2);
+    neuron::lif_destroy(l2);
+    sim_destroy(sim);
+    region_destroy(region);
+    neuron::lif_destroy(l1);
+}
+
 // A Simulation from a YAML file (nrn::config::load): populations with
 // synapse channels and STDP, run on the GPU, spikes recorded.
 TEST(Config, LoadAndRunSimulation) {
