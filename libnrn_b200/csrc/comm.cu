@@ -73,11 +73,29 @@ int poll_stream(void* ctx) {
 
 }  // namespace
 
+// Aborts the communicator on a helper thread, waiting for it at most
+// kAbortWait seconds: an abort that does not end (it may wait on peers) is
+// abandoned, the communicator being unusable either way.
+constexpr double kAbortWait = 30.0;
+
 nrn_status_t comm_abort(ncclComm_t* c) {
-    if (*c != nullptr) {
-        ncclCommAbort(*c);
-        *c = nullptr;
-    }
+    if (*c == nullptr) return NRN_OK;
+    struct Job {
+        ncclComm_t comm;
+        std::atomic<bool> done{false};
+    };
+    auto job = std::make_shared<Job>();
+    job->comm = *c;
+    *c = nullptr;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::thread([job, dev] {
+        cudaSetDevice(dev);
+        ncclCommAbort(job->comm);
+        job->done.store(true);
+    }).detach();
+    nrn_comm_bounded_wait([](void* ctx) -> int { return static_cast<Job*>(ctx)->done.load() ? 1 : 0; }, job.get(),
+                          kAbortWait);
     return NRN_OK;
 }
 
@@ -113,7 +131,8 @@ nrn_status_t comm_init(ncclComm_t* out, int world, const uint8_t id[128], int ra
         return fail(NRN_ERR_COMM, "NCCL communicator set-up timed out after " + std::to_string(timeout_s) +
                                       " s: every rank must call nrn_engine_set_partition with the same id");
     if (job->r != ncclSuccess) {
-        if (job->comm) ncclCommAbort(job->comm);
+        ncclComm_t c = job->comm;
+        comm_abort(&c);
         return fail(NRN_ERR_COMM, std::string("NCCL communicator set-up: ") + ncclGetErrorString(job->r));
     }
     *out = job->comm;
@@ -181,7 +200,7 @@ nrn_status_t comm_destroy(ncclComm_t* c, double timeout_s) {
     cudaGetDevice(&dev);
     std::thread([job, dev] {
         cudaSetDevice(dev);
-        if (ncclCommDestroy(job->comm) != ncclSuccess) ncclCommAbort(job->comm);
+        ncclCommDestroy(job->comm);
         job->done.store(true);
     }).detach();
     nrn_comm_bounded_wait([](void* ctx) -> int { return static_cast<Job*>(ctx)->done.load() ? 1 : 0; }, job.get(),

@@ -138,7 +138,7 @@ def _fail_worker(rank, world, port, scenario, q):
         spec = spec_of("brunel", 60)
         max_rate = 2000.0 if not (scenario == "layout" and rank == 1) else 1000.0
         try:
-            nw = Network.from_spec(spec, device=rank, partition=(rank, world, uid, max_rate), comm_timeout=20.0)
+            nw = Network.from_spec(spec, device=rank, partition=(rank, world, uid, max_rate), comm_timeout=10.0)
         except N.NrnError as ex:
             out["build"] = str(ex)
             q.put(out)
