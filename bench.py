@@ -660,7 +660,13 @@ def main():
                     help="mean firing rate bound (Hz) that sizes the multi-GPU spike exchange buffers")
     ap.add_argument("--scale", type=float, default=1.0,
                     help="network size factor (profiling of small cases only; the bench line uses 1)")
+    ap.add_argument("--probe-l2", action="store_true",
+                    help="run the random-access throughput probe (libnrn_b200/_lib/l2_probe) and exit")
     args = ap.parse_args()
+    if args.probe_l2:
+        from libnrn_b200 import build as B
+        subprocess.run([B.build_probe()], check=True)
+        return
     args.warmup = max(3, args.warmup)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

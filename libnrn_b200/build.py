@@ -155,6 +155,23 @@ def build_cpp_tests(verbose: bool = False) -> dict:
     return out
 
 
+PROBE = os.path.join(OUT, "l2_probe")
+
+
+def build_probe(verbose: bool = False) -> str:
+    """The random-access throughput probe (csrc/l2_probe.cu), a standalone
+    program run by bench.py --probe-l2."""
+    os.makedirs(OUT, exist_ok=True)
+    src = os.path.join(CSRC, "l2_probe.cu")
+    if _stale(PROBE, [src]):
+        r = subprocess.run([NVCC, *ARCH, "-O3", "-o", PROBE, src], capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"nvcc failed on {src}:\n{r.stderr[-4000:]}")
+    if verbose:
+        print(PROBE)
+    return PROBE
+
+
 def build(force: bool = False, verbose: bool = False) -> str:
     os.makedirs(OBJ, exist_ok=True)
     srcs = [os.path.join(CSRC, s) for s in SOURCES]

@@ -17,6 +17,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <vector>
 
 #include "common.cuh"
@@ -379,46 +380,65 @@ __device__ __forceinline__ float4 ld4(const float* p, int i) { return *reinterpr
 __device__ __forceinline__ void st4(float* p, int i, float4 x) { *reinterpret_cast<float4*>(p + i) = x; }
 __device__ __forceinline__ float& at(float4& x, int k) { return k == 0 ? x.x : k == 1 ? x.y : k == 2 ? x.z : x.w; }
 
-// LIF with uniform parameters, four neurons per thread (float4 state, n a
-// multiple of 4, arrays 16-byte aligned): the same arithmetic as pop_body
-// (lif_math), with wider memory transactions.
+// LIF with uniform parameters, four neurons per group (float4 state, n a
+// multiple of 4, arrays 16-byte aligned), G groups per thread, blockDim.x*4
+// neurons apart (coalesced): the same arithmetic as pop_body (lif_math),
+// with wider memory transactions and the loads of all G groups issued
+// before any is used.
+template <int G>
 __global__ void __launch_bounds__(256) lif4_group_kernel(const __grid_constant__ PopGroup g) {
     int q = 0;
     while (q + 1 < g.n && static_cast<int>(blockIdx.x) >= g.start[q + 1]) ++q;
     const PopArgs& a = g.p[q];
-    const int i0 = 4 * ((static_cast<int>(blockIdx.x) - g.start[q]) * blockDim.x + threadIdx.x);
+    const int stride = 4 * static_cast<int>(blockDim.x);
+    const int ib = 4 * ((static_cast<int>(blockIdx.x) - g.start[q]) * G * static_cast<int>(blockDim.x) +
+                        static_cast<int>(threadIdx.x));
     const int lane = threadIdx.x & 31;
     long long step = a.step;
     if (a.step_base) step += *a.step_base;
-    int sp[4] = {0, 0, 0, 0};
-    if (i0 < a.n) {
-        float4 I = a.i_syn ? ld4(a.i_syn, i0) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const bool traces_now = a.n_traces > 0 && (a.trace_slow_ratio <= 1 || step % a.trace_slow_ratio == 0);
+    const long long ring_mask = a.trace_ring_depth - 1;
+    float4 I[G], v[G], ref[G], x0[G];
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+        const int i0 = ib + j * stride;
+        if (i0 >= a.n) continue;
+        I[j] = a.i_syn ? ld4(a.i_syn, i0) : make_float4(0.f, 0.f, 0.f, 0.f);
         if (a.drive_kind != NRN_DRIVE_NONE) {
             float4 x;
             if (a.drive_values) x = ld4(a.drive_values, i0);
             else x = drive_value4(a, static_cast<uint32_t>(a.gid_offset + i0), static_cast<uint32_t>(step));
-            I.x = I.x + x.x; I.y = I.y + x.y; I.z = I.z + x.z; I.w = I.w + x.w;
+            I[j].x = I[j].x + x.x; I[j].y = I[j].y + x.y; I[j].z = I[j].z + x.z; I[j].w = I[j].w + x.w;
         }
-        float4 v = ld4(a.v, i0), ref = ld4(a.ref, i0);
+        v[j] = ld4(a.v, i0);
+        ref[j] = ld4(a.ref, i0);
         // the first trace is loaded with the state (the stores below could
         // alias it, so it would otherwise wait for them)
-        const bool traces_now = a.n_traces > 0 && (a.trace_slow_ratio <= 1 || step % a.trace_slow_ratio == 0);
-        const long long ring_mask = a.trace_ring_depth - 1;
-        float4 x0 = make_float4(0.f, 0.f, 0.f, 0.f);
+        x0[j] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (traces_now)
-            x0 = a.trace_ring[0] != nullptr ? ld4(a.trace_ring[0] + ((step - 1) & ring_mask) * a.n, i0)
-                                            : ld4(a.trace[0], i0);
-        const float* u = a.uniform;
+            x0[j] = a.trace_ring[0] != nullptr ? ld4(a.trace_ring[0] + ((step - 1) & ring_mask) * a.n, i0)
+                                               : ld4(a.trace[0], i0);
+    }
+    int sp[4 * G];
+#pragma unroll
+    for (int k = 0; k < 4 * G; ++k) sp[k] = 0;
+    const float* u = a.uniform;
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+        const int i0 = ib + j * stride;
+        if (i0 >= a.n) continue;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
             float vn, r;
-            sp[k] = lif_math(at(v, k), at(ref, k), at(I, k), a.dtf, u[0], u[1], u[2], u[3], u[4], u[5], u[6], vn, r);
-            at(v, k) = vn;
-            at(ref, k) = r;
+            sp[4 * j + k] = lif_math(at(v[j], k), at(ref[j], k), at(I[j], k), a.dtf, u[0], u[1], u[2], u[3], u[4],
+                                     u[5], u[6], vn, r);
+            at(v[j], k) = vn;
+            at(ref[j], k) = r;
         }
-        st4(a.v, i0, v);
-        st4(a.ref, i0, ref);
-        const float4 s4 = make_float4(sp[0] ? 1.f : 0.f, sp[1] ? 1.f : 0.f, sp[2] ? 1.f : 0.f, sp[3] ? 1.f : 0.f);
+        st4(a.v, i0, v[j]);
+        st4(a.ref, i0, ref[j]);
+        const float4 s4 = make_float4(sp[4 * j] ? 1.f : 0.f, sp[4 * j + 1] ? 1.f : 0.f, sp[4 * j + 2] ? 1.f : 0.f,
+                                      sp[4 * j + 3] ? 1.f : 0.f);
         if (a.spike) st4(a.spike, i0, s4);
         if (traces_now) {
             for (int k = 0; k < a.n_traces; ++k) {
@@ -426,10 +446,10 @@ __global__ void __launch_bounds__(256) lif4_group_kernel(const __grid_constant__
                 float4 x;
                 float* dst;
                 if (a.trace_ring[k] != nullptr) {
-                    x = k == 0 ? x0 : ld4(a.trace_ring[k] + ((step - 1) & ring_mask) * a.n, i0);
+                    x = k == 0 ? x0[j] : ld4(a.trace_ring[k] + ((step - 1) & ring_mask) * a.n, i0);
                     dst = a.trace_ring[k] + (step & ring_mask) * a.n;
                 } else {
-                    x = k == 0 ? x0 : ld4(a.trace[k], i0);
+                    x = k == 0 ? x0[j] : ld4(a.trace[k], i0);
                     dst = a.trace[k];
                 }
                 x.x = x.x * d + s4.x; x.y = x.y * d + s4.y; x.z = x.z * d + s4.z; x.w = x.w * d + s4.w;
@@ -442,7 +462,9 @@ __global__ void __launch_bounds__(256) lif4_group_kernel(const __grid_constant__
     // lane 31 issues all the warp's list reservations at once, so a warp
     // with spikes waits for one atomic round trip, overlapped with the
     // updates of its neurons' spike records.
-    const int cnt = sp[0] + sp[1] + sp[2] + sp[3];
+    int cnt = 0;
+#pragma unroll
+    for (int k = 0; k < 4 * G; ++k) cnt += sp[k];
     int incl = cnt;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -476,9 +498,9 @@ __global__ void __launch_bounds__(256) lif4_group_kernel(const __grid_constant__
     }
     if (cnt > 0) {
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
+        for (int k = 0; k < 4 * G; ++k) {
             if (!sp[k]) continue;
-            const int i = i0 + k;
+            const int i = ib + (k / 4) * stride + (k % 4);
             if (a.post_recent != nullptr) {
                 const int t = static_cast<int>(step);
                 const int4 r = a.post_recent[i];
@@ -496,9 +518,9 @@ __global__ void __launch_bounds__(256) lif4_group_kernel(const __grid_constant__
     if (cnt > 0) {
         int pos = base + incl - cnt;
         unsigned long long rpos = rbase + static_cast<unsigned long long>(incl - cnt);
-        for (int k = 0; k < 4; ++k) {
+        for (int k = 0; k < 4 * G; ++k) {
             if (!sp[k]) continue;
-            const int id = i0 + k;
+            const int id = ib + (k / 4) * stride + (k % 4);
             if (list_ids) {
                 if (pos < list_cap) list_ids[pos] = a.id_offset + id;
                 else if (a.err) atomicCAS(a.err, 0, 4);
@@ -753,14 +775,20 @@ nrn_status_t pop_step_group(const nrn_pop_step_t* list, int n, cudaStream_t s) {
             done[r] = 1;
         }
         if (list[q].model == NRN_MODEL_LIF && !het && lif4_ok(g)) {
-            // four neurons a thread: block ranges in units of 4 * kPopThreads neurons
+            // groups of four neurons, two groups a thread: block ranges in
+            // units of 8 * kPopThreads neurons
+            static const int groups = [] {
+                const char* e = std::getenv("NRN_LIF_GROUPS");
+                return e && e[0] == '1' ? 1 : 2;
+            }();
             int b = 0;
             for (int k = 0; k < g.n; ++k) {
                 g.start[k] = b;
-                b += (g.p[k].n + 4 * kPopThreads - 1) / (4 * kPopThreads);
+                b += (g.p[k].n + 4 * groups * kPopThreads - 1) / (4 * groups * kPopThreads);
             }
             g.start[g.n] = b;
-            lif4_group_kernel<<<b, kPopThreads, 0, s>>>(g);
+            if (groups == 1) lif4_group_kernel<1><<<b, kPopThreads, 0, s>>>(g);
+            else lif4_group_kernel<2><<<b, kPopThreads, 0, s>>>(g);
         } else {
             launch_group(g, list[q].model, het, cond, s);
         }
