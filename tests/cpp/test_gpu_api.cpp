@@ -334,14 +334,16 @@ TEST(Simulation, ProbesEqualDirectReadsAndStepLoopEqualsRun) {
     region_add_population(region, pop);
     auto* sim = sim_create(region, SimulationOptions().dt_fast(1e-4));
     sim_record(sim, pop, {"v", "spike"});
+    // 300 steps: past the first spikes (about 140 steps from rest at this
+    // drive) and past one probe ring of 256 rows
     std::vector<torch::Tensor> direct;
-    for (int k = 0; k < 40; ++k) {
+    for (int k = 0; k < 300; ++k) {
         sim_step(sim);
         direct.push_back(state_get(pop->state, "v").cpu().clone());
     }
     auto rec = sim_get_recorded(sim, pop, "v");
-    ASSERT_TRUE(rec.size(0) == 40);
-    for (int k = 0; k < 40; ++k) EXPECT_TRUE(torch::equal(rec[k], direct[k]));
+    ASSERT_TRUE(rec.size(0) == 300);
+    for (int k = 0; k < 300; ++k) EXPECT_TRUE(torch::equal(rec[k], direct[k]));
     auto sp_steps = sim_get_spikes(sim, pop).clone();
     neuron::LIFNeuron* l2 = nullptr;
     auto pop2 = make(&l2);
@@ -349,7 +351,7 @@ TEST(Simulation, ProbesEqualDirectReadsAndStepLoopEqualsRun) {
     region_add_population(region2, pop2);
     auto* sim2 = sim_create(region2, SimulationOptions().dt_fast(1e-4));
     sim_record(sim2, pop2, {"spike"});
-    sim_run_steps(sim2, 40);
+    sim_run_steps(sim2, 300);
     auto sp_run = sim_get_spikes(sim2, pop2);
     EXPECT_GT(sp_run.size(0), 0);
     EXPECT_TRUE(torch::equal(sp_steps, sp_run));
