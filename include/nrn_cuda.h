@@ -552,6 +552,20 @@ NRN_API nrn_status_t nrn_engine_sync(nrn_engine* e);
 NRN_API nrn_status_t nrn_engine_set_step(nrn_engine* e, int64_t step);
 NRN_API nrn_status_t nrn_engine_stream(nrn_engine* e, nrn_stream_t* stream);
 NRN_API int64_t nrn_engine_step(const nrn_engine* e);
+/* What a caller needs to pace its reads: the window (steps between spike
+ * exchanges and trace snapshots; runs that start and end on window
+ * boundaries replay the fewest distinct graphs), and the raster's capacity
+ * in spikes over the neurons it records (a caller that reads the raster at
+ * least every raster_capacity / recorded_neurons steps cannot overflow it).
+ * Valid after nrn_engine_finalize. */
+typedef struct {
+    int32_t window;
+    int32_t n_pops;
+    int64_t raster_capacity;
+    int64_t recorded_neurons;
+    int64_t step;
+} nrn_engine_info_t;
+NRN_API nrn_status_t nrn_engine_info(const nrn_engine* e, nrn_engine_info_t* out);
 /* Recorded spikes since the last call (host buffers), sorted by step and,
  * within a step, by ascending global id; *n receives the count
  * (if above cap, nothing is copied and NRN_ERR_CAPACITY is returned). */

@@ -30,6 +30,7 @@ EXPORTS = [
     "nrn_engine_create", "nrn_engine_destroy", "nrn_engine_add_population", "nrn_engine_set_params",
     "nrn_engine_add_projection", "nrn_engine_generate_projection", "nrn_engine_set_stdp",
     "nrn_engine_finalize", "nrn_engine_run", "nrn_engine_sync", "nrn_engine_stream", "nrn_engine_step",
+    "nrn_engine_info",
     "nrn_engine_raster", "nrn_engine_weights", "nrn_engine_nnz", "nrn_engine_counters",
     "nrn_engine_profile", "nrn_engine_weights_device", "nrn_engine_set_state", "nrn_engine_set_step",
     "nrn_cuda_block_deliver", "nrn_cuda_block_stdp", "nrn_cuda_compact", "nrn_cuda_gather_ring",
@@ -131,6 +132,13 @@ class GenDesc(C.Structure):
     ]
 
 
+class EngineInfo(C.Structure):
+    _fields_ = [
+        ("window", C.c_int32), ("n_pops", C.c_int32), ("raster_capacity", C.c_int64),
+        ("recorded_neurons", C.c_int64), ("step", C.c_int64),
+    ]
+
+
 _lib = None
 
 
@@ -197,6 +205,7 @@ def lib() -> C.CDLL:
             "nrn_engine_add_probe": [vp, i32, i32, vp, i32, C.POINTER(i32)],
             "nrn_engine_clear_probes": [vp],
             "nrn_engine_profile_kernels": [vp, i64, C.POINTER(C.c_double), C.POINTER(i64)],
+            "nrn_engine_info": [vp, C.POINTER(EngineInfo)],
         }
         for name, args in sig.items():
             f = getattr(L, name)

@@ -158,8 +158,14 @@ struct SimEngine {
     // the plastic weights changed since the last write-back
     int64_t pending_first = 0, pending_steps = 0;
     bool weights_dirty = false;
+    // the engine's window, and the most steps between raster reads that
+    // cannot overflow the raster (every recorded neuron spiking every step)
+    int64_t window = 1, raster_every = 64;
+    // orders the engine stream after the caller's stream and back
+    cudaEvent_t order_ev = nullptr;
 
     ~SimEngine() {
+        if (order_ev) cudaEventDestroy(order_ev);
         if (e) nrn_engine_destroy(e);
     }
 };
@@ -433,6 +439,11 @@ void build_engine(Simulation* sim) {
     detail::check(nrn_engine_finalize(eng->e, 0), "sim: finalize");
     // continue the clock's step numbering (slow-clock boundaries, raster)
     detail::check(nrn_engine_set_step(eng->e, static_cast<int64_t>(sim->clock.step())), "sim: step");
+    nrn_engine_info_t info{};
+    detail::check(nrn_engine_info(eng->e, &info), "sim: engine info");
+    eng->window = std::max<int64_t>(1, info.window);
+    if (info.recorded_neurons > 0) eng->raster_every = std::max<int64_t>(1, info.raster_capacity / info.recorded_neurons);
+    TORCH_CHECK(cudaEventCreateWithFlags(&eng->order_ev, cudaEventDisableTiming) == cudaSuccess, "sim: cudaEventCreate");
     eng->n_pops = region->populations.size();
     eng->n_conns = region->connections.size();
     sim->engine = eng;
@@ -474,19 +485,18 @@ void drain_raster(Simulation* sim, int64_t first_step, int64_t n_steps) {
     bool any = false;
     for (auto& r : sim->recorders) any = any || r.ops == &spike_recorder_ops;
     if (!any) return;
+    // one call into the host buffers; a second only when they must grow
+    // (the call reports the count without copying)
     int64_t n = 0;
-    nrn_stream_t s = nullptr;
-    detail::check(nrn_engine_stream(g.e, &s), "sim");
-    // size query: a zero-capacity call reports the count without copying
-    nrn_status_t st = nrn_engine_raster(g.e, nullptr, nullptr, 0, &n);
-    if (st == NRN_ERR_CAPACITY && n > 0) {
-        g.raster_step.resize(n);
-        g.raster_gid.resize(n);
-        detail::check(nrn_engine_raster(g.e, g.raster_step.data(), g.raster_gid.data(), n, &n), "sim: raster");
-    } else {
-        detail::check(st, "sim: raster");
-        n = 0;
+    const auto cap = static_cast<int64_t>(g.raster_step.size());
+    nrn_status_t st = nrn_engine_raster(g.e, g.raster_step.data(), g.raster_gid.data(), cap, &n);
+    if (st == NRN_ERR_CAPACITY && n > cap) {
+        g.raster_step.resize(n + n / 2);
+        g.raster_gid.resize(n + n / 2);
+        st = nrn_engine_raster(g.e, g.raster_step.data(), g.raster_gid.data(),
+                               static_cast<int64_t>(g.raster_step.size()), &n);
     }
+    detail::check(st, "sim: raster");
     // each spike recorder counts its calls per step and keeps every
     // subsample-th step's spikes (spike_recorder.cpp semantics)
     const double dt = sim->options.dt_fast();
@@ -550,9 +560,9 @@ void sync_weights(Simulation* sim) {
 void drain(Simulation* sim) {
     SimEngine& g = *sim->engine;
     if (g.pending_steps == 0) return;
-    detail::check(nrn_engine_sync(g.e), "sim");
-    drain_raster(sim, g.pending_first, g.pending_steps);
+    drain_raster(sim, g.pending_first, g.pending_steps);   // waits for the engine stream
     if (!g.probes.empty()) {
+        detail::check(nrn_engine_sync(g.e), "sim");
         const double dt = sim->options.dt_fast();
         std::map<StateRecorderState*, std::vector<SimEngine::Probe*>> by_rec;
         for (auto& pr : g.probes) by_rec[pr.rec].push_back(&pr);
@@ -575,10 +585,11 @@ void drain(Simulation* sim) {
 }
 
 // Runs n steps.  No host wait per step: the spike raster and the state
-// probes are read back when a callback or a query needs them, when the
-// probe rings are full, and at the end of a multi-step call, which also
-// writes the plastic weights back (bulk=true); sim_step leaves both on the
-// device until then.
+// probes are read back when a callback or a query needs them, before the
+// probe rings or the raster can fill (at window boundaries where the limit
+// allows, so the engine replays whole-window graphs), and at the end of a
+// multi-step call, which also writes the plastic weights back (bulk=true);
+// sim_step leaves both on the device until then.
 void run_steps(Simulation* sim, int64_t n, bool bulk) {
     if (n <= 0) return;
     Region* region = sim->region;
@@ -597,8 +608,7 @@ void run_steps(Simulation* sim, int64_t n, bool bulk) {
     nrn_stream_t es = nullptr;
     detail::check(nrn_engine_stream(g.e, &es), "sim");
     // the engine stream starts after the caller's queued work
-    cudaEvent_t ev;
-    cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+    cudaEvent_t ev = g.order_ev;
     cudaEventRecord(ev, c10::cuda::getCurrentCUDAStream(g.device).stream());
     cudaStreamWaitEvent(reinterpret_cast<cudaStream_t>(es), ev, 0);
     const int64_t chunk = sim->options.use_cuda_graphs() ? 50 : 1;
@@ -618,8 +628,18 @@ void run_steps(Simulation* sim, int64_t n, bool bulk) {
             const int64_t k = ((first + every - 1) / every) * every;
             seg = std::min(seg, k - step + 1);
         }
-        if (!g.probes.empty()) seg = std::min<int64_t>(seg, g.probe_depth - g.pending_steps);
-        if (any_spike_rec) seg = std::min<int64_t>(seg, std::max<int64_t>(1, 64 - g.pending_steps));
+        // the next read-back: within the probe ring and the raster bound of
+        // the first step not yet read, rounded down to a window boundary
+        int64_t limit = 0;
+        if (!g.probes.empty()) limit = g.probe_depth;
+        if (any_spike_rec) limit = limit > 0 ? std::min(limit, g.raster_every) : g.raster_every;
+        int64_t read_at = -1;
+        if (limit > 0) {
+            read_at = g.pending_first + limit;
+            const int64_t aligned = read_at / g.window * g.window;
+            if (aligned > step) read_at = aligned;
+            seg = std::min(seg, read_at - step);
+        }
         seg = std::max<int64_t>(seg, 1);
         detail::check(nrn_engine_run(g.e, seg, static_cast<int32_t>(std::min(seg, chunk))), "sim: run");
         g.pending_steps += seg;
@@ -636,8 +656,7 @@ void run_steps(Simulation* sim, int64_t n, bool bulk) {
                 }
             sim->clock.advance_fast();
         }
-        if ((!g.probes.empty() && g.pending_steps >= g.probe_depth) || (any_spike_rec && g.pending_steps >= 64))
-            drain(sim);
+        if (read_at >= 0 && static_cast<int64_t>(sim->clock.step()) >= read_at) drain(sim);
         done += seg;
     }
     if (bulk) {
@@ -647,7 +666,6 @@ void run_steps(Simulation* sim, int64_t n, bool bulk) {
     // the caller's stream continues after the engine's work
     cudaEventRecord(ev, reinterpret_cast<cudaStream_t>(es));
     cudaStreamWaitEvent(c10::cuda::getCurrentCUDAStream(g.device).stream(), ev, 0);
-    cudaEventDestroy(ev);
 }
 
 }  // namespace

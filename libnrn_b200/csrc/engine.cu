@@ -933,6 +933,20 @@ nrn_status_t nrn_engine_stream(nrn_engine* e, nrn_stream_t* stream) {
 
 int64_t nrn_engine_step(const nrn_engine* e) { return e ? e->step : -1; }
 
+nrn_status_t nrn_engine_info(const nrn_engine* e, nrn_engine_info_t* out) {
+    NRN_CHECK_ARG(e != nullptr && out != nullptr, "nrn_engine_info: null argument");
+    NRN_CHECK_ARG(e->finalized, "nrn_engine_info: finalize first");
+    out->window = e->windows ? e->win : 1;
+    out->n_pops = static_cast<int32_t>(e->pops.size());
+    out->raster_capacity = e->raster_cap;
+    int64_t rec = 0;
+    for (const auto& p : e->pops)
+        if (p.d.record) rec += p.d.n;
+    out->recorded_neurons = rec;
+    out->step = e->step;
+    return NRN_OK;
+}
+
 nrn_status_t nrn_engine_add_population(nrn_engine* e, const nrn_pop_desc_t* d, int32_t* id) {
     ENGINE_GUARD(e);
     NRN_CHECK_ARG(d != nullptr, "null population");
@@ -1371,7 +1385,7 @@ nrn_status_t nrn_engine_finalize(nrn_engine* e, int32_t init_update) {
     for (auto& p : e->pops)
         if (p.d.record) rec_n += p.d.n;
     if (rec_n > 0) {
-        e->raster_cap = std::max<int64_t>(int64_t(1) << 20, std::min<int64_t>(rec_n * 64, int64_t(1) << 26));
+        e->raster_cap = std::max<int64_t>(int64_t(1) << 22, std::min<int64_t>(rec_n * 64, int64_t(1) << 26));
         NRN_TRY(dalloc0(&e->raster_step, e->raster_cap, e->stream));
         NRN_TRY(dalloc0(&e->raster_gid, e->raster_cap, e->stream));
     }
@@ -1446,14 +1460,25 @@ nrn_status_t nrn_engine_run(nrn_engine* e, int64_t steps, int32_t chunk) {
         // window first completes it, then runs whole windows (chunks a
         // multiple of the window), then the rest; the graphs of each shape
         // are captured once and replayed.
+        //
+        // The pieces off the window grid (the steps up to the first window
+        // boundary and a tail shorter than a window) run as one-step graphs,
+        // keyed by phase, so a caller whose runs start and stop anywhere
+        // meets at most w + 3 shapes; without windows a tail shorter than a
+        // chunk runs as power-of-two graphs.
         const int w = e->windows ? e->win : 1;
         if (e->windows) chunk = std::max(w, chunk / w * w);
         while (left > 0) {
             const int phase = static_cast<int>(s % w);
             int c;
-            if (phase != 0) c = static_cast<int>(std::min<int64_t>(left, w - phase));
-            else if (left >= w) c = static_cast<int>(std::min<int64_t>(chunk, left / w * w));
-            else c = static_cast<int>(left);
+            if (phase != 0) c = 1;
+            else if (left >= w && w > 1) c = static_cast<int>(std::min<int64_t>(chunk, left / w * w));
+            else if (w > 1) c = 1;
+            else if (left >= chunk) c = chunk;
+            else {
+                c = 1;
+                while (2 * c <= left) c *= 2;
+            }
             cudaGraphExec_t g = nullptr;
             NRN_TRY(e->graph_for(c, &g, phase));
             NRN_CUDA_TRY(cudaGraphLaunch(g, e->stream));

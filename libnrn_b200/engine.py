@@ -202,6 +202,13 @@ class Network:
     def step(self) -> int:
         return int(self.L.nrn_engine_step(self.h))
 
+    def info(self) -> dict:
+        """The window, raster capacity and recorded neuron count
+        (nrn_engine_info)."""
+        i = N.EngineInfo()
+        N.check(self.L.nrn_engine_info(self.h, C.byref(i)), "info")
+        return {f: int(getattr(i, f)) for f, _ in N.EngineInfo._fields_}
+
     def raster(self, cap: int | None = None, out=None):
         """Spikes recorded since the last call: (step, gid), sorted by step then
         id (the engine sorts on the device before the copy).  ``out``: two
