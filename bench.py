@@ -461,16 +461,12 @@ def run_network(args, rank: int, world: int, local: int) -> None:
         sec = ms / 1e3
         value = events / sec
 
-        # e2e: this rank's initial state from pinned host, run, raster to
-        # host, all timed (wall clock, max over ranks).  The copies run on
-        # torch's stream; the engine stream starts after them.
-        host_state = []
-        for p in nw.pops:
-            for k in ("v", "ref"):
-                t = p[k]
-                if t is not None:
-                    host_state.append((t, t.cpu().pin_memory()))
-        h2d = sum(h.numel() * 4 for _, h in host_state)
+        # e2e: this rank's state from pinned host, run, raster to host, all
+        # timed (wall clock, max over ranks).  The copies run on torch's
+        # stream; the engine stream starts after them.  The host copy is the
+        # state the engine holds when the timed region starts (a state from
+        # an earlier step would put neurons out of step with their spike
+        # history and traces).
         # the raster is read into page-locked host arrays allocated up front
         rcap = sum(p["n"] for p in nw.pops) * 64
         rcap = min(max(rcap, 1 << 20), 1 << 26)
@@ -481,6 +477,13 @@ def run_network(args, rank: int, world: int, local: int) -> None:
             nw.run(pad, args.chunk)
         nw.sync()
         nw.raster()
+        host_state = []
+        for p in nw.pops:
+            for k in ("v", "ref"):
+                t = p[k]
+                if t is not None:
+                    host_state.append((t, t.cpu().pin_memory()))
+        h2d = sum(h.numel() * 4 for _, h in host_state)
         barrier()
         t0 = time.perf_counter()
         for dev_t, h in host_state:
@@ -507,6 +510,36 @@ def run_network(args, rank: int, world: int, local: int) -> None:
     prof, cnt = nw.profile_kernels(args.profile_steps)
     finish_network_line(args, spec, nw, world, rank, dist, all_reduce, peaks, peaks_kind, clk, ms, value, events,
                         spikes, nnz, setup_s, prof, cnt, e2e, e2e_s, h2d, d2h, (t0, t_up, t_run, t1))
+
+
+# Random-access ceilings of one B200 (operations per second, one kind alone;
+# libnrn_b200/csrc/l2_probe.cu, `bench.py --probe-l2`).
+L2_RED_PER_S = 186e9       # float reductions into a 4 MB array
+L2_LD16_PER_S = 222e9      # 16-byte loads from a 16 MB array
+L2_LD4_PER_S = 285e9       # 4-byte loads from a 4 MB array
+
+
+def l2_floor(kernel, cnt, prof, steps):
+    """The dominant kernel's floor set by its random L2 operations at the
+    probe's ceilings: a walk event is one 16-byte load (the target's newest
+    spike steps), one 4-byte load (its trace at the source spike) and one
+    reduction; a static event is one reduction."""
+    if kernel == "walk_kernel":
+        ev = cnt["walk_events"]
+        floor_s = ev / L2_LD16_PER_S + ev / L2_LD4_PER_S + ev / L2_RED_PER_S
+        ms = prof["stdp_walks"]
+    elif kernel == "deliver_kernel":
+        ev = cnt["static_events"]
+        floor_s = ev / L2_RED_PER_S
+        ms = prof["static_delivery"]
+    else:
+        return None
+    if ms <= 0 or steps <= 0:
+        return None
+    return {"floor_ms_per_launch": floor_s * 1e3 / steps, "ms_per_launch": ms / steps,
+            "frac": floor_s * 1e3 / ms,
+            "note": "random L2 operations per launch at the measured one-kind ceilings (186 G/s reductions, "
+                    "222 G/s 16-byte loads, 285 G/s 4-byte loads): the bound of this kernel"}
 
 
 def finish_network_line(args, spec, nw, world, rank, dist, all_reduce, peaks, peaks_kind, clk, ms, value, events,
@@ -617,6 +650,7 @@ def finish_network_line(args, spec, nw, world, rank, dist, all_reduce, peaks, pe
                      "traffic": traffic,
                      "traffic_note": "DRAM bytes per step of walk_kernel + deliver_kernel from ncu captures at "
                                      "262,144 neurons, x4 to the bench size" if traffic else None,
+                     "l2_floor": l2_floor(dom, cnt, prof, P),
                      "l2_random_ops_per_s": l2_ops / (deliv_ms / 1e3) if deliv_ms > 0 else None,
                      "l2_note": "random L2 reductions and loads of static delivery + walks per second of their "
                                 "serialised time; measured ceilings of one kind alone: 186 G/s reductions, 222 G/s "

@@ -131,3 +131,15 @@ def test_modulatory_gains_walk_equals_per_step_kernels():
         assert np.array_equal(a, b)
     for a, b in zip(walk[2], eager[2]):
         assert np.array_equal(a, b)
+
+
+def test_engine_info_reports_window_and_raster_bound():
+    net = S.realize(burst_spec(10))
+    nw = Network.from_net(net)
+    try:
+        info = nw.info()
+    finally:
+        nw.close()
+    assert info["window"] == 4                  # the smallest delay of the STDP projection
+    assert info["raster_capacity"] >= 1 << 22
+    assert info["recorded_neurons"] == sum(p["n"] for p in net["pops"])
