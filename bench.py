@@ -512,25 +512,24 @@ def run_network(args, rank: int, world: int, local: int) -> None:
                         spikes, nnz, setup_s, prof, cnt, e2e, e2e_s, h2d, d2h, (t0, t_up, t_run, t1))
 
 
-# Random-access ceilings of one B200 (operations per second, one kind alone;
-# libnrn_b200/csrc/l2_probe.cu, `bench.py --probe-l2`).
-L2_RED_PER_S = 186e9       # float reductions into a 4 MB array
-L2_LD16_PER_S = 222e9      # 16-byte loads from a 16 MB array
-L2_LD4_PER_S = 285e9       # 4-byte loads from a 4 MB array
+# Random-access ceilings of one B200, measured by libnrn_b200/csrc/l2_probe.cu
+# (`bench.py --probe-l2`) with the delivery kernels' memory pattern and
+# array sizes, and nothing else (no dependent chains, no STDP logic):
+WALK_EVENTS_PER_S = 85.2e9     # a 16-byte and a 4-byte load and a reduction at one random
+                               # target, with the synapse's 12 B sequential stream
+STATIC_EVENTS_PER_S = 155.4e9  # a reduction at a random target with the 8 B sequential stream
 
 
 def l2_floor(kernel, cnt, prof, steps):
-    """The dominant kernel's floor set by its random L2 operations at the
-    probe's ceilings: a walk event is one 16-byte load (the target's newest
-    spike steps), one 4-byte load (its trace at the source spike) and one
-    reduction; a static event is one reduction."""
+    """The dominant kernel's floor: its events at the probe's rate for the
+    same memory pattern.  A walk event is one 16-byte load (the target's
+    newest spike steps), one 4-byte load (its trace at the source spike) and
+    one reduction; a static event is one reduction."""
     if kernel == "walk_kernel":
-        ev = cnt["walk_events"]
-        floor_s = ev / L2_LD16_PER_S + ev / L2_LD4_PER_S + ev / L2_RED_PER_S
+        floor_s = cnt["walk_events"] / WALK_EVENTS_PER_S
         ms = prof["stdp_walks"]
     elif kernel == "deliver_kernel":
-        ev = cnt["static_events"]
-        floor_s = ev / L2_RED_PER_S
+        floor_s = cnt["static_events"] / STATIC_EVENTS_PER_S
         ms = prof["static_delivery"]
     else:
         return None
@@ -538,8 +537,8 @@ def l2_floor(kernel, cnt, prof, steps):
         return None
     return {"floor_ms_per_launch": floor_s * 1e3 / steps, "ms_per_launch": ms / steps,
             "frac": floor_s * 1e3 / ms,
-            "note": "random L2 operations per launch at the measured one-kind ceilings (186 G/s reductions, "
-                    "222 G/s 16-byte loads, 285 G/s 4-byte loads): the bound of this kernel"}
+            "note": "the kernel's events at the measured rate of their memory pattern alone (walk event: "
+                    "85.2 G/s; static event: 155.4 G/s): the bound of this kernel"}
 
 
 def finish_network_line(args, spec, nw, world, rank, dist, all_reduce, peaks, peaks_kind, clk, ms, value, events,
@@ -654,7 +653,7 @@ def finish_network_line(args, spec, nw, world, rank, dist, all_reduce, peaks, pe
                      "l2_random_ops_per_s": l2_ops / (deliv_ms / 1e3) if deliv_ms > 0 else None,
                      "l2_note": "random L2 reductions and loads of static delivery + walks per second of their "
                                 "serialised time; measured ceilings of one kind alone: 186 G/s reductions, 222 G/s "
-                                "16-byte loads, 285 G/s 4-byte loads"},
+                                "16-byte loads, 285 G/s 4-byte loads; mixed as in a walk event: 256 G/s"},
         "e2e": {"value": e2e, "unit": "events/s", "h2d_bytes_per_step": h2d / args.steps,
                 "d2h_bytes_per_step": d2h / args.steps,
                 "seconds": {"upload": t_up - t0, "run": t_run - t_up, "raster": t1 - t_run}},

@@ -1428,14 +1428,10 @@ nrn_status_t nrn_engine_finalize(nrn_engine* e, int32_t init_update) {
         NRN_TRY(need_history(e->pops[q.src_pop]));
         NRN_TRY(need_history(e->pops[q.tgt_pop]));
     }
-    // The drive is drawn ahead on the side stream into drive_buf, or (with
-    // NRN_DRIVE_INLINE=1) by the neuron update itself; both call the same
-    // sampler with the same counters, so the values are identical.
-    const char* inl = std::getenv("NRN_DRIVE_INLINE");
-    const bool drive_inline = inl != nullptr && inl[0] == '1';
+    // The drive is drawn ahead on the side stream (drawing it inside the
+    // neuron update, on the critical path, measured 8 us a step slower).
     for (auto& p : e->pops)
-        if (p.d.drive.kind != NRN_DRIVE_NONE && !drive_inline)
-            NRN_TRY(dalloc0(&p.drive_buf, static_cast<size_t>(p.d.n), e->stream));
+        if (p.d.drive.kind != NRN_DRIVE_NONE) NRN_TRY(dalloc0(&p.drive_buf, static_cast<size_t>(p.d.n), e->stream));
     if (e->spike_stats)
         for (auto& p : e->pops) NRN_TRY(dalloc0(&p.stats, static_cast<size_t>(p.d.n), e->stream));
     if (init_update) {

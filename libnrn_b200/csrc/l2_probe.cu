@@ -83,6 +83,42 @@ __global__ void dram_seq(const int4* big, long long n, int* out) {
     if (s == 0x12345) out[0] = s;
 }
 
+// The STDP walk's memory pattern per plastic event: at one random target i,
+// a 16-byte load (its newest spike steps), a 4-byte load (its trace) and a
+// float reduction (its input); with `stream`, also the synapse's sequential
+// target index and weight read and the weight written back (12 B).
+__global__ void walk_like(const int4* recent, const float* trace, float* acc, uint32_t mask, long long n_ev,
+                          const uint32_t* tgt, float* w, int stream, float* out) {
+    long long tid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    long long nt = (long long)gridDim.x * blockDim.x;
+    float s = 0;
+    for (long long k = tid; k < n_ev; k += nt) {
+        const uint32_t i = (stream ? tgt[k] : hash((uint32_t)k)) & mask;
+        const int4 r = recent[i];
+        const float x = trace[i];
+        const float wv = stream ? w[k] : 1.0f;
+        const float w1 = wv + (r.x == 0x7fffffff ? 1.0f : 0.0f) * x;
+        if (stream) w[k] = w1;
+        atomicAdd(acc + i, w1);
+        s += x;
+    }
+    if (s == 123.25f) out[0] = s;
+}
+
+// Static delivery per event: a float reduction at a random target, with the
+// synapse's sequential target index and weight (8 B).
+__global__ void deliver_like(float* acc, uint32_t mask, long long n_ev, const uint32_t* tgt, const float* w) {
+    long long tid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    long long nt = (long long)gridDim.x * blockDim.x;
+    for (long long k = tid; k < n_ev; k += nt) atomicAdd(acc + (tgt[k] & mask), w[k]);
+}
+
+__global__ void fill_hash(uint32_t* t, long long n) {
+    long long tid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    long long nt = (long long)gridDim.x * blockDim.x;
+    for (long long k = tid; k < n; k += nt) t[k] = hash((uint32_t)k * 2654435761u + 17u);
+}
+
 int main() {
     int sms = 0; cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
     float* acc; int4* tab16; float* tab4; int* outi; float* outf; int4* big;
@@ -135,6 +171,34 @@ int main() {
             cudaEventElapsedTime(&ms, a, b);
         }
         printf("blocks/SM %d  DRAM seq read 4GB: %.0f GB/s\n", bps, BIG / (ms * 1e6));
+    }
+    {
+        // mixed patterns at the walk's array sizes (1M targets), 8 blocks/SM
+        const long long E2 = 1ll << 26;
+        uint32_t* tg; float* wv;
+        CK(cudaMalloc(&tg, E2 * 4)); CK(cudaMalloc(&wv, E2 * 4));
+        fill_hash<<<sms * 8, 256>>>(tg, E2);
+        CK(cudaMemset(wv, 0, E2 * 4));
+        const int grid = sms * 8;
+        float ms;
+        for (int st = 0; st < 2; ++st) {
+            for (int rep = 0; rep < 2; ++rep) {
+                cudaEventRecord(a);
+                walk_like<<<grid, 256>>>(tab16, tab4, acc, N1 - 1, E2, tg, wv, st, outf);
+                cudaEventRecord(b); CK(cudaEventSynchronize(b));
+                cudaEventElapsedTime(&ms, a, b);
+            }
+            printf("walk-like event (LD.128 + LD.32 + RED at one random target%s): %.1f G events/s = %.1f G random ops/s\n",
+                   st ? ", + 12 B sequential synapse stream" : "", E2 / (ms * 1e6), 3.0 * E2 / (ms * 1e6));
+        }
+        for (int rep = 0; rep < 2; ++rep) {
+            cudaEventRecord(a); deliver_like<<<grid, 256>>>(acc, N1 - 1, E2, tg, wv); cudaEventRecord(b);
+            CK(cudaEventSynchronize(b));
+            cudaEventElapsedTime(&ms, a, b);
+        }
+        printf("delivery-like event (RED at a random target + 8 B sequential synapse stream): %.1f G events/s\n",
+               E2 / (ms * 1e6));
+        cudaFree(tg); cudaFree(wv);
     }
     CK(cudaGetLastError());
     return 0;
