@@ -196,10 +196,15 @@ def cpu_reference(args, world_steps_hint=None):
     return out
 
 
-# dram__bytes_read.sum + dram__bytes_write.sum of walk_kernel (8.349 MB) and
-# deliver_kernel (2.812 MB) per launch in ncu captures of the bench network at
-# 262,144 neurons (bench.py --scale 0.25), scaled x4 to 1,048,576 neurons
-DELIVERY_TRAFFIC_PER_STEP = 4 * (8.349184e6 + 2.811904e6)
+# dram__bytes_read.sum + dram__bytes_write.sum of one walk_kernel launch in an
+# ncu capture of the bench network at 262,144 neurons (bench.py --scale 0.25
+# --burn-in 200, launch 301), and the walk events of a step at that size;
+# the bench line scales the bytes by its own walk events per step.
+WALK_TRAFFIC_CAPTURED = 13.138432e6 + 0.0
+WALK_EVENTS_CAPTURED = 632_380.0
+# the same for the full-size block-sparse product (one launch, 262,144
+# neurons, 64 trials)
+BSR_TRAFFIC_CAPTURED = 2.854493e9 + 44.104192e6
 
 BSR_N = 262_144          # pre = post neurons of the batched block-sparse workload
 BSR_DENSITY = 0.02       # fraction of the 64x64 block slots present
@@ -328,7 +333,9 @@ def run_bsr(args, rank: int, world: int, local: int) -> None:
         "gpu_launches": 2 * args.steps,
         "roofline": {"kernel": "bsr_kernel", "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "peak_kind": peaks_kind,
-                     "traffic": None, "tensor_frac": flops / (k_ms / 1e3) / 1e12 / peaks.get("bf16_tflops", 1590.0)},
+                     "traffic": BSR_TRAFFIC_CAPTURED if n == BSR_N else None,
+                     "traffic_note": "DRAM bytes of one full-size bsr_kernel launch from an ncu capture",
+                     "tensor_frac": flops / (k_ms / 1e3) / 1e12 / peaks.get("bf16_tflops", 1590.0)},
         "e2e": {"value": e2e, "unit": "updates/s", "h2d_bytes_per_step": tiles.numel() * 2,
                 "d2h_bytes_per_step": cur.numel() * 4 / k_e2e},
         "clocks": clk.summary(),
@@ -584,7 +591,9 @@ def finish_network_line(args, spec, nw, world, rank, dist, all_reduce, peaks, pe
     # plastic event two loads (the target's spike steps and its trace).
     l2_ops = cnt["static_events"] + cnt["walk_events"] * 3
     deliv_ms = prof["static_delivery"] + prof["stdp_walks"]
-    traffic = DELIVERY_TRAFFIC_PER_STEP if args.workload == "brunel_stdp" and args.scale == 1.0 else None
+    traffic = None
+    if args.workload == "brunel_stdp" and dom == "walk_kernel" and cnt["walk_events"] > 0:
+        traffic = WALK_TRAFFIC_CAPTURED * (cnt["walk_events"] / P) / WALK_EVENTS_CAPTURED
 
     exch_ms = None
     if dist is not None:
@@ -647,8 +656,8 @@ def finish_network_line(args, spec, nw, world, rank, dist, all_reduce, peaks, pe
                      "step_frac": (walk_bytes + deliver_bytes + neuron_bytes) / P / (ms / args.steps / 1e3) / 1e9
                      / peaks["hbm_gbs"],
                      "traffic": traffic,
-                     "traffic_note": "DRAM bytes per step of walk_kernel + deliver_kernel from ncu captures at "
-                                     "262,144 neurons, x4 to the bench size" if traffic else None,
+                     "traffic_note": "DRAM bytes of one walk_kernel launch from an ncu capture at 262,144 neurons, "
+                                     "scaled by walk events per step to this run" if traffic else None,
                      "l2_floor": l2_floor(dom, cnt, prof, P),
                      "l2_random_ops_per_s": l2_ops / (deliv_ms / 1e3) if deliv_ms > 0 else None,
                      "l2_note": "random L2 reductions and loads of static delivery + walks per second of their "

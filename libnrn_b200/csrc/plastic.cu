@@ -262,31 +262,41 @@ __device__ __forceinline__ void build_table(const WalkArgs& a, const Seg& g, flo
     const int W = a.win, e = g.e;
     const int m0 = (g.T + 1) / W + 1;   // window ends b = m*W - 1 in (T, e): m = m0, m0+1, ...
     const int n_pieces = 1 + (m0 * W - 1 < e ? (e - (m0 * W - 1) + W - 1) / W : 0);
-    for (int pc = lane; pc < n_pieces; pc += 32) {
-        int start;
-        float x;
-        if (pc == 0) {
-            start = g.T;
-            x = xT;
-        } else {
-            const int m = m0 + pc - 1;
-            start = m * W - 1;
-            if (m_new - m >= a.pre_depth) set_err(a.err, ERR_SNAPSHOT);
-            x = a.pre_snap[static_cast<long long>(m & (a.pre_depth - 1)) * a.n_src + g.j];
-        }
-        const int stop = pc == 0 ? (m0 * W - 1 < e ? m0 * W - 1 : e) : (start + W < e ? start + W : e);
-        int q = 0;
-        while (q < g.P.n && g.P[q] <= start) ++q;
-        int next = q < g.P.n ? g.P[q] : INT_MAX;
-        for (int u = start + 1; u <= stop; ++u) {
-            float sp = 0.0f;
-            if (next == u) {
-                sp = 1.0f;
-                ++q;
-                next = q < g.P.n ? g.P[q] : INT_MAX;
+    // a lane's pieces kBatch at a time, their snapshot loads issued together
+    // (short windows make many pieces: one per step for a one-step window)
+    constexpr int kBatch = 4;
+    for (int pc0 = lane; pc0 < n_pieces; pc0 += 32 * kBatch) {
+        float xs[kBatch];
+#pragma unroll
+        for (int b = 0; b < kBatch; ++b) {
+            const int pc = pc0 + 32 * b;
+            xs[b] = xT;
+            if (pc > 0 && pc < n_pieces) {
+                const int m = m0 + pc - 1;
+                if (m_new - m >= a.pre_depth) set_err(a.err, ERR_SNAPSHOT);
+                xs[b] = __ldg(a.pre_snap + static_cast<long long>(m & (a.pre_depth - 1)) * a.n_src + g.j);
             }
-            x = x * a.decay_pre + sp;
-            sX[u - g.T - 1] = x;
+        }
+#pragma unroll
+        for (int b = 0; b < kBatch; ++b) {
+            const int pc = pc0 + 32 * b;
+            if (pc >= n_pieces) break;
+            const int start = pc == 0 ? g.T : (m0 + pc - 1) * W - 1;
+            float x = xs[b];
+            const int stop = pc == 0 ? (m0 * W - 1 < e ? m0 * W - 1 : e) : (start + W < e ? start + W : e);
+            int q = 0;
+            while (q < g.P.n && g.P[q] <= start) ++q;
+            int next = q < g.P.n ? g.P[q] : INT_MAX;
+            for (int u = start + 1; u <= stop; ++u) {
+                float sp = 0.0f;
+                if (next == u) {
+                    sp = 1.0f;
+                    ++q;
+                    next = q < g.P.n ? g.P[q] : INT_MAX;
+                }
+                x = x * a.decay_pre + sp;
+                sX[u - g.T - 1] = x;
+            }
         }
     }
 }

@@ -1,6 +1,7 @@
 // api_bench -- the Brunel network of the reference's example configuration
 // (10,000 E + 2,500 I LIF, connection probability 0.1, so in-degree about
-// 1,000 + 250, delay 1.5 ms, dt 0.1 ms, pair STDP on E->E) built and run
+// 1,000 + 250, dt 0.1 ms, pair STDP on E->E; the random topology gives every
+// synapse a delay of one step, as the reference's does) built and run
 // only through the nrn:: C++ API, as a user program of the reference would.
 // It times the same number of steps twice on the GPU engine behind the API:
 // one sim_run_steps(N) call, and N sim_step calls; each measurement ends
@@ -51,7 +52,7 @@ Net build(int64_t ne, int64_t ni) {
     auto* syn = synapse::static_synapse_create(1);
     auto sm = synapse::static_synapse_as_module(syn);
     const double je = 0.1e-3 * 250e-12 / 1e-4 * 2.0, ji = -5.0 * je;   // mean weight J c_m / dt
-    auto opt = [](double w) { return ConnectOptions().block_size(256).weight_scale(w).default_delay(1.5e-3); };
+    auto opt = [](double w) { return ConnectOptions().block_size(256).weight_scale(w); };
     auto ee = connect(n.exc, n.exc, &gen, sm, opt(je));
     auto ei = connect(n.exc, n.inh, &gen, sm, opt(je));
     auto ie = connect(n.inh, n.exc, &gen, sm, opt(ji));
@@ -109,7 +110,7 @@ int main(int argc, char** argv) {
     const double dt = 1e-4;
     std::printf(
         "{\"metric\": \"synaptic_events_per_s\", \"path\": \"nrn:: C++ API (libnrn.so)\", \"workload\": "
-        "\"Brunel 10,000 E + 2,500 I, p = 0.1, delay 1.5 ms, STDP on E->E\", \"steps\": %lld, \"synapses\": %lld, "
+        "\"Brunel 10,000 E + 2,500 I, p = 0.1, delay 1 step, STDP on E->E\", \"steps\": %lld, \"synapses\": %lld, "
         "\"sim_run_steps\": {\"ms_per_step\": %.5f, \"rtf\": %.4f, \"events_per_s\": %.4e, \"spikes\": %lld}, "
         "\"sim_step_loop\": {\"ms_per_step\": %.5f, \"host_ms_per_step\": %.5f, \"rtf\": %.4f, \"events_per_s\": %.4e, "
         "\"spikes\": %lld}, "
