@@ -39,6 +39,7 @@ constexpr int kMaxPairs = 1024;   // (projection, delay) pairs per launch
 constexpr int kChunk = 128;       // synapses per warp work unit of the STDP kernels (4 per lane)
 constexpr int kDeliverVec = 4;    // synapses per lane of one delivery unit
 constexpr int kDeliverChunk = 32 * kDeliverVec;
+constexpr int kInFlight = 2;      // delivery units whose loads are in flight together
 
 struct DeliverParams {
     nrn_proj_t proj[NRN_MAX_PROJ];
@@ -80,7 +81,7 @@ size_t pair_smem(int npairs) {
 // kDeliverChunk) units (units past the segment's end are empty), so the units of
 // one step are numbered without a prefix over segment lengths and spread
 // evenly over a full-occupancy grid.
-__global__ void __launch_bounds__(kThreads) deliver_kernel(const __grid_constant__ DeliverParams P) {
+__global__ void __launch_bounds__(kThreads, 5) deliver_kernel(const __grid_constant__ DeliverParams P) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const PairView tab = pair_view(smem_raw, P.npairs);
     using Scan = cub::BlockScan<long long, kThreads>;
@@ -127,44 +128,75 @@ __global__ void __launch_bounds__(kThreads) deliver_kernel(const __grid_constant
     __syncthreads();
     const long long n_units = tab.start[P.npairs];
 
+    // Warp w takes units w, w + n_warps, w + 2 n_warps, ...  The lanes first
+    // resolve the headers of 32 of them at once (spike id, then segment
+    // bounds: two dependent loads, paid once per 32 units), then the warp
+    // streams those units kInFlight at a time, the target and weight loads
+    // of all of them issued before their reductions.
     const int lane = threadIdx.x & 31;
     const long long warp = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
     const long long n_warps = (static_cast<long long>(gridDim.x) * kThreads) >> 5;
+    const long long mine = warp < n_units ? (n_units - warp + n_warps - 1) / n_warps : 0;   // this warp's units
     unsigned long long my_events = 0;
-    for (long long u = warp; u < n_units; u += n_warps) {
-        int lo = 0, hi = P.npairs - 1;
-        while (lo < hi) {
-            const int mid = (lo + hi + 1) >> 1;
-            if (tab.start[mid] <= u) lo = mid; else hi = mid - 1;
+    for (long long hb = 0; hb < mine; hb += 32) {
+        const long long u = warp + (hb + lane) * n_warps;
+        long long s0 = 0;
+        int len = 0, q = 0;
+        if (hb + lane < mine) {
+            int lo = 0, hi = P.npairs - 1;
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (tab.start[mid] <= u) lo = mid; else hi = mid - 1;
+            }
+            const long long local = u - tab.start[lo];
+            const int chunks = tab.chunks[lo];
+            const long long spike = local / chunks;
+            const int chunk = static_cast<int>(local - spike * chunks);
+            q = tab.proj[lo];
+            const nrn_proj_t& pr = P.proj[q];
+            const nrn_spike_hist_t& h = P.hist[pr.src_hist];
+            const int j = h.ids[static_cast<long long>(tab.slot[lo]) * h.cap + spike];
+            const long long seg = static_cast<long long>(j) * pr.nd + tab.k[lo];
+            const long long e0 = pr.seg_ptr[seg + 1];
+            s0 = pr.seg_ptr[seg] + static_cast<long long>(chunk) * kDeliverChunk;
+            const long long s1 = s0 + kDeliverChunk < e0 ? s0 + kDeliverChunk : e0;
+            len = s1 > s0 ? static_cast<int>(s1 - s0) : 0;
+            my_events += static_cast<unsigned long long>(len);
         }
-        const long long local = u - tab.start[lo];
-        const int chunks = tab.chunks[lo];
-        const long long spike = local / chunks;
-        const int chunk = static_cast<int>(local - spike * chunks);
-        const nrn_proj_t& pr = P.proj[tab.proj[lo]];
-        const nrn_spike_hist_t& h = P.hist[pr.src_hist];
-        const int j = h.ids[static_cast<long long>(tab.slot[lo]) * h.cap + spike];
-        const long long seg = static_cast<long long>(j) * pr.nd + tab.k[lo];
-        const long long e0 = pr.seg_ptr[seg + 1];
-        const long long s0 = pr.seg_ptr[seg] + static_cast<long long>(chunk) * kDeliverChunk;
-        const long long s1 = s0 + kDeliverChunk < e0 ? s0 + kDeliverChunk : e0;
-        if (s0 >= s1) continue;
-        if (lane == 0) my_events += static_cast<unsigned long long>(s1 - s0);
-        uint32_t t[kDeliverVec];
-        float w[kDeliverVec];
+        const int nh = mine - hb < 32 ? static_cast<int>(mine - hb) : 32;
+        for (int i = 0; i < nh; i += kInFlight) {
+            uint32_t t[kInFlight][kDeliverVec];
+            float w[kInFlight][kDeliverVec];
+            int n[kInFlight], qa[kInFlight];   // this lane's synapses of the unit: lane + 32 v < n
 #pragma unroll
-        for (int v = 0; v < kDeliverVec; ++v) {
-            const long long syn = s0 + lane + 32 * v;
-            if (syn < s1) {
-                t[v] = __ldg(pr.tgt + syn);
-                w[v] = __ldg(pr.w + syn);
-                if (pr.mod != nullptr) w[v] = w[v] * __ldg(pr.mod + syn);
+            for (int f = 0; f < kInFlight; ++f) {
+                // every lane takes part in the shuffles; units past nh are empty
+                const long long a0 = __shfl_sync(0xffffffffu, s0, (i + f) & 31);
+                n[f] = __shfl_sync(0xffffffffu, len, (i + f) & 31);
+                qa[f] = __shfl_sync(0xffffffffu, q, (i + f) & 31);
+                if (i + f >= nh) n[f] = 0;
+                const nrn_proj_t& pr = P.proj[qa[f]];
+#pragma unroll
+                for (int v = 0; v < kDeliverVec; ++v) {
+                    if (lane + 32 * v < n[f]) {
+                        const long long syn = a0 + lane + 32 * v;
+                        t[f][v] = __ldg(pr.tgt + syn);
+                        w[f][v] = __ldg(pr.w + syn);
+                        if (pr.mod != nullptr) w[f][v] = w[f][v] * __ldg(pr.mod + syn);
+                    }
+                }
+            }
+#pragma unroll
+            for (int f = 0; f < kInFlight; ++f) {
+                float* acc = P.proj[qa[f]].acc;
+#pragma unroll
+                for (int v = 0; v < kDeliverVec; ++v)
+                    if (lane + 32 * v < n[f]) atomicAdd(acc + t[f][v], w[f][v]);
             }
         }
-#pragma unroll
-        for (int v = 0; v < kDeliverVec; ++v)
-            if (s0 + lane + 32 * v < s1) atomicAdd(pr.acc + t[v], w[v]);
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) my_events += __shfl_down_sync(0xffffffffu, my_events, o);
     if (P.events && lane == 0 && my_events) atomicAdd(P.events, my_events);
 }
 
