@@ -49,7 +49,8 @@ namespace nrn {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kMinBlocks = 4;    // 64 registers a thread
+constexpr int kMinBlocks = 1024 / kThreads;   // 64 registers a thread
+constexpr int kPairsPer = (256 + kThreads - 1) / kThreads;   // delay values per thread in the prologue
 constexpr int kMaxPost = 64;     // target spike steps one walk may need (the ring depth)
 constexpr int kMaxPre = 8;       // source spike steps one walk may need
 constexpr int kMaxSpan = 1280;   // steps one walk may cover (x_pre table per warp)
@@ -559,15 +560,22 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) walk_kernel(const __grid
         // Arrivals: spikes of step - (dmin + k) through the delay-k
         // segments, one unit each; then the sweep: the segments of rows
         // [r0, r0 + rows), kGroup per unit.
-        long long units = 0;
-        if (tid < a.nd) {
-            const long long src_step = step - (a.dmin + tid);
-            slot[tid] = src_step >= 0 ? static_cast<int>(src_step % a.hist_src.depth) : 0;
-            if (src_step >= 0) units = a.hist_src.count[slot[tid]];
+        long long units[kPairsPer];
+#pragma unroll
+        for (int r = 0; r < kPairsPer; ++r) {
+            const int k = tid * kPairsPer + r;   // the scan's blocked arrangement
+            units[r] = 0;
+            if (k < a.nd) {
+                const long long src_step = step - (a.dmin + k);
+                slot[k] = src_step >= 0 ? static_cast<int>(src_step % a.hist_src.depth) : 0;
+                if (src_step >= 0) units[r] = a.hist_src.count[slot[k]];
+            }
         }
-        long long excl, n_arr;
+        long long excl[kPairsPer], n_arr;
         Scan(scan_tmp).ExclusiveSum(units, excl, n_arr);
-        if (tid < a.nd) start[tid] = excl;
+#pragma unroll
+        for (int r = 0; r < kPairsPer; ++r)
+            if (tid * kPairsPer + r < a.nd) start[tid * kPairsPer + r] = excl[r];
         if (tid == 0) {
             start[a.nd] = n_arr;
             const long long r0 = (step % a.sweep_period) * a.sweep_rows;
