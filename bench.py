@@ -434,7 +434,11 @@ def run_network(args, rank: int, world: int, local: int) -> None:
     # by the window phase and length of each piece of a run; one untimed run
     # of the timed length from the same window phase captures the graphs the
     # timed run replays, so no graph is captured inside the timed region.
-    win = 15
+    win = nw.info()["window"]
+    # the timed run starts on a window boundary (whole-window graphs first)
+    lead = (-(nw.step + args.warmup)) % win
+    if lead:
+        nw.run(lead, args.chunk)
     phase0 = (nw.step + args.warmup) % win
     nw.run(args.warmup, args.chunk)
     nw.run(args.steps, args.chunk)
