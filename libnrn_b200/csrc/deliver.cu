@@ -179,10 +179,12 @@ __global__ void __launch_bounds__(kThreads, 5) deliver_kernel(const __grid_const
 #pragma unroll
                 for (int v = 0; v < kDeliverVec; ++v) {
                     if (lane + 32 * v < n[f]) {
+                        // the synapse stream is read once a step: evict first, so the
+                        // accumulators and spike records stay in L2
                         const long long syn = a0 + lane + 32 * v;
-                        t[f][v] = __ldg(pr.tgt + syn);
-                        w[f][v] = __ldg(pr.w + syn);
-                        if (pr.mod != nullptr) w[f][v] = w[f][v] * __ldg(pr.mod + syn);
+                        t[f][v] = __ldcs(pr.tgt + syn);
+                        w[f][v] = __ldcs(pr.w + syn);
+                        if (pr.mod != nullptr) w[f][v] = w[f][v] * __ldcs(pr.mod + syn);
                     }
                 }
             }
