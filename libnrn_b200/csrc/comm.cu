@@ -1,15 +1,17 @@
 // comm.cu -- the engine's NCCL communicator, with bounded host waits.
 //
 // A partitioned network exchanges spikes with one NCCL all-gather per
-// window.  A blocking communicator turns any rank that dies, stops early or
-// disagrees on the exchange layout into a hang of every other rank inside
-// NCCL.  Here the communicator is created non-blocking and every host wait
-// on it (its set-up, a call that returns ncclInProgress, the engine stream
-// of a partitioned run) polls with a time limit.  On an NCCL error or a
-// timeout the communicator is aborted (ncclCommAbort ends the NCCL kernels
-// still waiting for a peer) and the call returns NRN_ERR_COMM; the engine
-// then refuses further runs.  The reference has no counterpart: its runner
-// is single-device (src/simulation/runner.cpp).
+// window.  Left alone, any rank that dies, stops early or disagrees on the
+// exchange layout would hang every other rank inside NCCL.  Here every host
+// wait on the communicator polls with a time limit: its set-up (run on a
+// helper thread, since the communicator is blocking so that its
+// collectives can be captured in CUDA graphs), a call that returns
+// ncclInProgress, and the engine stream of a partitioned run (polling
+// cudaStreamQuery and ncclCommGetAsyncError).  On an NCCL error or a
+// timeout the communicator is aborted on a helper thread (ncclCommAbort
+// ends the NCCL kernels still waiting for a peer) and the call returns
+// NRN_ERR_COMM; the engine then refuses further runs.  The reference has no
+// counterpart: its runner is single-device (src/simulation/runner.cpp).
 #include <cuda_runtime.h>
 #include <nccl.h>
 
