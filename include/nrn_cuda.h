@@ -497,8 +497,8 @@ NRN_API nrn_status_t nrn_engine_destroy(nrn_engine* e);
  * Every rank must run the same step counts.  No counterpart in the
  * reference (its runner is single-device, src/simulation/runner.cpp). */
 NRN_API nrn_status_t nrn_comm_unique_id(uint8_t id[128]);
-/* The communicator is non-blocking and every host wait on it is bounded
- * (nrn_engine_set_comm_timeout, default 120 s): its set-up here, the layout
+/* Every host wait on the communicator is bounded (nrn_engine_set_comm_timeout,
+ * default 120 s): its set-up here (on a helper thread), the layout
  * check in nrn_engine_finalize (every rank must build the same network:
  * otherwise NRN_ERR_COMM), and every wait on the engine stream of a
  * partitioned run (nrn_engine_sync, raster and weight reads, checkpoints).

@@ -222,9 +222,10 @@ struct UnpackArgs {
 };
 nrn_status_t unpack_launch(const UnpackArgs& a, long long step_off, const long long* step_base, cudaStream_t s);
 
-// The engine's NCCL communicator (comm.cu): non-blocking, every host wait
-// bounded by timeout_s; on an error or a timeout the communicator is
-// aborted (*c becomes null) and NRN_ERR_COMM returned.
+// The engine's NCCL communicator (comm.cu): blocking (its collectives are
+// captured in CUDA graphs), every host wait on it bounded by timeout_s; on
+// an error or a timeout the communicator is aborted (*c becomes null) and
+// NRN_ERR_COMM returned.
 nrn_status_t comm_init(ncclComm_t* out, int world, const uint8_t id[128], int rank, double timeout_s);
 // After an NCCL call that returned r.
 nrn_status_t comm_settle(ncclComm_t* c, ncclResult_t r, double timeout_s, const char* what);
