@@ -430,28 +430,24 @@ def run_network(args, rank: int, world: int, local: int) -> None:
         nw.sync()
         nw.raster()
         burn -= k
-    # Priming (untimed): the engine runs every step inside CUDA graphs keyed
-    # by the window phase and length of each piece of a run; one untimed run
-    # of the timed length from the same window phase captures the graphs the
-    # timed run replays, so no graph is captured inside the timed region.
+    # The timed run starts on a window boundary (whole-window graphs first).
     win = nw.info()["window"]
-    # the timed run starts on a window boundary (whole-window graphs first)
     lead = (-(nw.step + args.warmup)) % win
     if lead:
         nw.run(lead, args.chunk)
-    phase0 = (nw.step + args.warmup) % win
-    nw.run(args.warmup, args.chunk)
-    nw.run(args.steps, args.chunk)
-    pad = (phase0 - nw.step) % win
-    if pad:
-        nw.run(pad, args.chunk)
+    # Graphs (untimed): the engine runs every step inside CUDA graphs keyed
+    # by the window phase and length of each piece of a run; the graphs the
+    # warm-up and the timed run replay are captured and uploaded here without
+    # running them, so none is captured inside the timed region.
+    nw.prepare(nw.step, args.warmup, args.chunk)
+    nw.prepare(nw.step + args.warmup, args.steps, args.chunk)
     nw.sync()
     nw.raster()
     # Clocks are sampled from the warm-up through the end-to-end run: a
     # short timed region (tens of steps) holds no sample of its own.
     with ClockSampler(local) as clk:
         clk.wait_first(2.0)
-        nw.run(args.warmup, args.chunk)     # the same phase and lengths as in the priming
+        nw.run(args.warmup, args.chunk)
         nw.sync()
         nw.raster()
         s0, e0 = nw.counters()
@@ -483,9 +479,7 @@ def run_network(args, rank: int, world: int, local: int) -> None:
         rcap = min(max(rcap, 1 << 20), 1 << 26)
         r_st = torch.empty(rcap, dtype=torch.int32).pin_memory().numpy()
         r_gid = torch.empty(rcap, dtype=torch.int32).pin_memory().numpy()
-        pad = (phase0 + args.warmup - nw.step) % win   # the timed run's phase: its graphs again
-        if pad:
-            nw.run(pad, args.chunk)
+        nw.prepare(nw.step, args.steps, args.chunk)   # the end-to-end run's graphs, untimed
         nw.sync()
         nw.raster()
         host_state = []

@@ -546,6 +546,11 @@ NRN_API nrn_status_t nrn_engine_set_deterministic(nrn_engine* e, int32_t on);
 NRN_API nrn_status_t nrn_engine_finalize(nrn_engine* e, int32_t init_update);
 /* Enqueues `steps` steps (CUDA graphs of `chunk` steps; 0 picks a size). */
 NRN_API nrn_status_t nrn_engine_run(nrn_engine* e, int64_t steps, int32_t chunk);
+/* Captures (without running them) the CUDA graphs that nrn_engine_run(e,
+ * steps, chunk) would replay when started at step first_step, so that a
+ * later run -- a timed one, or the first steps of a simulation -- captures
+ * none. */
+NRN_API nrn_status_t nrn_engine_prepare(nrn_engine* e, int64_t first_step, int64_t steps, int32_t chunk);
 NRN_API nrn_status_t nrn_engine_sync(nrn_engine* e);
 /* Sets the number of the next step (drive counters, slow-clock boundaries,
  * raster step numbers); spikes already in flight keep their ring slots. */

@@ -30,7 +30,7 @@ EXPORTS = [
     "nrn_engine_create", "nrn_engine_destroy", "nrn_engine_add_population", "nrn_engine_set_params",
     "nrn_engine_add_projection", "nrn_engine_generate_projection", "nrn_engine_set_stdp",
     "nrn_engine_finalize", "nrn_engine_run", "nrn_engine_sync", "nrn_engine_stream", "nrn_engine_step",
-    "nrn_engine_info",
+    "nrn_engine_info", "nrn_engine_prepare",
     "nrn_engine_raster", "nrn_engine_weights", "nrn_engine_nnz", "nrn_engine_counters",
     "nrn_engine_profile", "nrn_engine_weights_device", "nrn_engine_set_state", "nrn_engine_set_step",
     "nrn_cuda_block_deliver", "nrn_cuda_block_stdp", "nrn_cuda_compact", "nrn_cuda_gather_ring",
@@ -206,6 +206,7 @@ def lib() -> C.CDLL:
             "nrn_engine_clear_probes": [vp],
             "nrn_engine_profile_kernels": [vp, i64, C.POINTER(C.c_double), C.POINTER(i64)],
             "nrn_engine_info": [vp, C.POINTER(EngineInfo)],
+            "nrn_engine_prepare": [vp, i64, i64, i32],
         }
         for name, args in sig.items():
             f = getattr(L, name)

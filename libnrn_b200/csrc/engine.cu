@@ -665,6 +665,25 @@ struct nrn_engine {
     }
 
     // A graph of `chunk` steps starting at a window start (when windows are on).
+    // Graph length of whole-window pieces (0 picks 50 steps, rounded to windows).
+    int run_chunk(int chunk) const {
+        if (chunk <= 0) chunk = 50;
+        const int w = windows ? win : 1;
+        return windows ? std::max(w, chunk / w * w) : chunk;
+    }
+    // The length of the next graph of a run that is at window phase `phase`
+    // with `left` steps to go.
+    int run_piece(int phase, int64_t left, int chunk) const {
+        const int w = windows ? win : 1;
+        if (phase != 0) return 1;
+        if (left >= w && w > 1) return static_cast<int>(std::min<int64_t>(chunk, left / w * w));
+        if (w > 1) return 1;
+        if (left >= chunk) return chunk;
+        int c = 1;
+        while (2 * c <= left) c *= 2;
+        return c;
+    }
+
     nrn_status_t graph_for(int chunk, cudaGraphExec_t* out, int phase = 0) {
         const auto key = std::make_pair(phase, chunk);
         auto it = graphs.find(key);
@@ -690,6 +709,12 @@ struct nrn_engine {
         e = cudaGraphInstantiate(&ex, g, 0);
         cudaGraphDestroy(g);
         if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
+        // the upload a first launch would do, done now (ahead of a timed run)
+        e = cudaGraphUpload(ex, stream);
+        if (e != cudaSuccess) {
+            cudaGraphExecDestroy(ex);
+            return cuda_fail(e, "cudaGraphUpload");
+        }
         graphs[key] = ex;
         *out = ex;
         return NRN_OK;
@@ -1445,6 +1470,25 @@ nrn_status_t nrn_engine_finalize(nrn_engine* e, int32_t init_update) {
     return NRN_OK;
 }
 
+nrn_status_t nrn_engine_prepare(nrn_engine* e, int64_t first_step, int64_t steps, int32_t chunk) {
+    ENGINE_GUARD(e);
+    NRN_CHECK_ARG(e->finalized, "nrn_engine_prepare: finalize first");
+    NRN_CHECK_ARG(steps >= 0 && first_step >= 0, "nrn_engine_prepare: negative step");
+    if (!e->use_graphs || steps == 0) return NRN_OK;
+    int64_t s = first_step, left = steps;
+    const int w = e->windows ? e->win : 1;
+    const int ch = e->run_chunk(chunk);
+    while (left > 0) {
+        const int phase = static_cast<int>(s % w);
+        const int c = e->run_piece(phase, left, ch);
+        cudaGraphExec_t g = nullptr;
+        NRN_TRY(e->graph_for(c, &g, phase));
+        s += c;
+        left -= c;
+    }
+    return NRN_OK;
+}
+
 nrn_status_t nrn_engine_run(nrn_engine* e, int64_t steps, int32_t chunk) {
     ENGINE_GUARD(e);
     NRN_CHECK_ARG(e->finalized, "nrn_engine_run: finalize first");
@@ -1452,7 +1496,6 @@ nrn_status_t nrn_engine_run(nrn_engine* e, int64_t steps, int32_t chunk) {
     if (e->comm_failed) return fail(NRN_ERR_STATE, "nrn_engine_run: the communicator was aborted after an error");
     if (steps == 0) return NRN_OK;
     NRN_TRY(e->prepare_plastic());
-    if (chunk <= 0) chunk = 50;
     int64_t s = e->step, left = steps;
     if (!e->use_graphs) {
         for (; left > 0; ++s, --left) NRN_TRY(e->eager_step(s));
@@ -1469,18 +1512,10 @@ nrn_status_t nrn_engine_run(nrn_engine* e, int64_t steps, int32_t chunk) {
         // meets at most w + 3 shapes; without windows a tail shorter than a
         // chunk runs as power-of-two graphs.
         const int w = e->windows ? e->win : 1;
-        if (e->windows) chunk = std::max(w, chunk / w * w);
+        chunk = e->run_chunk(chunk);
         while (left > 0) {
             const int phase = static_cast<int>(s % w);
-            int c;
-            if (phase != 0) c = 1;
-            else if (left >= w && w > 1) c = static_cast<int>(std::min<int64_t>(chunk, left / w * w));
-            else if (w > 1) c = 1;
-            else if (left >= chunk) c = chunk;
-            else {
-                c = 1;
-                while (2 * c <= left) c *= 2;
-            }
+            const int c = e->run_piece(phase, left, chunk);
             cudaGraphExec_t g = nullptr;
             NRN_TRY(e->graph_for(c, &g, phase));
             NRN_CUDA_TRY(cudaGraphLaunch(g, e->stream));

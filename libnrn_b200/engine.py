@@ -202,6 +202,11 @@ class Network:
     def step(self) -> int:
         return int(self.L.nrn_engine_step(self.h))
 
+    def prepare(self, first_step: int, steps: int, chunk: int = 0) -> None:
+        """Captures the graphs a run of `steps` steps from `first_step` will
+        replay, without running it (nrn_engine_prepare)."""
+        N.check(self.L.nrn_engine_prepare(self.h, int(first_step), int(steps), int(chunk)), "prepare")
+
     def info(self) -> dict:
         """The window, raster capacity and recorded neuron count
         (nrn_engine_info)."""

@@ -76,3 +76,24 @@ def test_single_step_runs_equal_one_run():
     for a, b in zip(whole[2], split[2]):
         assert np.array_equal(a, b)
     assert np.array_equal(whole[3], split[3])
+
+
+def test_prepared_graphs_change_nothing():
+    # capturing a run's graphs ahead (nrn_engine_prepare) runs no step
+    net = S.realize(W.brunel(800, 200, 80, 20, stdp=True, steps=75, seed=9))
+    whole = run(net)
+    nw = Network.from_net(net, deterministic=True)
+    try:
+        step0 = nw.step
+        nw.prepare(step0, 75)
+        nw.prepare(step0 + 7, 33)
+        assert nw.step == step0
+        assert len(nw.raster()[0]) == 0
+        nw.run(75)
+        st, gid = nw.raster()
+        w = [nw.weights(q) for q in range(len(net["projs"]))]
+    finally:
+        nw.close()
+    assert np.array_equal(st, whole[0]) and np.array_equal(gid, whole[1])
+    for a, b in zip(w, whole[2]):
+        assert np.array_equal(a, b)
