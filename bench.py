@@ -579,8 +579,11 @@ def finish_network_line(args, spec, nw, world, rank, dist, all_reduce, peaks, pe
     walk_bytes = 12.0 * cnt["walk_events"] + 32.0 * arrivals
     deliver_bytes = 8.0 * cnt["static_events"] + 16.0 * segs
     neuron_bytes = 40.0 * sum(p_["n"] for p_ in nw.pops) * P
+    # the neuron update of uniform-parameter LIF populations runs four neurons
+    # a thread (lif4_group_kernel); other models run pop_group_kernel
+    neuron_kernel = "lif4_group_kernel" if all(p_["model"] == "lif" for p_ in spec["pops"]) else "pop_group_kernel"
     kern = {"walk_kernel": ("stdp_walks", walk_bytes), "deliver_kernel": ("static_delivery", deliver_bytes),
-            "lif4_group_kernel": ("neuron_update", neuron_bytes)}
+            neuron_kernel: ("neuron_update", neuron_bytes)}
     dom = max(kern, key=lambda k: prof[kern[k][0]])
     dom_ms = prof[kern[dom][0]]
     dom_bytes = kern[dom][1]
