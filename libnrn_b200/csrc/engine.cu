@@ -677,7 +677,7 @@ struct nrn_engine {
         const int w = windows ? win : 1;
         if (phase != 0) return 1;
         if (left >= w && w > 1) return static_cast<int>(std::min<int64_t>(chunk, left / w * w));
-        if (w > 1) return 1;
+        if (w > 1) return static_cast<int>(left);   // a tail shorter than a window: one graph
         if (left >= chunk) return chunk;
         int c = 1;
         while (2 * c <= left) c *= 2;
@@ -1506,11 +1506,11 @@ nrn_status_t nrn_engine_run(nrn_engine* e, int64_t steps, int32_t chunk) {
         // multiple of the window), then the rest; the graphs of each shape
         // are captured once and replayed.
         //
-        // The pieces off the window grid (the steps up to the first window
-        // boundary and a tail shorter than a window) run as one-step graphs,
-        // keyed by phase, so a caller whose runs start and stop anywhere
-        // meets at most w + 3 shapes; without windows a tail shorter than a
-        // chunk runs as power-of-two graphs.
+        // The steps up to the first window boundary run as one-step graphs,
+        // keyed by phase, and a tail shorter than a window as one graph, so a
+        // caller whose runs start and stop anywhere meets at most 2w + 2
+        // shapes; without windows a tail shorter than a chunk runs as
+        // power-of-two graphs.
         const int w = e->windows ? e->win : 1;
         chunk = e->run_chunk(chunk);
         while (left > 0) {
